@@ -1,0 +1,459 @@
+/*
+ * vb_oracle.c -- CPU oracle for the Qwen3 decode path (TEST INFRASTRUCTURE).
+ *
+ * Restates the reference engine's CPU arithmetic (verbum.cpp) in C, operation
+ * for operation; see vb_oracle.h for the contract and how it is pinned.
+ * Build flags matter for bit-exactness: -O2 -ffp-contract=off, no -ffast-math,
+ * x86-64 baseline ISA (no FMA), exactly as the reference compiles.
+ */
+#include "vb_oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static __thread char g_err[256];
+static void set_err(const char* msg) {
+    snprintf(g_err, sizeof g_err, "%s", msg);
+}
+const char* or_last_error(void) { return g_err; }
+
+void or_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+/* nn.cpp:8-42 */
+void or_rmsnorm(const float* x, const float* w, float eps, float* out,
+                int64_t rows, int64_t dim) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float* xr = x + r * dim;
+        float* orow = out + r * dim;
+        double sumsq = 0.0;
+        for (int64_t i = 0; i < dim; i++) sumsq += (double)xr[i] * (double)xr[i];
+        const float scale = 1.0f / sqrtf((float)(sumsq / (double)dim) + eps);
+        for (int64_t i = 0; i < dim; i++) orow[i] = xr[i] * scale * w[i];
+    }
+}
+
+/* nn.cpp:44-74 */
+int or_build_rope_table(int head_dim, int max_pos, float theta,
+                        float* cos_tab, float* sin_tab) {
+    if (head_dim % 2 != 0) return -1;
+    const int half = head_dim / 2;
+    for (int pos = 0; pos < max_pos; pos++) {
+        for (int i = 0; i < half; i++) {
+            const double inv_freq =
+                1.0 / pow((double)theta, (double)(2 * i) / (double)head_dim);
+            const double angle = (double)pos * inv_freq;
+            const float c = (float)cos(angle);
+            const float s = (float)sin(angle);
+            const size_t base = (size_t)pos * head_dim;
+            cos_tab[base + i] = c;
+            cos_tab[base + i + half] = c;
+            sin_tab[base + i] = s;
+            sin_tab[base + i + half] = s;
+        }
+    }
+    return 0;
+}
+
+/* nn.cpp:76-101 */
+int or_apply_rope(float* x, int64_t heads, int head_dim, int pos, int max_pos,
+                  const float* cos_tab, const float* sin_tab) {
+    if (pos < 0 || pos >= max_pos) {
+        set_err("position is outside the rope table");
+        return OR_ERR_ROPE;
+    }
+    const int half = head_dim / 2;
+    const float* c = cos_tab + (size_t)pos * head_dim;
+    const float* s = sin_tab + (size_t)pos * head_dim;
+    for (int64_t h = 0; h < heads; h++) {
+        float* row = x + h * head_dim;
+        for (int i = 0; i < half; i++) {
+            const float a = row[i];
+            const float b = row[i + half];
+            row[i] = a * c[i] - b * s[i];
+            row[i + half] = b * c[i + half] + a * s[i + half];
+        }
+    }
+    return 0;
+}
+
+/* ops.cpp:42-70; rows are independent so they may run on separate threads. */
+void or_matmul_nt(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                  int64_t K) {
+    for (int64_t i = 0; i < M; i++) {
+        const float* arow = A + i * K;
+#pragma omp parallel for schedule(static) if (N * K > (1 << 18))
+        for (int64_t j = 0; j < N; j++) {
+            const float* brow = B + j * K;
+            float sum = 0.0f;
+            for (int64_t k = 0; k < K; k++) sum += arow[k] * brow[k];
+            C[i * N + j] = sum;
+        }
+    }
+}
+
+/* quant.cpp:9-41 */
+void or_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_t* q,
+                      float* scales) {
+#pragma omp parallel for schedule(static) if (rows * cols > (1 << 18))
+    for (int64_t r = 0; r < rows; r++) {
+        const float* row = W + r * cols;
+        float amax = 0.0f;
+        for (int64_t c = 0; c < cols; c++) {
+            const float a = fabsf(row[c]);
+            if (amax < a) amax = a; /* std::max(amax, a) */
+        }
+        const float scale = (amax > 0.0f) ? amax / 127.0f : 1.0f;
+        scales[r] = scale;
+        const float inv = 1.0f / scale;
+        for (int64_t c = 0; c < cols; c++) {
+            int v = (int)lrintf(row[c] * inv);
+            if (v > 127) v = 127;
+            if (v < -127) v = -127;
+            q[r * cols + c] = (int8_t)v;
+        }
+    }
+}
+
+/* quant.cpp:43-70 */
+void or_matmul_nt_q8(const float* A, const int8_t* Bq, const float* scales,
+                     float* C, int64_t M, int64_t N, int64_t K) {
+    for (int64_t i = 0; i < M; i++) {
+        const float* arow = A + i * K;
+#pragma omp parallel for schedule(static) if (N * K > (1 << 18))
+        for (int64_t j = 0; j < N; j++) {
+            const int8_t* brow = Bq + j * K;
+            float acc = 0.0f;
+            for (int64_t k = 0; k < K; k++) acc += arow[k] * (float)brow[k];
+            C[i * N + j] = acc * scales[j];
+        }
+    }
+}
+
+/* quant.cpp:72-82 */
+void or_dequantize(const int8_t* q, const float* scales, int64_t rows,
+                   int64_t cols, float* out) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++)
+            out[r * cols + c] = (float)q[r * cols + c] * scales[r];
+}
+
+/* generate.cpp:73-105.  Heads are independent; each head's loops run in the
+ * reference's order. */
+void or_attention_decode(const float* q, const float* kcache,
+                         const float* vcache, int64_t row_stride, int H,
+                         int KVH, int D, int n, float* ctx) {
+    const int group = H / KVH;
+    const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+    memset(ctx, 0, sizeof(float) * (size_t)H * D);
+#pragma omp parallel if ((int64_t)n * H * D > (1 << 16))
+    {
+        float* scores = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+#pragma omp for schedule(static)
+        for (int h = 0; h < H; h++) {
+            const int kvh = h / group;
+            const float* qh = q + (size_t)h * D;
+            float m = -INFINITY;
+            for (int j = 0; j < n; j++) {
+                const float* kj = kcache + (size_t)j * row_stride + (size_t)kvh * D;
+                float dot = 0.0f;
+                for (int d = 0; d < D; d++) dot += qh[d] * kj[d];
+                scores[j] = dot * inv_sqrt_d;
+                m = (m < scores[j]) ? scores[j] : m; /* std::max(m, s) */
+            }
+            double sum = 0.0;
+            for (int j = 0; j < n; j++) {
+                scores[j] = expf(scores[j] - m);
+                sum += scores[j];
+            }
+            const float inv = (float)(1.0 / sum);
+            float* c = ctx + (size_t)h * D;
+            for (int j = 0; j < n; j++) {
+                const float p = scores[j] * inv;
+                const float* vj = vcache + (size_t)j * row_stride + (size_t)kvh * D;
+                for (int d = 0; d < D; d++) c[d] += p * vj[d];
+            }
+        }
+        free(scores);
+    }
+}
+
+/* model.cpp:15-18 and 44-46 */
+void or_silu_mul(float* gate, const float* up, int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        const float g = gate[i];
+        gate[i] = (g / (1.0f + expf(-g))) * up[i];
+    }
+}
+
+/* generate.cpp:199-206 */
+int or_argmax(const float* logits, int64_t vocab) {
+    int best = 0;
+    for (int64_t i = 1; i < vocab; i++)
+        if (logits[i] > logits[best]) best = (int)i;
+    return best;
+}
+
+/* ------------------------------------------------------------------------ */
+/* whole model                                                              */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    int8_t* q;
+    float* s;
+    int64_t rows, cols;
+} qt;
+
+struct or_model {
+    or_config c;
+    const float* embed;
+    const float* final_norm;
+    or_layer_weights* L;
+    int quantized;
+    qt* Q; /* [layers*7] */
+    float* rope_cos;
+    float* rope_sin;
+    /* caches */
+    int max_seq, len;
+    float** kc;
+    float** vc;
+    /* scratch */
+    float *x, *normed, *attn_out, *ffn_out, *q, *k, *v, *ctx, *gate, *up, *next;
+};
+
+static void* xcalloc(size_t n, size_t sz) {
+    void* p = calloc(n ? n : 1, sz);
+    return p;
+}
+
+or_model* or_model_create(const or_config* cfg, const float* embed,
+                          const float* final_norm,
+                          const or_layer_weights* layers) {
+    if (!cfg || !embed || !final_norm || !layers) return NULL;
+    if (cfg->heads % cfg->kv_heads != 0 || cfg->head_dim % 2 != 0) return NULL;
+    or_model* m = (or_model*)xcalloc(1, sizeof(or_model));
+    m->c = *cfg;
+    m->embed = embed;
+    m->final_norm = final_norm;
+    m->L = (or_layer_weights*)xcalloc((size_t)cfg->layers, sizeof(or_layer_weights));
+    memcpy(m->L, layers, sizeof(or_layer_weights) * (size_t)cfg->layers);
+    m->rope_cos = (float*)xcalloc((size_t)cfg->rope_positions * cfg->head_dim, sizeof(float));
+    m->rope_sin = (float*)xcalloc((size_t)cfg->rope_positions * cfg->head_dim, sizeof(float));
+    or_build_rope_table(cfg->head_dim, cfg->rope_positions, cfg->theta, m->rope_cos,
+                        m->rope_sin);
+    const size_t hd = (size_t)cfg->hidden, qd = (size_t)cfg->heads * cfg->head_dim,
+                 kd = (size_t)cfg->kv_heads * cfg->head_dim, fd = (size_t)cfg->ffn;
+    m->x = (float*)xcalloc(hd, 4);
+    m->next = (float*)xcalloc(hd, 4);
+    m->normed = (float*)xcalloc(hd, 4);
+    m->attn_out = (float*)xcalloc(hd, 4);
+    m->ffn_out = (float*)xcalloc(hd, 4);
+    m->q = (float*)xcalloc(qd, 4);
+    m->k = (float*)xcalloc(kd, 4);
+    m->v = (float*)xcalloc(kd, 4);
+    m->ctx = (float*)xcalloc(qd, 4);
+    m->gate = (float*)xcalloc(fd, 4);
+    m->up = (float*)xcalloc(fd, 4);
+    return m;
+}
+
+static void free_caches(or_model* m) {
+    if (m->kc) {
+        for (int l = 0; l < m->c.layers; l++) {
+            free(m->kc[l]);
+            free(m->vc[l]);
+        }
+        free(m->kc);
+        free(m->vc);
+    }
+    m->kc = m->vc = NULL;
+}
+
+void or_model_free(or_model* m) {
+    if (!m) return;
+    free_caches(m);
+    if (m->Q) {
+        for (int i = 0; i < m->c.layers * 7; i++) {
+            free(m->Q[i].q);
+            free(m->Q[i].s);
+        }
+        free(m->Q);
+    }
+    free(m->L);
+    free(m->rope_cos);
+    free(m->rope_sin);
+    free(m->x); free(m->next); free(m->normed); free(m->attn_out); free(m->ffn_out);
+    free(m->q); free(m->k); free(m->v); free(m->ctx); free(m->gate); free(m->up);
+    free(m);
+}
+
+static const float* proj_ptr(const or_layer_weights* L, int which) {
+    switch (which) {
+        case 0: return L->wq; case 1: return L->wk; case 2: return L->wv;
+        case 3: return L->wo; case 4: return L->wg; case 5: return L->wu;
+        default: return L->wd;
+    }
+}
+
+static void proj_shape(const or_config* c, int which, int64_t* rows, int64_t* cols) {
+    const int64_t qd = (int64_t)c->heads * c->head_dim, kd = (int64_t)c->kv_heads * c->head_dim;
+    switch (which) {
+        case 0: *rows = qd; *cols = c->hidden; break;
+        case 1: case 2: *rows = kd; *cols = c->hidden; break;
+        case 3: *rows = c->hidden; *cols = qd; break;
+        case 4: case 5: *rows = c->ffn; *cols = c->hidden; break;
+        default: *rows = c->hidden; *cols = c->ffn; break;
+    }
+}
+
+/* model.cpp:313-338 */
+int or_model_quantize(or_model* m) {
+    if (m->quantized) return 0;
+    m->Q = (qt*)xcalloc((size_t)m->c.layers * 7, sizeof(qt));
+    for (int l = 0; l < m->c.layers; l++) {
+        for (int w = 0; w < 7; w++) {
+            qt* t = &m->Q[l * 7 + w];
+            proj_shape(&m->c, w, &t->rows, &t->cols);
+            t->q = (int8_t*)xcalloc((size_t)(t->rows * t->cols), 1);
+            t->s = (float*)xcalloc((size_t)t->rows, 4);
+            if (!t->q || !t->s) { set_err("out of memory"); return OR_ERR_OOM; }
+            or_quantize_rows(proj_ptr(&m->L[l], w), t->rows, t->cols, t->q, t->s);
+        }
+    }
+    m->quantized = 1;
+    return 0;
+}
+
+int or_model_is_quantized(const or_model* m) { return m->quantized; }
+
+int or_model_quant_tensor(const or_model* m, int layer, int which,
+                          const int8_t** q, const float** scales, int64_t* rows,
+                          int64_t* cols) {
+    if (!m->quantized || layer < 0 || layer >= m->c.layers || which < 0 || which > 6)
+        return OR_ERR_ARG;
+    const qt* t = &m->Q[layer * 7 + which];
+    *q = t->q; *scales = t->s; *rows = t->rows; *cols = t->cols;
+    return 0;
+}
+
+/* model.cpp:277-282, generate.cpp:14-22 */
+int or_model_reset_cache(or_model* m, int max_seq) {
+    if (max_seq <= 0) return OR_ERR_ARG;
+    free_caches(m);
+    const size_t n = (size_t)max_seq * m->c.kv_heads * m->c.head_dim;
+    m->kc = (float**)xcalloc((size_t)m->c.layers, sizeof(float*));
+    m->vc = (float**)xcalloc((size_t)m->c.layers, sizeof(float*));
+    for (int l = 0; l < m->c.layers; l++) {
+        m->kc[l] = (float*)xcalloc(n, 4);
+        m->vc[l] = (float*)xcalloc(n, 4);
+        if (!m->kc[l] || !m->vc[l]) { set_err("out of memory"); return OR_ERR_OOM; }
+    }
+    m->max_seq = max_seq;
+    m->len = 0;
+    return 0;
+}
+
+int or_model_cache_len(const or_model* m) { return m->len; }
+
+const float* or_model_kv(const or_model* m, int layer, int which) {
+    if (!m->kc || layer < 0 || layer >= m->c.layers) return NULL;
+    return which == 0 ? m->kc[layer] : m->vc[layer];
+}
+
+static void proj(const or_model* m, int l, int which, const float* x, float* y) {
+    int64_t rows, cols;
+    proj_shape(&m->c, which, &rows, &cols);
+    if (m->quantized) {
+        const qt* t = &m->Q[l * 7 + which];
+        or_matmul_nt_q8(x, t->q, t->s, y, 1, rows, cols);
+    } else {
+        or_matmul_nt(x, proj_ptr(&m->L[l], which), y, 1, rows, cols);
+    }
+}
+
+/* generate.cpp:24-108 (f32) and 110-195 (int8); the cache-full and rope
+ * checks run before anything is written, so an error leaves the model as it
+ * was. */
+static int attention_step(or_model* m, int l, const float* x, float* out, int pos) {
+    const or_config* c = &m->c;
+    const int H = c->heads, KVH = c->kv_heads, D = c->head_dim;
+    const or_layer_weights* L = &m->L[l];
+    proj(m, l, 0, x, m->q);
+    proj(m, l, 1, x, m->k);
+    proj(m, l, 2, x, m->v);
+    /* per-head q/k rmsnorm (generate.cpp:52-64): in place is equivalent to the
+     * reference's tmp copies since each head only reads itself */
+    or_rmsnorm(m->q, L->q_norm, c->eps, m->q, H, D);
+    int rc = or_apply_rope(m->q, H, D, pos, c->rope_positions, m->rope_cos, m->rope_sin);
+    if (rc) return rc;
+    or_rmsnorm(m->k, L->k_norm, c->eps, m->k, KVH, D);
+    rc = or_apply_rope(m->k, KVH, D, pos, c->rope_positions, m->rope_cos, m->rope_sin);
+    if (rc) return rc;
+    const size_t w = (size_t)KVH * D;
+    memcpy(m->kc[l] + (size_t)pos * w, m->k, w * 4);
+    memcpy(m->vc[l] + (size_t)pos * w, m->v, w * 4);
+    or_attention_decode(m->q, m->kc[l], m->vc[l], (int64_t)w, H, KVH, D, pos + 1, m->ctx);
+    proj(m, l, 3, m->ctx, out);
+    return 0;
+}
+
+/* model.cpp:284-311 with layer_step (235-254) / layer_step_q (256-275) */
+int or_model_step(or_model* m, int token, float* logits) {
+    const or_config* c = &m->c;
+    if (!m->kc) { set_err("call reset_cache() first"); return OR_ERR_NO_CACHE; }
+    if (token < 0 || token >= c->vocab) {
+        set_err("token id out of range for the embedding table");
+        return OR_ERR_TOKEN;
+    }
+    if (m->len >= m->max_seq) { set_err("kv cache is full"); return OR_ERR_CACHE_FULL; }
+    if (m->len >= c->rope_positions) {
+        set_err("position is outside the rope table");
+        return OR_ERR_ROPE;
+    }
+    const int64_t hd = c->hidden;
+    const int pos = m->len;
+    memcpy(m->x, m->embed + (size_t)token * hd, (size_t)hd * 4);
+    for (int l = 0; l < c->layers; l++) {
+        const or_layer_weights* L = &m->L[l];
+        or_rmsnorm(m->x, L->input_norm, c->eps, m->normed, 1, hd);
+        int rc = attention_step(m, l, m->normed, m->attn_out, pos);
+        if (rc) return rc;
+        for (int64_t i = 0; i < hd; i++) m->next[i] = m->x[i] + m->attn_out[i];
+        or_rmsnorm(m->next, L->post_norm, c->eps, m->normed, 1, hd);
+        proj(m, l, 4, m->normed, m->gate);
+        proj(m, l, 5, m->normed, m->up);
+        or_silu_mul(m->gate, m->up, c->ffn);
+        proj(m, l, 6, m->gate, m->ffn_out);
+        for (int64_t i = 0; i < hd; i++) m->next[i] += m->ffn_out[i];
+        memcpy(m->x, m->next, (size_t)hd * 4);
+    }
+    m->len++;
+    or_rmsnorm(m->x, m->final_norm, c->eps, m->normed, 1, hd);
+    or_matmul_nt(m->normed, m->embed, logits, 1, c->vocab, hd);
+    return 0;
+}
+
+/* model.cpp:340-365 (tied embeddings: lm_head_ is empty) */
+size_t or_model_weight_bytes(const or_model* m) {
+    const or_config* c = &m->c;
+    size_t total = (size_t)c->vocab * c->hidden * 4 + (size_t)c->hidden * 4;
+    for (int l = 0; l < c->layers; l++) {
+        total += (size_t)(2 * c->hidden + 2 * c->head_dim) * 4;
+        for (int w = 0; w < 7; w++) {
+            int64_t r, cc;
+            proj_shape(c, w, &r, &cc);
+            total += m->quantized ? (size_t)(r * cc) + (size_t)r * 4 : (size_t)(r * cc) * 4;
+        }
+    }
+    return total;
+}

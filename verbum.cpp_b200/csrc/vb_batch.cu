@@ -1,0 +1,344 @@
+// vb_batch.cu -- batched independent-sequence decode: B sequences share one
+// engine's weights (read once per step for all B rows) and each owns a KV
+// cache.  Per layer: rmsnorm rows -> QKV GEMM -> q/k norm + RoPE + append ->
+// split-K attention over B caches -> o GEMM + residual -> rmsnorm -> gate/up
+// GEMM + SwiGLU -> down GEMM + residual; then final norm -> lm_head GEMM ->
+// per-row argmax.  The step is graph-captured and replayed.
+#include <string>
+
+#include "vb_engine.cuh"
+
+struct vb_batch {
+    vb_engine* e = nullptr;
+    int B = 0;
+    int max_seq = 0;
+    int len = 0;
+    float* kc = nullptr;
+    float* vc = nullptr;
+    float* x = nullptr;
+    float* xn = nullptr;
+    float* qkv = nullptr;
+    float* q = nullptr;
+    float* ctx = nullptr;
+    float* h = nullptr;
+    float* logits = nullptr;
+    float* attn_ws = nullptr;
+    int attn_splits = 1;
+    float* gemm_ws = nullptr;
+    size_t gemm_ws_floats = 0;
+    int* d_tok = nullptr;
+    int* d_pos = nullptr;
+    int* d_next = nullptr;
+    int* d_err = nullptr;
+    int* h_io = nullptr;  // pinned [2*B]
+    cudaGraphExec_t graph = nullptr;
+    bool graph_q8 = false;
+};
+
+namespace vb {
+namespace {
+
+template <class T>
+vb_status balloc(T** p, size_t count, const char* what) {
+    *p = nullptr;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), (count ? count : 1) * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return VB_OK;
+}
+template <class T>
+void bfree(T*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
+    vb_engine* e = b->e;
+    const vb_config& c = e->cfg;
+    const bool q8 = e->quantized;
+    const int B = b->B;
+    vb_status st;
+    if ((st = launch_embed(e->embed, b->d_tok, B, c.hidden, c.vocab, b->x, b->d_err, s))) return st;
+    const size_t per_seq = (size_t)c.kv_heads * b->max_seq * c.head_dim;
+    const size_t layer_kv = per_seq * B;
+    auto gemm = [&](const float* A, const void* W, const float* sc, float* C, int N, int K,
+                    int ldc, int epi, bool wq8) {
+        GemmArgs g{};
+        g.A = A;
+        g.W = W;
+        g.scales = sc;
+        g.C = C;
+        g.M = B;
+        g.N = N;
+        g.K = K;
+        g.ldc = ldc;
+        g.ws = b->gemm_ws;
+        g.ws_floats = b->gemm_ws_floats;
+        return launch_gemm(g, wq8, epi, s);
+    };
+    for (int l = 0; l < c.layers; l++) {
+        const vb_layer_dev& L = e->L[l];
+        if ((st = launch_rmsnorm_rows(b->x, L.in_norm, b->xn, B, c.hidden, c.eps, s))) return st;
+        if ((st = gemm(b->xn, q8 ? (const void*)L.qqkv : (const void*)L.wqkv, L.sqkv, b->qkv,
+                       e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8)))
+            return st;
+        QkNormArgs qa{};
+        qa.qkv = b->qkv;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.cos_tab = e->rope_cos;
+        qa.sin_tab = e->rope_sin;
+        qa.pos = b->d_pos;
+        qa.q_out = b->q;
+        qa.kc = b->kc + l * layer_kv;
+        qa.vc = b->vc + l * layer_kv;
+        qa.stride_b = (int64_t)per_seq;
+        qa.stride_pos = c.head_dim;
+        qa.stride_h = (int64_t)b->max_seq * c.head_dim;
+        qa.B = B;
+        qa.H = c.heads;
+        qa.KVH = c.kv_heads;
+        qa.D = c.head_dim;
+        qa.rope_positions = c.rope_positions < b->max_seq ? c.rope_positions : b->max_seq;
+        qa.eps = c.eps;
+        qa.err = b->d_err;
+        if ((st = launch_qk_norm_rope_append(qa, s))) return st;
+        AttnArgs aa{};
+        aa.q = b->q;
+        aa.k = qa.kc;
+        aa.v = qa.vc;
+        aa.out = b->ctx;
+        aa.pos = b->d_pos;
+        aa.B = B;
+        aa.H = c.heads;
+        aa.KVH = c.kv_heads;
+        aa.D = c.head_dim;
+        aa.n_max = b->max_seq;
+        aa.stride_b = qa.stride_b;
+        aa.stride_pos = qa.stride_pos;
+        aa.stride_h = qa.stride_h;
+        aa.splits = b->attn_splits;
+        aa.ws = b->attn_ws;
+        if ((st = launch_attention(aa, s))) return st;
+        if ((st = gemm(b->ctx, q8 ? (const void*)L.qo : (const void*)L.wo, L.so, b->x, c.hidden,
+                       e->q_width, c.hidden, kEpiResidual, q8)))
+            return st;
+        if ((st = launch_rmsnorm_rows(b->x, L.post_norm, b->xn, B, c.hidden, c.eps, s))) return st;
+        if ((st = gemm(b->xn, q8 ? (const void*)L.qgu : (const void*)L.wgu, L.sgu, b->h,
+                       2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8)))
+            return st;
+        if ((st = gemm(b->h, q8 ? (const void*)L.qd : (const void*)L.wd, L.sd, b->x, c.hidden,
+                       c.ffn, c.hidden, kEpiResidual, q8)))
+            return st;
+    }
+    if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, c.hidden, c.eps, s))) return st;
+    if ((st = gemm(b->xn, e->embed, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore,
+                   false)))
+        return st;
+    if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
+    return launch_advance(b->d_pos, b->d_tok, b->d_next, B, s);
+}
+
+vb_status batch_graph(vb_batch* b) {
+    if (b->graph && b->graph_q8 == b->e->quantized) return VB_OK;
+    if (b->graph) cudaGraphExecDestroy(b->graph);
+    b->graph = nullptr;
+    cudaStream_t s = b->e->stream;
+    cudaGraph_t g = nullptr;
+    VB_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    vb_status st = enqueue_batch_step(b, s);
+    cudaError_t ce = cudaStreamEndCapture(s, &g);
+    if (st) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    ce = cudaGraphInstantiate(&b->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+        b->graph = nullptr;
+        return cuda_fail(ce, "cudaGraphInstantiate");
+    }
+    b->graph_q8 = b->e->quantized;
+    return VB_OK;
+}
+
+vb_status batch_check_err(vb_batch* b) {
+    int err = 0;
+    VB_CUDA_TRY(cudaMemcpy(&err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!err) return VB_OK;
+    cudaMemset(b->d_err, 0, sizeof(int));
+    if (err == kErrBadToken) return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    if (err == kErrCacheFull) return fail(VB_ERR_CACHE_FULL, "kv cache is full");
+    return fail(VB_ERR_CUDA, "device error word set: " + std::to_string(err));
+}
+
+struct Dev {
+    int prev = -1;
+    explicit Dev(int d) {
+        cudaGetDevice(&prev);
+        if (prev != d) cudaSetDevice(d);
+    }
+    ~Dev() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" {
+
+vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) {
+    if (!e || !out) return fail(VB_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (batch <= 0 || batch > 64) return fail(VB_ERR_UNSUPPORTED, "batch must be 1..64");
+    if (max_seq <= 0) return fail(VB_ERR_ARG, "max_seq must be positive");
+    Dev dg(e->device);
+    const vb_config& c = e->cfg;
+    vb_batch* b = new vb_batch();
+    b->e = e;
+    b->B = batch;
+    b->max_seq = max_seq;
+    auto bail = [&](vb_status s) {
+        vb_batch_destroy(b);
+        return s;
+    };
+    const size_t kvn = (size_t)c.layers * batch * c.kv_heads * max_seq * c.head_dim;
+    vb_status st;
+    if ((st = balloc(&b->kc, kvn, "batch kv cache"))) return bail(st);
+    if ((st = balloc(&b->vc, kvn, "batch kv cache"))) return bail(st);
+    if (cudaMemset(b->kc, 0, kvn * 4) || cudaMemset(b->vc, 0, kvn * 4))
+        return bail(fail(VB_ERR_CUDA, "kv cache memset failed"));
+    if ((st = balloc(&b->x, (size_t)batch * c.hidden, "x"))) return bail(st);
+    if ((st = balloc(&b->xn, (size_t)batch * c.hidden, "xn"))) return bail(st);
+    if ((st = balloc(&b->qkv, (size_t)batch * e->qkv_rows, "qkv"))) return bail(st);
+    if ((st = balloc(&b->q, (size_t)batch * e->q_width, "q"))) return bail(st);
+    if ((st = balloc(&b->ctx, (size_t)batch * e->q_width, "ctx"))) return bail(st);
+    if ((st = balloc(&b->h, (size_t)batch * c.ffn, "h"))) return bail(st);
+    if ((st = balloc(&b->logits, (size_t)batch * c.vocab, "logits"))) return bail(st);
+    b->attn_splits = attn_splits_for(batch, c.kv_heads, max_seq);
+    if ((st = balloc(&b->attn_ws, attn_ws_bytes(batch, c.heads, b->attn_splits) / 4 + 1, "attn ws")))
+        return bail(st);
+    size_t ws = 0;
+    auto upd = [&](int N, int K, bool q8) {
+        const size_t w = gemm_ws_floats(batch, N, K, q8);
+        if (w > ws) ws = w;
+    };
+    for (int q8 = 0; q8 < 2; q8++) {
+        upd(e->qkv_rows, c.hidden, q8);
+        upd(c.hidden, e->q_width, q8);
+        upd(2 * c.ffn, c.hidden, q8);
+        upd(c.hidden, c.ffn, q8);
+    }
+    upd(c.vocab, c.hidden, false);
+    b->gemm_ws_floats = ws;
+    if ((st = balloc(&b->gemm_ws, ws, "gemm ws"))) return bail(st);
+    if ((st = balloc(&b->d_tok, batch, "tok"))) return bail(st);
+    if ((st = balloc(&b->d_pos, batch, "pos"))) return bail(st);
+    if ((st = balloc(&b->d_next, batch, "next"))) return bail(st);
+    if ((st = balloc(&b->d_err, 1, "err"))) return bail(st);
+    cudaMemset(b->d_pos, 0, sizeof(int) * batch);
+    cudaMemset(b->d_tok, 0, sizeof(int) * batch);
+    cudaMemset(b->d_err, 0, sizeof(int));
+    if (cudaMallocHost(&b->h_io, sizeof(int) * 2 * batch) != cudaSuccess)
+        return bail(fail(VB_ERR_CUDA, "cudaMallocHost failed"));
+    *out = b;
+    return VB_OK;
+}
+
+vb_status vb_batch_destroy(vb_batch* b) {
+    if (!b) return VB_OK;
+    Dev dg(b->e->device);
+    cudaStreamSynchronize(b->e->stream);
+    if (b->graph) cudaGraphExecDestroy(b->graph);
+    bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->qkv); bfree(b->q);
+    bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
+    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err);
+    if (b->h_io) cudaFreeHost(b->h_io);
+    delete b;
+    return VB_OK;
+}
+
+static vb_status batch_pre(vb_batch* b, int n) {
+    vb_engine* e = b->e;
+    if (!e->globals_set) return fail(VB_ERR_STATE, "engine weights not uploaded");
+    for (int l = 0; l < e->cfg.layers; l++)
+        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "layer not uploaded");
+    if (b->len + n > b->max_seq) return fail(VB_ERR_CACHE_FULL, "kv cache is full");
+    if (b->len + n > e->cfg.rope_positions)
+        return fail(VB_ERR_ROPE, "position is outside the rope table");
+    return batch_graph(b);
+}
+
+vb_status vb_batch_step(vb_batch* b, const int* tokens_host, float* logits_host, int* next_host) {
+    if (!b || !tokens_host) return fail(VB_ERR_ARG, "null argument");
+    Dev dg(b->e->device);
+    vb_status st = batch_pre(b, 1);
+    if (st) return st;
+    for (int i = 0; i < b->B; i++) {
+        if (tokens_host[i] < 0 || tokens_host[i] >= b->e->cfg.vocab)
+            return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+        b->h_io[i] = tokens_host[i];
+    }
+    cudaStream_t s = b->e->stream;
+    VB_CUDA_TRY(cudaMemcpyAsync(b->d_tok, b->h_io, sizeof(int) * b->B, cudaMemcpyHostToDevice, s));
+    VB_CUDA_TRY(cudaGraphLaunch(b->graph, s));
+    if (logits_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(logits_host, b->logits, sizeof(float) * b->B * b->e->cfg.vocab,
+                                    cudaMemcpyDeviceToHost, s));
+    if (next_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
+                                    cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    if ((st = batch_check_err(b))) return st;
+    if (next_host)
+        for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
+    b->len += 1;
+    return VB_OK;
+}
+
+vb_status vb_batch_decode(vb_batch* b, const int* tokens_host, int n, int* next_host) {
+    if (!b) return fail(VB_ERR_ARG, "null batch");
+    if (n <= 0) return VB_OK;
+    Dev dg(b->e->device);
+    vb_status st = batch_pre(b, n);
+    if (st) return st;
+    cudaStream_t s = b->e->stream;
+    if (tokens_host) {
+        for (int i = 0; i < b->B; i++) {
+            if (tokens_host[i] < 0 || tokens_host[i] >= b->e->cfg.vocab)
+                return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+            b->h_io[i] = tokens_host[i];
+        }
+        VB_CUDA_TRY(cudaMemcpyAsync(b->d_tok, b->h_io, sizeof(int) * b->B, cudaMemcpyHostToDevice, s));
+    }
+    for (int i = 0; i < n; i++) VB_CUDA_TRY(cudaGraphLaunch(b->graph, s));
+    if (next_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
+                                    cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    if ((st = batch_check_err(b))) return st;
+    if (next_host)
+        for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
+    b->len += n;
+    return VB_OK;
+}
+
+int vb_batch_cache_len(const vb_batch* b) { return b ? b->len : 0; }
+
+vb_status vb_batch_reset(vb_batch* b) {
+    if (!b) return fail(VB_ERR_ARG, "null batch");
+    Dev dg(b->e->device);
+    cudaStreamSynchronize(b->e->stream);
+    const vb_config& c = b->e->cfg;
+    const size_t kvn = (size_t)c.layers * b->B * c.kv_heads * b->max_seq * c.head_dim;
+    VB_CUDA_TRY(cudaMemset(b->kc, 0, kvn * 4));
+    VB_CUDA_TRY(cudaMemset(b->vc, 0, kvn * 4));
+    VB_CUDA_TRY(cudaMemset(b->d_pos, 0, sizeof(int) * b->B));
+    b->len = 0;
+    return VB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,131 @@
+// vb_common.cuh -- shared device/host helpers for the sm_100a decode kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "verbum_b200.h"
+
+namespace vb {
+
+// ---------------------------------------------------------------------------
+// host-side error plumbing: every C-ABI call returns a vb_status; the message
+// of the last failure on the calling thread is kept for vb_last_error().
+// ---------------------------------------------------------------------------
+void set_error(const std::string& msg);
+vb_status fail(vb_status code, const std::string& msg);
+vb_status cuda_fail(cudaError_t e, const char* what);
+
+#define VB_CUDA_TRY(expr)                                         \
+    do {                                                          \
+        cudaError_t _e = (expr);                                  \
+        if (_e != cudaSuccess) return ::vb::cuda_fail(_e, #expr); \
+    } while (0)
+
+#define VB_LAUNCH_CHECK(what)                                     \
+    do {                                                          \
+        cudaError_t _e = cudaGetLastError();                      \
+        if (_e != cudaSuccess) return ::vb::cuda_fail(_e, what);  \
+    } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming 16-byte global load that does not allocate in L1 (weights and KV
+// rows are touched exactly once per step).
+__device__ __forceinline__ float4 ld_stream_f4(const void* p) {
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Exact int8 -> f32 for the four signed bytes of `w` without I2F.
+// Each biased byte u = b + 128 is dropped into the low mantissa bits of
+// 2^23 (bit pattern 0x4B000000), giving the float 2^23 + u exactly; one
+// subtraction of 2^23 + 128 then leaves b exactly.  This is the standard
+// "magic number" integer-to-float construction (IEEE-754 binary32 has a
+// 23-bit mantissa, so every integer below 2^24 is representable).
+struct f4 {
+    float v[4];
+};
+__device__ __forceinline__ f4 i8x4_to_f32(uint32_t w) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float bias = 8388736.0f;  // 2^23 + 128
+    f4 r;
+    r.v[0] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - bias;
+    r.v[1] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - bias;
+    r.v[2] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - bias;
+    r.v[3] = __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - bias;
+    return r;
+}
+
+// Block-wide double sum for blockDim.x == NT (multiple of 32). `red` holds
+// NT/32 doubles. Every thread gets the total.
+template <int NT>
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+    v = warp_sum_d(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < NT / 32; i++) t += red[i];
+    __syncthreads();
+    return t;
+}
+
+// RMSNorm scale exactly as the reference computes it (nn.cpp:31-34):
+// double sum of squares -> float mean + eps -> 1/sqrt in float.
+__device__ __forceinline__ float rms_scale(double sumsq, int dim, float eps) {
+    const float mean = (float)(sumsq / (double)dim);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// ---------------------------------------------------------------------------
+// device-side error word: bounded waits record where they gave up instead of
+// spinning forever; the host reads it after the step.
+// ---------------------------------------------------------------------------
+enum : int {
+    kErrNone = 0,
+    kErrBarrierTimeout = 1,
+    kErrPipeTimeout = 2,
+    kErrBadToken = 3,
+    kErrCacheFull = 4,
+};
+
+}  // namespace vb

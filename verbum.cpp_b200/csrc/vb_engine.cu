@@ -1,0 +1,583 @@
+// vb_engine.cu -- batch-1 decode engine: weights, KV cache and scratch in
+// HBM; one step = embedding -> L x (fused-norm QKV GEMV, q/k norm + RoPE + KV
+// append, split-K attention, o_proj + residual, fused-norm gate/up + SwiGLU,
+// down + residual) -> fused-norm lm_head with argmax partials -> argmax.
+// The step reads its token and position from device memory, so the whole
+// step is captured once in a CUDA graph and replayed; greedy decode feeds
+// each argmax back on the device with no host round trip.
+//
+// Mirrors verbum::Model (core/include/verbum/model.h:47-116): to_cuda
+// (model.cpp:367-443), reset_cache (277-282), step / step_cuda (284-311,
+// 446-497), quantize (313-338), weight_bytes (340-365).
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+
+#include "vb_engine.cuh"
+
+namespace vb {
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <class T>
+vb_status dalloc(T** p, size_t count, const char* what) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return VB_OK;
+}
+
+template <class T>
+void dfree(T*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+// pos += 1, token = pick, history[step++] = pick  (single thread).
+__global__ void engine_advance_kernel(int* pos, int* tok, const int* next, int* hist,
+                                      int* step, int hist_cap) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        const int t = *next;
+        *pos += 1;
+        *tok = t;
+        const int s = *step;
+        if (s >= 0 && s < hist_cap) hist[s] = t;
+        *step = s + 1;
+    }
+}
+
+void free_cache(vb_engine* e) {
+    dfree(e->kc);
+    dfree(e->vc);
+    dfree(e->attn_ws);
+    dfree(e->d_hist);
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    e->graph = nullptr;
+}
+
+}  // namespace
+
+void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s) {
+    // nn.cpp:44-74: inv_freq = 1 / theta^(2i/D) in double, angle in double,
+    // cos/sin rounded to float, the same value stored for i and i + D/2.
+    const int half = head_dim / 2;
+    for (int pos = 0; pos < max_pos; pos++) {
+        for (int i = 0; i < half; i++) {
+            const double inv_freq =
+                1.0 / std::pow((double)theta, (double)(2 * i) / (double)head_dim);
+            const double angle = (double)pos * inv_freq;
+            const float cv = (float)std::cos(angle);
+            const float sv = (float)std::sin(angle);
+            const size_t b = (size_t)pos * head_dim;
+            c[b + i] = cv;
+            c[b + i + half] = cv;
+            s[b + i] = sv;
+            s[b + i + half] = sv;
+        }
+    }
+}
+
+vb_status engine_check_err(vb_engine* e) {
+    int err = 0;
+    VB_CUDA_TRY(cudaMemcpy(&err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err == kErrNone) return VB_OK;
+    cudaMemset(e->d_err, 0, sizeof(int));
+    switch (err) {
+        case kErrBadToken:
+            return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+        case kErrCacheFull: return fail(VB_ERR_CACHE_FULL, "kv cache is full");
+        case kErrBarrierTimeout:
+        case kErrPipeTimeout:
+            return fail(VB_ERR_TIMEOUT, "a bounded device wait timed out in the fused step");
+        default: return fail(VB_ERR_CUDA, "device error word set: " + std::to_string(err));
+    }
+}
+
+vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
+    const vb_config& c = e->cfg;
+    const bool q8 = e->quantized;
+    vb_status st;
+    if ((st = launch_embed(e->embed, e->d_tok, 1, c.hidden, c.vocab, e->x, e->d_err, s))) return st;
+    const size_t layer_kv = (size_t)c.kv_heads * e->max_seq * c.head_dim;
+    for (int l = 0; l < c.layers; l++) {
+        const vb_layer_dev& L = e->L[l];
+        GemvArgs g{};
+        g.x = e->x;
+        g.norm_w = L.in_norm;
+        g.eps = c.eps;
+        g.W = q8 ? (const void*)L.qqkv : (const void*)L.wqkv;
+        g.scales = L.sqkv;
+        g.y = e->qkv;
+        g.N = e->qkv_rows;
+        g.K = c.hidden;
+        if ((st = launch_gemv(g, q8, kProRms, kEpiStore, s))) return st;
+
+        QkNormArgs qa{};
+        qa.qkv = e->qkv;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.cos_tab = e->rope_cos;
+        qa.sin_tab = e->rope_sin;
+        qa.pos = e->d_pos;
+        qa.q_out = e->q;
+        qa.kc = e->kc + l * layer_kv;
+        qa.vc = e->vc + l * layer_kv;
+        qa.stride_b = (int64_t)layer_kv;
+        qa.stride_pos = c.head_dim;
+        qa.stride_h = (int64_t)e->max_seq * c.head_dim;
+        qa.B = 1;
+        qa.H = c.heads;
+        qa.KVH = c.kv_heads;
+        qa.D = c.head_dim;
+        qa.rope_positions = std::min(c.rope_positions, e->max_seq);
+        qa.eps = c.eps;
+        qa.err = e->d_err;
+        if ((st = launch_qk_norm_rope_append(qa, s))) return st;
+
+        AttnArgs aa{};
+        aa.q = e->q;
+        aa.k = qa.kc;
+        aa.v = qa.vc;
+        aa.out = e->ctx;
+        aa.lens = nullptr;
+        aa.pos = e->d_pos;
+        aa.B = 1;
+        aa.H = c.heads;
+        aa.KVH = c.kv_heads;
+        aa.D = c.head_dim;
+        aa.n_max = e->max_seq;
+        aa.stride_b = qa.stride_b;
+        aa.stride_pos = qa.stride_pos;
+        aa.stride_h = qa.stride_h;
+        aa.splits = e->attn_splits;
+        aa.ws = e->attn_ws;
+        if ((st = launch_attention(aa, s))) return st;
+
+        GemvArgs o{};
+        o.x = e->ctx;
+        o.W = q8 ? (const void*)L.qo : (const void*)L.wo;
+        o.scales = L.so;
+        o.y = e->x;
+        o.N = c.hidden;
+        o.K = e->q_width;
+        if ((st = launch_gemv(o, q8, kProNone, kEpiResidual, s))) return st;
+
+        GemvArgs gu{};
+        gu.x = e->x;
+        gu.norm_w = L.post_norm;
+        gu.eps = c.eps;
+        gu.W = q8 ? (const void*)L.qgu : (const void*)L.wgu;
+        gu.scales = L.sgu;
+        gu.y = e->h;
+        gu.N = 2 * c.ffn;
+        gu.K = c.hidden;
+        if ((st = launch_gemv(gu, q8, kProRms, kEpiSwiGLU, s))) return st;
+
+        GemvArgs dn{};
+        dn.x = e->h;
+        dn.W = q8 ? (const void*)L.qd : (const void*)L.wd;
+        dn.scales = L.sd;
+        dn.y = e->x;
+        dn.N = c.hidden;
+        dn.K = c.ffn;
+        if ((st = launch_gemv(dn, q8, kProNone, kEpiResidual, s))) return st;
+    }
+    GemvArgs lm{};
+    lm.x = e->x;
+    lm.norm_w = e->final_norm;
+    lm.eps = c.eps;
+    lm.W = e->embed;
+    lm.y = e->logits;
+    lm.N = c.vocab;
+    lm.K = c.hidden;
+    lm.part_val = e->part_val;
+    lm.part_idx = e->part_idx;
+    int parts = 0;
+    if ((st = launch_gemv(lm, false, kProRms, kEpiArgmax, s, &parts))) return st;
+    if ((st = launch_argmax_parts(e->part_val, e->part_idx, parts, e->d_next, s))) return st;
+    engine_advance_kernel<<<1, 32, 0, s>>>(e->d_pos, e->d_tok, e->d_next, e->d_hist, e->d_step,
+                                           e->max_seq);
+    VB_LAUNCH_CHECK("engine_advance_kernel");
+    return VB_OK;
+}
+
+static vb_status ensure_graph(vb_engine* e) {
+    if (e->graph) return VB_OK;
+    cudaGraph_t g = nullptr;
+    VB_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    vb_status st = (e->path == 0 && e->mega) ? mega_enqueue_step(e, e->stream)
+                                             : enqueue_step_ops(e, e->stream);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    ce = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+        e->graph = nullptr;
+        return cuda_fail(ce, "cudaGraphInstantiate");
+    }
+    return VB_OK;
+}
+
+static vb_status check_ready(vb_engine* e) {
+    if (!e->globals_set) return fail(VB_ERR_STATE, "engine weights not uploaded (set_globals)");
+    for (int l = 0; l < e->cfg.layers; l++)
+        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "layer " + std::to_string(l) + " not uploaded");
+    if (!e->kc) return fail(VB_ERR_NO_CACHE, "call reset_cache() first");
+    return VB_OK;
+}
+
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" {
+
+vb_status vb_engine_create(const vb_config* cfg, int device, vb_engine** out) {
+    if (!cfg || !out) return fail(VB_ERR_ARG, "null argument");
+    *out = nullptr;
+    const vb_config& c = *cfg;
+    if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.ffn <= 0 ||
+        c.vocab <= 0 || c.rope_positions <= 0)
+        return fail(VB_ERR_ARG, "config has a non-positive dimension");
+    if (c.head_dim != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (c.heads % c.kv_heads) return fail(VB_ERR_ARG, "attention heads must be a multiple of kv heads");
+    const int G = c.heads / c.kv_heads;
+    if (G != 1 && G != 2 && G != 4) return fail(VB_ERR_UNSUPPORTED, "GQA group must be 1, 2 or 4");
+    if (c.hidden % 32 || c.ffn % 32) return fail(VB_ERR_UNSUPPORTED, "hidden and ffn must be multiples of 32");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(VB_ERR_CUDA, "no CUDA device found");
+    if (device < 0 || device >= ndev) return fail(VB_ERR_ARG, "device index out of range");
+    DeviceGuard dg(device);
+
+    vb_engine* e = new vb_engine();
+    e->cfg = c;
+    e->device = device;
+    e->qkv_rows = (c.heads + 2 * c.kv_heads) * c.head_dim;
+    e->q_width = c.heads * c.head_dim;
+    e->kv_width = c.kv_heads * c.head_dim;
+    const size_t hd = c.hidden;
+    e->per_layer_f32 = (size_t)e->qkv_rows * hd + hd * e->q_width + 2 * (size_t)c.ffn * hd +
+                       hd * (size_t)c.ffn;
+    e->per_layer_i8 = e->per_layer_f32;
+    e->per_layer_rows = (size_t)e->qkv_rows + hd + 2 * (size_t)c.ffn + hd;
+    e->L.resize(c.layers);
+    e->layer_set.assign(c.layers, 0);
+
+    vb_status st = VB_OK;
+    auto bail = [&](vb_status s) {
+        vb_engine_destroy(e);
+        return s;
+    };
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(VB_ERR_CUDA, "cudaStreamCreate failed"));
+    if ((st = dalloc(&e->embed, (size_t)c.vocab * hd, "embed"))) return bail(st);
+    if ((st = dalloc(&e->final_norm, hd, "final_norm"))) return bail(st);
+    const size_t rope_n = (size_t)c.rope_positions * c.head_dim;
+    if ((st = dalloc(&e->rope_cos, rope_n, "rope"))) return bail(st);
+    if ((st = dalloc(&e->rope_sin, rope_n, "rope"))) return bail(st);
+    {
+        std::vector<float> hc(rope_n), hs(rope_n);
+        build_rope_table_host(c.head_dim, c.rope_positions, c.theta, hc.data(), hs.data());
+        if (cudaMemcpy(e->rope_cos, hc.data(), rope_n * 4, cudaMemcpyHostToDevice) ||
+            cudaMemcpy(e->rope_sin, hs.data(), rope_n * 4, cudaMemcpyHostToDevice))
+            return bail(fail(VB_ERR_CUDA, "rope table upload failed"));
+    }
+    const size_t norms_per_layer = 2 * hd + 2 * (size_t)c.head_dim;
+    if ((st = dalloc(&e->norms, norms_per_layer * c.layers, "norms"))) return bail(st);
+    if ((st = dalloc(&e->wf32, e->per_layer_f32 * c.layers, "f32 projections"))) return bail(st);
+    for (int l = 0; l < c.layers; l++) {
+        vb_layer_dev& L = e->L[l];
+        float* nb = e->norms + norms_per_layer * l;
+        L.in_norm = nb;
+        L.post_norm = nb + hd;
+        L.q_norm = nb + 2 * hd;
+        L.k_norm = nb + 2 * hd + c.head_dim;
+        float* wb = e->wf32 + e->per_layer_f32 * l;
+        L.wqkv = wb;
+        L.wo = L.wqkv + (size_t)e->qkv_rows * hd;
+        L.wgu = L.wo + hd * e->q_width;
+        L.wd = L.wgu + 2 * (size_t)c.ffn * hd;
+    }
+    if ((st = dalloc(&e->x, hd, "x"))) return bail(st);
+    if ((st = dalloc(&e->qkv, e->qkv_rows, "qkv"))) return bail(st);
+    if ((st = dalloc(&e->q, e->q_width, "q"))) return bail(st);
+    if ((st = dalloc(&e->ctx, e->q_width, "ctx"))) return bail(st);
+    if ((st = dalloc(&e->h, c.ffn, "h"))) return bail(st);
+    if ((st = dalloc(&e->logits, c.vocab, "logits"))) return bail(st);
+    const int parts = gemv_grid(c.vocab, false, kEpiArgmax);
+    if ((st = dalloc(&e->part_val, parts, "argmax parts"))) return bail(st);
+    if ((st = dalloc(&e->part_idx, parts, "argmax parts"))) return bail(st);
+    if ((st = dalloc(&e->d_tok, 1, "tok"))) return bail(st);
+    if ((st = dalloc(&e->d_pos, 1, "pos"))) return bail(st);
+    if ((st = dalloc(&e->d_next, 1, "next"))) return bail(st);
+    if ((st = dalloc(&e->d_err, 1, "err"))) return bail(st);
+    if ((st = dalloc(&e->d_step, 1, "step"))) return bail(st);
+    cudaMemset(e->d_err, 0, sizeof(int));
+    cudaMemset(e->d_pos, 0, sizeof(int));
+    if (cudaMallocHost(&e->h_pinned_i, 64 * sizeof(int)) != cudaSuccess)
+        return bail(fail(VB_ERR_CUDA, "cudaMallocHost failed"));
+    *out = e;
+    return VB_OK;
+}
+
+vb_status vb_engine_destroy(vb_engine* e) {
+    if (!e) return VB_OK;
+    DeviceGuard dg(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    mega_release(e);
+    free_cache(e);
+    dfree(e->embed); dfree(e->final_norm); dfree(e->rope_cos); dfree(e->rope_sin);
+    dfree(e->norms); dfree(e->wf32); dfree(e->wi8); dfree(e->wscale);
+    dfree(e->x); dfree(e->qkv); dfree(e->q); dfree(e->ctx); dfree(e->h); dfree(e->logits);
+    dfree(e->part_val); dfree(e->part_idx); dfree(e->d_tok); dfree(e->d_pos); dfree(e->d_next);
+    dfree(e->d_err); dfree(e->d_step);
+    if (e->h_pinned_i) cudaFreeHost(e->h_pinned_i);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return VB_OK;
+}
+
+vb_status vb_engine_set_globals(vb_engine* e, const float* embed, const float* final_norm) {
+    if (!e || !embed || !final_norm) return fail(VB_ERR_ARG, "null argument");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    VB_CUDA_TRY(cudaMemcpy(e->embed, embed, (size_t)c.vocab * c.hidden * 4, cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(cudaMemcpy(e->final_norm, final_norm, (size_t)c.hidden * 4, cudaMemcpyHostToDevice));
+    e->globals_set = true;
+    return VB_OK;
+}
+
+vb_status vb_engine_set_layer(vb_engine* e, int layer, const vb_layer_host* w) {
+    if (!e || !w) return fail(VB_ERR_ARG, "null argument");
+    if (layer < 0 || layer >= e->cfg.layers) return fail(VB_ERR_ARG, "layer index out of range");
+    if (e->quantized) return fail(VB_ERR_STATE, "engine already quantized; upload f32 layers first");
+    if (!w->input_norm || !w->post_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->q_norm ||
+        !w->k_norm || !w->wg || !w->wu || !w->wd)
+        return fail(VB_ERR_ARG, "null weight pointer");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const size_t hd = c.hidden, D = c.head_dim;
+    vb_layer_dev& L = e->L[layer];
+    auto up = [](void* d, const void* h, size_t bytes) {
+        return cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice);
+    };
+    VB_CUDA_TRY(up(L.in_norm, w->input_norm, hd * 4));
+    VB_CUDA_TRY(up(L.post_norm, w->post_norm, hd * 4));
+    VB_CUDA_TRY(up(L.q_norm, w->q_norm, D * 4));
+    VB_CUDA_TRY(up(L.k_norm, w->k_norm, D * 4));
+    VB_CUDA_TRY(up(L.wqkv, w->wq, (size_t)e->q_width * hd * 4));
+    VB_CUDA_TRY(up(L.wqkv + (size_t)e->q_width * hd, w->wk, (size_t)e->kv_width * hd * 4));
+    VB_CUDA_TRY(up(L.wqkv + (size_t)(e->q_width + e->kv_width) * hd, w->wv,
+                   (size_t)e->kv_width * hd * 4));
+    VB_CUDA_TRY(up(L.wo, w->wo, hd * e->q_width * 4));
+    // gate row j -> row 2j, up row j -> row 2j+1
+    VB_CUDA_TRY(cudaMemcpy2D(L.wgu, 2 * hd * 4, w->wg, hd * 4, hd * 4, c.ffn,
+                             cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(cudaMemcpy2D(L.wgu + hd, 2 * hd * 4, w->wu, hd * 4, hd * 4, c.ffn,
+                             cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(up(L.wd, w->wd, hd * (size_t)c.ffn * 4));
+    e->layer_set[layer] = 1;
+    return VB_OK;
+}
+
+vb_status vb_engine_quantize(vb_engine* e) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    if (e->quantized) return VB_OK;  // model.cpp:314
+    for (int l = 0; l < e->cfg.layers; l++)
+        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "quantize before all layers are uploaded");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const size_t hd = c.hidden;
+    vb_status st;
+    if ((st = dalloc(&e->wi8, e->per_layer_i8 * c.layers, "int8 projections"))) return st;
+    if ((st = dalloc(&e->wscale, e->per_layer_rows * c.layers, "scales"))) return st;
+    for (int l = 0; l < c.layers; l++) {
+        vb_layer_dev& L = e->L[l];
+        int8_t* qb = e->wi8 + e->per_layer_i8 * l;
+        float* sb = e->wscale + e->per_layer_rows * l;
+        L.qqkv = qb;
+        L.qo = L.qqkv + (size_t)e->qkv_rows * hd;
+        L.qgu = L.qo + hd * e->q_width;
+        L.qd = L.qgu + 2 * (size_t)c.ffn * hd;
+        L.sqkv = sb;
+        L.so = L.sqkv + e->qkv_rows;
+        L.sgu = L.so + hd;
+        L.sd = L.sgu + 2 * c.ffn;
+        if ((st = launch_quantize_rows(L.wqkv, e->qkv_rows, hd, L.qqkv, L.sqkv, e->stream))) return st;
+        if ((st = launch_quantize_rows(L.wo, hd, e->q_width, L.qo, L.so, e->stream))) return st;
+        if ((st = launch_quantize_rows(L.wgu, 2 * c.ffn, hd, L.qgu, L.sgu, e->stream))) return st;
+        if ((st = launch_quantize_rows(L.wd, hd, c.ffn, L.qd, L.sd, e->stream))) return st;
+    }
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    // model.cpp:329-335: the f32 originals are released.
+    dfree(e->wf32);
+    for (auto& L : e->L) L.wqkv = L.wo = L.wgu = L.wd = nullptr;
+    e->quantized = true;
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    e->graph = nullptr;
+    mega_release(e);
+    return VB_OK;
+}
+
+int vb_engine_is_quantized(const vb_engine* e) { return e && e->quantized ? 1 : 0; }
+
+size_t vb_engine_weight_bytes(const vb_engine* e) {
+    if (!e) return 0;
+    const vb_config& c = e->cfg;
+    size_t total = ((size_t)c.vocab * c.hidden + c.hidden) * 4;
+    total += (size_t)c.layers * (2 * (size_t)c.hidden + 2 * (size_t)c.head_dim) * 4;
+    if (e->quantized)
+        total += (size_t)c.layers * (e->per_layer_i8 + e->per_layer_rows * 4);
+    else
+        total += (size_t)c.layers * e->per_layer_f32 * 4;
+    return total;
+}
+
+vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    if (max_seq <= 0) return fail(VB_ERR_ARG, "max_seq must be positive");
+    DeviceGuard dg(e->device);
+    cudaStreamSynchronize(e->stream);
+    const vb_config& c = e->cfg;
+    if (e->kc && e->max_seq == max_seq) {
+        // same geometry: keep the buffers, zero them (generate.cpp:19-21)
+        const size_t n = (size_t)c.layers * c.kv_heads * max_seq * c.head_dim;
+        VB_CUDA_TRY(cudaMemset(e->kc, 0, n * 4));
+        VB_CUDA_TRY(cudaMemset(e->vc, 0, n * 4));
+    } else {
+        free_cache(e);
+        mega_release(e);
+        const size_t n = (size_t)c.layers * c.kv_heads * max_seq * c.head_dim;
+        vb_status st;
+        if ((st = dalloc(&e->kc, n, "kv cache"))) return st;
+        if ((st = dalloc(&e->vc, n, "kv cache"))) return st;
+        VB_CUDA_TRY(cudaMemset(e->kc, 0, n * 4));
+        VB_CUDA_TRY(cudaMemset(e->vc, 0, n * 4));
+        e->max_seq = max_seq;
+        e->attn_splits = attn_splits_for(1, c.kv_heads, max_seq);
+        if ((st = dalloc(&e->attn_ws, attn_ws_bytes(1, c.heads, e->attn_splits) / 4 + 1, "attn ws")))
+            return st;
+        if ((st = dalloc(&e->d_hist, max_seq, "history"))) return st;
+    }
+    VB_CUDA_TRY(cudaMemset(e->d_pos, 0, sizeof(int)));
+    e->len = 0;
+    return VB_OK;
+}
+
+int vb_engine_cache_len(const vb_engine* e) { return e ? e->len : 0; }
+
+static vb_status pre_step(vb_engine* e, int n_tokens) {
+    vb_status st = check_ready(e);
+    if (st) return st;
+    if (e->len + n_tokens > e->max_seq) return fail(VB_ERR_CACHE_FULL, "kv cache is full");
+    if (e->len + n_tokens > e->cfg.rope_positions)
+        return fail(VB_ERR_ROPE, "position is outside the rope table");
+    if (e->path == 0 && !e->mega) {
+        st = mega_prepare(e);
+        if (st == VB_ERR_UNSUPPORTED) e->path = 1;
+        else if (st) return st;
+    }
+    return ensure_graph(e);
+}
+
+vb_status vb_engine_step(vb_engine* e, int token, float* logits_host) {
+    if (!e || !logits_host) return fail(VB_ERR_ARG, "null argument");
+    DeviceGuard dg(e->device);
+    vb_status st = pre_step(e, 1);
+    if (st) return st;
+    if (token < 0 || token >= e->cfg.vocab)
+        return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    e->h_pinned_i[0] = token;
+    e->h_pinned_i[1] = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->h_pinned_i, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    VB_CUDA_TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->cfg.vocab * 4,
+                                cudaMemcpyDeviceToHost, e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if ((st = engine_check_err(e))) return st;
+    e->len += 1;
+    return VB_OK;
+}
+
+vb_status vb_engine_decode(vb_engine* e, int first_token, int n, int* tokens_host,
+                           float* logits_host) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    if (n <= 0) return VB_OK;
+    DeviceGuard dg(e->device);
+    vb_status st = pre_step(e, n);
+    if (st) return st;
+    if (first_token < 0 || first_token >= e->cfg.vocab)
+        return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    e->h_pinned_i[0] = first_token;
+    e->h_pinned_i[1] = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->h_pinned_i, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    for (int i = 0; i < n; i++) VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    if (tokens_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(tokens_host, e->d_hist, (size_t)n * sizeof(int),
+                                    cudaMemcpyDeviceToHost, e->stream));
+    if (logits_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->cfg.vocab * 4,
+                                    cudaMemcpyDeviceToHost, e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if ((st = engine_check_err(e))) return st;
+    e->len += n;
+    return VB_OK;
+}
+
+vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host) {
+    if (!e || !host) return fail(VB_ERR_ARG, "null argument");
+    if (!e->kc) return fail(VB_ERR_NO_CACHE, "call reset_cache() first");
+    if (layer < 0 || layer >= e->cfg.layers) return fail(VB_ERR_ARG, "layer index out of range");
+    if (e->len == 0) return VB_OK;
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const size_t layer_kv = (size_t)c.kv_heads * e->max_seq * c.head_dim;
+    const float* base = (which == 0 ? e->kc : e->vc) + layer * layer_kv;
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    for (int h = 0; h < c.kv_heads; h++) {
+        VB_CUDA_TRY(cudaMemcpy2D(host + (size_t)h * c.head_dim, (size_t)e->kv_width * 4,
+                                 base + (size_t)h * e->max_seq * c.head_dim,
+                                 (size_t)c.head_dim * 4, (size_t)c.head_dim * 4, e->len,
+                                 cudaMemcpyDeviceToHost));
+    }
+    return VB_OK;
+}
+
+vb_status vb_engine_set_path(vb_engine* e, int path) {
+    if (!e || path < 0 || path > 1) return fail(VB_ERR_ARG, "path must be 0 or 1");
+    DeviceGuard dg(e->device);
+    cudaStreamSynchronize(e->stream);
+    if (e->path != path) {
+        e->path = path;
+        if (e->graph) cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    return VB_OK;
+}
+
+void* vb_engine_stream(vb_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+}  // extern "C"

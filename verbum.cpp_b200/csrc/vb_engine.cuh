@@ -1,0 +1,108 @@
+// vb_engine.cuh -- device-resident state of one decode engine (one GPU).
+#pragma once
+
+#include <vector>
+
+#include "vb_kernels.cuh"
+
+// HBM layout (all row-major, HF [out, in] orientation):
+//   wqkv  [L][(H+2KVH)*D, hidden]   q | k | v rows of each layer stacked
+//   wo    [L][hidden, H*D]
+//   wgu   [L][2*ffn, hidden]        gate row j at 2j, up row j at 2j+1
+//   wd    [L][hidden, ffn]
+// (INT8 mode: the same shapes as int8 plus one f32 scale per row.)
+//   embed [vocab, hidden] f32 (tied lm_head)
+//   kc/vc [L][B][KVH][max_seq][D] f32 -- one contiguous stream per (layer,
+//          sequence, kv head), so a split of the attention reads one span.
+struct vb_layer_dev {
+    float* in_norm;
+    float* post_norm;
+    float* q_norm;
+    float* k_norm;
+    float* wqkv;
+    float* wo;
+    float* wgu;
+    float* wd;
+    int8_t* qqkv;
+    int8_t* qo;
+    int8_t* qgu;
+    int8_t* qd;
+    float* sqkv;
+    float* so;
+    float* sgu;
+    float* sd;
+};
+
+struct vb_engine {
+    vb_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool quantized = false;
+    int path = 1;
+
+    // sizes
+    int qkv_rows = 0;    // (H + 2 KVH) * D
+    int q_width = 0;     // H * D
+    int kv_width = 0;    // KVH * D
+    size_t per_layer_f32 = 0;  // floats of projections per layer
+    size_t per_layer_i8 = 0;   // bytes of int8 projections per layer
+    size_t per_layer_rows = 0; // scale entries per layer
+
+    // weights
+    float* embed = nullptr;
+    float* final_norm = nullptr;
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    float* norms = nullptr;    // all per-layer norm vectors
+    float* wf32 = nullptr;     // all f32 projections
+    int8_t* wi8 = nullptr;     // all int8 projections
+    float* wscale = nullptr;   // all scales
+    std::vector<vb_layer_dev> L;
+    std::vector<int> layer_set;
+    bool globals_set = false;
+
+    // cache (batch 1)
+    int max_seq = 0;
+    int len = 0;
+    float* kc = nullptr;
+    float* vc = nullptr;
+
+    // scratch
+    float* x = nullptr;
+    float* qkv = nullptr;
+    float* q = nullptr;
+    float* ctx = nullptr;
+    float* h = nullptr;
+    float* logits = nullptr;
+    float* attn_ws = nullptr;
+    int attn_splits = 1;
+    float* part_val = nullptr;
+    int* part_idx = nullptr;
+    int* d_tok = nullptr;
+    int* d_pos = nullptr;
+    int* d_next = nullptr;
+    int* d_err = nullptr;
+    int* d_hist = nullptr;     // decode history [max_seq]
+    int* d_step = nullptr;     // decode history write index
+    int* h_pinned_i = nullptr; // pinned host staging
+    float* h_logits = nullptr;
+
+    cudaGraphExec_t graph = nullptr;
+
+    // persistent fused step (vb_mega.cu)
+    void* mega = nullptr;
+};
+
+namespace vb {
+// Enqueue one full decode step (token in d_tok, position in d_pos) using the
+// per-op kernels.  Leaves logits in e->logits and the greedy pick in d_next,
+// then advances d_pos / d_tok and appends the pick to the history.
+vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s);
+// Fused persistent step (vb_mega.cu). Returns VB_ERR_UNSUPPORTED when the
+// shapes are outside what it handles.
+vb_status mega_prepare(vb_engine* e);
+vb_status mega_enqueue_step(vb_engine* e, cudaStream_t s);
+void mega_release(vb_engine* e);
+vb_status engine_check_err(vb_engine* e);
+void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s);
+}  // namespace vb

@@ -1,0 +1,872 @@
+// vb_kernels.cu -- one-op-per-kernel sm_100a building blocks of the decode
+// step: streaming GEMV (f32 / INT8 with fused dequant), split-K SIMT GEMM for
+// small batches, per-row quantisation, RMSNorm, per-head q/k norm + RoPE + KV
+// append, split-K GQA decode attention, argmax, embedding.
+//
+// These kernels back the C ABI's kernel entry points (the counterparts of the
+// reference launchers in kernels/cuda_ops.cu:181-292), the graph-captured
+// per-op step path, and the batched engine.
+#include <float.h>
+#include <limits.h>
+#include <math.h>
+
+#include "vb_kernels.cuh"
+
+namespace vb {
+
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kNumSMs = 148;
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+    return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ float silu_f(float g) {
+    // model.cpp:15-18: x / (1 + exp(-x)), IEEE division, accurate expf.
+    return g / (1.0f + expf(-g));
+}
+
+// Position of x[i] inside the per-CTA shared copy.  INT8 lanes load 16
+// consecutive weights; storing the matching activations lane-interleaved per
+// 512-element chunk makes every lane's float4 reads bank-conflict free.
+template <bool Q8>
+__device__ __forceinline__ int xs_index(int i) {
+    if (!Q8) return i;
+    const int c = i >> 9, r = i & 511;
+    const int l = r >> 4, j = (r >> 2) & 3, e = r & 3;
+    return (c << 9) + (j << 7) + (l << 2) + e;
+}
+
+// ---------------------------------------------------------------------------
+// GEMV: y = W . x with W [N, K] row-major (f32 or int8 + per-row scale).
+// One warp owns R consecutive rows at a time; lanes stride K with 16-byte
+// streaming loads, all of a row group's loads issued before the FMAs.
+// ---------------------------------------------------------------------------
+template <bool Q8, int R, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ double red[kGemvWarps];
+    __shared__ float sbv[kGemvWarps];
+    __shared__ int sbi[kGemvWarps];
+
+    const int K = a.K;
+    const float* x = a.x;
+    if (a.x_tok) x += (size_t)(*a.x_tok) * (size_t)K;
+
+    float sc = 1.0f;
+    if (PRO == kProRms) {
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < K; i += kGemvThreads) {
+            const float v = x[i];
+            ss += (double)v * (double)v;
+        }
+        sc = rms_scale(block_sum_d<kGemvThreads>(ss, red), K, a.eps);
+    }
+    for (int i = threadIdx.x; i < K; i += kGemvThreads) {
+        float v = x[i];
+        if (PRO == kProRms) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[i]);
+        xs[xs_index<Q8>(i)] = v;
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int N = a.N;
+    const int ngroups = (N + R - 1) / R;
+    float best_v = -INFINITY;
+    int best_i = INT_MAX;
+
+    for (int g = blockIdx.x * kGemvWarps + warp; g < ngroups; g += gridDim.x * kGemvWarps) {
+        const int r0 = g * R;
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = 0.0f;
+
+        if (!Q8) {
+            const float* W = static_cast<const float*>(a.W);
+            const int K4 = K >> 2;
+            constexpr int U = 8;
+            for (int kb = 0; kb < K4; kb += 32 * U) {
+                float4 w[R][U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int k4 = kb + 32 * u + lane;
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        if (k4 < K4 && r0 + r < N)
+                            w[r][u] = ld_stream_f4(W + (size_t)(r0 + r) * K + 4 * (size_t)k4);
+                        else
+                            w[r][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int k4 = kb + 32 * u + lane;
+                    if (k4 < K4) {
+                        const float4 xv = *reinterpret_cast<const float4*>(xs + 4 * k4);
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            acc[r] = fmaf(w[r][u].x, xv.x, acc[r]);
+                            acc[r] = fmaf(w[r][u].y, xv.y, acc[r]);
+                            acc[r] = fmaf(w[r][u].z, xv.z, acc[r]);
+                            acc[r] = fmaf(w[r][u].w, xv.w, acc[r]);
+                        }
+                    }
+                }
+            }
+        } else {
+            const int8_t* W = static_cast<const int8_t*>(a.W);
+            const int G16 = K >> 4;  // 16-byte groups per row
+            constexpr int U = 4;
+            for (int gb = 0; gb < G16; gb += 32 * U) {
+                uint4 w[R][U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int gi = gb + 32 * u + lane;
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        if (gi < G16 && r0 + r < N)
+                            w[r][u] = ld_stream_u4(W + (size_t)(r0 + r) * K + 16 * (size_t)gi);
+                        else
+                            w[r][u] = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int gi = gb + 32 * u + lane;
+                    if (gi < G16) {
+                        const float* xc = xs + ((gi >> 5) << 9) + 4 * lane;
+                        const float4 x0 = *reinterpret_cast<const float4*>(xc);
+                        const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
+                        const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
+                        const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            f4 a0 = i8x4_to_f32(w[r][u].x);
+                            f4 a1 = i8x4_to_f32(w[r][u].y);
+                            f4 a2 = i8x4_to_f32(w[r][u].z);
+                            f4 a3 = i8x4_to_f32(w[r][u].w);
+                            float s = acc[r];
+                            s = fmaf(a0.v[0], x0.x, s); s = fmaf(a0.v[1], x0.y, s);
+                            s = fmaf(a0.v[2], x0.z, s); s = fmaf(a0.v[3], x0.w, s);
+                            s = fmaf(a1.v[0], x1.x, s); s = fmaf(a1.v[1], x1.y, s);
+                            s = fmaf(a1.v[2], x1.z, s); s = fmaf(a1.v[3], x1.w, s);
+                            s = fmaf(a2.v[0], x2.x, s); s = fmaf(a2.v[1], x2.y, s);
+                            s = fmaf(a2.v[2], x2.z, s); s = fmaf(a2.v[3], x2.w, s);
+                            s = fmaf(a3.v[0], x3.x, s); s = fmaf(a3.v[1], x3.y, s);
+                            s = fmaf(a3.v[2], x3.z, s); s = fmaf(a3.v[3], x3.w, s);
+                            acc[r] = s;
+                        }
+                    }
+                }
+            }
+        }
+
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = warp_sum(acc[r]);
+            if (Q8 && r0 + r < N) acc[r] = acc[r] * a.scales[r0 + r];
+        }
+
+        if (EPI == kEpiSwiGLU) {
+#pragma unroll
+            for (int p = 0; p < R / 2; p++) {
+                const int rg = r0 + 2 * p;
+                if (lane == p && rg + 1 < N) a.y[rg >> 1] = silu_f(acc[2 * p]) * acc[2 * p + 1];
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int row = r0 + r;
+                if (row < N) {
+                    if (lane == r) {
+                        if (EPI == kEpiResidual) a.y[row] = a.y[row] + acc[r];
+                        else a.y[row] = acc[r];
+                    }
+                    if (EPI == kEpiArgmax && better(acc[r], row, best_v, best_i)) {
+                        best_v = acc[r];
+                        best_i = row;
+                    }
+                }
+            }
+        }
+    }
+
+    if (EPI == kEpiArgmax) {
+        if (lane == 0) {
+            sbv[warp] = best_v;
+            sbi[warp] = best_i;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float bv = sbv[0];
+            int bi = sbi[0];
+            for (int w = 1; w < kGemvWarps; w++)
+                if (better(sbv[w], sbi[w], bv, bi)) { bv = sbv[w]; bi = sbi[w]; }
+            a.part_val[blockIdx.x] = bv;
+            a.part_idx[blockIdx.x] = bi;
+        }
+    }
+}
+
+__global__ void argmax_parts_kernel(const float* pv, const int* pi, int parts, int* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int i = threadIdx.x; i < parts; i += blockDim.x)
+        if (better(pv[i], pi[i], bv, bi)) { bv = pv[i]; bi = pi[i]; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        bv = sv[0]; bi = si[0];
+        for (int i = 1; i < nw; i++)
+            if (better(sv[i], si[i], bv, bi)) { bv = sv[i]; bi = si[i]; }
+        *out = (bi == INT_MAX) ? 0 : bi;
+    }
+}
+
+// One block per row of logits.
+__global__ void argmax_rows_kernel(const float* logits, int64_t n, int* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* row = logits + (size_t)blockIdx.x * (size_t)n;
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+        if (better(row[i], (int)i, bv, bi)) { bv = row[i]; bi = (int)i; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bv = sv[0]; bi = si[0];
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++)
+            if (better(sv[i], si[i], bv, bi)) { bv = sv[i]; bi = si[i]; }
+        out[blockIdx.x] = (bi == INT_MAX) ? 0 : bi;
+    }
+}
+
+// quant.cpp:9-41 with IEEE-exact device ops: the row max is order-free, the
+// division, reciprocal and product are correctly rounded, and
+// __float2int_rn is round-half-even like lrintf under the default mode.
+__global__ void quantize_rows_kernel(const float* W, int64_t rows, int64_t cols, int8_t* q,
+                                     float* scales) {
+    __shared__ float red[32];
+    __shared__ float s_inv;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float* row = W + r * cols;
+        float amax = 0.0f;
+        for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+            const float v = fabsf(row[c]);
+            amax = (amax < v) ? v : amax;
+        }
+        amax = warp_max(amax);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float m = 0.0f;
+            for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = (m < red[i]) ? red[i] : m;
+            const float scale = (m > 0.0f) ? __fdiv_rn(m, 127.0f) : 1.0f;
+            scales[r] = scale;
+            s_inv = __fdiv_rn(1.0f, scale);
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+            int v = __float2int_rn(__fmul_rn(row[c], inv));
+            v = v > 127 ? 127 : (v < -127 ? -127 : v);
+            q[r * cols + c] = (int8_t)v;
+        }
+        __syncthreads();
+    }
+}
+
+// nn.cpp:8-42, one block per row.
+__global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int dim,
+                                    float eps) {
+    __shared__ double red[8];
+    const float* xr = x + (size_t)blockIdx.x * dim;
+    float* orow = out + (size_t)blockIdx.x * dim;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        const float v = xr[i];
+        ss += (double)v * (double)v;
+    }
+    const float sc = rms_scale(block_sum_d<256>(ss, red), dim, eps);
+    for (int i = threadIdx.x; i < dim; i += 256) orow[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+}
+
+// generate.cpp:52-71 for B sequences: per-head RMSNorm (q_norm / k_norm),
+// split-half RoPE from the host table, k and v rows written at pos[b].
+// grid (H + KVH, B), block D (= 128).
+__global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
+    const float eps = a.eps;
+    __shared__ double red[4];
+    __shared__ float ys[128];
+    const int hd = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int D = a.D, half = D >> 1;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.rope_positions) {
+        if (d == 0 && a.err) atomicExch(a.err, kErrCacheFull);
+        return;
+    }
+    const int QW = a.H * D, KW = a.KVH * D;
+    const float* row = a.qkv + (size_t)b * (QW + 2 * KW);
+    const bool isq = hd < a.H;
+    const int h = isq ? hd : hd - a.H;
+    const float* src = isq ? row + h * D : row + QW + h * D;
+    const float* nw = isq ? a.q_norm : a.k_norm;
+    const float xv = src[d];
+    const float sc = rms_scale(block_sum_d<128>((double)xv * (double)xv, red), D, eps);
+    ys[d] = __fmul_rn(__fmul_rn(xv, sc), nw[d]);
+    __syncthreads();
+    const float* c = a.cos_tab + (size_t)pos * D;
+    const float* s = a.sin_tab + (size_t)pos * D;
+    float o;
+    if (d < half) {
+        o = __fsub_rn(__fmul_rn(ys[d], c[d]), __fmul_rn(ys[d + half], s[d]));
+    } else {
+        o = __fadd_rn(__fmul_rn(ys[d], c[d]), __fmul_rn(ys[d - half], s[d]));
+    }
+    if (isq) {
+        a.q_out[((size_t)b * a.H + h) * D + d] = o;
+    } else {
+        const size_t off = (size_t)b * a.stride_b + (size_t)pos * a.stride_pos +
+                           (size_t)h * a.stride_h + d;
+        a.kc[off] = o;
+        a.vc[off] = row[QW + KW + h * D + d];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Split-K GQA decode attention (flash-decoding).  grid (splits, KVH, B),
+// 8 warps.  Each CTA takes one contiguous slice of one sequence's cache for
+// one KV head and serves all G query heads of that group from a single read
+// of each K/V row.  Each warp runs an online softmax over every 8th block of
+// 4 positions; warps merge in shared memory and the CTA writes (m, l, acc).
+// ---------------------------------------------------------------------------
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = 8;
+constexpr int kAttnPB = 4;  // positions per warp iteration
+
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = a.lens ? a.lens[b] : a.pos[b] + 1;
+    const int chunk = (n + a.splits - 1) / a.splits;
+    const int p0 = split * chunk;
+    const int p1 = min(n, p0 + chunk);
+    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)a.D));
+
+    float4 q[G];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+        q[g] = *reinterpret_cast<const float4*>(a.q + ((size_t)b * a.H + kvh * G + g) * 128 +
+                                                4 * lane);
+    float m[G], l[G];
+    float4 acc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float* kb = a.k + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
+    const float* vb = a.v + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
+
+    for (int base = p0 + warp * kAttnPB; base < p1; base += kAttnWarps * kAttnPB) {
+        float4 kk[kAttnPB], vv[kAttnPB];
+#pragma unroll
+        for (int u = 0; u < kAttnPB; u++) {
+            const int p = base + u;
+            if (p < p1) {
+                kk[u] = ld_stream_f4(kb + (size_t)p * a.stride_pos);
+                vv[u] = ld_stream_f4(vb + (size_t)p * a.stride_pos);
+            } else {
+                kk[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[u] = kk[u];
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float s[kAttnPB];
+            float mx = m[g];
+#pragma unroll
+            for (int u = 0; u < kAttnPB; u++) {
+                float d = q[g].x * kk[u].x;
+                d = fmaf(q[g].y, kk[u].y, d);
+                d = fmaf(q[g].z, kk[u].z, d);
+                d = fmaf(q[g].w, kk[u].w, d);
+                d = warp_sum(d) * inv_sqrt_d;
+                s[u] = (base + u < p1) ? d : -INFINITY;
+                mx = fmaxf(mx, s[u]);
+            }
+            const float corr = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mx);
+            l[g] *= corr;
+            acc[g].x *= corr; acc[g].y *= corr; acc[g].z *= corr; acc[g].w *= corr;
+#pragma unroll
+            for (int u = 0; u < kAttnPB; u++) {
+                const float e = (s[u] == -INFINITY) ? 0.0f : expf(s[u] - mx);
+                l[g] += e;
+                acc[g].x = fmaf(e, vv[u].x, acc[g].x);
+                acc[g].y = fmaf(e, vv[u].y, acc[g].y);
+                acc[g].z = fmaf(e, vv[u].z, acc[g].z);
+                acc[g].w = fmaf(e, vv[u].w, acc[g].w);
+            }
+            m[g] = mx;
+        }
+    }
+
+    __shared__ float sm_m[kAttnWarps][G], sm_l[kAttnWarps][G];
+    __shared__ float4 sm_acc[kAttnWarps][G][32];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+        sm_acc[warp][g][lane] = acc[g];
+    }
+    __syncthreads();
+    // thread -> (g, float index); G*128 values per CTA
+    const int S = a.splits;
+    for (int t = threadIdx.x; t < G * 128; t += kAttnThreads) {
+        const int g = t >> 7, di = t & 127;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm_m[w][g]);
+        float L = 0.0f, A = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; w++) {
+                if (sm_m[w][g] == -INFINITY) continue;
+                const float f = expf(sm_m[w][g] - M);
+                L = fmaf(sm_l[w][g], f, L);
+                const float* av = reinterpret_cast<const float*>(&sm_acc[w][g][0]);
+                A = fmaf(av[di], f, A);
+            }
+        }
+        const int h = kvh * G + g;
+        float* part = a.ws + (((size_t)b * a.H + h) * S + split) * (128 + 2);
+        part[2 + di] = A;
+        if (di == 0) { part[0] = M; part[1] = L; }
+    }
+}
+
+// grid (H, B), block 128: merges the splits of one (b, h).
+__global__ void attn_merge_kernel(AttnArgs a) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int S = a.splits;
+    const float* base = a.ws + ((size_t)b * a.H + h) * S * (128 + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, base[s * 130]);
+    float L = 0.0f, A = 0.0f;
+    for (int s = 0; s < S; s++) {
+        const float ms = base[s * 130];
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - M);
+        L = fmaf(base[s * 130 + 1], f, L);
+        A = fmaf(base[s * 130 + 2 + d], f, A);
+    }
+    a.out[((size_t)b * a.H + h) * 128 + d] = A / L;
+}
+
+__global__ void embed_kernel(const float* E, const int* tokens, int dim, int vocab, float* out,
+                             int* err) {
+    const int b = blockIdx.x;
+    int tok = tokens[b];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && err) atomicExch(err, kErrBadToken);
+        tok = 0;
+    }
+    const float4* src = reinterpret_cast<const float4*>(E + (size_t)tok * dim);
+    float4* dst = reinterpret_cast<float4*>(out + (size_t)b * dim);
+    for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void advance_kernel(int* pos, int* tokens, const int* next, int B) {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        pos[b] += 1;
+        if (tokens && next) tokens[b] = next[b];
+    }
+}
+
+__global__ void rope_kernel(float* x, const float* c, const float* s, int pos, int heads, int D) {
+    const int half = D / 2;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= heads * half) return;
+    const int h = t / half, i = t % half;
+    float* row = x + (size_t)h * D;
+    const float* cr = c + (size_t)pos * D;
+    const float* sr = s + (size_t)pos * D;
+    const float av = row[i], bv = row[i + half];
+    row[i] = __fsub_rn(__fmul_rn(av, cr[i]), __fmul_rn(bv, sr[i]));
+    row[i + half] = __fadd_rn(__fmul_rn(bv, cr[i + half]), __fmul_rn(av, sr[i + half]));
+}
+
+__global__ void silu_mul_kernel(float* g, const float* u, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) g[i] = silu_f(g[i]) * u[i];
+}
+
+__global__ void add_kernel(float* a, const float* b, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) a[i] = a[i] + b[i];
+}
+
+__global__ void cache_append_kernel(float* kc, float* vc, const float* kn, const float* vn,
+                                    int pos, int width) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < width) {
+        kc[(size_t)pos * width + i] = kn[i];
+        vc[(size_t)pos * width + i] = vn[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Batched SIMT GEMM with split-K partials: P[s, m, n] = sum_k A[m,k] W[n,k]
+// over split s's K range.  64x64 output tile, 256 threads, 4x4 per thread.
+// ---------------------------------------------------------------------------
+constexpr int kGM = 64, kGN = 64, kGK = 32;
+
+template <bool Q8>
+__global__ void __launch_bounds__(256) gemm_partial_kernel(GemmArgs a, int kper) {
+    __shared__ __align__(16) float As[kGK][kGM + 4];
+    __shared__ __align__(16) float Ws[kGK][kGN + 4];
+    const int n0 = blockIdx.x * kGN, split = blockIdx.y;
+    const int kbeg = split * kper, kend = min(a.K, kbeg + kper);
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int M = a.M, N = a.N, K = a.K;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+
+    for (int k0 = kbeg; k0 < kend; k0 += kGK) {
+#pragma unroll
+        for (int it = 0; it < 2; it++) {
+            const int idx = tid + 256 * it;
+            const int m = idx >> 3, kq = idx & 7;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m < M) v = *reinterpret_cast<const float4*>(a.A + (size_t)m * K + k0 + 4 * kq);
+            As[4 * kq + 0][m] = v.x; As[4 * kq + 1][m] = v.y;
+            As[4 * kq + 2][m] = v.z; As[4 * kq + 3][m] = v.w;
+        }
+        if (!Q8) {
+            const float* W = static_cast<const float*>(a.W);
+#pragma unroll
+            for (int it = 0; it < 2; it++) {
+                const int idx = tid + 256 * it;
+                const int n = idx >> 3, kq = idx & 7;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n0 + n < N) v = ld_stream_f4(W + (size_t)(n0 + n) * K + k0 + 4 * kq);
+                Ws[4 * kq + 0][n] = v.x; Ws[4 * kq + 1][n] = v.y;
+                Ws[4 * kq + 2][n] = v.z; Ws[4 * kq + 3][n] = v.w;
+            }
+        } else if (tid < 128) {
+            const int8_t* W = static_cast<const int8_t*>(a.W);
+            const int n = tid >> 1, hf = tid & 1;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (n0 + n < N) v = ld_stream_u4(W + (size_t)(n0 + n) * K + k0 + 16 * hf);
+            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const f4 f = i8x4_to_f32(wv[j]);
+#pragma unroll
+                for (int e = 0; e < 4; e++) Ws[16 * hf + 4 * j + e][n] = f.v[e];
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kGK; kk++) {
+            const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&Ws[kk][tx * 4]);
+            const float ar[4] = {av.x, av.y, av.z, av.w};
+            const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(ar[i], wr[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+    float* P = a.ws + (size_t)split * M * N;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx * 4 + j;
+            if (n < N) P[(size_t)m * N + n] = acc[i][j];
+        }
+    }
+}
+
+// Sums the split partials in fixed order and applies the epilogue.
+template <bool Q8, int EPI>
+__global__ void gemm_reduce_kernel(GemmArgs a, int splits) {
+    const int M = a.M, N = a.N;
+    const int outN = (EPI == kEpiSwiGLU) ? N / 2 : N;
+    const size_t total = (size_t)M * outN;
+    for (size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(t / outN), j = (int)(t % outN);
+        if (EPI == kEpiSwiGLU) {
+            float gsum = 0.f, usum = 0.f;
+            for (int s = 0; s < splits; s++) {
+                const float* P = a.ws + (size_t)s * M * N + (size_t)m * N;
+                gsum += P[2 * j];
+                usum += P[2 * j + 1];
+            }
+            if (Q8) { gsum *= a.scales[2 * j]; usum *= a.scales[2 * j + 1]; }
+            a.C[(size_t)m * a.ldc + j] = silu_f(gsum) * usum;
+        } else {
+            float v = 0.f;
+            for (int s = 0; s < splits; s++) v += a.ws[(size_t)s * M * N + (size_t)m * N + j];
+            if (Q8) v *= a.scales[j];
+            float* dst = a.C + (size_t)m * a.ldc + j;
+            if (EPI == kEpiResidual) *dst = *dst + v;
+            else *dst = v;
+        }
+    }
+}
+
+template <bool Q8>
+int gemm_splits(int N, int K) {
+    const int tiles = (N + kGN - 1) / kGN;
+    int s = (2 * kNumSMs + tiles - 1) / tiles;
+    const int maxs = K / kGK;
+    if (s > maxs) s = maxs;
+    if (s > 16) s = 16;
+    if (s < 1) s = 1;
+    return s;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+
+static int gemv_rows_per_warp(int N, bool q8, int epi) {
+    if (epi == kEpiSwiGLU) return q8 ? 4 : 2;
+    if (q8) return N >= 4096 ? 4 : 2;
+    return N >= 4096 ? 2 : 1;
+}
+
+int gemv_grid(int N, bool q8, int epi) {
+    const int R = gemv_rows_per_warp(N, q8, epi);
+    const int groups = (N + R - 1) / R;
+    int blocks = (groups + kGemvWarps - 1) / kGemvWarps;
+    const int cap = kNumSMs * 8;
+    return blocks < cap ? blocks : cap;
+}
+
+template <bool Q8, int R, int PRO>
+static void gemv_dispatch_epi(const GemvArgs& a, int epi, int grid, size_t smem,
+                              cudaStream_t s) {
+    switch (epi) {
+        case kEpiStore: gemv_kernel<Q8, R, PRO, kEpiStore><<<grid, kGemvThreads, smem, s>>>(a); break;
+        case kEpiResidual: gemv_kernel<Q8, R, PRO, kEpiResidual><<<grid, kGemvThreads, smem, s>>>(a); break;
+        case kEpiSwiGLU:  // launch_gemv only picks even R for this epilogue
+            gemv_kernel<Q8, (R % 2 == 0 ? R : 2), PRO, kEpiSwiGLU><<<grid, kGemvThreads, smem, s>>>(a);
+            break;
+        default: gemv_kernel<Q8, R, PRO, kEpiArgmax><<<grid, kGemvThreads, smem, s>>>(a); break;
+    }
+}
+
+template <bool Q8, int R>
+static void gemv_dispatch_pro(const GemvArgs& a, int pro, int epi, int grid, size_t smem,
+                              cudaStream_t s) {
+    if (pro == kProRms) gemv_dispatch_epi<Q8, R, kProRms>(a, epi, grid, smem, s);
+    else gemv_dispatch_epi<Q8, R, kProNone>(a, epi, grid, smem, s);
+}
+
+vb_status launch_gemv(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s,
+                      int* grid_out) {
+    if (a.N <= 0 || a.K <= 0) return fail(VB_ERR_ARG, "gemv: empty shape");
+    if (q8 ? (a.K % 16) : (a.K % 4)) return fail(VB_ERR_UNSUPPORTED, "gemv: K alignment");
+    if (a.K > 12288) return fail(VB_ERR_UNSUPPORTED, "gemv: K > 12288");
+    if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemv: swiglu needs even N");
+    const int R = gemv_rows_per_warp(a.N, q8, epi);
+    const int grid = gemv_grid(a.N, q8, epi);
+    const size_t smem = sizeof(float) * (size_t)(q8 ? ((a.K + 511) / 512) * 512 : a.K);
+    if (q8) {
+        if (R == 4) gemv_dispatch_pro<true, 4>(a, pro, epi, grid, smem, s);
+        else gemv_dispatch_pro<true, 2>(a, pro, epi, grid, smem, s);
+    } else {
+        if (R == 2) gemv_dispatch_pro<false, 2>(a, pro, epi, grid, smem, s);
+        else gemv_dispatch_pro<false, 1>(a, pro, epi, grid, smem, s);
+    }
+    if (grid_out) *grid_out = grid;
+    VB_LAUNCH_CHECK("gemv_kernel");
+    return VB_OK;
+}
+
+vb_status launch_argmax_parts(const float* pv, const int* pi, int parts, int* out,
+                              cudaStream_t s) {
+    argmax_parts_kernel<<<1, 1024, 0, s>>>(pv, pi, parts, out);
+    VB_LAUNCH_CHECK("argmax_parts_kernel");
+    return VB_OK;
+}
+
+vb_status launch_argmax_rows(const float* logits, int rows, int64_t n, int* out,
+                             cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return fail(VB_ERR_ARG, "argmax: empty input");
+    argmax_rows_kernel<<<rows, 1024, 0, s>>>(logits, n, out);
+    VB_LAUNCH_CHECK("argmax_rows_kernel");
+    return VB_OK;
+}
+
+vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_t* q,
+                               float* scales, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return fail(VB_ERR_ARG, "quantize_rows: empty shape");
+    const int grid = (int)(rows < 4096 ? rows : 4096);
+    quantize_rows_kernel<<<grid, 256, 0, s>>>(W, rows, cols, q, scales);
+    VB_LAUNCH_CHECK("quantize_rows_kernel");
+    return VB_OK;
+}
+
+vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows, int dim,
+                              float eps, cudaStream_t s) {
+    if (rows <= 0 || dim <= 0) return fail(VB_ERR_ARG, "rmsnorm: empty shape");
+    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, dim, eps);
+    VB_LAUNCH_CHECK("rmsnorm_rows_kernel");
+    return VB_OK;
+}
+
+vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
+    if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
+    dim3 grid(a.H + a.KVH, a.B);
+    qk_norm_rope_kernel<<<grid, 128, 0, s>>>(a);
+    VB_LAUNCH_CHECK("qk_norm_rope_kernel");
+    return VB_OK;
+}
+
+int attn_splits_for(int B, int KVH, int n_max) {
+    const int target = kNumSMs * 4;
+    int by_len = (n_max + 63) / 64;
+    int by_grid = (target + B * KVH - 1) / (B * KVH);
+    int s = by_len < by_grid ? by_len : by_grid;
+    return s < 1 ? 1 : s;
+}
+
+size_t attn_ws_bytes(int B, int H, int splits) {
+    return sizeof(float) * (size_t)B * H * splits * (128 + 2);
+}
+
+vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
+    if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "attention: head_dim must be 128");
+    if (a.H % a.KVH) return fail(VB_ERR_ARG, "attention: heads % kv_heads != 0");
+    const int G = a.H / a.KVH;
+    dim3 grid(a.splits, a.KVH, a.B);
+    switch (G) {
+        case 1: attn_split_kernel<1><<<grid, kAttnThreads, 0, s>>>(a); break;
+        case 2: attn_split_kernel<2><<<grid, kAttnThreads, 0, s>>>(a); break;
+        case 4: attn_split_kernel<4><<<grid, kAttnThreads, 0, s>>>(a); break;
+        default: return fail(VB_ERR_UNSUPPORTED, "attention: GQA group must be 1, 2 or 4");
+    }
+    VB_LAUNCH_CHECK("attn_split_kernel");
+    attn_merge_kernel<<<dim3(a.H, a.B), 128, 0, s>>>(a);
+    VB_LAUNCH_CHECK("attn_merge_kernel");
+    return VB_OK;
+}
+
+vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
+                       float* out, int* err, cudaStream_t s) {
+    if (dim % 4) return fail(VB_ERR_UNSUPPORTED, "embed: dim % 4");
+    embed_kernel<<<B, 256, 0, s>>>(E, tokens, dim, vocab, out, err);
+    VB_LAUNCH_CHECK("embed_kernel");
+    return VB_OK;
+}
+
+vb_status launch_advance(int* pos, int* tokens, const int* next, int B, cudaStream_t s) {
+    advance_kernel<<<1, 128, 0, s>>>(pos, tokens, next, B);
+    VB_LAUNCH_CHECK("advance_kernel");
+    return VB_OK;
+}
+
+vb_status launch_rope(float* x, const float* c, const float* sn, int pos, int heads, int D,
+                      cudaStream_t s) {
+    if (D % 2 || heads <= 0) return fail(VB_ERR_ARG, "rope: bad shape");
+    const int pairs = heads * (D / 2);
+    rope_kernel<<<(pairs + 255) / 256, 256, 0, s>>>(x, c, sn, pos, heads, D);
+    VB_LAUNCH_CHECK("rope_kernel");
+    return VB_OK;
+}
+
+vb_status launch_silu_mul(float* g, const float* u, int n, cudaStream_t s) {
+    if (n <= 0) return fail(VB_ERR_ARG, "silu_mul: n <= 0");
+    silu_mul_kernel<<<(n + 255) / 256, 256, 0, s>>>(g, u, n);
+    VB_LAUNCH_CHECK("silu_mul_kernel");
+    return VB_OK;
+}
+
+vb_status launch_add(float* a, const float* b, int n, cudaStream_t s) {
+    if (n <= 0) return fail(VB_ERR_ARG, "add: n <= 0");
+    add_kernel<<<(n + 255) / 256, 256, 0, s>>>(a, b, n);
+    VB_LAUNCH_CHECK("add_kernel");
+    return VB_OK;
+}
+
+vb_status launch_cache_append(float* kc, float* vc, const float* kn, const float* vn, int pos,
+                              int width, cudaStream_t s) {
+    if (width <= 0 || pos < 0) return fail(VB_ERR_ARG, "cache_append: bad args");
+    cache_append_kernel<<<(width + 255) / 256, 256, 0, s>>>(kc, vc, kn, vn, pos, width);
+    VB_LAUNCH_CHECK("cache_append_kernel");
+    return VB_OK;
+}
+
+size_t gemm_ws_floats(int M, int N, int K, bool q8) {
+    const int s = q8 ? gemm_splits<true>(N, K) : gemm_splits<false>(N, K);
+    return (size_t)s * M * N;
+}
+
+vb_status launch_gemm(const GemmArgs& a, bool q8, int epi, cudaStream_t s) {
+    if (a.M <= 0 || a.M > kGM) return fail(VB_ERR_UNSUPPORTED, "gemm: M must be 1..64");
+    if (a.K % kGK) return fail(VB_ERR_UNSUPPORTED, "gemm: K must be a multiple of 32");
+    if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemm: swiglu needs even N");
+    const int splits = q8 ? gemm_splits<true>(a.N, a.K) : gemm_splits<false>(a.N, a.K);
+    if ((size_t)splits * a.M * a.N > a.ws_floats) return fail(VB_ERR_ARG, "gemm: workspace too small");
+    int kper = (a.K + splits - 1) / splits;
+    kper = (kper + kGK - 1) / kGK * kGK;
+    dim3 grid((a.N + kGN - 1) / kGN, splits);
+    if (q8) gemm_partial_kernel<true><<<grid, 256, 0, s>>>(a, kper);
+    else gemm_partial_kernel<false><<<grid, 256, 0, s>>>(a, kper);
+    VB_LAUNCH_CHECK("gemm_partial_kernel");
+    const int outN = epi == kEpiSwiGLU ? a.N / 2 : a.N;
+    const size_t total = (size_t)a.M * outN;
+    int rb = (int)((total + 255) / 256);
+    if (rb > kNumSMs * 8) rb = kNumSMs * 8;
+#define VB_RED(Q, E) gemm_reduce_kernel<Q, E><<<rb, 256, 0, s>>>(a, splits)
+    if (q8) {
+        if (epi == kEpiResidual) VB_RED(true, kEpiResidual);
+        else if (epi == kEpiSwiGLU) VB_RED(true, kEpiSwiGLU);
+        else VB_RED(true, kEpiStore);
+    } else {
+        if (epi == kEpiResidual) VB_RED(false, kEpiResidual);
+        else if (epi == kEpiSwiGLU) VB_RED(false, kEpiSwiGLU);
+        else VB_RED(false, kEpiStore);
+    }
+#undef VB_RED
+    VB_LAUNCH_CHECK("gemm_reduce_kernel");
+    return VB_OK;
+}
+
+}  // namespace vb

@@ -1,0 +1,110 @@
+// vb_kernels.cuh -- internal launchers shared by the C ABI and the engines.
+#pragma once
+
+#include "vb_common.cuh"
+
+namespace vb {
+
+// GEMV prologue: the input vector is used as is, or RMS-normalised with a
+// weight vector first (the rmsnorm that precedes every projection).
+enum GemvPro : int { kProNone = 0, kProRms = 1 };
+// GEMV epilogue.
+enum GemvEpi : int {
+    kEpiStore = 0,     // y[j] = dot_j
+    kEpiResidual = 1,  // y[j] += dot_j                        (o_proj / down_proj + residual)
+    kEpiSwiGLU = 2,    // rows interleaved gate/up: y[j] = silu(dot_2j) * dot_2j+1
+    kEpiArgmax = 3,    // y[j] = dot_j and per-CTA (max, argmax) partials
+};
+
+struct GemvArgs {
+    const float* x;        // [K] input (or embedding row base when x_tok != null)
+    const int* x_tok;      // optional: x = x + (*x_tok) * K  (embedding lookup fused)
+    const float* norm_w;   // [K] rmsnorm weight (kProRms)
+    float eps;
+    const void* W;         // [N, K] f32 or int8
+    const float* scales;   // [N] (int8 only)
+    float* y;              // output
+    int N, K;
+    float* part_val;       // [gridDim] (kEpiArgmax)
+    int* part_idx;         // [gridDim]
+};
+
+// Launch config chosen so every SM streams weights even for 1024-row outputs.
+vb_status launch_gemv(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s,
+                      int* grid_out = nullptr);
+int gemv_grid(int N, bool q8, int epi);
+
+// Final reduction of argmax partials: out_idx[0] = argmax, optional value.
+vb_status launch_argmax_parts(const float* part_val, const int* part_idx, int parts,
+                              int* out_idx, cudaStream_t s);
+
+vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_t* q,
+                               float* scales, cudaStream_t s);
+vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows,
+                              int dim, float eps, cudaStream_t s);
+
+// Per-head q/k RMSNorm + RoPE for B sequences, writing rotated q to q_out
+// [B, H, D] and k / v rows into the caches at each sequence's position.
+struct QkNormArgs {
+    const float* qkv;       // [B, (H + 2*KVH) * D]  (q | k | v)
+    const float* q_norm;    // [D]
+    const float* k_norm;    // [D]
+    const float* cos_tab;   // [rope_positions, D]
+    const float* sin_tab;
+    const int* pos;         // [B] device positions (write row)
+    float* q_out;           // [B, H, D]
+    float* kc;              // cache base
+    float* vc;
+    int64_t stride_b, stride_pos, stride_h;  // cache strides (floats)
+    int B, H, KVH, D, rope_positions;
+    float eps;
+    int* err;               // device error word (may be null)
+};
+vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s);
+
+// Split-K decode attention.  lens[b] = number of valid cache rows.
+struct AttnArgs {
+    const float* q;        // [B, H, D]
+    const float* k;        // cache base
+    const float* v;
+    float* out;            // [B, H, D]
+    const int* lens;       // [B] (device)
+    const int* pos;        // alternative to lens: lens[b] = pos[b] + 1 (may be null)
+    int B, H, KVH, D, n_max;
+    int64_t stride_b, stride_pos, stride_h;
+    int splits;            // splits per (b, kvh)
+    float* ws;             // partials
+};
+int attn_splits_for(int B, int KVH, int n_max);
+size_t attn_ws_bytes(int B, int H, int splits);
+vb_status launch_attention(const AttnArgs& a, cudaStream_t s);
+
+vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
+                       float* out, int* err, cudaStream_t s);
+vb_status launch_argmax_rows(const float* logits, int rows, int64_t n, int* out_idx,
+                             cudaStream_t s);
+vb_status launch_rope(float* x, const float* cos_tab, const float* sin_tab, int pos,
+                      int heads, int D, cudaStream_t s);
+vb_status launch_silu_mul(float* gate, const float* up, int n, cudaStream_t s);
+vb_status launch_add(float* a, const float* b, int n, cudaStream_t s);
+vb_status launch_cache_append(float* kc, float* vc, const float* kn, const float* vn,
+                              int pos, int width, cudaStream_t s);
+// pos[b] += 1; tokens[b] = next[b]
+vb_status launch_advance(int* pos, int* tokens, const int* next, int B, cudaStream_t s);
+
+// Batched (M <= 64) GEMM, C = A . W^T with split-K partials and a fused
+// reduction epilogue.
+struct GemmArgs {
+    const float* A;        // [M, K]
+    const void* W;         // [N, K] f32 or int8
+    const float* scales;   // [N] int8 only
+    float* C;              // output (layout depends on epi)
+    int M, N, K;
+    int ldc;               // row stride of C in floats
+    float* ws;             // split-K partial workspace
+    size_t ws_floats;
+};
+size_t gemm_ws_floats(int M, int N, int K, bool q8);
+vb_status launch_gemm(const GemmArgs& a, bool q8, int epi, cudaStream_t s);
+
+}  // namespace vb
