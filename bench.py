@@ -1,0 +1,483 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200 engine on the Qwen3-0.6B architecture.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload batched-int8|bs1-f32|bs1-int8] [--prompt P]
+                    [--no-extras] [--no-cpu]
+
+Headline workload (default, every N): batched independent-sequence INT8
+decode -- 64 sequences per GPU, each with a 2048-token uniform-random prompt,
+then greedy decode; weights replicated per GPU, sequences sharded, no
+collective on the token path (weak scaling).  One step = one decode token for
+all 64 sequences of every GPU.  value = tokens/s over all GPUs, timed with
+CUDA events on the engine's stream over exactly K graph-replayed steps after
+W warm-up steps, max over ranks.
+
+At N=1 rank 0 also reports, in the same JSON line:
+  bs1_f32  -- batch-1 f32 decode, 32-token prompt + 128 greedy tokens
+  bs1_int8 -- batch-1 INT8 decode, 512-token prompt + 512 greedy tokens
+and the CPU baseline: the reference engine itself (oracle/_ref, compiled from
+its own sources) timed on this host's cores on a bounded sample.
+
+--impl reference times the reference's CPU implementation (Model::step of
+oracle/_ref) on the same workload and prints the same JSON line with
+"impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "verbum.cpp_b200"), str(ROOT / "oracle")]
+
+METRIC = "Qwen3-0.6B decode tok/s (bs1 f32/int8; batched 1-8 GPU) + % HBM roofline"
+WEIGHT_SEED = 1234
+FALLBACK_HBM_GBS = 6650.0
+KV_BYTES_PER_POS = 28 * 2 * 8 * 128 * 4  # 229,376 B: K and V rows of all layers
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during a timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                if int(f[0]) not in self.gpus:
+                    continue
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "power_w_max": max(power), "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def write_model(tmpdir, cfg, weights):
+    import vbsynth
+    return vbsynth.write_model_dir(Path(tmpdir) / "qwen3-0.6b-synth", cfg, weights)
+
+
+# ---------------------------------------------------------------------------
+# reference (CPU) timing -- oracle/_ref is the reference engine itself
+# ---------------------------------------------------------------------------
+
+def _ref_worker(args):
+    model_dir, mode, ctx, warm, steps, first_token = args
+    import oracle
+    m = oracle.RefModel(model_dir)
+    if mode == "int8":
+        m.quantize()
+    m.reset_cache(ctx + warm + steps + 8)
+    m.set_cache_len(ctx)
+    if warm:
+        m.greedy_steps(first_token, warm)
+    _, secs = m.greedy_steps(first_token, steps)
+    m.close()
+    return [float(s) for s in secs]
+
+
+def ref_time(model_dir, mode, ctx, warm, steps, procs):
+    """Times Model::step of the reference at context length ctx on `procs`
+    single-threaded processes (the engine is single-threaded), each decoding
+    its own sequence.  Returns (aggregate tok/s, per-step seconds)."""
+    jobs = [(str(model_dir), mode, ctx, warm, steps, 1000 + i) for i in range(procs)]
+    with mp.get_context("spawn").Pool(procs) as pool:
+        res = pool.map(_ref_worker, jobs)
+    per_proc_rate = [len(r) / sum(r) for r in res]
+    return sum(per_proc_rate), [s for r in res for s in r]
+
+
+def ref_procs(max_procs=16, gb_per_proc=5.0):
+    n = os.cpu_count() or 1
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available / 1e9
+        n = min(n, max(1, int(avail // gb_per_proc)))
+    except Exception:
+        pass
+    return max(1, min(n, max_procs))
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# GPU workloads
+# ---------------------------------------------------------------------------
+
+def step_kv_bytes(n_ctx):
+    """KV traffic of one decode step at context n_ctx (reads n_ctx rows incl.
+    the new one, writes 1)."""
+    return KV_BYTES_PER_POS * (n_ctx + 1)
+
+
+def run_batched(args, grp, weights, cfg):
+    import numpy as np
+    import torch
+
+    import vb200
+    import vbdist
+    import vbsynth
+
+    B = args.batch
+    P = args.prompt
+    K, W = args.steps, args.warmup
+    dev = grp.local_rank
+    torch.cuda.set_device(dev)
+    eng = vb200.Engine(cfg, device=dev).load(weights)
+    eng.quantize()
+    bt = vb200.Batch(eng, B, P + W + 2 * K + 8)
+    gidx = list(vbdist.shard(B * grp.world, grp.rank, grp.world))
+    prompts = np.stack([vbsynth.prompt_ids(P, vbdist.sequence_seed(g), cfg["vocab_size"])
+                        for g in gidx])
+    t0 = time.perf_counter()
+    nx = bt.prefill(prompts.T.copy())
+    prefill_s = time.perf_counter() - t0
+    if W:
+        nx = bt.decode(nx, W)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(list(range(grp.world)) if grp.world > 1 else [dev]).start() \
+        if grp.rank == 0 else None
+    grp.barrier()
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    nx = bt.decode(nx, K)
+    ev1.record(stream)
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    grp.barrier()
+    ms = ev0.elapsed_time(ev1)
+    # end to end through the C ABI with host buffers: tokens in, next tokens out
+    grp.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        _, nx = bt.step(nx, want_logits=False, want_next=True)
+    e2e_s = time.perf_counter() - t0
+    grp.barrier()
+    clocks = clk.stop() if clk else None
+    ms_max = grp.reduce_max(ms)
+    e2e_max = grp.reduce_max(e2e_s)
+    checksum = grp.gather_ints([int(x) for x in nx[:4]])
+    n_mid = P + W + K // 2
+    res = {
+        "ms": ms_max, "e2e_s": e2e_max, "prefill_s": grp.reduce_max(prefill_s),
+        "graph_nodes": bt.graph_nodes(), "n_mid": n_mid, "clocks": clocks,
+        "checksum": checksum, "weight_bytes": eng.weight_bytes(),
+    }
+    # dominant kernel: split-K attention over the 64 caches, timed standalone on
+    # this workload's shape at the mid context (28 launches = one step's worth)
+    res["attn"] = time_attention(B, n_mid, dev, launches=28)
+    bt.close()
+    eng.close()
+    return res
+
+
+def time_attention(B, n, dev, launches=28, H=16, KVH=8, D=128):
+    import torch
+
+    import vb200
+    g = torch.Generator(device=f"cuda:{dev}").manual_seed(5)
+    q = torch.randn(B, H, D, device=f"cuda:{dev}", generator=g)
+    # [B, KVH, n, D]: the engine's cache layout
+    k = torch.randn(B, KVH, n, D, device=f"cuda:{dev}", generator=g)
+    v = torch.randn(B, KVH, n, D, device=f"cuda:{dev}", generator=g)
+    lens = torch.full((B,), n, dtype=torch.int32, device=f"cuda:{dev}")
+    out = torch.empty(B, H, D, device=f"cuda:{dev}")
+    ws = torch.empty(vb200.attn_workspace_bytes(B, H, n) // 4 + 1, device=f"cuda:{dev}")
+    s = torch.cuda.current_stream(dev)
+    args = (q, k, v, out, lens, B, H, KVH, D, n, KVH * n * D, D, n * D, ws)
+    for _ in range(3):
+        vb200.attn_decode_batched(*args, stream=s.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(s)
+    for _ in range(launches):
+        vb200.attn_decode_batched(*args, stream=s.cuda_stream)
+    e1.record(s)
+    e1.synchronize()
+    per = e0.elapsed_time(e1) / launches / 1e3
+    bytes_ = B * n * KVH * D * 4 * 2
+    del k, v
+    torch.cuda.empty_cache()
+    return {"kernel": "attn_split_kernel<2> + attn_merge_kernel", "sec_per_launch": per,
+            "bytes_per_launch": bytes_, "B": B, "n": n}
+
+
+def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
+    import numpy as np
+    import torch
+
+    import vb200
+    import vbsynth
+    e = vb200.Engine(cfg, device=dev).load(weights)
+    if mode == "int8":
+        e.quantize()
+    prompt = vbsynth.prompt_ids(prompt_len, 77 + prompt_len, cfg["vocab_size"])
+    max_seq = prompt_len + n_new + 8
+    # warm-up pass
+    e.reset_cache(max_seq)
+    lg = e.prefill(prompt, want_logits=True)
+    e.decode(int(np.argmax(lg)), warm)
+    # timed pass: n_new greedy tokens, device-side feedback
+    e.reset_cache(max_seq)
+    lg = e.prefill(prompt, want_logits=True)
+    first = int(np.argmax(lg))
+    stream = torch.cuda.ExternalStream(e.stream(), device=dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    toks = e.decode(first, n_new)
+    ev1.record(stream)
+    ev1.synchronize()
+    sec = ev0.elapsed_time(ev1) / 1e3
+    # end to end, reference semantics: step(token) -> logits in host memory
+    e.reset_cache(max_seq)
+    e.prefill(prompt)
+    tok = first
+    t0 = time.perf_counter()
+    lat = []
+    for _ in range(n_new):
+        t1 = time.perf_counter()
+        lg = e.step(tok)
+        lat.append(time.perf_counter() - t1)
+        tok = int(np.argmax(lg))
+    e2e = time.perf_counter() - t0
+    wb = e.weight_bytes()
+    nodes = e.graph_nodes()
+    e.close()
+    mean_ctx = prompt_len + (n_new - 1) / 2.0
+    bytes_tok = wb + step_kv_bytes(mean_ctx)
+    lat.sort()
+    return {"tok_s": n_new / sec, "ms_per_token": 1e3 * sec / n_new, "bytes_per_token": bytes_tok,
+            "achieved_gbs": bytes_tok * n_new / sec / 1e9, "e2e_tok_s": n_new / e2e,
+            "e2e_p50_ms": 1e3 * lat[len(lat) // 2], "e2e_p99_ms": 1e3 * lat[min(len(lat) - 1, int(0.99 * len(lat)))],
+            "graph_nodes": nodes, "weight_bytes": wb, "prompt": prompt_len, "decode_tokens": n_new,
+            "first_tokens": [int(t) for t in toks[:4]]}
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=252)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["batched-int8"], default="batched-int8")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=2048)
+    ap.add_argument("--no-extras", action="store_true", help="skip the bs1 lines")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 0 or args.steps <= 0:
+        raise SystemExit("--steps must be > 0")
+
+    import vbdist
+    rank, world, local_rank = vbdist.env_rank()
+    if args.impl == "reference":
+        return main_reference(args, rank, world)
+
+    # CPU-baseline processes are spawned before any GPU work
+    import vbsynth
+    cfg = vbsynth.qwen3_config()
+    weights = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+    grp = vbdist.Group()
+    peak, peak_kind = hbm_peak()
+
+    res = run_batched(args, grp, weights, cfg)
+    B, K, N = args.batch, args.steps, grp.world
+    sec = res["ms"] / 1e3
+    value = N * B * K / sec
+    attn = res["attn"]
+    a_gbs = attn["bytes_per_launch"] / attn["sec_per_launch"] / 1e9
+    step_bytes = res["weight_bytes"] + B * step_kv_bytes(res["n_mid"])
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": N,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["ms"] / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "weights": "int8 (per-row absmax) projections, f32 embedding/lm_head",
+        "data": "synthetic: seeded N(0,0.02) random-init weights, uniform random prompt ids",
+        "config": {
+            "workload": f"batched-int8: {B} independent sequences per GPU, {args.prompt}-token "
+                        f"prompts, greedy decode steps {args.warmup}+{K} (warm-up+timed)",
+            "model": "Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8 heads, D 128, "
+                     "ffn 3072, vocab 151936, tied)",
+            "global_batch": B * N, "seq_len": args.prompt + args.warmup + K,
+            "parallelism": f"replicas x{N}: sequences sharded, weights replicated, no collective",
+            "l2": "inputs larger than L2 (>=1.06 GB of weights and ~32 GB of KV per step)",
+            "step_roofline_frac": round(step_bytes / (sec / K) / 1e9 / peak, 4),
+            "step_bytes": step_bytes,
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": attn["kernel"],
+            "achieved": round(a_gbs, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(a_gbs / peak, 4), "peak_kind": peak_kind,
+            "traffic": None,
+            "algorithmic_bytes_per_launch": attn["bytes_per_launch"],
+            "launch_shape": f"B={attn['B']} n={attn['n']} KVH=8 D=128 f32",
+        },
+        "clocks": res["clocks"],
+        "e2e": {"value": round(N * B * K / res["e2e_s"], 2), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B * N, "d2h_bytes_per_step": 4 * B * N,
+                "api": "vb_batch_step (host token ids in, host greedy ids out, per step)"},
+        "gpu_launches": res["graph_nodes"] * K,
+        "prefill_s": round(res["prefill_s"], 3),
+    }
+    if grp.rank == 0 and N == 1 and not args.no_extras:
+        for mode, P, G in (("f32", 32, 128), ("int8", 512, 512)):
+            r = run_bs1(mode, P, G, weights, cfg, dev=local_rank)
+            r["roofline_frac"] = round(r["achieved_gbs"] / peak, 4)
+            line[f"bs1_{mode}"] = r
+    if grp.rank == 0 and N == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(cfg, weights, args)
+    grp.close()
+    if grp.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(cfg, weights, args):
+    import oracle
+    if not oracle.have_ref():
+        return {"value": None, "unit": "tok/s", "kind": "reference",
+                "sample": "oracle/_ref not built"}
+    procs = ref_procs()
+    with tempfile.TemporaryDirectory() as td:
+        mdir = write_model(td, cfg, weights)
+        rate, secs = ref_time(mdir, "int8", args.prompt, 1, 3, procs)
+        out = {"value": round(rate, 4), "unit": "tok/s", "cores": procs, "kind": "reference",
+               "sample": f"reference Model::step (oracle/_ref), INT8, context {args.prompt}, "
+                         f"{procs} single-threaded processes x 3 timed decode steps "
+                         f"(+1 warm-up), one sequence each",
+               "cpu": cpu_model(), "nproc": os.cpu_count(),
+               "step_s_median": round(statistics.median(secs), 3)}
+        if not args.no_extras:
+            r32, s32 = ref_time(mdir, "f32", 32 + 64, 0, 2, 1)
+            r8, s8 = ref_time(mdir, "int8", 512 + 256, 0, 2, 1)
+            out["bs1_f32"] = {"value": round(r32, 4), "cores": 1,
+                              "sample": "2 decode steps at context 96 (config 1 mid-point)"}
+            out["bs1_int8"] = {"value": round(r8, 4), "cores": 1,
+                               "sample": "2 decode steps at context 768 (config 3 mid-point)"}
+    return out
+
+
+def main_reference(args, rank, world):
+    """Reference arm: the reference's own CPU decode (oracle/_ref), same workload."""
+    if rank != 0:
+        return 0
+    import oracle
+    import vbsynth
+    if not oracle.have_ref():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libverbum_ref.so not built"}))
+        return 0
+    cfg = vbsynth.qwen3_config()
+    weights = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+    procs = ref_procs()
+    # each "step" is one decode token for each of `procs` sequences; bounded so
+    # the whole run stays within a few minutes (~1.3 s per step at context 2048)
+    steps = max(1, min(args.steps, 6))
+    warm = 1 if args.warmup > 0 else 0
+    with tempfile.TemporaryDirectory() as td:
+        mdir = write_model(td, cfg, weights)
+        del weights
+        rate, secs = ref_time(mdir, "int8", args.prompt, warm, steps, procs)
+    sample = (f"reference Model::step (oracle/_ref, compiled from the reference sources), INT8, "
+              f"context {args.prompt}, {procs} single-threaded processes x {steps} timed steps "
+              f"(+{warm} warm-up); one sequence per process")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": warm,
+        "ms_per_step": round(1e3 * statistics.mean(secs), 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) random-init weights",
+        "config": {"workload": f"batched-int8 decode at context {args.prompt} (CPU sample)",
+                   "model": "Qwen3-0.6B architecture", "parallelism": f"{procs} CPU processes"},
+        "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": procs,
+                         "kind": "reference", "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

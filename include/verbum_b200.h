@@ -217,6 +217,13 @@ VB_API vb_status vb_engine_step(vb_engine* e, int token, float* logits_host);
  * receives the last step's logits. */
 VB_API vb_status vb_engine_decode(vb_engine* e, int first_token, int n, int* tokens_host,
                            float* logits_host);
+/* Prefill: feeds tokens_host[0..n) one position at a time (the token-by-token
+ * prefill of tools/generate.cpp:75-77) with no host synchronisation between
+ * tokens; logits_host, if not NULL, receives the last token's logits. */
+VB_API vb_status vb_engine_prefill(vb_engine* e, const int* tokens_host, int n,
+                                   float* logits_host);
+/* Kernel launches in one captured step (graph nodes), 0 before the first step. */
+VB_API int vb_engine_graph_nodes(const vb_engine* e);
 /* Copies layer `layer`'s K (which=0) or V cache rows [0, len) into host
  * memory as [len, KVH*D] (the reference KVCache layout). */
 VB_API vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host);
@@ -241,6 +248,11 @@ VB_API vb_status vb_batch_step(vb_batch* b, const int* tokens_host, float* logit
 /* n greedy steps on the device from the tokens fed last (or tokens_host if not
  * NULL); next tokens after the last step go to next_host [B] if not NULL. */
 VB_API vb_status vb_batch_decode(vb_batch* b, const int* tokens_host, int n, int* next_host);
+/* Prefill P positions for all B sequences: tokens_host is [P][B]
+ * (position-major); next_host [B] (may be NULL) gets the greedy pick after
+ * the last position. */
+VB_API vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, int* next_host);
+VB_API int vb_batch_graph_nodes(const vb_batch* b);
 VB_API int vb_batch_cache_len(const vb_batch* b);
 VB_API vb_status vb_batch_reset(vb_batch* b);
 

@@ -33,6 +33,9 @@ struct vb_batch {
     int* h_io = nullptr;  // pinned [2*B]
     cudaGraphExec_t graph = nullptr;
     bool graph_q8 = false;
+    int graph_nodes = 0;
+    int* d_prompt = nullptr;  // [P][B] prefill tokens
+    int prompt_cap = 0;
 };
 
 namespace vb {
@@ -152,6 +155,9 @@ vb_status batch_graph(vb_batch* b) {
         return st;
     }
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    b->graph_nodes = (int)nn;
     ce = cudaGraphInstantiate(&b->graph, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) {
@@ -255,7 +261,7 @@ vb_status vb_batch_destroy(vb_batch* b) {
     if (b->graph) cudaGraphExecDestroy(b->graph);
     bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->qkv); bfree(b->q);
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
-    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err);
+    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err); bfree(b->d_prompt);
     if (b->h_io) cudaFreeHost(b->h_io);
     delete b;
     return VB_OK;
@@ -325,6 +331,41 @@ vb_status vb_batch_decode(vb_batch* b, const int* tokens_host, int n, int* next_
     b->len += n;
     return VB_OK;
 }
+
+vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, int* next_host) {
+    if (!b || !tokens_host) return fail(VB_ERR_ARG, "null argument");
+    if (P <= 0) return VB_OK;
+    Dev dg(b->e->device);
+    vb_status st = batch_pre(b, P);
+    if (st) return st;
+    const size_t n = (size_t)P * b->B;
+    for (size_t i = 0; i < n; i++)
+        if (tokens_host[i] < 0 || tokens_host[i] >= b->e->cfg.vocab)
+            return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    if (b->prompt_cap < (int)n) {
+        bfree(b->d_prompt);
+        if ((st = balloc(&b->d_prompt, n, "prompt"))) return st;
+        b->prompt_cap = (int)n;
+    }
+    cudaStream_t s = b->e->stream;
+    VB_CUDA_TRY(cudaMemcpyAsync(b->d_prompt, tokens_host, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+    for (int t = 0; t < P; t++) {
+        VB_CUDA_TRY(cudaMemcpyAsync(b->d_tok, b->d_prompt + (size_t)t * b->B, sizeof(int) * b->B,
+                                    cudaMemcpyDeviceToDevice, s));
+        VB_CUDA_TRY(cudaGraphLaunch(b->graph, s));
+    }
+    if (next_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
+                                    cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    if ((st = batch_check_err(b))) return st;
+    if (next_host)
+        for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
+    b->len += P;
+    return VB_OK;
+}
+
+int vb_batch_graph_nodes(const vb_batch* b) { return b ? b->graph_nodes : 0; }
 
 int vb_batch_cache_len(const vb_batch* b) { return b ? b->len : 0; }
 

@@ -67,6 +67,7 @@ void free_cache(vb_engine* e) {
     dfree(e->vc);
     dfree(e->attn_ws);
     dfree(e->d_hist);
+    dfree(e->d_prompt);
     if (e->graph) cudaGraphExecDestroy(e->graph);
     e->graph = nullptr;
 }
@@ -229,6 +230,9 @@ static vb_status ensure_graph(vb_engine* e) {
         return st;
     }
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    size_t nn = 0;
+    cudaGraphGetNodes(g, nullptr, &nn);
+    e->graph_nodes = (int)nn;
     ce = cudaGraphInstantiate(&e->graph, g, 0);
     cudaGraphDestroy(g);
     if (ce != cudaSuccess) {
@@ -479,6 +483,7 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
         if ((st = dalloc(&e->attn_ws, attn_ws_bytes(1, c.heads, e->attn_splits) / 4 + 1, "attn ws")))
             return st;
         if ((st = dalloc(&e->d_hist, max_seq, "history"))) return st;
+        if ((st = dalloc(&e->d_prompt, max_seq, "prompt"))) return st;
     }
     VB_CUDA_TRY(cudaMemset(e->d_pos, 0, sizeof(int)));
     e->len = 0;
@@ -546,6 +551,35 @@ vb_status vb_engine_decode(vb_engine* e, int first_token, int n, int* tokens_hos
     e->len += n;
     return VB_OK;
 }
+
+vb_status vb_engine_prefill(vb_engine* e, const int* tokens_host, int n, float* logits_host) {
+    if (!e || !tokens_host) return fail(VB_ERR_ARG, "null argument");
+    if (n <= 0) return VB_OK;
+    DeviceGuard dg(e->device);
+    vb_status st = pre_step(e, n);
+    if (st) return st;
+    for (int i = 0; i < n; i++)
+        if (tokens_host[i] < 0 || tokens_host[i] >= e->cfg.vocab)
+            return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_prompt, tokens_host, sizeof(int) * n, cudaMemcpyHostToDevice,
+                                e->stream));
+    e->h_pinned_i[1] = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    for (int i = 0; i < n; i++) {
+        VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->d_prompt + i, sizeof(int),
+                                    cudaMemcpyDeviceToDevice, e->stream));
+        VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    }
+    if (logits_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->cfg.vocab * 4,
+                                    cudaMemcpyDeviceToHost, e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if ((st = engine_check_err(e))) return st;
+    e->len += n;
+    return VB_OK;
+}
+
+int vb_engine_graph_nodes(const vb_engine* e) { return e ? e->graph_nodes : 0; }
 
 vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host) {
     if (!e || !host) return fail(VB_ERR_ARG, "null argument");

@@ -88,6 +88,8 @@ struct vb_engine {
     float* h_logits = nullptr;
 
     cudaGraphExec_t graph = nullptr;
+    int graph_nodes = 0;
+    int* d_prompt = nullptr;   // prefill tokens [max_seq]
 
     // persistent fused step (vb_mega.cu)
     void* mega = nullptr;

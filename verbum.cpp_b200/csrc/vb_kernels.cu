@@ -369,7 +369,8 @@ template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = a.lens ? a.lens[b] : a.pos[b] + 1;
+    int n = a.lens ? a.lens[b] : a.pos[b] + 1;
+    n = n < 0 ? 0 : (n > a.n_max ? a.n_max : n);
     const int chunk = (n + a.splits - 1) / a.splits;
     const int p0 = split * chunk;
     const int p1 = min(n, p0 + chunk);
@@ -482,7 +483,7 @@ __global__ void attn_merge_kernel(AttnArgs a) {
         L = fmaf(base[s * 130 + 1], f, L);
         A = fmaf(base[s * 130 + 2 + d], f, A);
     }
-    a.out[((size_t)b * a.H + h) * 128 + d] = A / L;
+    a.out[((size_t)b * a.H + h) * 128 + d] = (L > 0.0f) ? A / L : 0.0f;
 }
 
 __global__ void embed_kernel(const float* E, const int* tokens, int dim, int vocab, float* out,
@@ -702,7 +703,7 @@ vb_status launch_gemv(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t
                       int* grid_out) {
     if (a.N <= 0 || a.K <= 0) return fail(VB_ERR_ARG, "gemv: empty shape");
     if (q8 ? (a.K % 16) : (a.K % 4)) return fail(VB_ERR_UNSUPPORTED, "gemv: K alignment");
-    if (a.K > 12288) return fail(VB_ERR_UNSUPPORTED, "gemv: K > 12288");
+    if (a.K > 8192) return fail(VB_ERR_UNSUPPORTED, "gemv: K > 8192");
     if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemv: swiglu needs even N");
     const int R = gemv_rows_per_warp(a.N, q8, epi);
     const int grid = gemv_grid(a.N, q8, epi);

@@ -88,6 +88,8 @@ _SIGS = {
     "vb_engine_step": (_I, [_P, _I, _P]),
     "vb_engine_decode": (_I, [_P, _I, _I, _P, _P]),
     "vb_engine_read_kv": (_I, [_P, _I, _I, _P]),
+    "vb_engine_prefill": (_I, [_P, _P, _I, _P]),
+    "vb_engine_graph_nodes": (_I, [_P]),
     "vb_engine_set_path": (_I, [_P, _I]),
     "vb_engine_stream": (_P, [_P]),
     "vb_batch_create": (_I, [_P, _I, _I, C.POINTER(C.c_void_p)]),
@@ -95,6 +97,8 @@ _SIGS = {
     "vb_batch_step": (_I, [_P, _P, _P, _P]),
     "vb_batch_decode": (_I, [_P, _P, _I, _P]),
     "vb_batch_cache_len": (_I, [_P]),
+    "vb_batch_prefill": (_I, [_P, _P, _I, _P]),
+    "vb_batch_graph_nodes": (_I, [_P]),
     "vb_batch_reset": (_I, [_P]),
 }
 
@@ -217,6 +221,16 @@ class Engine:
                                      _ptr(lg) if lg is not None else None))
         return (toks, lg) if want_logits else toks
 
+    def prefill(self, tokens, want_logits=False):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        lg = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        check(lib().vb_engine_prefill(self.h, _ptr(t), int(t.size),
+                                      _ptr(lg) if lg is not None else None))
+        return lg
+
+    def graph_nodes(self) -> int:
+        return lib().vb_engine_graph_nodes(self.h)
+
     def read_kv(self, layer: int, which: int) -> np.ndarray:
         n = self.cache_len()
         out = np.empty((n, self.vcfg.kv_heads * self.vcfg.head_dim), dtype=np.float32)
@@ -265,6 +279,17 @@ class Batch:
         nx = np.empty(self.B, dtype=np.int32)
         check(lib().vb_batch_decode(self.h, _ptr(t) if t is not None else None, int(n), _ptr(nx)))
         return nx
+
+    def prefill(self, tokens_pb):
+        """tokens_pb: [P, B] position-major prompt ids; returns next ids [B]."""
+        t = np.ascontiguousarray(tokens_pb, dtype=np.int32)
+        assert t.ndim == 2 and t.shape[1] == self.B
+        nx = np.empty(self.B, dtype=np.int32)
+        check(lib().vb_batch_prefill(self.h, _ptr(t), int(t.shape[0]), _ptr(nx)))
+        return nx
+
+    def graph_nodes(self) -> int:
+        return lib().vb_batch_graph_nodes(self.h)
 
     def cache_len(self) -> int:
         return lib().vb_batch_cache_len(self.h)
