@@ -273,6 +273,102 @@ def time_attention(B, n, dev, launches=28, H=16, KVH=8, D=128):
             "bytes_per_launch": bytes_, "B": B, "n": n}
 
 
+GEMV_SHAPES = [("q", 1024, 2048), ("k", 1024, 1024), ("v", 1024, 1024), ("o", 2048, 1024),
+               ("gate", 1024, 3072), ("up", 1024, 3072), ("down", 3072, 1024),
+               ("lm_head", 1024, 151936)]
+
+
+def _graph_time(fn, launches, dev):
+    """Captures `launches` calls of fn(i) in one CUDA graph and times its replay
+    with CUDA events (back-to-back launches, no host overhead between them)."""
+    import torch
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(launches):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    e1.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / (reps * launches)
+    del g
+    return sec
+
+
+def gemv_microbench(dev=0, shapes=None, dtypes=("f32", "int8"), min_bytes=2 * 126 * 2**20):
+    """Config 2: each GEMV shape, f32 and INT8, rotating through enough weight
+    copies that the weights come from HBM (>= 2x L2 per rotation)."""
+    import torch
+
+    import vb200
+    out = {}
+    for name, K, N in (shapes or GEMV_SHAPES):
+        for dt in dtypes:
+            wbytes = N * K * (4 if dt == "f32" else 1) + (0 if dt == "f32" else 4 * N)
+            copies = max(1, -(-min_bytes // wbytes))
+            x = torch.randn(1, K, device=f"cuda:{dev}")
+            y = torch.empty(1, N, device=f"cuda:{dev}")
+            if dt == "f32":
+                Ws = [torch.randn(N, K, device=f"cuda:{dev}") * 0.02 for _ in range(copies)]
+                fn = lambda i: vb200.matmul_nt_f32(x, Ws[i % copies], y,
+                                                   stream=torch.cuda.current_stream().cuda_stream)
+            else:
+                Ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device=f"cuda:{dev}")
+                      for _ in range(copies)]
+                sc = [torch.rand(N, device=f"cuda:{dev}") * 1e-3 for _ in range(copies)]
+                fn = lambda i: vb200.matmul_nt_q8(x, Ws[i % copies], sc[i % copies], y,
+                                                  stream=torch.cuda.current_stream().cuda_stream)
+            launches = max(copies * 2, 20)
+            sec = _graph_time(fn, launches, dev)
+            alg = wbytes + 4 * K + 4 * N
+            out[f"{name}_{dt}"] = {"K": K, "N": N, "us": round(sec * 1e6, 2),
+                                   "gbs": round(alg / sec / 1e9, 1)}
+            del Ws
+            torch.cuda.empty_cache()
+    return out
+
+
+def attn_microbench(dev=0, ns=(512, 2048, 8192, 32768), Bs=(1, 32), H=16, KVH=8, D=128):
+    """Config 4: isolated GQA decode attention, K/V [B, n, 8, 128] f32 ~ N(0,1),
+    RoPE pre-applied; GB/s on KV reads (each KV head read once)."""
+    import torch
+
+    import vb200
+    out = {}
+    for B in Bs:
+        for n in ns:
+            g = torch.Generator(device=f"cuda:{dev}").manual_seed(n + B)
+            q = torch.randn(B, H, D, device=f"cuda:{dev}", generator=g)
+            k = torch.randn(B, n, KVH, D, device=f"cuda:{dev}", generator=g)
+            v = torch.randn(B, n, KVH, D, device=f"cuda:{dev}", generator=g)
+            lens = torch.full((B,), n, dtype=torch.int32, device=f"cuda:{dev}")
+            o = torch.empty(B, H, D, device=f"cuda:{dev}")
+            ws = torch.empty(vb200.attn_workspace_bytes(B, H, n) // 4 + 1, device=f"cuda:{dev}")
+            kv_bytes = B * n * KVH * D * 4 * 2
+            launches = max(4, min(64, int(4e9 // kv_bytes)))
+
+            def fn(i):
+                vb200.attn_decode_batched(q, k, v, o, lens, B, H, KVH, D, n, n * KVH * D, KVH * D,
+                                          D, ws, stream=torch.cuda.current_stream().cuda_stream)
+            sec = _graph_time(fn, launches, dev)
+            out[f"B{B}_n{n}"] = {"us": round(sec * 1e6, 2), "gbs": round(kv_bytes / sec / 1e9, 1),
+                                 "kv_bytes": kv_bytes}
+            del k, v
+            torch.cuda.empty_cache()
+    return out
+
+
 def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
     import numpy as np
     import torch
@@ -340,6 +436,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-extras", action="store_true", help="skip the bs1 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--only", choices=["gemv", "attn"], help="one kernel family (for profiling)")
+    ap.add_argument("--ctx", type=int, default=2048, help="--only attn: context length")
+    ap.add_argument("--shape", default=None, help="--only gemv: one of q,k,v,o,gate,up,down,lm_head")
     args = ap.parse_args()
     if args.warmup < 0 or args.steps <= 0:
         raise SystemExit("--steps must be > 0")
@@ -348,6 +447,14 @@ def main():
     rank, world, local_rank = vbdist.env_rank()
     if args.impl == "reference":
         return main_reference(args, rank, world)
+    if args.only == "gemv":
+        shapes = [s for s in GEMV_SHAPES if args.shape in (None, s[0])]
+        print(json.dumps({"gemv": gemv_microbench(local_rank, shapes)}), flush=True)
+        return 0
+    if args.only == "attn":
+        print(json.dumps({"attn": attn_microbench(local_rank, ns=(args.ctx,), Bs=(args.batch,))}),
+              flush=True)
+        return 0
 
     # CPU-baseline processes are spawned before any GPU work
     import vbsynth
@@ -408,6 +515,8 @@ def main():
             r = run_bs1(mode, P, G, weights, cfg, dev=local_rank)
             r["roofline_frac"] = round(r["achieved_gbs"] / peak, 4)
             line[f"bs1_{mode}"] = r
+        line["gemv"] = gemv_microbench(local_rank)
+        line["attn_sweep"] = attn_microbench(local_rank)
     if grp.rank == 0 and N == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg, weights, args)
     grp.close()
