@@ -126,6 +126,23 @@ VB_API vb_status vb_cache_append(float* kcache, float* vcache, const float* knew
 VB_API vb_status vb_attn_decode(const float* q, const float* kcache, const float* vcache,
                          float* out, int H, int KVH, int D, int n, void* stream);
 
+/* Same computation as vb_attn_decode, for callers that must not allocate
+ * device memory (a host framework that owns all device memory through its own
+ * budgeted pool, a plugin whose enqueue path may not allocate, a serving loop
+ * that cannot afford cudaMalloc's implicit synchronisation).  No counterpart
+ * in the reference.  The split partials live in a 1 MiB array compiled into
+ * the library (held by every GPU that loads it until the process exits);
+ * shapes needing more (H * splits * 130 floats + 256 B; Qwen3-0.6B's 16/8
+ * heads need at most 616 KB) return VB_ERR_UNSUPPORTED.  The first call on a
+ * device looks up the array's device address, so make that call before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (different streams, or devices sharing nothing but this array's name) race
+ * and must be serialised by the caller.  Nothing in it needs clearing between
+ * calls.  Calls no cudaMalloc, cudaFree or allocating routine. */
+VB_API vb_status vb_attn_decode_noalloc(const float* q, const float* kcache,
+                                        const float* vcache, float* out, int H, int KVH,
+                                        int D, int n, void* stream);
+
 /* Batched/strided decode attention for B independent sequences.
  * q [B, H, D]; element (b, pos, kvh, d) of K/V is at
  *   base + b*stride_b + pos*stride_pos + kvh*stride_h + d   (floats);

@@ -72,6 +72,7 @@ _SIGS = {
     "vb_add": (_I, [_P, _P, _I, _P]),
     "vb_cache_append": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "vb_attn_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "vb_attn_decode_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_attn_workspace_bytes": (_Z, [_I, _I, _I]),
     "vb_attn_decode_batched": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _L, _L, _L, _P, _P]),
     "vb_argmax_rows": (_I, [_P, _I, _L, _P, _P]),
@@ -365,6 +366,12 @@ def cache_append(kc, vc, kn, vn, pos, stream=None):
 def attn_decode(q, kc, vc, out, H, KVH, D, n, stream=None):
     check(lib().vb_attn_decode(_tp(q), _tp(kc), _tp(vc), _tp(out), H, KVH, D, int(n),
                                _stream(stream)))
+
+
+def attn_decode_noalloc(q, kc, vc, out, H, KVH, D, n, stream=None):
+    """vb_attn_decode without any device allocation (static scratch)."""
+    check(lib().vb_attn_decode_noalloc(_tp(q), _tp(kc), _tp(vc), _tp(out), H, KVH, D, int(n),
+                                       _stream(stream)))
 
 
 def attn_workspace_bytes(B, H, n_max):
