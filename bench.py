@@ -58,6 +58,17 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def ncu_traffic(kernel, units):
+    """DRAM bytes (read + write) per launch from an ncu capture of `kernel`
+    (profiles/ncu_traffic.json), scaled to `units` by proportion: the kernel
+    streams each sequence-position once, so its traffic grows linearly."""
+    try:
+        d = json.loads((ROOT / "profiles" / "ncu_traffic.json").read_text())[kernel]
+        return int(d["dram_bytes_per_launch"] * units / d["units_per_launch"])
+    except Exception:
+        return None
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during a timed region."""
 
@@ -499,7 +510,7 @@ def main():
             "bound": "hbm", "kernel": attn["kernel"],
             "achieved": round(a_gbs, 1), "peak": peak, "unit": "GB/s",
             "frac": round(a_gbs / peak, 4), "peak_kind": peak_kind,
-            "traffic": None,
+            "traffic": ncu_traffic("attn_split_kernel", attn["B"] * attn["n"]),
             "algorithmic_bytes_per_launch": attn["bytes_per_launch"],
             "launch_shape": f"B={attn['B']} n={attn['n']} KVH=8 D=128 f32",
         },
