@@ -380,7 +380,39 @@ def attn_microbench(dev=0, ns=(512, 2048, 8192, 32768), Bs=(1, 32), H=16, KVH=8,
     return out
 
 
-def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
+PHASES = ("qkv", "att", "o", "gu", "d")
+
+
+def trace_breakdown(tr, layers=28):
+    """Per-phase time split of one fused step from the %globaltimer marks:
+    load = activation load (+ norm), work = the phase's stages, wait = grid
+    barrier.  Entries: start, then per layer and phase (load, work, barrier)
+    marks, then the LM phase's three marks."""
+    out = {}
+    for name, base in (("cta0", 0), ("cta_last", 1024)):
+        t = [int(x) for x in tr[base:base + 1 + layers * 15 + 3]]
+        if len(t) < 1 + layers * 15 + 3 or t[0] == 0:
+            continue
+        acc = {ph: [0.0, 0.0, 0.0] for ph in PHASES}
+        prev = t[0]
+        for l in range(layers):
+            for k, ph in enumerate(PHASES):
+                a, b, c = t[1 + l * 15 + 3 * k: 4 + l * 15 + 3 * k]
+                acc[ph][0] += (a - prev) / 1e3
+                acc[ph][1] += (b - a) / 1e3
+                acc[ph][2] += (c - b) / 1e3
+                prev = c
+        a, b, c = t[1 + layers * 15: 4 + layers * 15]
+        res = {ph: {"load_us": round(v[0], 1), "work_us": round(v[1], 1), "wait_us": round(v[2], 1)}
+               for ph, v in acc.items()}
+        res["lm"] = {"load_us": round((a - prev) / 1e3, 1), "work_us": round((b - a) / 1e3, 1),
+                     "wait_us": round((c - b) / 1e3, 1)}
+        res["total_us"] = round((c - t[0]) / 1e3, 1)
+        out[name] = res
+    return out
+
+
+def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=False):
     import numpy as np
     import torch
 
@@ -389,6 +421,7 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
     e = vb200.Engine(cfg, device=dev).load(weights)
     if mode == "int8":
         e.quantize()
+    e.set_path(path)
     prompt = vbsynth.prompt_ids(prompt_len, 77 + prompt_len, cfg["vocab_size"])
     max_seq = prompt_len + n_new + 8
     # warm-up pass
@@ -421,6 +454,13 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
     e2e = time.perf_counter() - t0
     wb = e.weight_bytes()
     nodes = e.graph_nodes()
+    tb = None
+    if trace and path == 0:
+        e.set_trace(True)
+        e.reset_cache(max_seq)
+        e.prefill(prompt)
+        e.decode(tok, 4)
+        tb = trace_breakdown(e.read_trace(), cfg["num_hidden_layers"])
     e.close()
     mean_ctx = prompt_len + (n_new - 1) / 2.0
     bytes_tok = wb + step_kv_bytes(mean_ctx)
@@ -429,7 +469,8 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8):
             "achieved_gbs": bytes_tok * n_new / sec / 1e9, "e2e_tok_s": n_new / e2e,
             "e2e_p50_ms": 1e3 * lat[len(lat) // 2], "e2e_p99_ms": 1e3 * lat[min(len(lat) - 1, int(0.99 * len(lat)))],
             "graph_nodes": nodes, "weight_bytes": wb, "prompt": prompt_len, "decode_tokens": n_new,
-            "first_tokens": [int(t) for t in toks[:4]]}
+            "path": "fused persistent step" if nodes == 1 else "per-op CUDA graph",
+            "first_tokens": [int(t) for t in toks[:4]], **({"trace": tb} if tb else {})}
 
 
 # ---------------------------------------------------------------------------
@@ -447,7 +488,10 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-extras", action="store_true", help="skip the bs1 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--only", choices=["gemv", "attn"], help="one kernel family (for profiling)")
+    ap.add_argument("--only", choices=["gemv", "attn", "bs1"], help="one workload (for profiling)")
+    ap.add_argument("--mode", choices=["f32", "int8"], default="int8", help="--only bs1: weights")
+    ap.add_argument("--path", type=int, default=0, help="--only bs1: 0 fused step, 1 per-op graph")
+    ap.add_argument("--trace", action="store_true", help="--only bs1: per-phase trace of the fused step")
     ap.add_argument("--ctx", type=int, default=2048, help="--only attn: context length")
     ap.add_argument("--shape", default=None, help="--only gemv: one of q,k,v,o,gate,up,down,lm_head")
     args = ap.parse_args()
@@ -461,6 +505,15 @@ def main():
     if args.only == "gemv":
         shapes = [s for s in GEMV_SHAPES if args.shape in (None, s[0])]
         print(json.dumps({"gemv": gemv_microbench(local_rank, shapes)}), flush=True)
+        return 0
+    if args.only == "bs1":
+        import vbsynth
+        cfg = vbsynth.qwen3_config()
+        w = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+        P, G = (32, 128) if args.mode == "f32" else (512, 512)
+        r = run_bs1(args.mode, P, min(G, args.steps), w, cfg, dev=local_rank, path=args.path,
+                    trace=args.trace)
+        print(json.dumps({"bs1": r}), flush=True)
         return 0
     if args.only == "attn":
         print(json.dumps({"attn": attn_microbench(local_rank, ns=(args.ctx,), Bs=(args.batch,))}),
@@ -523,8 +576,11 @@ def main():
     }
     if grp.rank == 0 and N == 1 and not args.no_extras:
         for mode, P, G in (("f32", 32, 128), ("int8", 512, 512)):
-            r = run_bs1(mode, P, G, weights, cfg, dev=local_rank)
+            r = run_bs1(mode, P, G, weights, cfg, dev=local_rank, path=0)
             r["roofline_frac"] = round(r["achieved_gbs"] / peak, 4)
+            r1 = run_bs1(mode, P, G, weights, cfg, dev=local_rank, path=1)
+            r["per_op_graph_tok_s"] = round(r1["tok_s"], 2)
+            r["per_op_graph_roofline_frac"] = round(r1["achieved_gbs"] / peak, 4)
             line[f"bs1_{mode}"] = r
         line["gemv"] = gemv_microbench(local_rank)
         line["attn_sweep"] = attn_microbench(local_rank)

@@ -249,6 +249,13 @@ VB_API vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, flo
 VB_API vb_status vb_engine_set_path(vb_engine* e, int path);
 /* The stream the engine runs on (a cudaStream_t). */
 VB_API void* vb_engine_stream(vb_engine* e);
+/* Phase tracing of the fused step (no reference counterpart; the reference
+ * times whole steps with steady_clock, tools/bench.cpp:63-69): when on, the
+ * next fused steps record %globaltimer nanoseconds at every phase boundary of
+ * CTA 0 (entries 0..1023) and of the last CTA (1024..2047).  read_trace copies
+ * up to cap entries of the last step and returns how many it copied. */
+VB_API vb_status vb_engine_set_trace(vb_engine* e, int on);
+VB_API int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap);
 
 /* ------------------------------------------------------------------------ */
 /* Batched independent-sequence decode (no reference counterpart; the

@@ -172,7 +172,8 @@ vb_status batch_check_err(vb_batch* b) {
     int err = 0;
     VB_CUDA_TRY(cudaMemcpy(&err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (!err) return VB_OK;
-    cudaMemset(b->d_err, 0, sizeof(int));
+    cudaMemsetAsync(b->d_err, 0, sizeof(int), b->e->stream);
+    cudaStreamSynchronize(b->e->stream);
     if (err == kErrBadToken) return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
     if (err == kErrCacheFull) return fail(VB_ERR_CACHE_FULL, "kv cache is full");
     return fail(VB_ERR_CUDA, "device error word set: " + std::to_string(err));
@@ -215,7 +216,8 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
     vb_status st;
     if ((st = balloc(&b->kc, kvn, "batch kv cache"))) return bail(st);
     if ((st = balloc(&b->vc, kvn, "batch kv cache"))) return bail(st);
-    if (cudaMemset(b->kc, 0, kvn * 4) || cudaMemset(b->vc, 0, kvn * 4))
+    cudaStream_t es = e->stream;  // non-blocking: memsets must be ordered on it
+    if (cudaMemsetAsync(b->kc, 0, kvn * 4, es) || cudaMemsetAsync(b->vc, 0, kvn * 4, es))
         return bail(fail(VB_ERR_CUDA, "kv cache memset failed"));
     if ((st = balloc(&b->x, (size_t)batch * c.hidden, "x"))) return bail(st);
     if ((st = balloc(&b->xn, (size_t)batch * c.hidden, "xn"))) return bail(st);
@@ -245,9 +247,10 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
     if ((st = balloc(&b->d_pos, batch, "pos"))) return bail(st);
     if ((st = balloc(&b->d_next, batch, "next"))) return bail(st);
     if ((st = balloc(&b->d_err, 1, "err"))) return bail(st);
-    cudaMemset(b->d_pos, 0, sizeof(int) * batch);
-    cudaMemset(b->d_tok, 0, sizeof(int) * batch);
-    cudaMemset(b->d_err, 0, sizeof(int));
+    if (cudaMemsetAsync(b->d_pos, 0, sizeof(int) * batch, es) ||
+        cudaMemsetAsync(b->d_tok, 0, sizeof(int) * batch, es) ||
+        cudaMemsetAsync(b->d_err, 0, sizeof(int), es) || cudaStreamSynchronize(es))
+        return bail(fail(VB_ERR_CUDA, "batch state init failed"));
     if (cudaMallocHost(&b->h_io, sizeof(int) * 2 * batch) != cudaSuccess)
         return bail(fail(VB_ERR_CUDA, "cudaMallocHost failed"));
     *out = b;
@@ -375,9 +378,10 @@ vb_status vb_batch_reset(vb_batch* b) {
     cudaStreamSynchronize(b->e->stream);
     const vb_config& c = b->e->cfg;
     const size_t kvn = (size_t)c.layers * b->B * c.kv_heads * b->max_seq * c.head_dim;
-    VB_CUDA_TRY(cudaMemset(b->kc, 0, kvn * 4));
-    VB_CUDA_TRY(cudaMemset(b->vc, 0, kvn * 4));
-    VB_CUDA_TRY(cudaMemset(b->d_pos, 0, sizeof(int) * b->B));
+    VB_CUDA_TRY(cudaMemsetAsync(b->kc, 0, kvn * 4, b->e->stream));
+    VB_CUDA_TRY(cudaMemsetAsync(b->vc, 0, kvn * 4, b->e->stream));
+    VB_CUDA_TRY(cudaMemsetAsync(b->d_pos, 0, sizeof(int) * b->B, b->e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(b->e->stream));
     b->len = 0;
     return VB_OK;
 }

@@ -98,14 +98,18 @@ vb_status engine_check_err(vb_engine* e) {
     int err = 0;
     VB_CUDA_TRY(cudaMemcpy(&err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err == kErrNone) return VB_OK;
-    cudaMemset(e->d_err, 0, sizeof(int));
+    const std::string where = mega_debug(e);
+    cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream);
+    cudaStreamSynchronize(e->stream);
+    mega_reset_counters(e);  // a step that stopped early leaves its tickets set
     switch (err) {
         case kErrBadToken:
             return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
         case kErrCacheFull: return fail(VB_ERR_CACHE_FULL, "kv cache is full");
         case kErrBarrierTimeout:
+            return fail(VB_ERR_TIMEOUT, "fused step: grid barrier wait timed out" + where);
         case kErrPipeTimeout:
-            return fail(VB_ERR_TIMEOUT, "a bounded device wait timed out in the fused step");
+            return fail(VB_ERR_TIMEOUT, "fused step: stage pipeline wait timed out" + where);
         default: return fail(VB_ERR_CUDA, "device error word set: " + std::to_string(err));
     }
 }
@@ -337,8 +341,12 @@ vb_status vb_engine_create(const vb_config* cfg, int device, vb_engine** out) {
     if ((st = dalloc(&e->d_next, 1, "next"))) return bail(st);
     if ((st = dalloc(&e->d_err, 1, "err"))) return bail(st);
     if ((st = dalloc(&e->d_step, 1, "step"))) return bail(st);
-    cudaMemset(e->d_err, 0, sizeof(int));
-    cudaMemset(e->d_pos, 0, sizeof(int));
+    // every memset goes on the engine's own stream (non-blocking: it does not
+    // order with the legacy default stream) and is waited for here
+    if (cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream) ||
+        cudaMemsetAsync(e->d_pos, 0, sizeof(int), e->stream) ||
+        cudaStreamSynchronize(e->stream))
+        return bail(fail(VB_ERR_CUDA, "engine state init failed"));
     if (cudaMallocHost(&e->h_pinned_i, 64 * sizeof(int)) != cudaSuccess)
         return bail(fail(VB_ERR_CUDA, "cudaMallocHost failed"));
     *out = e;
@@ -467,8 +475,8 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
     if (e->kc && e->max_seq == max_seq) {
         // same geometry: keep the buffers, zero them (generate.cpp:19-21)
         const size_t n = (size_t)c.layers * c.kv_heads * max_seq * c.head_dim;
-        VB_CUDA_TRY(cudaMemset(e->kc, 0, n * 4));
-        VB_CUDA_TRY(cudaMemset(e->vc, 0, n * 4));
+        VB_CUDA_TRY(cudaMemsetAsync(e->kc, 0, n * 4, e->stream));
+        VB_CUDA_TRY(cudaMemsetAsync(e->vc, 0, n * 4, e->stream));
     } else {
         free_cache(e);
         mega_release(e);
@@ -476,8 +484,8 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
         vb_status st;
         if ((st = dalloc(&e->kc, n, "kv cache"))) return st;
         if ((st = dalloc(&e->vc, n, "kv cache"))) return st;
-        VB_CUDA_TRY(cudaMemset(e->kc, 0, n * 4));
-        VB_CUDA_TRY(cudaMemset(e->vc, 0, n * 4));
+        VB_CUDA_TRY(cudaMemsetAsync(e->kc, 0, n * 4, e->stream));
+        VB_CUDA_TRY(cudaMemsetAsync(e->vc, 0, n * 4, e->stream));
         e->max_seq = max_seq;
         e->attn_splits = attn_splits_for(1, c.kv_heads, max_seq);
         if ((st = dalloc(&e->attn_ws, attn_ws_bytes(1, c.heads, e->attn_splits) / 4 + 1, "attn ws")))
@@ -485,7 +493,8 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
         if ((st = dalloc(&e->d_hist, max_seq, "history"))) return st;
         if ((st = dalloc(&e->d_prompt, max_seq, "prompt"))) return st;
     }
-    VB_CUDA_TRY(cudaMemset(e->d_pos, 0, sizeof(int)));
+    VB_CUDA_TRY(cudaMemsetAsync(e->d_pos, 0, sizeof(int), e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
     e->len = 0;
     return VB_OK;
 }
@@ -613,5 +622,24 @@ vb_status vb_engine_set_path(vb_engine* e, int path) {
 }
 
 void* vb_engine_stream(vb_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+vb_status vb_engine_set_trace(vb_engine* e, int on) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    DeviceGuard dg(e->device);
+    if (e->trace_on != (on != 0)) {
+        cudaStreamSynchronize(e->stream);
+        e->trace_on = on != 0;
+        mega_release(e);
+        if (e->graph) cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    return VB_OK;
+}
+
+int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap) {
+    if (!e || !out || cap <= 0) return 0;
+    DeviceGuard dg(e->device);
+    return mega_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
+}
 
 }  // extern "C"

@@ -93,6 +93,7 @@ struct vb_engine {
 
     // persistent fused step (vb_mega.cu)
     void* mega = nullptr;
+    bool trace_on = false;
 };
 
 namespace vb {
@@ -105,6 +106,9 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s);
 vb_status mega_prepare(vb_engine* e);
 vb_status mega_enqueue_step(vb_engine* e, cudaStream_t s);
 void mega_release(vb_engine* e);
+void mega_reset_counters(vb_engine* e);
+std::string mega_debug(vb_engine* e);
+int mega_read_trace(vb_engine* e, unsigned long long* host, int cap);
 vb_status engine_check_err(vb_engine* e);
 void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s);
 }  // namespace vb

@@ -93,6 +93,8 @@ _SIGS = {
     "vb_engine_graph_nodes": (_I, [_P]),
     "vb_engine_set_path": (_I, [_P, _I]),
     "vb_engine_stream": (_P, [_P]),
+    "vb_engine_set_trace": (_I, [_P, _I]),
+    "vb_engine_read_trace": (_I, [_P, _P, _I]),
     "vb_batch_create": (_I, [_P, _I, _I, C.POINTER(C.c_void_p)]),
     "vb_batch_destroy": (_I, [_P]),
     "vb_batch_step": (_I, [_P, _P, _P, _P]),
@@ -240,6 +242,14 @@ class Engine:
 
     def set_path(self, path: int):
         check(lib().vb_engine_set_path(self.h, int(path)))
+
+    def set_trace(self, on: bool):
+        check(lib().vb_engine_set_trace(self.h, int(bool(on))))
+
+    def read_trace(self) -> np.ndarray:
+        out = np.zeros(2048, dtype=np.uint64)
+        n = lib().vb_engine_read_trace(self.h, _ptr(out), 2048)
+        return out[:n]
 
     def stream(self) -> int:
         return lib().vb_engine_stream(self.h) or 0
