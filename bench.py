@@ -383,32 +383,61 @@ def attn_microbench(dev=0, ns=(512, 2048, 8192, 32768), Bs=(1, 32), H=16, KVH=8,
 PHASES = ("qkv", "att", "o", "gu", "d")
 
 
-def trace_breakdown(tr, layers=28):
-    """Per-phase time split of one fused step from the %globaltimer marks:
-    load = activation load (+ norm), work = the phase's stages, wait = grid
-    barrier.  Entries: start, then per layer and phase (load, work, barrier)
-    marks, then the LM phase's three marks."""
+def trace_breakdown(tr, layers=28, stride=1024, words=6):
+    """Timeline of one fused step from per-CTA %globaltimer words (6 per phase
+    b: activation loaded, first stage observed, arrival at / release from grid
+    barrier b, first / last stage issued by the producer).  Per phase type,
+    medians over layers and CTAs, in us, relative to the previous release:
+      loaded, first, arrive, release   (consumer)
+      issue0, issueN                   (producer: first / last stage issued)
+    plus spread = last - first arrival."""
+    import numpy as np
+    G = len(tr) // stride
+    if G == 0:
+        return None
+    t = np.asarray(tr, dtype=np.int64).reshape(G, stride).astype(np.float64)
+    nb = 5 * layers
+    w = t[:, 1:1 + words * nb].reshape(G, nb, words)
+    if t[0, 0] == 0 or (w[:, :, 3] == 0).any():
+        return None
+    rel = w[..., 3]
+    prev = np.concatenate([np.full((G, 1), t[:, 0].max()), rel[:, :-1]], axis=1)
+    prev = np.median(prev, axis=0, keepdims=True)
     out = {}
-    for name, base in (("cta0", 0), ("cta_last", 1024)):
-        t = [int(x) for x in tr[base:base + 1 + layers * 15 + 3]]
-        if len(t) < 1 + layers * 15 + 3 or t[0] == 0:
-            continue
-        acc = {ph: [0.0, 0.0, 0.0] for ph in PHASES}
-        prev = t[0]
-        for l in range(layers):
-            for k, ph in enumerate(PHASES):
-                a, b, c = t[1 + l * 15 + 3 * k: 4 + l * 15 + 3 * k]
-                acc[ph][0] += (a - prev) / 1e3
-                acc[ph][1] += (b - a) / 1e3
-                acc[ph][2] += (c - b) / 1e3
-                prev = c
-        a, b, c = t[1 + layers * 15: 4 + layers * 15]
-        res = {ph: {"load_us": round(v[0], 1), "work_us": round(v[1], 1), "wait_us": round(v[2], 1)}
-               for ph, v in acc.items()}
-        res["lm"] = {"load_us": round((a - prev) / 1e3, 1), "work_us": round((b - a) / 1e3, 1),
-                     "wait_us": round((c - b) / 1e3, 1)}
-        res["total_us"] = round((c - t[0]) / 1e3, 1)
-        out[name] = res
+    med = lambda x: round(float(np.median(x)) / 1e3, 2)
+    for k, ph in enumerate(PHASES):
+        i = np.arange(k, nb, 5)
+        d = {}
+        for j, name in enumerate(("loaded", "first", "arrive", "release", "issue0", "issueN")):
+            x = w[:, i, j]
+            d[name] = med(np.where(x > 0, x - prev[:, i], np.nan)[~np.isnan(np.where(x > 0, x, np.nan))]) \
+                if (x > 0).any() else None
+        d["spread"] = med(w[:, i, 2].max(0) - w[:, i, 2].min(0))
+        out[ph] = d
+    out["total_us"] = round(float(rel[:, -1].max() - t[:, 0].min()) / 1e3, 1)
+    return out
+
+
+STEPS2 = ("A.norm", "A.qkv", "A.gather", "A.attn", "A.merge", "A.oproj", "A.barrier",
+          "B.norm", "B.gateup", "B.down", "B.reduce", "B.barrier")
+
+
+def trace_breakdown2(tr, layers=28, stride=1024):
+    """Two-barrier step: median (over layers and CTAs) duration of each of the
+    12 marked steps of a layer, and the median step time, in us."""
+    import numpy as np
+    G = len(tr) // stride
+    if G == 0:
+        return None
+    t = np.asarray(tr, dtype=np.int64).reshape(G, stride).astype(np.float64)
+    m = t[:, 1:1 + 12 * layers].reshape(G, layers, 12)
+    if t[0, 0] == 0 or (m == 0).any():
+        return None
+    prev = np.concatenate([t[:, :1, None].repeat(1, 1), m[:, :-1, 11:12]], axis=1)  # [G, L, 1]
+    d = np.diff(np.concatenate([prev, m], axis=2), axis=2)  # [G, L, 12]
+    out = {name: round(float(np.median(d[:, :, i])) / 1e3, 2) for i, name in enumerate(STEPS2)}
+    out["layer_us"] = round(float(np.median(m[:, 1:, 11] - m[:, :-1, 11])) / 1e3, 2)
+    out["total_us"] = round(float(m[:, -1, 11].max() - t[:, 0].min()) / 1e3, 1)
     return out
 
 
@@ -455,12 +484,16 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
     wb = e.weight_bytes()
     nodes = e.graph_nodes()
     tb = None
-    if trace and path == 0:
+    if trace and path in (0, 2):
         e.set_trace(True)
         e.reset_cache(max_seq)
         e.prefill(prompt)
         e.decode(tok, 4)
-        tb = trace_breakdown(e.read_trace(), cfg["num_hidden_layers"])
+        raw = e.read_trace()
+        if os.environ.get("VB_TRACE_DUMP"):
+            import numpy as np
+            np.save(os.environ["VB_TRACE_DUMP"] + f"_{mode}.npy", raw)
+        tb = (trace_breakdown if path == 0 else trace_breakdown2)(raw, cfg["num_hidden_layers"])
     e.close()
     mean_ctx = prompt_len + (n_new - 1) / 2.0
     bytes_tok = wb + step_kv_bytes(mean_ctx)

@@ -244,16 +244,19 @@ VB_API int vb_engine_graph_nodes(const vb_engine* e);
 /* Copies layer `layer`'s K (which=0) or V cache rows [0, len) into host
  * memory as [len, KVH*D] (the reference KVCache layout). */
 VB_API vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host);
-/* Selects the bs1 step implementation: 0 = persistent fused kernel (default
- * when available), 1 = one kernel per op in a CUDA graph. */
+/* Selects the bs1 step implementation: 0 = persistent fused kernel with five
+ * grid barriers per layer, 1 = one kernel per op in a CUDA graph (default),
+ * 2 = persistent kernel on KV-head clusters with two grid barriers per layer.
+ * A fused path whose shape requirements are not met falls back to 1. */
 VB_API vb_status vb_engine_set_path(vb_engine* e, int path);
 /* The stream the engine runs on (a cudaStream_t). */
 VB_API void* vb_engine_stream(vb_engine* e);
 /* Phase tracing of the fused step (no reference counterpart; the reference
- * times whole steps with steady_clock, tools/bench.cpp:63-69): when on, the
- * next fused steps record %globaltimer nanoseconds at every phase boundary of
- * CTA 0 (entries 0..1023) and of the last CTA (1024..2047).  read_trace copies
- * up to cap entries of the last step and returns how many it copied. */
+ * times whole steps with steady_clock, tools/bench.cpp:63-69): when on, each
+ * CTA c of the next fused steps records %globaltimer nanoseconds in words
+ * [c*512, c*512+512): word 0 = start, 2b-1 / 2b = arrival at / release from
+ * grid barrier b (b = 1..5*layers).  read_trace copies up to cap words of the
+ * last step and returns how many it copied (grid * 512 at most). */
 VB_API vb_status vb_engine_set_trace(vb_engine* e, int on);
 VB_API int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap);
 

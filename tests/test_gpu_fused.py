@@ -20,7 +20,13 @@ def cfg512():
                                 num_key_value_heads=2, intermediate_size=1024, vocab_size=2000)
 
 
-def run_pair(cfg, w, mode, prompt, n_new, max_seq):
+def cfg_wide():
+    """Full Qwen3-0.6B widths (hidden 1024, 16/8 heads, ffn 3072), 2 layers,
+    small vocab: the shapes the two-barrier clustered step is laid out for."""
+    return vbsynth.qwen3_config(num_hidden_layers=2, vocab_size=4096)
+
+
+def run_pair(cfg, w, mode, prompt, n_new, max_seq, path=0):
     orc = oracle.OracleModel(cfg, w)
     e = vb200.Engine(cfg).load(w)
     if mode == "int8":
@@ -28,7 +34,7 @@ def run_pair(cfg, w, mode, prompt, n_new, max_seq):
         e.quantize()
     orc.reset_cache(max_seq)
     e.reset_cache(max_seq)
-    e.set_path(0)
+    e.set_path(path)
     worst = 0.0
     for t in prompt:
         lo, lg = orc.step(int(t)), e.step(int(t))
@@ -65,19 +71,40 @@ def test_fused_small_model(mode):
     e.close()
 
 
-def test_fused_full_f32_prompt32_decode128():
+@pytest.mark.parametrize("mode", ["f32", "int8"])
+def test_two_barrier_step_wide_model(mode):
+    """Path 2 on full widths: chunks spread over the cluster (cache length 300
+    -> 10 chunks, 2 on some CTAs), KV rows and decode() as well."""
+    cfg = cfg_wide()
+    w = vbsynth.make_weights(cfg, seed=71)
+    prompt = vbsynth.prompt_ids(270, 13, cfg["vocab_size"])
+    e, orc, worst, to, tg = run_pair(cfg, w, mode, prompt, 24, 300, path=2)
+    assert tg == to and worst <= TOL[mode], worst
+    for layer in range(cfg["num_hidden_layers"]):
+        for which in (0, 1):
+            assert np.max(np.abs(e.read_kv(layer, which) - orc.kv(layer, which))) < 1e-4
+    e.reset_cache(300)
+    lg = e.prefill(prompt, want_logits=True)
+    toks = e.decode(int(np.argmax(lg)), 24)
+    assert [int(np.argmax(lg))] + list(toks[:-1]) == to
+    e.close()
+
+
+@pytest.mark.parametrize("path", [0, 2])
+def test_fused_full_f32_prompt32_decode128(path):
     cfg = vbsynth.qwen3_config()
     w = vbsynth.make_weights(cfg, seed=1234)
     prompt = vbsynth.prompt_ids(32, 1235, cfg["vocab_size"])
-    e, orc, worst, to, tg = run_pair(cfg, w, "f32", prompt, 128, 168)
+    e, orc, worst, to, tg = run_pair(cfg, w, "f32", prompt, 128, 168, path=path)
     assert tg == to and worst <= TOL["f32"], worst
     e.close()
 
 
-def test_fused_full_int8_prompt512_decode64():
+@pytest.mark.parametrize("path", [0, 2])
+def test_fused_full_int8_prompt512_decode64(path):
     cfg = vbsynth.qwen3_config()
     w = vbsynth.make_weights(cfg, seed=4321)
     prompt = vbsynth.prompt_ids(512, 4322, cfg["vocab_size"])
-    e, orc, worst, to, tg = run_pair(cfg, w, "int8", prompt, 64, 584)
+    e, orc, worst, to, tg = run_pair(cfg, w, "int8", prompt, 64, 584, path=path)
     assert tg == to and worst <= TOL["int8"], worst
     e.close()

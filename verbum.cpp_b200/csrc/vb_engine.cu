@@ -102,6 +102,7 @@ vb_status engine_check_err(vb_engine* e) {
     cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream);
     cudaStreamSynchronize(e->stream);
     mega_reset_counters(e);  // a step that stopped early leaves its tickets set
+    mega2_reset_counters(e);
     switch (err) {
         case kErrBadToken:
             return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
@@ -226,8 +227,9 @@ static vb_status ensure_graph(vb_engine* e) {
     if (e->graph) return VB_OK;
     cudaGraph_t g = nullptr;
     VB_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    vb_status st = (e->path == 0 && e->mega) ? mega_enqueue_step(e, e->stream)
-                                             : enqueue_step_ops(e, e->stream);
+    vb_status st = (e->path == 0 && e->mega)    ? mega_enqueue_step(e, e->stream)
+                   : (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream)
+                                                : enqueue_step_ops(e, e->stream);
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (st) {
         if (g) cudaGraphDestroy(g);
@@ -358,6 +360,7 @@ vb_status vb_engine_destroy(vb_engine* e) {
     DeviceGuard dg(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
     mega_release(e);
+    mega2_release(e);
     free_cache(e);
     dfree(e->embed); dfree(e->final_norm); dfree(e->rope_cos); dfree(e->rope_sin);
     dfree(e->norms); dfree(e->wf32); dfree(e->wi8); dfree(e->wscale);
@@ -449,6 +452,7 @@ vb_status vb_engine_quantize(vb_engine* e) {
     if (e->graph) cudaGraphExecDestroy(e->graph);
     e->graph = nullptr;
     mega_release(e);
+    mega2_release(e);
     return VB_OK;
 }
 
@@ -480,6 +484,7 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
     } else {
         free_cache(e);
         mega_release(e);
+    mega2_release(e);
         const size_t n = (size_t)c.layers * c.kv_heads * max_seq * c.head_dim;
         vb_status st;
         if ((st = dalloc(&e->kc, n, "kv cache"))) return st;
@@ -509,6 +514,11 @@ static vb_status pre_step(vb_engine* e, int n_tokens) {
         return fail(VB_ERR_ROPE, "position is outside the rope table");
     if (e->path == 0 && !e->mega) {
         st = mega_prepare(e);
+        if (st == VB_ERR_UNSUPPORTED) e->path = 1;
+        else if (st) return st;
+    }
+    if (e->path == 2 && !e->mega2) {
+        st = mega2_prepare(e);
         if (st == VB_ERR_UNSUPPORTED) e->path = 1;
         else if (st) return st;
     }
@@ -610,7 +620,7 @@ vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* hos
 }
 
 vb_status vb_engine_set_path(vb_engine* e, int path) {
-    if (!e || path < 0 || path > 1) return fail(VB_ERR_ARG, "path must be 0 or 1");
+    if (!e || path < 0 || path > 2) return fail(VB_ERR_ARG, "path must be 0, 1 or 2");
     DeviceGuard dg(e->device);
     cudaStreamSynchronize(e->stream);
     if (e->path != path) {
@@ -630,6 +640,7 @@ vb_status vb_engine_set_trace(vb_engine* e, int on) {
         cudaStreamSynchronize(e->stream);
         e->trace_on = on != 0;
         mega_release(e);
+    mega2_release(e);
         if (e->graph) cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;
     }
@@ -639,6 +650,7 @@ vb_status vb_engine_set_trace(vb_engine* e, int on) {
 int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap) {
     if (!e || !out || cap <= 0) return 0;
     DeviceGuard dg(e->device);
+    if (e->mega2) return mega2_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
     return mega_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
 }
 

@@ -93,6 +93,8 @@ struct vb_engine {
 
     // persistent fused step (vb_mega.cu)
     void* mega = nullptr;
+    // two-barrier clustered step (vb_mega2.cu)
+    void* mega2 = nullptr;
     bool trace_on = false;
 };
 
@@ -108,6 +110,11 @@ vb_status mega_enqueue_step(vb_engine* e, cudaStream_t s);
 void mega_release(vb_engine* e);
 void mega_reset_counters(vb_engine* e);
 std::string mega_debug(vb_engine* e);
+vb_status mega2_prepare(vb_engine* e);
+vb_status mega2_enqueue_step(vb_engine* e, cudaStream_t s);
+void mega2_release(vb_engine* e);
+void mega2_reset_counters(vb_engine* e);
+int mega2_read_trace(vb_engine* e, unsigned long long* host, int cap);
 int mega_read_trace(vb_engine* e, unsigned long long* host, int cap);
 vb_status engine_check_err(vb_engine* e);
 void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s);

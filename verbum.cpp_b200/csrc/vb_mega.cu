@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "vb_engine.cuh"
+#include "vb_pipe.cuh"
 
 namespace vb {
 namespace {
@@ -44,7 +45,7 @@ constexpr int kConsumers = kConsumerWarps * 32;  // 256
 constexpr int kThreads = kConsumers + 32;        // + 1 producer warp
 constexpr int kChunk = 32;                       // attention positions per unit
 constexpr int kXsFloats = 4096;                  // activation vector capacity
-constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr int kTraceStride = 1024;  // trace words per CTA
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kXsFloats * sizeof(float);
 
 enum Phase : int { kQKV = 0, kATT = 1, kO = 2, kGU = 3, kD = 4, kLM = 5 };
@@ -90,144 +91,29 @@ struct MegaParams {
     int* step;
     int* err;
     int* dbg;  // where a bounded wait gave up: {code, cta, site, index, extra}
-    unsigned long long* trace;  // optional per-phase timestamps of CTAs 0 and G-1
+    unsigned long long* trace;  // optional: per CTA, start + (arrive, leave) of every grid barrier
     int hidden, nlayers, heads, kvh, ffn, vocab, qkv_rows, q_width, max_seq, max_chunks;
     float eps;
 };
 
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ unsigned smem_addr(const void* p) {
-    return (unsigned)__cvta_generic_to_shared(p);
+// Trace words of phase b (1-based, the phase closed by grid barrier b) for
+// this CTA, 6 per phase: 0 activation loaded, 1 first stage observed,
+// 2 arrival, 3 release (consumer thread 0), 4 first and 5 last stage issued
+// (producer).
+constexpr int kTraceWords = 6;
+__device__ __forceinline__ void trace_at(const MegaParams& p, int b, int w) {
+    if (p.trace && kTraceWords * b < kTraceStride)
+        p.trace[(size_t)blockIdx.x * kTraceStride + kTraceWords * (b - 1) + 1 + w] = now_ns();
 }
-__device__ __forceinline__ unsigned long long now_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
+__device__ __forceinline__ void trace_mark(const MegaParams& p, int b, int w) {
+    if (threadIdx.x == 0) trace_at(p, b, w);
 }
-__device__ __forceinline__ void mbar_init(unsigned a, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned a, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned a) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(unsigned a, unsigned parity) {
-    unsigned ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ int err_read(const int* err) {
-    return *reinterpret_cast<const volatile int*>(err);
-}
-// Wait sites recorded in the debug words when a bounded wait gives up.
-enum Site : int { kSiteEmpty = 1, kSiteFull = 2, kSiteAttFull = 3, kSiteGrid = 4 };
-
-// First failure wins: sets the error word and, if it was the first, records
-// where the kernel gave up.
-__device__ void record_fail(int* err, int* dbg, int code, int site, int index, int extra) {
-    if (atomicCAS(err, 0, code) == 0 && dbg) {
-        dbg[1] = blockIdx.x;
-        dbg[2] = site;
-        dbg[3] = index;
-        dbg[4] = extra;
-        __threadfence();
-        dbg[0] = code;
+__device__ __forceinline__ void trace_first(const MegaParams& p, int b) {
+    if (p.trace && kTraceWords * b < kTraceStride) {
+        unsigned long long* q =
+            p.trace + (size_t)blockIdx.x * kTraceStride + kTraceWords * (b - 1) + 2;
+        if (*q == 0) *q = now_ns();
     }
-}
-
-// Bounded wait for the phase of parity `parity` of mbarrier `a` to complete.
-__device__ bool mbar_wait(unsigned a, unsigned parity, int* err, int* dbg, int site, int index) {
-    if (mbar_try(a, parity)) return true;
-    const unsigned long long t0 = now_ns();
-    for (unsigned it = 1;; it++) {
-        if (mbar_try(a, parity)) return true;
-        if ((it & 255u) == 0) {
-            if (err_read(err)) return false;
-            if (now_ns() - t0 > kWaitNs) {
-                record_fail(err, dbg, kErrPipeTimeout, site, index, (int)parity);
-                return false;
-            }
-        }
-    }
-}
-// Bounded wait until the previous round of `slot` (stage s - kStages) has been
-// observed by its consumer.
-__device__ bool seq_wait(volatile int* seq, int slot, int s, int* err, int* dbg) {
-    const int want = s - kStages;
-    if (seq[slot] == want) return true;
-    const unsigned long long t0 = now_ns();
-    for (unsigned it = 1;; it++) {
-        if (seq[slot] == want) return true;
-        if ((it & 255u) == 0) {
-            if (err_read(err)) return false;
-            if (now_ns() - t0 > kWaitNs) {
-                record_fail(err, dbg, kErrPipeTimeout, 5, s, seq[slot]);
-                return false;
-            }
-        }
-    }
-}
-
-// Warp-uniform wait: lane 0 waits (bounded) and broadcasts the outcome; on
-// success the other lanes observe the already-completed phase themselves so
-// that each of them acquires the stage's contents.
-__device__ bool warp_wait(unsigned a, unsigned parity, int* err, int* dbg, int index,
-                          volatile int* seq, int slot) {
-    const int lane = threadIdx.x & 31;
-    int ok = 1;
-    if (lane == 0) {
-        ok = (seq_wait(seq, slot, index, err, dbg) &&
-              mbar_wait(a, parity, err, dbg, kSiteFull, index)) ? 1 : 0;
-        if (ok) {
-            seq[slot] = index;
-            __threadfence_block();
-        }
-    }
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok && lane != 0) {
-        for (int i = 0; i < 1024 && !mbar_try(a, parity); i++) {
-        }
-    }
-    return ok != 0;
-}
-
-__device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes,
-                                         unsigned mbar, unsigned long long pol) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(mbar), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-}
-// Named barrier over the consumer threads that also ANDs a per-thread flag,
-// so every consumer thread leaves with the same decision.
-__device__ __forceinline__ bool consumers_sync_and(bool v) {
-    unsigned r;
-    asm volatile(
-        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 1, %2, p; selp.u32 %0, 1, 0, q; }"
-        : "=r"(r)
-        : "r"((unsigned)v), "n"(kConsumers)
-        : "memory");
-    return r != 0;
-}
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
-    return v > bv || (v == bv && i < bi);
 }
 
 // ------------------------------------------------------------- the schedule
@@ -298,16 +184,29 @@ struct __align__(16) Smem {
     // consumer therefore waits for stage s only once seq[slot] == s - kStages,
     // i.e. once the slot's previous round is known to have completed.
     volatile int seq[kStages];
+    int cur_b;  // index of the grid barrier that closes the current phase (tracing)
 };
 
 // Loads an activation vector (written by other CTAs this launch: read via L2)
 // into shared memory, optionally RMS-normalised (nn.cpp:8-42 arithmetic),
 // laid out lane-interleaved per 512 elements for INT8 phases.
-__device__ void load_act(const float* src, const float* norm_w, float eps, int K, bool perm,
-                         float* xs, Smem& S, bool l2) {
+constexpr int kMaxPer = kXsFloats / kConsumers;  // 16 vector elements per consumer thread
+
+// Loads the norm weight elements this thread will need into registers; issued
+// before a grid barrier so the (HBM) latency hides under the wait.
+__device__ __forceinline__ void prefetch_norm(const float* w, int K, float (&nw)[kMaxPer]) {
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < kMaxPer; k++) {
+        const int i = t + k * kConsumers;
+        nw[k] = (w && i < K) ? __ldg(w + i) : 0.f;
+    }
+}
+
+__device__ void load_act(const float* src, const float* norm_w, const float (&nw)[kMaxPer],
+                         float eps, int K, bool perm, float* xs, Smem& S, bool l2) {
     // one read of the vector into registers (K <= kXsFloats = 16 per thread)
     const int t = threadIdx.x;
-    constexpr int kMaxPer = kXsFloats / kConsumers;
     float v[kMaxPer];
     double ss = 0.0;
 #pragma unroll
@@ -323,7 +222,7 @@ __device__ void load_act(const float* src, const float* norm_w, float eps, int K
     if (norm_w) {
         ss = warp_sum_d(ss);
         if ((t & 31) == 0) S.red[t >> 5] = ss;
-        consumers_sync();
+        consumers_sync<kConsumers>();
         double tot = 0.0;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; w++) tot += S.red[w];
@@ -334,7 +233,7 @@ __device__ void load_act(const float* src, const float* norm_w, float eps, int K
         const int i = t + k * kConsumers;
         if (i < K) {
             float x = v[k];
-            if (norm_w) x = __fmul_rn(__fmul_rn(x, sc), norm_w[i]);
+            if (norm_w) x = __fmul_rn(__fmul_rn(x, sc), nw[k]);
             int dst = i;
             if (perm) {
                 const int c = i >> 9, r = i & 511;
@@ -343,7 +242,7 @@ __device__ void load_act(const float* src, const float* norm_w, float eps, int K
             xs[dst] = x;
         }
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
 }
 
 __device__ __forceinline__ float dot_row_f32(const float* wrow, const float* xs, int K, int lane) {
@@ -405,8 +304,9 @@ __device__ bool gemv_phase(const MegaParams& p, const GemvPlan& g, int layer, in
         const int gs = gbase + j;
         const int slot = gs % kStages;
         if (!warp_wait(smem_addr(&S.full[slot]), (unsigned)(gs / kStages) & 1u, p.err, p.dbg, gs,
-                       S.seq, slot))
+                       S.seq, slot, kStages))
             return false;
+        if (lane == 0) trace_first(p, S.cur_b);
         const char* st = ring + (size_t)slot * kStageBytes;
         const int rA = g.r0 + j * g.rps;
         const int nr = min(g.rps, g.r1 - rA);
@@ -439,9 +339,76 @@ __device__ bool gemv_phase(const MegaParams& p, const GemvPlan& g, int layer, in
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_addr(&S.empty[slot]));
+        if (lane == 0) mbar_arrive(smem_addr(&S.empty[slot]), kConsumerWarps);
     }
     return true;
+}
+
+// Cooperative variant for INT8 weights: every warp takes every stage (in
+// order, so no slot-order gate is needed) and the stage's rows are dealt out
+// across the warps -- an INT8 stage holds 5-16 rows, too much dequantisation
+// work for one warp.  Each warp releases the slot with one arrival.
+template <int KIND>
+__device__ bool gemv_phase_coop(const MegaParams& p, const GemvPlan& g, int layer, int gbase,
+                                const char* ring, Smem& S, const float* xs, const float* emb_row) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const MegaLayer& L = p.layers[layer];
+    const float* scales = KIND == kQKV ? L.sqkv : KIND == kO ? L.so : KIND == kGU ? L.sgu : L.sd;
+    for (int j = 0; j < g.nstages; j++) {
+        const int gs = gbase + j;
+        const int slot = gs % kStages;
+        const unsigned par = (unsigned)(gs / kStages) & 1u;
+        int ok = 1;
+        if (lane == 0) {
+            ok = mbar_wait(smem_addr(&S.full[slot]), par, p.err, p.dbg, kSiteFull, gs) ? 1 : 0;
+            if (ok) {
+                S.seq[slot] = gs;
+                trace_first(p, S.cur_b);
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return false;
+        if (lane != 0)
+            for (int i = 0; i < 1024 && !mbar_try(smem_addr(&S.full[slot]), par); i++) {
+            }
+        const char* st = ring + (size_t)slot * kStageBytes;
+        const int rA = g.r0 + j * g.rps;
+        const int nr = min(g.rps, g.r1 - rA);
+        if (KIND == kGU) {
+            for (int pr = warp; 2 * pr + 1 < nr; pr += kConsumerWarps) {
+                const int8_t* w0 = reinterpret_cast<const int8_t*>(st + (size_t)(2 * pr) * g.row_bytes);
+                const float gsum = dot_row_i8(w0, xs, g.K, lane) * __ldg(scales + rA + 2 * pr);
+                const float usum = dot_row_i8(w0 + g.row_bytes, xs, g.K, lane) *
+                                   __ldg(scales + rA + 2 * pr + 1);
+                if (lane == 0) p.h[(rA >> 1) + pr] = silu_f(gsum) * usum;
+            }
+        } else {
+            for (int r = warp; r < nr; r += kConsumerWarps) {
+                const int row = rA + r;
+                const float acc = dot_row_i8(reinterpret_cast<const int8_t*>(st + (size_t)r * g.row_bytes),
+                                             xs, g.K, lane) * __ldg(scales + row);
+                if (lane == 0) {
+                    if (KIND == kQKV) {
+                        p.qkv[row] = acc;
+                    } else {
+                        const float base = (KIND == kO && layer == 0) ? emb_row[row] : __ldcg(p.x + row);
+                        p.x[row] = base + acc;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&S.empty[slot]), 1);
+    }
+    return true;
+}
+
+template <int KIND>
+__device__ __forceinline__ bool run_gemv(const MegaParams& p, const GemvPlan& g, int layer,
+                                         int gbase, const char* ring, Smem& S, const float* xs,
+                                         const float* emb_row, float& bv, int& bi) {
+    if (KIND != kLM && g.q8) return gemv_phase_coop<KIND>(p, g, layer, gbase, ring, S, xs, emb_row);
+    return gemv_phase<KIND>(p, g, layer, gbase, ring, S, xs, emb_row, bv, bi);
 }
 
 // One attention unit (kv head kvh, chunk c) by all consumer warps; K tile in
@@ -460,7 +427,7 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
         S.red[warp] = sq;
         S.red[8 + warp] = sk;
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     const double tq = S.red[hs * 4] + S.red[hs * 4 + 1] + S.red[hs * 4 + 2] + S.red[hs * 4 + 3];
     const float scq = rms_scale(tq, 128, p.eps);
     S.tq[hs][d] = __fmul_rn(__fmul_rn(qv, scq), L.q_norm[d]);
@@ -470,7 +437,7 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
         S.tk[d] = __fmul_rn(__fmul_rn(kv, sck), L.k_norm[d]);
         S.vn[d] = __ldcg(p.qkv + QW + KW + kvh * 128 + d);
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     {
         const float* cr = p.rope_cos + (size_t)pos * 128;
         const float* sr = p.rope_sin + (size_t)pos * 128;
@@ -488,17 +455,18 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
     const int kslot = ks % kStages, vslot = vs % kStages;
     const unsigned kpar = (unsigned)(ks / kStages) & 1u, vpar = (unsigned)(vs / kStages) & 1u;
     if (t == 0) {
-        S.wflag = seq_wait(S.seq, kslot, ks, p.err, p.dbg) &&
+        S.wflag = seq_wait(S.seq, kslot, ks, kStages, p.err, p.dbg) &&
                   mbar_wait(smem_addr(&S.full[kslot]), kpar, p.err, p.dbg, kSiteAttFull, ks) &&
-                  seq_wait(S.seq, vslot, vs, p.err, p.dbg) &&
+                  seq_wait(S.seq, vslot, vs, kStages, p.err, p.dbg) &&
                   mbar_wait(smem_addr(&S.full[vslot]), vpar, p.err, p.dbg, kSiteAttFull, vs);
         if (S.wflag) {
             S.seq[kslot] = ks;
             S.seq[vslot] = vs;
             __threadfence_block();
+            trace_first(p, S.cur_b);
         }
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     if (!S.wflag) return false;  // same value in every consumer thread
     for (int i = 0; i < 1024 && !mbar_try(smem_addr(&S.full[kslot]), kpar); i++) {
     }
@@ -529,7 +497,7 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
             }
         }
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     if (warp < 2) {
         const float s = S.sc[warp][lane];
         const float m = warp_max(s);
@@ -541,7 +509,7 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
             S.l[warp] = l;
         }
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     {
         float acc = 0.f;
         const int nv = min(kChunk, n - p0);
@@ -561,16 +529,16 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
         p.kc[off] = S.kn[t];
         p.vc[off] = S.vn[t];
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     if (t == 0) {
-        mbar_arrive(smem_addr(&S.empty[kslot]));
-        mbar_arrive(smem_addr(&S.empty[vslot]));
+        mbar_arrive(smem_addr(&S.empty[kslot]), kConsumerWarps);
+        mbar_arrive(smem_addr(&S.empty[vslot]), kConsumerWarps);
         __threadfence();
         const int old = atomicAdd(p.att_ticket + kvh, 1);
         S.tflag = (old == nchunks - 1);
         __threadfence();
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     if (S.tflag) {  // last unit of this kv head: merge the chunks
         const float* base = p.att_part + (size_t)(2 * kvh + hs) * p.max_chunks * 130;
         float M = -INFINITY;
@@ -584,23 +552,26 @@ __device__ bool att_unit(const MegaParams& p, int layer, int kvh, int c, int pos
             A = fmaf(__ldcg(base + cc * 130 + 2 + d), f, A);
         }
         p.ctx[(2 * kvh + hs) * 128 + d] = (Lsum > 0.f) ? A / Lsum : 0.f;
-        consumers_sync();
+        consumers_sync<kConsumers>();
         if (t == 0) p.att_ticket[kvh] = 0;
     }
-    consumers_sync();  // the shared scratch is reused by the next unit
+    consumers_sync<kConsumers>();  // the shared scratch is reused by the next unit
     return true;
 }
 
 // Grid-wide barrier across the consumer groups of all CTAs.  Called by all
 // consumer threads; thread 0 arrives and spins (bounded) on the counter.
 __device__ bool grid_barrier(const MegaParams& p, unsigned target, Smem& S, bool ok_in) {
-    if (!consumers_sync_and(ok_in)) {
+    if (!consumers_sync_and<kConsumers>(ok_in)) {
         if (threadIdx.x == 0) atomicCAS(p.err, 0, kErrPipeTimeout);
         return false;
     }
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(p.bar, 1u);
+        const int bi = (int)(target / gridDim.x);
+        trace_mark(p, bi, 2);
+        // one-way release arrival; the CTA barrier above orders every consumer
+        // thread's writes before it (release is cumulative)
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.bar), "r"(1u) : "memory");
         bool ok = true;
         if (ld_acquire(p.bar) < target) {
             const unsigned long long t0 = now_ns();
@@ -618,8 +589,9 @@ __device__ bool grid_barrier(const MegaParams& p, unsigned target, Smem& S, bool
             }
         }
         S.gflag = ok ? 1 : 0;
+        trace_mark(p, bi, 3);
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     return S.gflag != 0;
 }
 
@@ -632,10 +604,13 @@ __global__ void __launch_bounds__(kThreads, 1) mega_step_kernel(const __grid_con
     const int cta = blockIdx.x, G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    if (p.trace)  // this CTA's trace words restart at zero every step
+        for (int i = threadIdx.x; i < kTraceStride; i += kThreads)
+            p.trace[(size_t)blockIdx.x * kTraceStride + i] = 0ull;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(smem_addr(&S.full[s]), 1);
-            mbar_init(smem_addr(&S.empty[s]), 1);
+            mbar_init(smem_addr(&S.empty[s]), kConsumerWarps);  // one arrival per consumer warp
             S.seq[s] = s - kStages;  // "stage s - kStages" = before the first round
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -667,11 +642,15 @@ __global__ void __launch_bounds__(kThreads, 1) mega_step_kernel(const __grid_con
                      smem_addr(&S.full[slot]), pol);
             g++;
         };
+        int pb = 1;  // phase being issued (= index of the barrier that closes it)
         auto issue_gemv = [&](const GemvPlan& pl) {
             for (int j = 0; j < pl.nstages && ok; j++) {
                 const int rows = min(pl.rps, pl.r1 - pl.r0 - j * pl.rps);
                 issue(pl.w + (size_t)j * pl.rps * pl.row_bytes, (unsigned)(rows * pl.row_bytes));
+                if (j == 0) trace_at(p, pb, 4);
             }
+            trace_at(p, pb, 5);
+            pb++;
         };
         for (int l = 0; l < p.nlayers && ok; l++) {
             issue_gemv(plan_gemv(p, l, kQKV, Q8, cta, G));
@@ -680,8 +659,11 @@ __global__ void __launch_bounds__(kThreads, 1) mega_step_kernel(const __grid_con
                 const int rows = min(kChunk, p.max_seq - c * kChunk);
                 const size_t off = ((size_t)(l * p.kvh + kvh) * p.max_seq + (size_t)c * kChunk) * 128;
                 issue(p.kc + off, (unsigned)(rows * 512));
+                if (i == 0) trace_at(p, pb, 4);
                 if (ok) issue(p.vc + off, (unsigned)(rows * 512));
             }
+            trace_at(p, pb, 5);
+            pb++;
             if (ok) issue_gemv(plan_gemv(p, l, kO, Q8, cta, G));
             if (ok) issue_gemv(plan_gemv(p, l, kGU, Q8, cta, G));
             if (ok) issue_gemv(plan_gemv(p, l, kD, Q8, cta, G));
@@ -703,14 +685,8 @@ __global__ void __launch_bounds__(kThreads, 1) mega_step_kernel(const __grid_con
     }
 
     // -------------------------------------------------------------- consumers
-    unsigned long long* tr = nullptr;
-    int ntr = 0;
-    if (p.trace && threadIdx.x == 0 && (cta == 0 || cta == G - 1))
-        tr = p.trace + (cta == 0 ? 0 : 1024);
-    auto mark = [&]() {
-        if (tr && ntr < 1024) tr[ntr++] = now_ns();
-    };
-    mark();
+    if (p.trace && threadIdx.x == 0) p.trace[(size_t)cta * kTraceStride] = now_ns();
+    if (threadIdx.x == 0) S.cur_b = 1;
     const int tok = *p.tok;
     const float* emb_row = p.embed + (size_t)tok * p.hidden;
     int g = 0;
@@ -718,82 +694,79 @@ __global__ void __launch_bounds__(kThreads, 1) mega_step_kernel(const __grid_con
     float best_v = -INFINITY;
     int best_i = INT_MAX;
     bool ok = true;
+    float nw[kMaxPer];
+    prefetch_norm(p.layers[0].in_norm, p.hidden, nw);
     for (int l = 0; l < p.nlayers && ok; l++) {
         const MegaLayer& L = p.layers[l];
         {   // QKV
             const GemvPlan pl = plan_gemv(p, l, kQKV, Q8, cta, G);
-            load_act(l == 0 ? emb_row : p.x, L.in_norm, p.eps, p.hidden, Q8, xs, S, l != 0);
-            mark();
-            const bool r = gemv_phase<kQKV>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
+            if (threadIdx.x == 0) S.cur_b = nbar + 1;
+            load_act(l == 0 ? emb_row : p.x, L.in_norm, nw, p.eps, p.hidden, Q8, xs, S, l != 0);
+            trace_mark(p, nbar + 1, 0);
+            const bool r = run_gemv<kQKV>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
             g += pl.nstages;
-            mark();
             ok = grid_barrier(p, (++nbar) * G, S, r);
-            mark();
             if (!ok) break;
         }
         {   // ATT
             bool r = true;
+            if (threadIdx.x == 0) S.cur_b = nbar + 1;
+            consumers_sync<kConsumers>();
+            trace_mark(p, nbar + 1, 0);
             for (int i = 0; i < my_units && r; i++) {
                 const int u = cta + i * G;
                 r = att_unit(p, l, u % p.kvh, u / p.kvh, pos, nchunks, g + 2 * i, g + 2 * i + 1,
                              ring, S);
             }
             g += 2 * my_units;
-            mark();
-            mark();
             ok = grid_barrier(p, (++nbar) * G, S, r);
-            mark();
             if (!ok) break;
         }
         {   // O + residual
             const GemvPlan pl = plan_gemv(p, l, kO, Q8, cta, G);
-            load_act(p.ctx, nullptr, p.eps, p.q_width, Q8, xs, S, true);
-            mark();
-            const bool r = gemv_phase<kO>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
+            if (threadIdx.x == 0) S.cur_b = nbar + 1;
+            load_act(p.ctx, nullptr, nw, p.eps, p.q_width, Q8, xs, S, true);
+            trace_mark(p, nbar + 1, 0);
+            const bool r = run_gemv<kO>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
             g += pl.nstages;
-            mark();
+            prefetch_norm(L.post_norm, p.hidden, nw);
             ok = grid_barrier(p, (++nbar) * G, S, r);
-            mark();
             if (!ok) break;
         }
         {   // gate/up + SwiGLU
             const GemvPlan pl = plan_gemv(p, l, kGU, Q8, cta, G);
-            load_act(p.x, L.post_norm, p.eps, p.hidden, Q8, xs, S, true);
-            mark();
-            const bool r = gemv_phase<kGU>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
+            if (threadIdx.x == 0) S.cur_b = nbar + 1;
+            load_act(p.x, L.post_norm, nw, p.eps, p.hidden, Q8, xs, S, true);
+            trace_mark(p, nbar + 1, 0);
+            const bool r = run_gemv<kGU>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
             g += pl.nstages;
-            mark();
             ok = grid_barrier(p, (++nbar) * G, S, r);
-            mark();
             if (!ok) break;
         }
         {   // down + residual
             const GemvPlan pl = plan_gemv(p, l, kD, Q8, cta, G);
-            load_act(p.h, nullptr, p.eps, p.ffn, Q8, xs, S, true);
-            mark();
-            const bool r = gemv_phase<kD>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
+            if (threadIdx.x == 0) S.cur_b = nbar + 1;
+            load_act(p.h, nullptr, nw, p.eps, p.ffn, Q8, xs, S, true);
+            trace_mark(p, nbar + 1, 0);
+            const bool r = run_gemv<kD>(p, pl, l, g, ring, S, xs, emb_row, best_v, best_i);
             g += pl.nstages;
-            mark();
+            prefetch_norm(l + 1 < p.nlayers ? p.layers[l + 1].in_norm : p.final_norm, p.hidden, nw);
             ok = grid_barrier(p, (++nbar) * G, S, r);
-            mark();
             if (!ok) break;
         }
     }
     if (!ok) return;  // uniform: every consumer thread saw the same barrier outcome
     {   // final norm + lm_head + argmax
         const GemvPlan pl = plan_gemv(p, 0, kLM, Q8, cta, G);
-        load_act(p.x, p.final_norm, p.eps, p.hidden, false, xs, S, true);
-        mark();
+        load_act(p.x, p.final_norm, nw, p.eps, p.hidden, false, xs, S, true);
         const bool r = gemv_phase<kLM>(p, pl, 0, g, ring, S, xs, emb_row, best_v, best_i);
-        mark();
-        if (!consumers_sync_and(r)) return;
-        mark();
+        if (!consumers_sync_and<kConsumers>(r)) return;
     }
     if (lane == 0) {
         S.bv[warp] = best_v;
         S.bi[warp] = best_i;
     }
-    consumers_sync();
+    consumers_sync<kConsumers>();
     if (threadIdx.x == 0) {
         float bv = S.bv[0];
         int bi = S.bi[0];
@@ -916,8 +889,9 @@ vb_status mega_prepare(vb_engine* e) {
     P.dbg = cnt + 128;
     P.trace = nullptr;
     if (e->trace_on) {
-        if (cudaMalloc(&m->trace, 2048 * sizeof(unsigned long long)) == cudaSuccess) {
-            cudaMemsetAsync(m->trace, 0, 2048 * sizeof(unsigned long long), e->stream);
+        const size_t tb = (size_t)sms * kTraceStride * sizeof(unsigned long long);
+        if (cudaMalloc(&m->trace, tb) == cudaSuccess) {
+            cudaMemsetAsync(m->trace, 0, tb, e->stream);
             cudaStreamSynchronize(e->stream);
             P.trace = m->trace;
         }
@@ -977,7 +951,8 @@ void mega_release(vb_engine* e) {
 int mega_read_trace(vb_engine* e, unsigned long long* host, int cap) {
     MegaState* m = static_cast<MegaState*>(e->mega);
     if (!m || !m->trace) return 0;
-    const int n = cap < 2048 ? cap : 2048;
+    const int total = m->grid * kTraceStride;
+    const int n = cap < total ? cap : total;
     cudaStreamSynchronize(e->stream);
     if (cudaMemcpy(host, m->trace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost) !=
         cudaSuccess)

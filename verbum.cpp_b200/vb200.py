@@ -247,8 +247,8 @@ class Engine:
         check(lib().vb_engine_set_trace(self.h, int(bool(on))))
 
     def read_trace(self) -> np.ndarray:
-        out = np.zeros(2048, dtype=np.uint64)
-        n = lib().vb_engine_read_trace(self.h, _ptr(out), 2048)
+        out = np.zeros(148 * 1024 * 2, dtype=np.uint64)
+        n = lib().vb_engine_read_trace(self.h, _ptr(out), out.size)
         return out[:n]
 
     def stream(self) -> int:
