@@ -418,26 +418,48 @@ def trace_breakdown(tr, layers=28, stride=1024, words=6):
     return out
 
 
-STEPS2 = ("A.norm", "A.qkv", "A.gather", "A.attn", "A.merge", "A.oproj", "A.barrier",
-          "B.norm", "B.gateup", "B.down", "B.reduce", "B.barrier")
+STEPS2 = ("A.poll", "A.norm", "A.qkv", "A.gather", "A.attn", "A.merge", "A.oproj",
+          "B.poll", "B.norm", "B.gateup", "B.down", "B.reduce")
 
 
-def trace_breakdown2(tr, layers=28, stride=1024):
-    """Two-barrier step: median (over layers and CTAs) duration of each of the
-    12 marked steps of a layer, and the median step time, in us."""
+def trace_breakdown2(tr, layers=28, stride=2048):
+    """Two-barrier step: median (over layers and the CTAs of the kv clusters)
+    duration of each of the 12 marked steps of a layer, and the median layer
+    time, in us."""
     import numpy as np
     G = len(tr) // stride
     if G == 0:
         return None
     t = np.asarray(tr, dtype=np.int64).reshape(G, stride).astype(np.float64)
     m = t[:, 1:1 + 12 * layers].reshape(G, layers, 12)
-    if t[0, 0] == 0 or (m == 0).any():
+    full = (m != 0).all(axis=(1, 2)) & (t[:, 0] != 0)
+    if not full.any():
         return None
-    prev = np.concatenate([t[:, :1, None].repeat(1, 1), m[:, :-1, 11:12]], axis=1)  # [G, L, 1]
+    t, m = t[full], m[full]
+    prev = np.concatenate([t[:, :1, None], m[:, :-1, 11:12]], axis=1)  # [G, L, 1]
     d = np.diff(np.concatenate([prev, m], axis=2), axis=2)  # [G, L, 12]
     out = {name: round(float(np.median(d[:, :, i])) / 1e3, 2) for i, name in enumerate(STEPS2)}
     out["layer_us"] = round(float(np.median(m[:, 1:, 11] - m[:, :-1, 11])) / 1e3, 2)
     out["total_us"] = round(float(m[:, -1, 11].max() - t[:, 0].min()) / 1e3, 1)
+    out["ctas"] = int(G)
+    # cycle profile of consumer thread 0 (words 400 + 16*l)
+    pr = t[:, 400:400 + 40 * layers].reshape(-1, layers, 40)
+    dc = pr[:, 1:, 14] - pr[:, :-1, 14]
+    dn = pr[:, 1:, 15] - pr[:, :-1, 15]
+    ok = dn > 0
+    if ok.any():
+        ghz = float(np.median(dc[ok] / dn[ok]))
+        out["sm_ghz"] = round(ghz, 3)
+        names = ["qkv.wait", "qkv.all", "o.wait", "o.all", "gu.wait", "gu.all", "d.wait", "d.all",
+                 "x.gather", "x.merge", "x.reduce", "attn.wait", "-", "attn", "-", "-",
+                 "qkv.first", "qkv.dot", "qkv.epi", "o.first", "o.dot", "o.epi", "gu.first", "gu.dot", "gu.epi"]
+        out["cycles_us"] = {n: round(float(np.median(pr[:, :, i])) / ghz / 1e3, 3)
+                            for i, n in enumerate(names) if n != "-"}
+        busy = pr[:, :, 12] > 0  # CTAs whose warp 0 had attention chunks
+        if busy.any():
+            out["cycles_us"]["attn.busy"] = round(float(np.median(pr[:, :, 13][busy])) / ghz / 1e3, 3)
+            out["cycles_us"]["attn.busy_wait"] = round(float(np.median(pr[:, :, 11][busy])) / ghz / 1e3, 3)
+            out["cycles_us"]["attn.chunks"] = round(float(np.median(pr[:, :, 12][busy])), 1)
     return out
 
 

@@ -1,27 +1,35 @@
-// vb_mega2.cu -- batch-1 decode step, persistent, TWO grid barriers per layer.
+// vb_mega2.cu -- batch-1 decode step as one persistent kernel with no grid
+// barrier: every cross-CTA dependency is carried by tagged data words.
 //
-// Grid = 8 thread-block clusters x 8 CTAs (one CTA per SM, 64 SMs: a 12-stage
-// TMA ring per CTA already saturates HBM from 64 SMs).  Cluster k owns KV
-// head k.  Per layer:
+// Grid = every co-resident thread-block cluster of 8 CTAs (one CTA per SM;
+// 15 clusters on a B200 at this shared-memory size).  Cluster k < kv_heads
+// owns KV head k; the other clusters sit phase A out.  Per layer:
 //
 //   phase A  (cluster k, CTA r)
-//     x += sum_c D-partials of the previous layer (fixed order), RMSNorm
-//     rows [64r, 64r+64) of the kv-head-k block of Wqkv  (q head 2k, 2k+1, k, v)
-//     cluster barrier; gather the 512 q/k/v values from the 8 CTAs (DSMEM)
+//     x += sum_c down partials of the previous layer (fixed order), RMSNorm
+//     rows [64r, 64r+64) of the kv-head-k block of Wqkv (q head 2k, 2k+1, k,
+//       v), each value pushed into all 8 CTAs' shared memory
 //     q/k RMSNorm + RoPE, KV append (r = 0), attention over this CTA's
-//     32-position chunks (chunk c on CTA c % 8) with an online softmax
-//     cluster barrier; merge the 8 CTA partials (DSMEM) -> ctx of heads 2k,2k+1
+//     32-position chunks (chunk c on CTA c % 8) with an online softmax; the
+//     partial (acc, max, sum) pushed to all 8 CTAs, merged in rank order
 //     split-K o_proj: rows [128r, 128r+128) of Wo[:, 256k:256k+256] . ctx
-//       -> partial_o[k]
-//   grid barrier
+//       -> o partial of head k (global)
 //   phase B  (every CTA b)
-//     x += sum_k partial_o[k] (fixed order), RMSNorm
+//     x += sum_k o partials (fixed order), RMSNorm
 //     its slice of gate/up pairs -> h slice (SwiGLU fused)
-//     split-K down: sum_{i in slice} h_i * Wd^T[i, :] -> 1024-wide partial
-//     cluster barrier; CTA r reduces elements [128r, 128r+128) over the 8
-//     CTAs of its cluster (DSMEM) -> partial_d[cluster]
-//   grid barrier
-// then LM (all CTAs): x += sum partial_d, final RMSNorm, logits rows + argmax.
+//     split-K down: sum_{i in slice} h_i * Wd^T[i, :]; outputs [128q, +128)
+//       pushed to CTA q of the cluster, which sums the 8 in rank order
+//       -> down partial of the cluster (global)
+// then LM (all CTAs): x += sum of down partials, final RMSNorm, logits rows +
+// argmax (the last CTA to finish picks the token).
+//
+// Exchange words are 64 bits: the f32 value and a tag naming the launch, the
+// layer and the exchange.  Producers store them (into a peer CTA's shared
+// memory, or global memory); consumers poll until the tag is the expected one.
+// The data is its own flag, so a consumer proceeds one memory round trip
+// after the last producer's store, with no barrier, fence or counter between.
+// Global partials alternate between two buffers by layer parity, which is
+// enough for no producer to overwrite a word some consumer has yet to read.
 //
 // Every CTA keeps its own copy of the residual stream x in shared memory; all
 // copies are bit-identical (same inputs summed in the same order).  Weights
@@ -32,10 +40,10 @@
 // A producer warp streams every byte the CTA needs for the whole token through
 // the shared-memory ring (cp.async.bulk + mbarriers) and never waits for
 // activations.  All waits are bounded (2 s of %globaltimer) and record where
-// they gave up.  Cluster barriers are mbarriers arrived on remotely at cluster
-// scope by each CTA's consumer thread 0, so the producer never joins them.
+// they gave up.
 #include <limits.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include <string>
 #include <vector>
@@ -51,11 +59,11 @@ constexpr int kStageBytes = 16384;
 constexpr int kStages = 11;
 constexpr int kCW = 8;              // consumer warps
 constexpr int kCT = kCW * 32;       // consumer threads
-constexpr int kThreads = kCT + 32;  // + producer warp
+constexpr int kThreads = kCT + 32;  // + ring producer warp
 constexpr int kChunk = 32;
 constexpr int kHid = 1024;          // hidden size this kernel is laid out for
-constexpr int kXs = 4096;           // normalised-input capacity (floats)
-constexpr int kPer = kXs / kCT;     // 16
+constexpr int kXs = kHid;           // normalised-input capacity (floats)
+constexpr int kPer = kXs / kCT;     // 4
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kXs * sizeof(float);
 
 struct M2Layer {
@@ -82,12 +90,12 @@ struct M2Params {
     float* kc;  // [L][KVH][max_seq][128]
     float* vc;
     float* logits;
-    float* part_o;  // [KVH][hidden]
-    float* part_d;  // [nclusters][hidden]
+    unsigned long long* xo;  // [2][KVH][hidden] tagged o_proj partials (by layer parity)
+    unsigned long long* xd;  // [2][nclusters][hidden] tagged down-proj partials
+    int* epoch;              // launches so far (tags of this launch use epoch + 1)
     float* am_val;
     int* am_idx;
     int* am_ticket;
-    unsigned* bar;
     int* tok;
     int* pos;
     int* next;
@@ -101,20 +109,45 @@ struct M2Params {
 };
 
 // Trace: word 0 = start, then per layer kTraceMarks %globaltimer stamps of
-// consumer thread 0: A residual+norm, A qkv rows, A gather, A attention,
-// A merge, A o_proj, A release, B residual+norm, B gate/up, B down,
-// B cluster reduce, B release.
-constexpr int kTraceStride2 = 1024;
+// consumer thread 0 after: A partials arrived, A norm, A qkv rows, A gather,
+// A attention, A merge, A o_proj, B partials arrived, B norm, B gate/up,
+// B down + push, B reduce.
+constexpr int kTraceStride2 = 2048;
 constexpr int kTraceMarks = 12;
 __device__ __forceinline__ void tmark(const M2Params& p, int l, int i) {
     if (p.trace && threadIdx.x == 0 && 1 + kTraceMarks * (l + 1) < kTraceStride2)
         p.trace[(size_t)blockIdx.x * kTraceStride2 + 1 + kTraceMarks * l + i] = now_ns();
 }
 
+// Cycle profile (tracing only, consumer thread 0): per layer kProfWords words
+// at kProfBase: [0..7] wait/total clock64 cycles of the qkv, o_proj, gate/up
+// and down phases, [8..10] cycles in the gather, merge and reduce exchanges,
+// [11] attention stage-wait cycles and [12] chunks of warp 0, [13] attention
+// cycles, [14] clock64 and [15] %globaltimer at the layer's start; [16 + 3i]
+// first-stage compute, [17 + 3i] dot+reduce, [18 + 3i] epilogue cycles of
+// gemv i (qkv, o, gate/up).
+constexpr int kProfBase = 400;
+constexpr int kProfWords = 40;
+__device__ __forceinline__ long long* prof_ptr(const M2Params& p, int l) {
+    if (!p.trace || threadIdx.x != 0 || kProfBase + kProfWords * (l + 1) > kTraceStride2) return nullptr;
+    return reinterpret_cast<long long*>(p.trace + (size_t)blockIdx.x * kTraceStride2 + kProfBase + kProfWords * l);
+}
+
+// Exchange words: {value bits, tag} in one 64-bit word, written by the
+// producing CTA (into a peer's shared memory, or global memory) and polled by
+// the consumer until the tag is the expected one -- the data is its own flag,
+// so no barrier, fence or counter sits between producer and consumer.
+// tag = (epoch + 1) << 8 | layer << 2 | kind.
+enum XKind : unsigned { kXQkv = 0, kXAtt = 1, kXRed = 2, kXGlobal = 3 };
+constexpr int kAttWords = 264;  // 256 acc + m[2] + l[2] (+ pad)
+
 struct __align__(16) S2 {
+    unsigned long long qkv64[512];          // pushed by the 8 CTAs: 64 rows each
+    union {
+        unsigned long long att64[kCS][kAttWords];  // attention partials of the 8 CTAs
+        unsigned long long red64[kCS][128];        // down partials for my 128 outputs
+    } xu;
     float xr[kHid];       // residual stream (identical in every CTA)
-    float accd[kHid];     // split-K down partial of this CTA
-    float qkv_part[64];   // this CTA's 64 rows of its kv-head block
     float qkv[512];       // gathered q(2 heads) | k | v
     float q[2][128];
     float tq[2][128];
@@ -123,20 +156,28 @@ struct __align__(16) S2 {
     float vn[128];
     float att_acc[2][128];  // this CTA's attention partial
     float att_m[2], att_l[2];
-    float sc[2][kChunk];
-    float e[2][kChunk];
-    float cm[2], cl[2];
+    float wacc[kCW][2][128];  // per-warp attention partials
+    float wm[kCW][2], wl[kCW][2];
     float h[64];
+    float sc_qkv[64];     // INT8 row scales of this CTA's phase-A rows
+    float sc_o[128];
+    float sc_gu[128];     // ... of its phase-B gate/up rows
+    float sc_d[128];      // ... of the down-proj outputs it reduces
     double red[16];
     float bv[kCW];
     int bi[kCW];
-    int gflag;
     int wflag;
     unsigned long long full[kStages];
     unsigned long long empty[kStages];
-    unsigned long long cbar;  // cluster barrier: kCS remote arrivals per phase
     volatile int seq[kStages];
 };
+
+// Functions below that take S2& / shared pointers and are not inlined tell
+// the compiler the pointers are shared-memory ones, so it keeps
+// shared-memory instructions; several are kept out of line on purpose: the
+// whole per-layer code path has to stay small enough for the instruction
+// caches, since every layer runs all of it once.
+#define VB_SHARED(ptr) __builtin_assume(__isShared(ptr))
 
 __device__ __forceinline__ unsigned cluster_rank() {
     unsigned r;
@@ -153,76 +194,103 @@ __device__ __forceinline__ unsigned mapa(unsigned local, unsigned rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float ld_dsmem(unsigned addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+
+__device__ __forceinline__ unsigned xtag(unsigned ep1, int l, unsigned kind) {
+    return (ep1 << 8) | ((unsigned)l << 2) | kind;
+}
+__device__ __forceinline__ unsigned long long xpack(float v, unsigned tag) {
+    return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ unsigned xtag_of(unsigned long long w) { return (unsigned)(w >> 32); }
+__device__ __forceinline__ float xval(unsigned long long w) { return __uint_as_float((unsigned)w); }
+
+__device__ __forceinline__ void st_peer(unsigned addr, unsigned long long v) {
+    asm volatile("st.relaxed.cluster.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_gpu(unsigned long long* ptr, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_gpu(const unsigned long long* ptr) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr));
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_own(unsigned saddr) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.cluster.shared::cta.u64 %0, [%1];" : "=l"(v) : "r"(saddr));
     return v;
 }
 
-// Cluster-wide barrier over the consumer threads of the kCS CTAs.
-__device__ bool cluster_sync(const M2Params& p, S2& S, unsigned& cphase) {
-    consumers_sync<kCT>();
-    if (threadIdx.x == 0) {
-        const unsigned la = smem_addr(&S.cbar);
-        for (unsigned r = 0; r < kCS; r++) {
-            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mapa(la, r))
-                         : "memory");
-        }
-        bool ok = true;
-        const unsigned par = cphase & 1u;
-        const unsigned long long t0 = now_ns();
-        for (unsigned it = 0;; it++) {
-            unsigned done;
-            asm volatile(
-                "{ .reg .pred q; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 q, [%1], %2; "
-                "selp.u32 %0, 1, 0, q; }"
-                : "=r"(done)
-                : "r"(la), "r"(par)
-                : "memory");
-            if (done) break;
-            if ((it & 255u) == 255u) {
-                if (err_read(p.err)) { ok = false; break; }
-                if (now_ns() - t0 > kWaitNs) {
-                    record_fail(p.err, p.dbg, kErrPipeTimeout, 6, (int)cphase, 0);
-                    ok = false;
-                    break;
-                }
+// Slow path of wait_own: bounded spin until the word at shared address
+// `saddr` carries `tag`.  Returns the word, or 0 (tag 0 is never live) after
+// the time bound (error recorded) or when another CTA has failed.
+__device__ __noinline__ unsigned long long spin_own(const M2Params& p, unsigned saddr, unsigned tag, int site) {
+    const unsigned long long t0 = now_ns();
+    for (unsigned it = 1;; it++) {
+        const unsigned long long v = ld_own(saddr);
+        if (xtag_of(v) == tag) return v;
+        if ((it & 63u) == 0) {
+            if (err_read(p.err)) return 0ull;
+            if (now_ns() - t0 > kWaitNs) {
+                record_fail(p.err, p.dbg, kErrPipeTimeout, site, (int)blockIdx.x, (int)xtag_of(v));
+                return 0ull;
             }
         }
-        S.wflag = ok ? 1 : 0;
     }
-    cphase++;
-    consumers_sync<kCT>();
-    return S.wflag != 0;
+}
+__device__ __forceinline__ bool wait_own(const M2Params& p, const unsigned long long* w, unsigned tag, int site,
+                                         float& out) {
+    const unsigned sa = smem_addr(w);
+    unsigned long long v = ld_own(sa);
+    if (xtag_of(v) != tag) {
+        v = spin_own(p, sa, tag, site);
+        if (xtag_of(v) != tag) return false;
+    }
+    out = xval(v);
+    return true;
 }
 
-__device__ bool grid_barrier2(const M2Params& p, unsigned target, S2& S, bool ok_in) {
-    if (!consumers_sync_and<kCT>(ok_in)) {
-        if (threadIdx.x == 0) atomicCAS(p.err, 0, kErrPipeTimeout);
-        return false;
-    }
-    if (threadIdx.x == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.bar), "r"(1u) : "memory");
-        bool ok = true;
-        if (ld_acquire(p.bar) < target) {
-            const unsigned long long t0 = now_ns();
-            for (unsigned it = 1;; it++) {
-                if (ld_acquire(p.bar) >= target) break;
-                if ((it & 63u) == 0) {
-                    if (err_read(p.err)) { ok = false; break; }
-                    if (now_ns() - t0 > kWaitNs) {
-                        record_fail(p.err, p.dbg, kErrBarrierTimeout, kSiteGrid, (int)target,
-                                    (int)ld_acquire(p.bar));
-                        ok = false;
-                        break;
-                    }
+// Sum over c < n (in c order) of the tagged partials parts[c][t + k*kCT],
+// k = 0..3, polling global memory until every word of a group of 8 partials
+// carries `tag` (all loads of a group in flight together).  A failed wait
+// leaves the error word set (the caller checks it).
+__device__ __noinline__ float4 sum_parts_tagged(const M2Params& p, const unsigned long long* parts, int n,
+                                                unsigned tag) {
+    const int t = threadIdx.x, H = p.hidden;
+    float add[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c0 = 0; c0 < n; c0 += 8) {
+        unsigned long long w[4][8];
+        unsigned long long t0 = 0;
+        for (unsigned it = 0;; it++) {
+            bool ready = true;
+#pragma unroll
+            for (int cc = 0; cc < 8; cc++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int c = c0 + cc;
+                    w[k][cc] = c < n ? ld_gpu(parts + (size_t)c * H + t + k * kCT) : xpack(0.f, tag);
+                }
+#pragma unroll
+            for (int cc = 0; cc < 8; cc++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) ready &= xtag_of(w[k][cc]) == tag;
+            if (ready) break;
+            if (it == 0) {
+                t0 = now_ns();
+            } else if ((it & 7u) == 0) {
+                if (err_read(p.err)) return make_float4(0.f, 0.f, 0.f, 0.f);
+                if (now_ns() - t0 > kWaitNs) {
+                    record_fail(p.err, p.dbg, kErrBarrierTimeout, kSiteGrid, (int)tag, c0);
+                    return make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
         }
-        S.gflag = ok ? 1 : 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+#pragma unroll
+            for (int cc = 0; cc < 8; cc++) add[k] += xval(w[k][cc]);
     }
-    consumers_sync<kCT>();
-    return S.gflag != 0;
+    return make_float4(add[0], add[1], add[2], add[3]);
 }
 
 // ------------------------------------------------------------------ plans
@@ -231,15 +299,11 @@ struct Plan {
     int row_bytes;
     int rps;           // rows per stage
     int r0, r1;        // rows of the CTA's range (relative to the matrix)
-    int K;
-    bool q8;
     int nstages;
 };
 
 __device__ __forceinline__ Plan make_plan(const void* W, int K, bool q8, int r0, int r1, int unit) {
     Plan g;
-    g.K = K;
-    g.q8 = q8;
     g.row_bytes = K * (q8 ? 1 : 4);
     g.rps = kStageBytes / g.row_bytes;
     if (unit == 2) g.rps &= ~1;
@@ -284,53 +348,15 @@ __device__ __forceinline__ Plan plan_lm(const M2Params& p, int b, int G) {
 }
 
 // --------------------------------------------------------------- consumers
-__device__ __forceinline__ float dot_f32(const float* wrow, const float* xs, int K, int lane) {
-    const float4* w4 = reinterpret_cast<const float4*>(wrow);
-    const float4* x4 = reinterpret_cast<const float4*>(xs);
-    float a0 = 0.f, a1 = 0.f;
-    for (int k = lane; k < (K >> 2); k += 64) {
-        const float4 w = w4[k], x = x4[k];
-        a0 = fmaf(w.x, x.x, a0); a0 = fmaf(w.y, x.y, a0); a0 = fmaf(w.z, x.z, a0); a0 = fmaf(w.w, x.w, a0);
-        if (k + 32 < (K >> 2)) {
-            const float4 w2 = w4[k + 32], x2 = x4[k + 32];
-            a1 = fmaf(w2.x, x2.x, a1); a1 = fmaf(w2.y, x2.y, a1); a1 = fmaf(w2.z, x2.z, a1); a1 = fmaf(w2.w, x2.w, a1);
-        }
-    }
-    return warp_sum(a0 + a1);
-}
-
-__device__ __forceinline__ float dot_i8(const int8_t* wrow, const float* xs, int K, int lane) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int gi = lane; gi < (K >> 4); gi += 32) {
-        const uint4 w = *reinterpret_cast<const uint4*>(wrow + 16 * gi);
-        const float* xc = xs + ((gi >> 5) << 9) + 4 * lane;
-        const float4 x0 = *reinterpret_cast<const float4*>(xc);
-        const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
-        const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
-        const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
-        const f4 b0 = i8x4_to_f32(w.x), b1 = i8x4_to_f32(w.y);
-        const f4 b2 = i8x4_to_f32(w.z), b3 = i8x4_to_f32(w.w);
-        a0 = fmaf(b0.v[0], x0.x, a0); a0 = fmaf(b0.v[1], x0.y, a0);
-        a1 = fmaf(b0.v[2], x0.z, a1); a1 = fmaf(b0.v[3], x0.w, a1);
-        a0 = fmaf(b1.v[0], x1.x, a0); a0 = fmaf(b1.v[1], x1.y, a0);
-        a1 = fmaf(b1.v[2], x1.z, a1); a1 = fmaf(b1.v[3], x1.w, a1);
-        a0 = fmaf(b2.v[0], x2.x, a0); a0 = fmaf(b2.v[1], x2.y, a0);
-        a1 = fmaf(b2.v[2], x2.z, a1); a1 = fmaf(b2.v[3], x2.w, a1);
-        a0 = fmaf(b3.v[0], x3.x, a0); a0 = fmaf(b3.v[1], x3.y, a0);
-        a1 = fmaf(b3.v[2], x3.z, a1); a1 = fmaf(b3.v[3], x3.w, a1);
-    }
-    return warp_sum(a0 + a1);
-}
-
 __device__ __forceinline__ int perm_index(int i) {
     const int c = i >> 9, r = i & 511;
     return (c << 9) + (((r >> 2) & 3) << 7) + ((r >> 4) << 2) + (r & 3);
 }
 
 // Stage wait shared by all consumer modes.  in_order: every warp takes every
-// stage (no slot-order gate needed); otherwise warps take every 8th stage and
-// wait for the slot's previous round first.
-__device__ bool stage_wait(const M2Params& p, S2& S, int gs, bool in_order) {
+// stage (no slot-order gate needed); otherwise warps take stages out of order
+// and wait for the slot's previous round first.
+__device__ __forceinline__ bool stage_wait(const M2Params& p, S2& S, int gs, bool in_order) {
     const int lane = threadIdx.x & 31;
     const int slot = gs % kStages;
     const unsigned par = (unsigned)(gs / kStages) & 1u;
@@ -347,98 +373,255 @@ __device__ bool stage_wait(const M2Params& p, S2& S, int gs, bool in_order) {
         }
     return ok != 0;
 }
+__device__ __forceinline__ void stage_release(S2& S, int gs, unsigned count) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(smem_addr(&S.empty[gs % kStages]), count);
+}
 
-// Epilogues of the row-dot phases (lane 0 of the warp that computed the row
-// stores; every lane sees the same reduced values).
-struct EpiQkvPart {  // phase A: this CTA's rows of its kv-head block
-    float* dst;
-    int base;
-    __device__ void operator()(int row, float a, float) const {
-        if ((threadIdx.x & 31) == 0) dst[row - base] = a;
-    }
-};
-struct EpiStore {  // phase A: o_proj partial of the cluster's kv head
-    float* dst;
-    __device__ void operator()(int row, float a, float) const {
-        if ((threadIdx.x & 31) == 0) dst[row] = a;
-    }
-};
-struct EpiSwiGLU {  // phase B: h slice
-    float* h;
+// Epilogue of the row-dot phases, run by the lane that owns the row (or the
+// gate/up pair) with the reduced, scaled values.
+enum EpiKind : int { kEpiQkvPush = 0, kEpiStoreTagged = 1, kEpiSwiGLU = 2, kEpiLogits = 3 };
+struct Epi {
+    int kind;
+    unsigned base;            // qkv push: shared address of qkv64
+    unsigned tag;
+    unsigned long long* dst;  // store: tagged o partial row 0
+    float* h;                 // swiglu: h slice, first pair p0
     int p0;
-    __device__ void operator()(int row, float g, float u) const {
-        if ((threadIdx.x & 31) == 0) h[(row >> 1) - p0] = silu_f(g) * u;
-    }
-};
-struct EpiLogits {  // LM: logits + running argmax of this lane
     float* logits;
-    float* bv;
-    int* bi;
-    __device__ void operator()(int row, float a, float) const {
-        if ((threadIdx.x & 31) == 0) logits[row] = a;
-        if (a > *bv || (a == *bv && row < *bi)) {
-            *bv = a;
-            *bi = row;
+};
+
+// Dot products of up to NR rows of one stage with xs, all rows in flight at
+// once.  f32: every lane takes float4 columns lane, lane+32, ...
+template <int NR, int K>
+__device__ __forceinline__ void dot_rows_f32(const char* st, int row_bytes, int cnt, const float* xs,
+                                             int lane, float (&acc)[NR]) {
+    static_assert(K % 128 == 0, "f32 rows: K multiple of 128");
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+#pragma unroll
+    for (int r = 0; r < NR; r++) acc[r] = 0.f;
+#pragma unroll 2
+    for (int it = 0; it < K / 128; it++) {
+        const int k = lane + 32 * it;
+        const float4 x = x4[k];
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            if (r < cnt) {
+                const float4 w = reinterpret_cast<const float4*>(st + (size_t)r * row_bytes)[k];
+                acc[r] = fmaf(w.x, x.x, acc[r]);
+                acc[r] = fmaf(w.y, x.y, acc[r]);
+                acc[r] = fmaf(w.z, x.z, acc[r]);
+                acc[r] = fmaf(w.w, x.w, acc[r]);
+            }
         }
     }
-};
+#pragma unroll
+    for (int off = 16; off; off >>= 1)
+#pragma unroll
+        for (int r = 0; r < NR; r++) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+}
 
-// Row-dot GEMV phase: result of row r (absolute) goes to epi(r, value).
-// warp mode (f32, rows per stage < 8): warp w takes stages w, w+8, ...
-// coop mode: every warp takes every stage, rows dealt out across warps.
-template <class Epi>
-__device__ bool gemv_rows(const M2Params& p, const Plan& g, int gbase, const char* ring, S2& S,
-                          const float* xs, const float* scales, bool coop, int pair, Epi epi) {
+__device__ __forceinline__ float dot16_i8(uint4 w, float4 x0, float4 x1, float4 x2, float4 x3, float a) {
+    const f4 b0 = i8x4_to_f32(w.x), b1 = i8x4_to_f32(w.y);
+    const f4 b2 = i8x4_to_f32(w.z), b3 = i8x4_to_f32(w.w);
+    a = fmaf(b0.v[0], x0.x, a); a = fmaf(b0.v[1], x0.y, a);
+    a = fmaf(b0.v[2], x0.z, a); a = fmaf(b0.v[3], x0.w, a);
+    a = fmaf(b1.v[0], x1.x, a); a = fmaf(b1.v[1], x1.y, a);
+    a = fmaf(b1.v[2], x1.z, a); a = fmaf(b1.v[3], x1.w, a);
+    a = fmaf(b2.v[0], x2.x, a); a = fmaf(b2.v[1], x2.y, a);
+    a = fmaf(b2.v[2], x2.z, a); a = fmaf(b2.v[3], x2.w, a);
+    a = fmaf(b3.v[0], x3.x, a); a = fmaf(b3.v[1], x3.y, a);
+    a = fmaf(b3.v[2], x3.z, a); a = fmaf(b3.v[3], x3.w, a);
+    return a;
+}
+
+// INT8 rows against the lane-interleaved xs.  K % 512 == 0: the whole warp on
+// each row; K == 256: two rows at a time, one per half-warp.
+template <int NR, int K>
+__device__ __forceinline__ void dot_rows_i8(const char* st, int row_bytes, int cnt, const float* xs,
+                                            int lane, float (&acc)[NR]) {
+    static_assert(K % 512 == 0 || K == 256, "INT8 rows: K multiple of 512, or 256");
+#pragma unroll
+    for (int r = 0; r < NR; r++) acc[r] = 0.f;
+    if constexpr (K >= 512) {
+#pragma unroll 1
+        for (int it = 0; it < K / 512; it++) {
+            const int gi = lane + 32 * it;
+            const float* xc = xs + ((gi >> 5) << 9) + 4 * lane;
+            const float4 x0 = *reinterpret_cast<const float4*>(xc);
+            const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
+            const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
+            const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
+#pragma unroll
+            for (int r = 0; r < NR; r++)
+                if (r < cnt)
+                    acc[r] = dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi),
+                                      x0, x1, x2, x3, acc[r]);
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1)
+#pragma unroll
+            for (int r = 0; r < NR; r++) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+    } else {  // K == 256: 16 groups per row
+        const int h = lane >> 4, gi = lane & 15;
+        const float* xc = xs + 4 * gi;
+        const float4 x0 = *reinterpret_cast<const float4*>(xc);
+        const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
+        const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
+        const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
+        float ap[(NR + 1) / 2];
+#pragma unroll
+        for (int q = 0; q < (NR + 1) / 2; q++) {
+            const int r = 2 * q + h;
+            ap[q] = r < cnt ? dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi),
+                                       x0, x1, x2, x3, 0.f)
+                            : 0.f;
+        }
+#pragma unroll
+        for (int off = 8; off; off >>= 1)
+#pragma unroll
+            for (int q = 0; q < (NR + 1) / 2; q++) ap[q] += __shfl_xor_sync(0xffffffffu, ap[q], off);
+#pragma unroll
+        for (int q = 0; q < (NR + 1) / 2; q++) {
+            acc[2 * q] = __shfl_sync(0xffffffffu, ap[q], 0);
+            if (2 * q + 1 < NR) acc[2 * q + 1] = __shfl_sync(0xffffffffu, ap[q], 16);
+        }
+    }
+}
+
+template <int NR>
+__device__ __forceinline__ float pick(const float (&v)[NR], int i) {
+    float r = 0.f;
+#pragma unroll
+    for (int k = 0; k < NR; k++)
+        if (k == i) r = v[k];
+    return r;
+}
+
+// Row-dot GEMV phase: the value of row r (absolute) goes to the epilogue,
+// scaled by scl[r - g.r0] (shared memory, INT8) when scl is set.
+// warp mode (f32 rows of 4 KB): warp w takes stages w, w+8, ... (all rows).
+// coop mode: every warp takes every stage, rows split evenly across warps.
+// pair: rows come in gate/up pairs.  Logits: the best (value, row) of this
+// warp lands in S.bv / S.bi.
+template <bool Q8, int NR, int K>
+__device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbase, const char* ring, S2& S,
+                                       const float* xs, const float* scl, bool coop, bool pair, const Epi epi,
+                                       long long* prof, long long* prof2) {
+    VB_SHARED(ring);
+    VB_SHARED(&S);
+    VB_SHARED(xs);
+    if (scl) VB_SHARED(scl);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rpw = coop ? g.rps / kCW : g.rps;
+    float best_v = -INFINITY;
+    int best_i = INT_MAX;
+    long long t_wait = 0, t_dot = 0, t_epi = 0, t_first = -1;
+    const long long t_start = clock64();
     for (int j = coop ? 0 : warp; j < g.nstages; j += coop ? 1 : kCW) {
         const int gs = gbase + j;
+        const long long tw = clock64();
         if (!stage_wait(p, S, gs, coop)) return false;
+        t_wait += clock64() - tw;
         const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
         const int rA = g.r0 + j * g.rps;
         const int nr = min(g.rps, g.r1 - rA);
-        const int step = pair ? 2 : 1;
-        const int first = coop ? warp * step : 0, stride = coop ? kCW * step : step;
-        for (int r = first; r + step - 1 < nr; r += stride) {
-            float a = g.q8 ? dot_i8(reinterpret_cast<const int8_t*>(st + (size_t)r * g.row_bytes), xs, g.K, lane)
-                           : dot_f32(reinterpret_cast<const float*>(st + (size_t)r * g.row_bytes), xs, g.K, lane);
-            if (g.q8) a *= __ldg(scales + rA + r);
-            float b = 0.f;
-            if (pair) {
-                b = g.q8 ? dot_i8(reinterpret_cast<const int8_t*>(st + (size_t)(r + 1) * g.row_bytes), xs, g.K, lane)
-                         : dot_f32(reinterpret_cast<const float*>(st + (size_t)(r + 1) * g.row_bytes), xs, g.K, lane);
-                if (g.q8) b *= __ldg(scales + rA + r + 1);
+        const int lo = coop ? warp * rpw : 0;
+        const int cnt = max(0, min(rpw, nr - lo));
+        float acc[NR];
+        const long long td = clock64();
+        if constexpr (Q8) dot_rows_i8<NR, K>(st + (size_t)lo * g.row_bytes, g.row_bytes, cnt, xs, lane, acc);
+        else dot_rows_f32<NR, K>(st + (size_t)lo * g.row_bytes, g.row_bytes, cnt, xs, lane, acc);
+        if (prof2) asm volatile("" : "+f"(acc[0]));
+        const long long te = clock64();
+        t_dot += te - td;
+        stage_release(S, gs, coop ? 1u : (unsigned)kCW);
+        const int row0 = rA + lo;
+        const int mine = pair ? 2 * lane : lane;
+        if (mine + (pair ? 1 : 0) < cnt) {
+            float a = pick(acc, mine), bval = pair ? pick(acc, mine + 1) : 0.f;
+            const int row = row0 + mine;
+            if (scl) {
+                a *= scl[row - g.r0];
+                if (pair) bval *= scl[row + 1 - g.r0];
             }
-            epi(rA + r, a, b);
+            switch (epi.kind) {
+            case kEpiQkvPush: {
+                const unsigned long long w = xpack(a, epi.tag);
+#pragma unroll 1
+                for (unsigned q = 0; q < kCS; q++) st_peer(mapa(epi.base + 8u * (unsigned)row, q), w);
+                break;
+            }
+            case kEpiStoreTagged:
+                st_gpu(epi.dst + row, xpack(a, epi.tag));
+                break;
+            case kEpiSwiGLU:
+                epi.h[(row >> 1) - epi.p0] = silu_f(a) * bval;
+                break;
+            default:
+                epi.logits[row] = a;
+                if (better(a, row, best_v, best_i)) {
+                    best_v = a;
+                    best_i = row;
+                }
+                break;
+            }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_addr(&S.empty[gs % kStages]), coop ? 1u : (unsigned)kCW);
+        const long long tf = clock64();
+        t_epi += tf - te;
+        if (t_first < 0) t_first = tf - td;
+    }
+    if (epi.kind == kEpiLogits) {
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, off);
+            if (better(ov, oi, best_v, best_i)) {
+                best_v = ov;
+                best_i = oi;
+            }
+        }
+        if (lane == 0) {
+            S.bv[warp] = best_v;
+            S.bi[warp] = best_i;
+        }
+    }
+    if (prof) {
+        prof[0] += t_wait;
+        prof[1] += clock64() - t_start;
+    }
+    if (prof2) {
+        prof2[0] += t_first;
+        prof2[1] += t_dot;
+        prof2[2] += t_epi;
     }
     return true;
 }
 
-// x += sum of `n` partial vectors (fixed order), then RMSNorm with the
-// pre-loaded norm registers into xs (lane-interleaved layout for INT8).
-__device__ void residual_norm(const M2Params& p, S2& S, float* xs, const float* parts, int n,
-                              const float* emb_row, const float (&nw)[kPer], bool perm) {
+// x += sum of `n` tagged partial vectors (fixed order), then RMSNorm with the
+// pre-loaded norm values into xs (lane-interleaved layout for INT8).  Trace
+// mark `mk` is stamped once the partials have arrived.  Returns false
+// (uniformly across the consumer threads) when a wait gave up.
+__device__ __noinline__ bool residual_norm(const M2Params& p, S2& S, float* xs, const unsigned long long* parts,
+                                           int n, unsigned tag, const float* emb_row, const float4 nw, bool perm,
+                                           int l, int mk) {
+    VB_SHARED(&S);
+    VB_SHARED(xs);
     const int t = threadIdx.x;
-    const int H = p.hidden;
+    float4 add = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!emb_row) add = sum_parts_tagged(p, parts, n, tag);
+    if (!consumers_sync_and<kCT>(err_read(p.err) == 0)) return false;
+    if (mk >= 0) tmark(p, l, mk);
+    const float av[4] = {add.x, add.y, add.z, add.w};
+    const float wv[4] = {nw.x, nw.y, nw.z, nw.w};
+    float v[4];
     double ss = 0.0;
-    float v[kHid / kCT];
 #pragma unroll
-    for (int k = 0; k < kHid / kCT; k++) {
+    for (int k = 0; k < 4; k++) {
         const int i = t + k * kCT;
-        float x = 0.f;
-        if (i < H) {
-            if (emb_row) {
-                x = emb_row[i];
-            } else {
-                float add = 0.f;
-                for (int c = 0; c < n; c++) add += __ldcg(parts + (size_t)c * H + i);
-                x = S.xr[i] + add;
-            }
-            S.xr[i] = x;
-            ss += (double)x * (double)x;
-        }
+        const float x = emb_row ? emb_row[i] : S.xr[i] + av[k];
+        S.xr[i] = x;
+        ss += (double)x * (double)x;
         v[k] = x;
     }
     ss = warp_sum_d(ss);
@@ -447,21 +630,38 @@ __device__ void residual_norm(const M2Params& p, S2& S, float* xs, const float* 
     double tot = 0.0;
 #pragma unroll
     for (int w = 0; w < kCW; w++) tot += S.red[w];
-    const float sc = rms_scale(tot, H, p.eps);
+    const float sc = rms_scale(tot, p.hidden, p.eps);
 #pragma unroll
-    for (int k = 0; k < kHid / kCT; k++) {
+    for (int k = 0; k < 4; k++) {
         const int i = t + k * kCT;
-        if (i < H) xs[perm ? perm_index(i) : i] = __fmul_rn(__fmul_rn(v[k], sc), nw[k]);
+        xs[perm ? perm_index(i) : i] = __fmul_rn(__fmul_rn(v[k], sc), wv[k]);
     }
     consumers_sync<kCT>();
+    return true;
 }
 
-__device__ __forceinline__ void load_norm(const float* w, int K, float (&nw)[kPer]) {
+// Residual update without a norm (CTAs that sit out phase A keep their copy
+// of x current while the kv clusters work).
+__device__ __noinline__ bool residual_only(const M2Params& p, S2& S, const unsigned long long* parts, int n,
+                                           unsigned tag, const float* emb_row) {
+    VB_SHARED(&S);
+    const int t = threadIdx.x;
+    float4 add = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!emb_row) add = sum_parts_tagged(p, parts, n, tag);
+    if (!consumers_sync_and<kCT>(err_read(p.err) == 0)) return false;
+    const float av[4] = {add.x, add.y, add.z, add.w};
 #pragma unroll
-    for (int k = 0; k < kPer; k++) {
-        const int i = threadIdx.x + k * kCT;
-        nw[k] = (w && i < K) ? __ldg(w + i) : 0.f;
+    for (int k = 0; k < 4; k++) {
+        const int i = t + k * kCT;
+        S.xr[i] = emb_row ? emb_row[i] : S.xr[i] + av[k];
     }
+    consumers_sync<kCT>();
+    return true;
+}
+
+__device__ __forceinline__ float4 load_norm(const float* w) {
+    const int t = threadIdx.x;
+    return make_float4(__ldg(w + t), __ldg(w + t + kCT), __ldg(w + t + 2 * kCT), __ldg(w + t + 3 * kCT));
 }
 
 __device__ __forceinline__ float rope1(const float* y, int d, const float* cr, const float* sr) {
@@ -469,180 +669,373 @@ __device__ __forceinline__ float rope1(const float* y, int d, const float* cr, c
                   : __fadd_rn(__fmul_rn(y[d], cr[d]), __fmul_rn(y[d - 64], sr[d]));
 }
 
-// Phase A for the cluster owning kv head k.
-template <bool Q8>
-__device__ bool phase_a(const M2Params& p, S2& S, const char* ring, float* xs, int l, int k,
-                        int rank, int pos, int nchunks, int& g, unsigned& cphase) {
+// Phase A step 2-3: wait for the kv head's 512 q/k/v values pushed by the 8
+// CTAs of the cluster; q/k RMSNorm + RoPE (generate.cpp:52-64), v as is; the
+// rank-0 CTA appends k, v to the cache.
+__device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, int rank, int pos, unsigned ep1,
+                                        long long* prof) {
+    VB_SHARED(&S);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const M2Layer& L = p.layers[l];
-    // 1. this CTA's 64 rows of the kv-head block of Wqkv
     {
-        const Plan pl = plan_qkv(p, l, Q8, k, rank);
-        const float* sc = Q8 ? L.sqkv + k * 512 : nullptr;
-        bool ok = gemv_rows(p, pl, g, ring, S, xs, sc, Q8, 0, EpiQkvPart{S.qkv_part, 64 * rank});
-        g += pl.nstages;
+        const long long c0 = clock64();
+        const unsigned tag = xtag(ep1, l, kXQkv);
+        bool ok = true;
+        for (int i = t; i < 512 && ok; i += kCT) ok = wait_own(p, &S.qkv64[i], tag, 7, S.qkv[i]);
         if (!consumers_sync_and<kCT>(ok)) return false;
-        tmark(p, l, 1);
-    }
-    // 2. gather the kv head's q/k/v from the 8 CTAs of the cluster
-    if (!cluster_sync(p, S, cphase)) return false;
-    {
-        const unsigned la = smem_addr(&S.qkv_part[0]);
-        for (int i = t; i < 512; i += kCT) S.qkv[i] = ld_dsmem(mapa(la + 4 * (i & 63), i >> 6));
-    }
-    consumers_sync<kCT>();
-    tmark(p, l, 2);
-    // 3. q/k RMSNorm + RoPE (generate.cpp:52-64), v as is
-    {
-        const int hs = t >> 7, d = t & 127;
-        const float qv = S.qkv[hs * 128 + d];
-        const float kv = t < 128 ? S.qkv[256 + d] : 0.f;
-        const double sq = warp_sum_d((double)qv * qv), sk = warp_sum_d((double)kv * kv);
-        if (lane == 0) {
-            S.red[warp] = sq;
-            S.red[8 + warp] = sk;
-        }
-        consumers_sync<kCT>();
-        const double tq = S.red[hs * 4] + S.red[hs * 4 + 1] + S.red[hs * 4 + 2] + S.red[hs * 4 + 3];
-        S.tq[hs][d] = __fmul_rn(__fmul_rn(qv, rms_scale(tq, 128, p.eps)), L.q_norm[d]);
-        if (t < 128) {
-            const double tk = S.red[8] + S.red[9] + S.red[10] + S.red[11];
-            S.tk[d] = __fmul_rn(__fmul_rn(kv, rms_scale(tk, 128, p.eps)), L.k_norm[d]);
-            S.vn[d] = S.qkv[384 + d];
-        }
-        consumers_sync<kCT>();
-        const float* cr = p.rope_cos + (size_t)pos * 128;
-        const float* sr = p.rope_sin + (size_t)pos * 128;
-        S.q[hs][d] = rope1(S.tq[hs], d, cr, sr);
-        if (t < 128) S.kn[d] = rope1(S.tk, d, cr, sr);
-        consumers_sync<kCT>();
-        if (rank == 0 && t < 128) {
-            const size_t off = ((size_t)(l * p.kvh + k) * p.max_seq + pos) * 128 + t;
-            p.kc[off] = S.kn[t];
-            p.vc[off] = S.vn[t];
-        }
-    }
-    // 4. attention over this CTA's chunks, online softmax across chunks
-    {
-        const int hs = t >> 7, d = t & 127;
-        float M = -INFINITY, Lsum = 0.f, acc = 0.f;
-        const int n = pos + 1;
-        const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-        for (int c = rank; c < nchunks; c += kCS) {
-            const int ks = g, vs = g + 1;
-            g += 2;
-            if (t == 0) {
-                S.wflag = mbar_wait(smem_addr(&S.full[ks % kStages]), (unsigned)(ks / kStages) & 1u,
-                                    p.err, p.dbg, kSiteAttFull, ks) &&
-                          mbar_wait(smem_addr(&S.full[vs % kStages]), (unsigned)(vs / kStages) & 1u,
-                                    p.err, p.dbg, kSiteAttFull, vs);
-                if (S.wflag) {
-                    S.seq[ks % kStages] = ks;
-                    S.seq[vs % kStages] = vs;
-                }
-            }
-            consumers_sync<kCT>();
-            if (!S.wflag) return false;
-            for (int i = 0; i < 1024 && !mbar_try(smem_addr(&S.full[ks % kStages]), (unsigned)(ks / kStages) & 1u); i++) {
-            }
-            for (int i = 0; i < 1024 && !mbar_try(smem_addr(&S.full[vs % kStages]), (unsigned)(vs / kStages) & 1u); i++) {
-            }
-            const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(ks % kStages) * kStageBytes);
-            const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(vs % kStages) * kStageBytes);
-            const int p0 = c * kChunk;
-            {
-                const float4 q0 = *reinterpret_cast<const float4*>(&S.q[0][4 * lane]);
-                const float4 q1 = *reinterpret_cast<const float4*>(&S.q[1][4 * lane]);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int pl = 4 * warp + u, pa = p0 + pl;
-                    const float4 k4 = (pa == pos) ? *reinterpret_cast<const float4*>(&S.kn[4 * lane])
-                                                  : *reinterpret_cast<const float4*>(Kt + pl * 128 + 4 * lane);
-                    float d0 = q0.x * k4.x, d1 = q1.x * k4.x;
-                    d0 = fmaf(q0.y, k4.y, d0); d0 = fmaf(q0.z, k4.z, d0); d0 = fmaf(q0.w, k4.w, d0);
-                    d1 = fmaf(q1.y, k4.y, d1); d1 = fmaf(q1.z, k4.z, d1); d1 = fmaf(q1.w, k4.w, d1);
-                    d0 = warp_sum(d0) * inv_sqrt_d;
-                    d1 = warp_sum(d1) * inv_sqrt_d;
-                    if (lane == 0) {
-                        S.sc[0][pl] = pa < n ? d0 : -INFINITY;
-                        S.sc[1][pl] = pa < n ? d1 : -INFINITY;
-                    }
-                }
-            }
-            consumers_sync<kCT>();
-            if (warp < 2) {
-                const float s = S.sc[warp][lane];
-                const float m = warp_max(s);
-                const float e = (s == -INFINITY) ? 0.f : expf(s - m);
-                const float lsum = warp_sum(e);
-                S.e[warp][lane] = e;
-                if (lane == 0) {
-                    S.cm[warp] = m;
-                    S.cl[warp] = lsum;
-                }
-            }
-            consumers_sync<kCT>();
-            float ac = 0.f;
-            const int nv = min(kChunk, n - p0);
-            for (int pl = 0; pl < nv; pl++) {
-                const float v = (p0 + pl == pos) ? S.vn[d] : Vt[pl * 128 + d];
-                ac = fmaf(S.e[hs][pl], v, ac);
-            }
-            const float mc = S.cm[hs], lc = S.cl[hs];
-            const float Mn = fmaxf(M, mc);
-            const float fo = (M == -INFINITY) ? 0.f : expf(M - Mn);
-            const float fc = expf(mc - Mn);
-            acc = acc * fo + ac * fc;
-            Lsum = Lsum * fo + lc * fc;
-            M = Mn;
-            consumers_sync<kCT>();
-            if (t == 0) {
-                mbar_arrive(smem_addr(&S.empty[ks % kStages]), kCW);
-                mbar_arrive(smem_addr(&S.empty[vs % kStages]), kCW);
-            }
-        }
-        S.att_acc[hs][d] = acc;
-        if (d == 0) {
-            S.att_m[hs] = M;
-            S.att_l[hs] = Lsum;
-        }
+        if (prof) prof[8] += clock64() - c0;
     }
     tmark(p, l, 3);
-    // 5. merge the 8 CTA partials of the cluster -> ctx of heads 2k, 2k+1
-    if (!cluster_sync(p, S, cphase)) return false;
-    {
-        const int hs = t >> 7, d = t & 127;
-        const unsigned am = smem_addr(&S.att_m[hs]), al = smem_addr(&S.att_l[hs]);
-        const unsigned aa = smem_addr(&S.att_acc[hs][d]);
-        float mr[kCS];
-        float M = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < kCS; r++) {
-            mr[r] = ld_dsmem(mapa(am, r));
-            M = fmaxf(M, mr[r]);
-        }
-        float Lsum = 0.f, A = 0.f;
-#pragma unroll
-        for (int r = 0; r < kCS; r++) {
-            if (mr[r] == -INFINITY) continue;
-            const float f = expf(mr[r] - M);
-            Lsum = fmaf(ld_dsmem(mapa(al, r)), f, Lsum);
-            A = fmaf(ld_dsmem(mapa(aa, r)), f, A);
-        }
-        const float cval = (Lsum > 0.f) ? A / Lsum : 0.f;
-        const int i = hs * 128 + d;
-        xs[Q8 ? perm_index(i) : i] = cval;
+    const int hs = t >> 7, d = t & 127;
+    const float qv = S.qkv[hs * 128 + d];
+    const float kv = t < 128 ? S.qkv[256 + d] : 0.f;
+    const double sq = warp_sum_d((double)qv * qv), sk = warp_sum_d((double)kv * kv);
+    if (lane == 0) {
+        S.red[warp] = sq;
+        S.red[8 + warp] = sk;
     }
     consumers_sync<kCT>();
-    tmark(p, l, 4);
-    // 6. split-K o_proj: rows [128r, 128r+128) of Wo[:, 256k:256k+256]
-    {
-        const Plan pl = plan_o(p, l, Q8, k, rank);
-        bool ok = gemv_rows(p, pl, g, ring, S, xs, L.so, true, 0,
-                            EpiStore{p.part_o + (size_t)k * p.hidden});
-        g += pl.nstages;
-        tmark(p, l, 5);
-        return ok;
+    const double tq = S.red[hs * 4] + S.red[hs * 4 + 1] + S.red[hs * 4 + 2] + S.red[hs * 4 + 3];
+    S.tq[hs][d] = __fmul_rn(__fmul_rn(qv, rms_scale(tq, 128, p.eps)), L.q_norm[d]);
+    if (t < 128) {
+        const double tk = S.red[8] + S.red[9] + S.red[10] + S.red[11];
+        S.tk[d] = __fmul_rn(__fmul_rn(kv, rms_scale(tk, 128, p.eps)), L.k_norm[d]);
+        S.vn[d] = S.qkv[384 + d];
+    }
+    consumers_sync<kCT>();
+    const float* cr = p.rope_cos + (size_t)pos * 128;
+    const float* sr = p.rope_sin + (size_t)pos * 128;
+    S.q[hs][d] = rope1(S.tq[hs], d, cr, sr);
+    if (t < 128) S.kn[d] = rope1(S.tk, d, cr, sr);
+    consumers_sync<kCT>();
+    if (rank == 0 && t < 128) {
+        const size_t off = ((size_t)(l * p.kvh + k) * p.max_seq + pos) * 128 + t;
+        p.kc[off] = S.kn[t];
+        p.vc[off] = S.vn[t];
+    }
+    return true;
+}
+
+// Phase A step 4: attention over this CTA's 32-position chunks c = rank,
+// rank + 8, ...; local chunk j goes to warp j % 8, which keeps an online
+// softmax over its chunks (lane p scores position p with a column skew that
+// keeps the K reads free of bank conflicts; for PV lane l owns dims 4l..4l+3).
+// The warps' partials are then merged (warp order) into S.att_*.
+__device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* ring, int l, int rank, int pos,
+                                       int nchunks, int g, long long* prof) {
+    VB_SHARED(&S);
+    VB_SHARED(ring);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int n = pos + 1;
+    const int njl = rank < nchunks ? (nchunks - rank + kCS - 1) / kCS : 0;
+    const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    bool ok = true;
+    for (int j = warp; j < njl && ok; j += kCW) {
+        const int c = rank + kCS * j;
+        const int gk = g + 2 * j, gv = gk + 1;
+        const long long tw = clock64();
+        ok = stage_wait(p, S, gk, false) && stage_wait(p, S, gv, false);
+        if (!ok) break;
+        if (prof) {
+            prof[11] += clock64() - tw;
+            prof[12] += 1;
+        }
+        const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(gk % kStages) * kStageBytes);
+        const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(gv % kStages) * kStageBytes);
+        const int p0 = c * kChunk;
+        const bool valid = p0 + lane < n;
+        const float* krow = (p0 + lane == pos) ? S.kn : Kt + lane * 128;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < 32; i++) {
+            const int c4 = 4 * ((i + lane) & 31);
+            const float4 k4 = *reinterpret_cast<const float4*>(krow + c4);
+            const float4 qa = *reinterpret_cast<const float4*>(&S.q[0][c4]);
+            const float4 qb = *reinterpret_cast<const float4*>(&S.q[1][c4]);
+            s0 = fmaf(qa.x, k4.x, s0); s0 = fmaf(qa.y, k4.y, s0); s0 = fmaf(qa.z, k4.z, s0); s0 = fmaf(qa.w, k4.w, s0);
+            s1 = fmaf(qb.x, k4.x, s1); s1 = fmaf(qb.y, k4.y, s1); s1 = fmaf(qb.z, k4.z, s1); s1 = fmaf(qb.w, k4.w, s1);
+        }
+        const float sc0 = valid ? s0 * inv_sqrt_d : -INFINITY;
+        const float sc1 = valid ? s1 * inv_sqrt_d : -INFINITY;
+        const float mn0 = fmaxf(m0, warp_max(sc0)), mn1 = fmaxf(m1, warp_max(sc1));
+        const float f0 = (m0 == -INFINITY) ? 0.f : expf(m0 - mn0);
+        const float f1 = (m1 == -INFINITY) ? 0.f : expf(m1 - mn1);
+        const float e0 = valid ? expf(sc0 - mn0) : 0.f;
+        const float e1 = valid ? expf(sc1 - mn1) : 0.f;
+        l0 = l0 * f0 + warp_sum(e0);
+        l1 = l1 * f1 + warp_sum(e1);
+        a0.x *= f0; a0.y *= f0; a0.z *= f0; a0.w *= f0;
+        a1.x *= f1; a1.y *= f1; a1.z *= f1; a1.w *= f1;
+        m0 = mn0;
+        m1 = mn1;
+        const int nv = min(kChunk, n - p0);
+#pragma unroll 4
+        for (int pp = 0; pp < kChunk; pp++) {
+            const float* vrow = (p0 + pp == pos) ? S.vn : Vt + pp * 128;
+            float4 v4 = *reinterpret_cast<const float4*>(vrow + 4 * lane);
+            if (pp >= nv) v4 = make_float4(0.f, 0.f, 0.f, 0.f);  // stale rows past the context
+            const float w0 = __shfl_sync(0xffffffffu, e0, pp), w1 = __shfl_sync(0xffffffffu, e1, pp);
+            a0.x = fmaf(w0, v4.x, a0.x); a0.y = fmaf(w0, v4.y, a0.y);
+            a0.z = fmaf(w0, v4.z, a0.z); a0.w = fmaf(w0, v4.w, a0.w);
+            a1.x = fmaf(w1, v4.x, a1.x); a1.y = fmaf(w1, v4.y, a1.y);
+            a1.z = fmaf(w1, v4.z, a1.z); a1.w = fmaf(w1, v4.w, a1.w);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(smem_addr(&S.empty[gk % kStages]), (unsigned)kCW);
+            mbar_arrive(smem_addr(&S.empty[gv % kStages]), (unsigned)kCW);
+        }
+    }
+    *reinterpret_cast<float4*>(&S.wacc[warp][0][4 * lane]) = a0;
+    *reinterpret_cast<float4*>(&S.wacc[warp][1][4 * lane]) = a1;
+    if (lane == 0) {
+        S.wm[warp][0] = m0;
+        S.wm[warp][1] = m1;
+        S.wl[warp][0] = l0;
+        S.wl[warp][1] = l1;
+    }
+    if (!consumers_sync_and<kCT>(ok)) return false;
+    const int hs = t >> 7, d = t & 127;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCW; w++) M = fmaxf(M, S.wm[w][hs]);
+    float Lsum = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCW; w++) {
+        const float mw = S.wm[w][hs];
+        if (mw == -INFINITY) continue;
+        const float f = expf(mw - M);
+        Lsum = fmaf(S.wl[w][hs], f, Lsum);
+        A = fmaf(S.wacc[w][hs][d], f, A);
+    }
+    S.att_acc[hs][d] = A;
+    if (d == 0) {
+        S.att_m[hs] = M;
+        S.att_l[hs] = Lsum;
+    }
+    return true;
+}
+
+// Phase A step 5: push this CTA's attention partial to the 8 CTAs of the
+// cluster, then merge the 8 partials (rank order) -> ctx of heads 2k, 2k+1
+// into xs (lane-interleaved layout for INT8).
+__device__ __noinline__ bool merge_ctx(const M2Params& p, S2& S, float* xs, int l, int rank, unsigned ep1,
+                                       bool perm, long long* prof) {
+    VB_SHARED(&S);
+    VB_SHARED(xs);
+    const int t = threadIdx.x;
+    const long long c0 = clock64();
+    const unsigned tag = xtag(ep1, l, kXAtt);
+    const int hs = t >> 7, d = t & 127;
+    const unsigned base = smem_addr(&S.xu.att64[rank][0]);
+    // each thread pushes what it wrote itself at the end of the attention
+    const unsigned long long wa = xpack(S.att_acc[hs][d], tag);
+#pragma unroll 1
+    for (unsigned q = 0; q < kCS; q++) st_peer(mapa(base + 8u * (unsigned)(hs * 128 + d), q), wa);
+    if (d == 0) {
+        const unsigned long long wm = xpack(S.att_m[hs], tag), wl = xpack(S.att_l[hs], tag);
+#pragma unroll 1
+        for (unsigned q = 0; q < kCS; q++) {
+            st_peer(mapa(base + 8u * (unsigned)(256 + hs), q), wm);
+            st_peer(mapa(base + 8u * (unsigned)(258 + hs), q), wl);
+        }
+    }
+    bool ok = true;
+    float M = -INFINITY;
+#pragma unroll 1
+    for (int r = 0; r < kCS && ok; r++) {
+        float mr = 0.f;
+        ok = wait_own(p, &S.xu.att64[r][256 + hs], tag, 8, mr);
+        M = fmaxf(M, mr);
+    }
+    float Lsum = 0.f, A = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < kCS && ok; r++) {
+        float mr = 0.f, lr = 0.f, ar = 0.f;
+        ok = wait_own(p, &S.xu.att64[r][256 + hs], tag, 8, mr) && wait_own(p, &S.xu.att64[r][258 + hs], tag, 8, lr) &&
+             wait_own(p, &S.xu.att64[r][hs * 128 + d], tag, 8, ar);
+        if (mr == -INFINITY) continue;
+        const float f = expf(mr - M);
+        Lsum = fmaf(lr, f, Lsum);
+        A = fmaf(ar, f, A);
+    }
+    if (!consumers_sync_and<kCT>(ok)) return false;
+    if (prof) prof[9] += clock64() - c0;
+    const float cval = (Lsum > 0.f) ? A / Lsum : 0.f;
+    const int i = hs * 128 + d;
+    xs[perm ? perm_index(i) : i] = cval;
+    consumers_sync<kCT>();
+    return true;
+}
+
+// Phase B split-K down: thread t owns outputs j = 4t..4t+3 of
+// sum_{i in slice} h_i * WdT[i][j]; the 4 values are pushed to the CTA of the
+// cluster that reduces them (rank 4t / 128).
+template <bool Q8>
+__device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* ring, const Plan pl, int g, int l,
+                                       int rank, unsigned ep1, long long* prof) {
+    VB_SHARED(&S);
+    VB_SHARED(ring);
+    const int t = threadIdx.x;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const long long d0 = clock64();
+    long long dw = 0;
+    for (int j = 0; j < pl.nstages; j++) {
+        const int gs = g + j;
+        const long long tw = clock64();
+        if (!stage_wait(p, S, gs, true)) return false;
+        dw += clock64() - tw;
+        const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
+        const int rA = pl.r0 + j * pl.rps;
+        const int nr = min(pl.rps, pl.r1 - rA);
+#pragma unroll 4
+        for (int rr = 0; rr < nr; rr++) {
+            const float hv = S.h[rA + rr - pl.r0];
+            if constexpr (Q8) {
+                const uint32_t wv = *reinterpret_cast<const uint32_t*>(st + (size_t)rr * pl.row_bytes + 4 * t);
+                const f4 f = i8x4_to_f32(wv);
+                acc.x = fmaf(hv, f.v[0], acc.x); acc.y = fmaf(hv, f.v[1], acc.y);
+                acc.z = fmaf(hv, f.v[2], acc.z); acc.w = fmaf(hv, f.v[3], acc.w);
+            } else {
+                const float4 w4 = *reinterpret_cast<const float4*>(st + (size_t)rr * pl.row_bytes + 16 * t);
+                acc.x = fmaf(hv, w4.x, acc.x); acc.y = fmaf(hv, w4.y, acc.y);
+                acc.z = fmaf(hv, w4.z, acc.z); acc.w = fmaf(hv, w4.w, acc.w);
+            }
+        }
+        stage_release(S, gs, 1u);
+    }
+    if (prof) {
+        prof[6] += dw;
+        prof[7] += clock64() - d0;
+    }
+    const unsigned tag = xtag(ep1, l, kXRed);
+    const int per = p.hidden / kCS;
+    const int q = (4 * t) / per, o = 4 * t - q * per;
+    const unsigned dst = mapa(smem_addr(&S.xu.red64[rank][o]), (unsigned)q);
+    st_peer(dst, xpack(acc.x, tag));
+    st_peer(dst + 8u, xpack(acc.y, tag));
+    st_peer(dst + 16u, xpack(acc.z, tag));
+    st_peer(dst + 24u, xpack(acc.w, tag));
+    return true;
+}
+
+// Phase B reduce: outputs [128 rank, +128) summed over the cluster's 8 CTAs
+// in rank order (x the INT8 row scale) -> tagged down partial of the cluster.
+__device__ __noinline__ bool reduce_store(const M2Params& p, S2& S, int l, int cid, int rank, unsigned ep1,
+                                          bool q8, long long* prof) {
+    VB_SHARED(&S);
+    const long long c0 = clock64();
+    const unsigned tag = xtag(ep1, l, kXRed);
+    const int t = threadIdx.x;
+    const int per = p.hidden / kCS;
+    bool ok = true;
+    if (t < per) {
+        float v = 0.f;
+#pragma unroll 1
+        for (int q = 0; q < kCS && ok; q++) {
+            float pv = 0.f;
+            ok = wait_own(p, &S.xu.red64[q][t], tag, 9, pv);
+            v += pv;
+        }
+        if (q8) v *= S.sc_d[t];
+        if (ok)
+            st_gpu(p.xd + ((size_t)(l & 1) * p.nclusters + cid) * p.hidden + rank * per + t,
+                   xpack(v, xtag(ep1, l, kXGlobal)));
+    }
+    if (!consumers_sync_and<kCT>(ok)) return false;
+    if (prof) prof[10] += clock64() - c0;
+    return true;
+}
+
+// ------------------------------------------------------------ stage walk
+// Every stage this CTA consumes in one token, in consumption order; f(src,
+// bytes) per stage, stopping early when f returns false.
+template <class F>
+__device__ bool plan_stages(const Plan& pl, F& f) {
+    for (int j = 0; j < pl.nstages; j++) {
+        const int rows = min(pl.rps, pl.r1 - pl.r0 - j * pl.rps);
+        if (!f(pl.w + (size_t)j * pl.rps * pl.row_bytes, (unsigned)(rows * pl.row_bytes))) return false;
+    }
+    return true;
+}
+template <bool Q8, class F>
+__device__ void walk_stages(const M2Params& p, int b, int G, int cid, int rank, int nchunks, F& f) {
+    const bool owns_kv = cid < p.kvh;
+    for (int l = 0; l < p.nlayers; l++) {
+        if (owns_kv) {
+            if (!plan_stages(plan_qkv(p, l, Q8, cid, rank), f)) return;
+            for (int c = rank; c < nchunks; c += kCS) {
+                const int rows = min(kChunk, p.max_seq - c * kChunk);
+                const size_t off = ((size_t)(l * p.kvh + cid) * p.max_seq + (size_t)c * kChunk) * 128;
+                if (!f(p.kc + off, (unsigned)(rows * 512))) return;
+                if (!f(p.vc + off, (unsigned)(rows * 512))) return;
+            }
+            if (!plan_stages(plan_o(p, l, Q8, cid, rank), f)) return;
+        }
+        if (!plan_stages(plan_gu(p, l, Q8, b, G), f)) return;
+        if (!plan_stages(plan_dt(p, l, Q8, b, G), f)) return;
+    }
+    plan_stages(plan_lm(p, b, G), f);
+}
+
+// Ring producer: waits for the slot to be free, then one bulk copy into it.
+struct RingIssue {
+    const M2Params* p;
+    S2* S;
+    char* ring;
+    unsigned long long pol;
+    int g;
+    bool ok;
+    __device__ bool operator()(const void* src, unsigned bytes) {
+        const int slot = g % kStages;
+        if (!mbar_wait(smem_addr(&S->empty[slot]), ((unsigned)(g / kStages) & 1u) ^ 1u, p->err, p->dbg,
+                       kSiteEmpty, g)) {
+            ok = false;
+            return false;
+        }
+        mbar_expect_tx(smem_addr(&S->full[slot]), bytes);
+        bulk_g2s(smem_addr(ring + (size_t)slot * kStageBytes), src, bytes, smem_addr(&S->full[slot]), pol);
+        g++;
+        return true;
+    }
+};
+
+// INT8 row scales of the next phase, loaded into registers before the wait
+// for that phase's inputs (so their latency hides behind it) and stored to
+// shared memory after it.
+struct PreScales {
+    float a, b;
+};
+__device__ __forceinline__ PreScales pre_scales_a(const M2Params& p, int l, int k, int rank) {
+    const M2Layer& L = p.layers[l];
+    const int t = threadIdx.x;
+    PreScales v{0.f, 0.f};
+    if (t < 64) v.a = __ldg(L.sqkv + k * 512 + 64 * rank + t);
+    if (t < 128) v.b = __ldg(L.so + 128 * rank + t);
+    return v;
+}
+__device__ __forceinline__ void put_scales_a(S2& S, const PreScales& v) {
+    const int t = threadIdx.x;
+    if (t < 64) S.sc_qkv[t] = v.a;
+    if (t < 128) S.sc_o[t] = v.b;
+}
+__device__ __forceinline__ PreScales pre_scales_b(const M2Params& p, int l, int b, int G, int rank) {
+    const M2Layer& L = p.layers[l];
+    const int t = threadIdx.x;
+    int r0, r1;
+    split(p.ffn, b, G, 2, r0, r1);
+    PreScales v{0.f, 0.f};
+    if (t < r1 - r0) v.a = __ldg(L.sgu + r0 + t);
+    if (t < 128) v.b = __ldg(L.sd + 128 * rank + t);
+    return v;
+}
+__device__ __forceinline__ void put_scales_b(S2& S, const PreScales& v) {
+    const int t = threadIdx.x;
+    if (t < 128) {
+        S.sc_gu[t] = v.a;
+        S.sc_d[t] = v.b;
     }
 }
 
@@ -659,6 +1052,10 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     if (p.trace)
         for (int i = threadIdx.x; i < kTraceStride2; i += kThreads)
             p.trace[(size_t)blockIdx.x * kTraceStride2 + i] = 0ull;
+    // exchange words start with tag 0, which no launch uses; the cluster
+    // barrier below orders this before any peer's push
+    for (int i = threadIdx.x; i < 512; i += kThreads) S.qkv64[i] = 0ull;
+    for (int i = threadIdx.x; i < kCS * kAttWords; i += kThreads) (&S.xu.att64[0][0])[i] = 0ull;
     if (threadIdx.x == 0) {
         if (p.trace) p.trace[(size_t)blockIdx.x * kTraceStride2] = now_ns();
         for (int s = 0; s < kStages; s++) {
@@ -666,10 +1063,10 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             mbar_init(smem_addr(&S.empty[s]), kCW);
             S.seq[s] = s - kStages;
         }
-        mbar_init(smem_addr(&S.cbar), kCS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // every CTA of the cluster has initialised its barriers before any remote arrive
+    // every CTA of the cluster has initialised its barriers and exchange
+    // words before any remote access
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 
@@ -686,43 +1083,10 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             asm volatile("barrier.cluster.arrive.release;" ::: "memory");
             return;
         }
-        unsigned long long pol;
-        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-        int g = 0;
-        bool ok = true;
-        auto issue = [&](const void* src, unsigned bytes) {
-            const int slot = g % kStages;
-            if (!mbar_wait(smem_addr(&S.empty[slot]), ((unsigned)(g / kStages) & 1u) ^ 1u, p.err,
-                           p.dbg, kSiteEmpty, g)) {
-                ok = false;
-                return;
-            }
-            mbar_expect_tx(smem_addr(&S.full[slot]), bytes);
-            bulk_g2s(smem_addr(ring + (size_t)slot * kStageBytes), src, bytes,
-                     smem_addr(&S.full[slot]), pol);
-            g++;
-        };
-        auto issue_plan = [&](const Plan& pl) {
-            for (int j = 0; j < pl.nstages && ok; j++) {
-                const int rows = min(pl.rps, pl.r1 - pl.r0 - j * pl.rps);
-                issue(pl.w + (size_t)j * pl.rps * pl.row_bytes, (unsigned)(rows * pl.row_bytes));
-            }
-        };
-        for (int l = 0; l < p.nlayers && ok; l++) {
-            if (owns_kv) {
-                issue_plan(plan_qkv(p, l, Q8, cid, rank));
-                for (int c = rank; c < nchunks && ok; c += kCS) {
-                    const int rows = min(kChunk, p.max_seq - c * kChunk);
-                    const size_t off = ((size_t)(l * p.kvh + cid) * p.max_seq + (size_t)c * kChunk) * 128;
-                    issue(p.kc + off, (unsigned)(rows * 512));
-                    if (ok) issue(p.vc + off, (unsigned)(rows * 512));
-                }
-                if (ok) issue_plan(plan_o(p, l, Q8, cid, rank));
-            }
-            if (ok) issue_plan(plan_gu(p, l, Q8, b, G));
-            if (ok) issue_plan(plan_dt(p, l, Q8, b, G));
-        }
-        if (ok) issue_plan(plan_lm(p, b, G));
+        RingIssue f{&p, &S, ring, 0ull, 0, true};
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(f.pol));
+        walk_stages<Q8>(p, b, G, cid, rank, nchunks, f);
+        const int g = f.g;
         const int first = g > kStages ? g - kStages : 0;
         for (int gs = first; gs < g; gs++) {
             const unsigned a = smem_addr(&S.full[gs % kStages]);
@@ -739,114 +1103,122 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     {
     const int tok = *p.tok;
     const float* emb_row = p.embed + (size_t)tok * p.hidden;
+    const unsigned ep1 = (unsigned)*p.epoch + 1u;
     int g = 0;
-    unsigned nbar = 0, cphase = 0;
     bool ok = true;
-    float nw[kPer];
-    load_norm(p.layers[0].in_norm, p.hidden, nw);
+    float4 nw = load_norm(p.layers[0].in_norm);
+    PreScales psc{0.f, 0.f};
+    if (Q8 && owns_kv) psc = pre_scales_a(p, 0, cid, rank);
     for (int l = 0; l < p.nlayers && ok; l++) {
         const M2Layer& L = p.layers[l];
-        // ---- phase A
-        bool r = true;
+        long long* prof = prof_ptr(p, l);
+        if (prof) {
+            prof[14] = clock64();
+            prof[15] = (long long)now_ns();
+        }
+        const unsigned long long* xd_prev = p.xd + (size_t)((l + 1) & 1) * p.nclusters * p.hidden;
+        const unsigned tag_prev = l > 0 ? xtag(ep1, l - 1, kXGlobal) : 0u;
+        // ---- phase A (kv clusters): qkv rows -> gather -> attention -> merge -> o_proj
         if (owns_kv) {
-            residual_norm(p, S, xs, p.part_d, p.nclusters, l == 0 ? emb_row : nullptr, nw, Q8);
-            tmark(p, l, 0);
-            r = phase_a<Q8>(p, S, ring, xs, l, cid, rank, pos, nchunks, g, cphase);
-        }
-        load_norm(L.post_norm, p.hidden, nw);
-        ok = grid_barrier2(p, (++nbar) * G, S, r);
-        tmark(p, l, 6);
-        if (!ok) break;
-        // ---- phase B
-        if (!owns_kv && l == 0) {
-            // CTAs outside the kv clusters start their residual copy here
-            for (int i = threadIdx.x; i < p.hidden; i += kCT) S.xr[i] = emb_row[i];
-            consumers_sync<kCT>();
-        } else if (!owns_kv) {
-            // catch up with the previous layer's D partials
-            for (int i = threadIdx.x; i < p.hidden; i += kCT) {
-                float add = 0.f;
-                for (int c = 0; c < p.nclusters; c++) add += __ldcg(p.part_d + (size_t)c * p.hidden + i);
-                S.xr[i] += add;
+            if (!residual_norm(p, S, xs, xd_prev, p.nclusters, tag_prev, l == 0 ? emb_row : nullptr, nw, Q8, l, 0)) {
+                ok = false;
+                break;
             }
+            if (Q8) {
+                put_scales_a(S, psc);
+                consumers_sync<kCT>();
+            }
+            tmark(p, l, 1);
+            {
+                const Plan pl = plan_qkv(p, l, Q8, cid, rank);
+                const Epi epi{kEpiQkvPush, smem_addr(&S.qkv64[0]), xtag(ep1, l, kXQkv), nullptr, nullptr, 0, nullptr};
+                bool r;
+                if constexpr (Q8) r = gemv_rows<true, 2, kHid>(p, pl, g, ring, S, xs, S.sc_qkv, true, false, epi, prof,
+                                                             prof ? prof + 16 : nullptr);
+                else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, false, epi, prof,
+                                                   prof ? prof + 16 : nullptr);
+                g += pl.nstages;
+                if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
+                tmark(p, l, 2);
+            }
+            if (!qkv_finish(p, S, l, cid, rank, pos, ep1, prof)) { ok = false; break; }
+            {
+                const long long t_att = clock64();
+                const bool r = attention(p, S, ring, l, rank, pos, nchunks, g, prof);
+                g += 2 * (rank < nchunks ? (nchunks - rank + kCS - 1) / kCS : 0);
+                if (!r) { ok = false; break; }
+                tmark(p, l, 4);
+                if (prof) prof[13] += clock64() - t_att;
+            }
+            if (!merge_ctx(p, S, xs, l, rank, ep1, Q8, prof)) { ok = false; break; }
+            tmark(p, l, 5);
+            {
+                const Plan pl = plan_o(p, l, Q8, cid, rank);
+                const Epi epi{kEpiStoreTagged, 0u, xtag(ep1, l, kXGlobal),
+                              p.xo + ((size_t)(l & 1) * p.kvh + cid) * p.hidden, nullptr, 0, nullptr};
+                bool r;
+                if constexpr (Q8) r = gemv_rows<true, 8, 256>(p, pl, g, ring, S, xs, S.sc_o, true, false, epi,
+                                                             prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
+                else r = gemv_rows<false, 2, 256>(p, pl, g, ring, S, xs, nullptr, true, false, epi,
+                                                  prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
+                g += pl.nstages;
+                if (!r) { ok = false; break; }
+                tmark(p, l, 6);
+            }
+        } else {
+            // CTAs outside the kv clusters bring their x up to date here, so
+            // that every read of the previous layer's down partials happens
+            // before any of this layer's are produced.
+            if (!residual_only(p, S, xd_prev, p.nclusters, tag_prev, l == 0 ? emb_row : nullptr)) {
+                ok = false;
+                break;
+            }
+        }
+        nw = load_norm(L.post_norm);
+        if (Q8) psc = pre_scales_b(p, l, b, G, rank);
+        // ---- phase B (all CTAs): waits for the o_proj partials of all kv heads
+        if (!residual_norm(p, S, xs, p.xo + (size_t)(l & 1) * p.kvh * p.hidden, p.kvh, xtag(ep1, l, kXGlobal),
+                           nullptr, nw, Q8, l, 7)) { ok = false; break; }
+        if (Q8) {
+            put_scales_b(S, psc);
             consumers_sync<kCT>();
         }
-        residual_norm(p, S, xs, p.part_o, p.kvh, nullptr, nw, Q8);
-        tmark(p, l, 7);
+        tmark(p, l, 8);
         {
             const Plan pl = plan_gu(p, l, Q8, b, G);
-            const int P0 = pl.r0 >> 1;
-            r = gemv_rows(p, pl, g, ring, S, xs, L.sgu, Q8 || pl.rps >= 8, 1, EpiSwiGLU{S.h, P0});
+            const Epi epi{kEpiSwiGLU, 0u, 0u, nullptr, S.h, pl.r0 >> 1, nullptr};
+            bool r;
+            if constexpr (Q8) r = gemv_rows<true, 2, kHid>(p, pl, g, ring, S, xs, S.sc_gu, true, true, epi,
+                                                         prof ? prof + 4 : nullptr, prof ? prof + 22 : nullptr);
+            else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, true, epi,
+                                               prof ? prof + 4 : nullptr, prof ? prof + 22 : nullptr);
             g += pl.nstages;
+            if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
         }
-        if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
-        tmark(p, l, 8);
-        {   // split-K down: accd[j] = sum_i h_i * WdT[i][j]; thread t owns j = 4t..4t+3
-            const Plan pl = plan_dt(p, l, Q8, b, G);
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            const int t = threadIdx.x;
-            for (int j = 0; j < pl.nstages && r; j++) {
-                const int gs = g + j;
-                if (!stage_wait(p, S, gs, true)) { r = false; break; }
-                const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
-                const int rA = pl.r0 + j * pl.rps;
-                const int nr = min(pl.rps, pl.r1 - rA);
-                for (int rr = 0; rr < nr; rr++) {
-                    const float hv = S.h[rA + rr - pl.r0];
-                    if (Q8) {
-                        const uint32_t wv = *reinterpret_cast<const uint32_t*>(st + (size_t)rr * pl.row_bytes + 4 * t);
-                        const f4 f = i8x4_to_f32(wv);
-                        acc.x = fmaf(hv, f.v[0], acc.x); acc.y = fmaf(hv, f.v[1], acc.y);
-                        acc.z = fmaf(hv, f.v[2], acc.z); acc.w = fmaf(hv, f.v[3], acc.w);
-                    } else {
-                        const float4 w4 = *reinterpret_cast<const float4*>(st + (size_t)rr * pl.row_bytes + 16 * t);
-                        acc.x = fmaf(hv, w4.x, acc.x); acc.y = fmaf(hv, w4.y, acc.y);
-                        acc.z = fmaf(hv, w4.z, acc.z); acc.w = fmaf(hv, w4.w, acc.w);
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_addr(&S.empty[gs % kStages]), 1u);
-            }
-            g += pl.nstages;
-            *reinterpret_cast<float4*>(&S.accd[4 * t]) = acc;
-        }
-        if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
         tmark(p, l, 9);
-        if (!cluster_sync(p, S, cphase)) { ok = false; break; }
-        {   // reduce the cluster's 8 partials: CTA rank reduces [128 rank, +128)
-            const int t = threadIdx.x;
-            const int per = p.hidden / kCS;
-            if (t < per) {
-                const int j = rank * per + t;
-                const unsigned a = smem_addr(&S.accd[j]);
-                float v = 0.f;
-#pragma unroll
-                for (int q = 0; q < kCS; q++) v += ld_dsmem(mapa(a, q));
-                if (Q8) v *= __ldg(L.sd + j);
-                p.part_d[(size_t)cid * p.hidden + j] = v;
-            }
+        {
+            const Plan pl = plan_dt(p, l, Q8, b, G);
+            const bool r = down_push<Q8>(p, S, ring, pl, g, l, rank, ep1, prof);
+            g += pl.nstages;
+            if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
         }
-        load_norm(l + 1 < p.nlayers ? p.layers[l + 1].in_norm : p.final_norm, p.hidden, nw);
         tmark(p, l, 10);
-        ok = grid_barrier2(p, (++nbar) * G, S, true);
+        if (!reduce_store(p, S, l, cid, rank, ep1, Q8, prof)) { ok = false; break; }
+        nw = load_norm(l + 1 < p.nlayers ? p.layers[l + 1].in_norm : p.final_norm);
+        if (Q8 && owns_kv && l + 1 < p.nlayers) psc = pre_scales_a(p, l + 1, cid, rank);
         tmark(p, l, 11);
     }
     if (!ok) goto consumer_exit;
     // ---- LM: final norm + lm_head + argmax
-    residual_norm(p, S, xs, p.part_d, p.nclusters, nullptr, nw, false);
-    float best_v = -INFINITY;
-    int best_i = INT_MAX;
+    if (!residual_norm(p, S, xs, p.xd + (size_t)((p.nlayers - 1) & 1) * p.nclusters * p.hidden, p.nclusters,
+                       xtag(ep1, p.nlayers - 1, kXGlobal), nullptr, nw, false, 0, -1))
+        goto consumer_exit;
     {
         const Plan pl = plan_lm(p, b, G);
-        const bool r = gemv_rows(p, pl, g, ring, S, xs, nullptr, false, 0,
-                                 EpiLogits{p.logits, &best_v, &best_i});
+        const Epi epi{kEpiLogits, 0u, 0u, nullptr, nullptr, 0, p.logits};
+        const bool r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, false, epi, nullptr, nullptr);
         if (!consumers_sync_and<kCT>(r)) goto consumer_exit;
     }
-    if (lane == 0) {
-        S.bv[warp] = best_v;
-        S.bi[warp] = best_i;
-    }
-    consumers_sync<kCT>();
     if (threadIdx.x == 0) {
         float bv = S.bv[0];
         int bi = S.bi[0];
@@ -870,13 +1242,13 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             *p.step = s + 1;
             *p.tok = pick;
             *p.pos = pos + 1;
-            *p.bar = 0u;
+            *p.epoch = (ep1 < (1u << 23)) ? (int)ep1 : 0;
             *p.am_ticket = 0;
         }
     }
     }
 consumer_exit:
-    // No CTA leaves while a peer of its cluster may still read its shared
+    // No CTA leaves while a peer of its cluster may still access its shared
     // memory: all consumer threads meet here on every path (the producer
     // warp arrived on its way out).
     asm volatile("barrier.cluster.arrive.release;" ::: "memory");
@@ -915,11 +1287,12 @@ struct Mega2State {
 vb_status mega2_prepare(vb_engine* e) {
     const vb_config& c = e->cfg;
     if (c.heads != 2 * c.kv_heads || c.head_dim != 128 || c.hidden != kHid || c.ffn % 512 ||
-        c.kv_heads * kCS > 148)
+        c.kv_heads * kCS > 148 || c.layers > 63)
         return fail(VB_ERR_UNSUPPORTED, "two-barrier step: needs hidden 1024, GQA 2, head_dim 128");
     if (!e->kc) return fail(VB_ERR_NO_CACHE, "call reset_cache() first");
     const bool q8 = e->quantized;
     auto kern = q8 ? mega2_kernel<true> : mega2_kernel<false>;
+    int nclusters = c.kv_heads;
     VB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     {
         cudaLaunchConfig_t cfg = {};
@@ -936,6 +1309,15 @@ vb_status mega2_prepare(vb_engine* e) {
         int nc = 0;
         VB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&nc, kern, &cfg));
         if (nc < c.kv_heads) return fail(VB_ERR_UNSUPPORTED, "two-barrier step: clusters do not fit");
+        // phase B and the lm_head run on every co-resident cluster; phase A
+        // on the first kv_heads of them
+        nclusters = nc;
+        if (const char* v = getenv("VB_STEP_CLUSTERS")) {
+            const int want = atoi(v);
+            if (want >= c.kv_heads && want <= nc) nclusters = want;
+        }
+        if ((c.ffn + nclusters * kCS - 1) / (nclusters * kCS) > 64)
+            return fail(VB_ERR_UNSUPPORTED, "two-barrier step: ffn slice too wide");
     }
     Mega2State* m = new Mega2State();
     cudaStream_t s = e->stream;
@@ -1003,7 +1385,7 @@ vb_status mega2_prepare(vb_engine* e) {
         M.q_norm = Ld.q_norm;
         M.k_norm = Ld.k_norm;
     }
-    const int G = c.kv_heads * kCS;
+    const int G = nclusters * kCS;
     m->grid = G;
     if (ce == cudaSuccess) {
         m->d_layers = static_cast<M2Layer*>(alloc(sizeof(M2Layer) * c.layers));
@@ -1011,8 +1393,10 @@ vb_status mega2_prepare(vb_engine* e) {
     }
     if (ce == cudaSuccess)
         ce = cudaMemcpyAsync(m->d_layers, hl.data(), sizeof(M2Layer) * c.layers, cudaMemcpyHostToDevice, s);
-    const size_t po = sizeof(float) * (size_t)c.kv_heads * hd;
-    const size_t pd = sizeof(float) * (size_t)c.kv_heads * hd;
+    // tagged exchange buffers (two layer parities each), argmax slots and
+    // counters: all zeroed together (tag 0 is never a live tag)
+    const size_t po = sizeof(unsigned long long) * 2 * (size_t)c.kv_heads * hd;
+    const size_t pd = sizeof(unsigned long long) * 2 * (size_t)nclusters * hd;
     const size_t am = sizeof(float) * (size_t)G * 2;
     const size_t cnt = 256 * sizeof(int);
     if (ce == cudaSuccess) {
@@ -1020,8 +1404,8 @@ vb_status mega2_prepare(vb_engine* e) {
         if (!m->ws) ce = cudaErrorMemoryAllocation;
     }
     if (ce == cudaSuccess) {
-        m->counters = m->ws + po + pd + am;
-        m->counters_bytes = cnt;
+        m->counters = m->ws;
+        m->counters_bytes = po + pd + am + cnt;
         ce = cudaMemsetAsync(m->ws, 0, po + pd + am + cnt, s);
     }
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
@@ -1039,12 +1423,12 @@ vb_status mega2_prepare(vb_engine* e) {
     P.kc = e->kc;
     P.vc = e->vc;
     P.logits = e->logits;
-    P.part_o = reinterpret_cast<float*>(m->ws);
-    P.part_d = reinterpret_cast<float*>(m->ws + po);
+    P.xo = reinterpret_cast<unsigned long long*>(m->ws);
+    P.xd = reinterpret_cast<unsigned long long*>(m->ws + po);
     P.am_val = reinterpret_cast<float*>(m->ws + po + pd);
     P.am_idx = reinterpret_cast<int*>(m->ws + po + pd + am / 2);
-    int* cn = reinterpret_cast<int*>(m->counters);
-    P.bar = reinterpret_cast<unsigned*>(cn);
+    int* cn = reinterpret_cast<int*>(m->ws + po + pd + am);
+    P.epoch = cn;
     P.am_ticket = cn + 32;
     P.dbg = cn + 128;
     P.tok = e->d_tok;
@@ -1059,7 +1443,7 @@ vb_status mega2_prepare(vb_engine* e) {
     P.ffn = c.ffn;
     P.vocab = c.vocab;
     P.max_seq = e->max_seq;
-    P.nclusters = c.kv_heads;
+    P.nclusters = nclusters;
     P.eps = c.eps;
     P.trace = nullptr;
     if (e->trace_on) {

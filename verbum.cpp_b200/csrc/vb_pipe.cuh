@@ -46,7 +46,7 @@ enum Site : int { kSiteEmpty = 1, kSiteFull = 2, kSiteAttFull = 3, kSiteGrid = 4
 
 // First failure wins: sets the error word and, if it was the first, records
 // where the kernel gave up.
-__device__ void record_fail(int* err, int* dbg, int code, int site, int index, int extra) {
+__device__ __noinline__ void record_fail(int* err, int* dbg, int code, int site, int index, int extra) {
     if (atomicCAS(err, 0, code) == 0 && dbg) {
         dbg[1] = blockIdx.x;
         dbg[2] = site;
