@@ -15,6 +15,8 @@
 #include <algorithm>
 #include <string>
 
+#include <stdlib.h>
+
 #include "vb_engine.cuh"
 
 namespace vb {
@@ -221,6 +223,23 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
                                            e->max_seq);
     VB_LAUNCH_CHECK("engine_advance_kernel");
     return VB_OK;
+}
+
+// One decode step on e->stream: the captured graph, or (VB_STEP_DIRECT=1 in
+// the environment, for profilers that cannot follow a cooperative launch
+// inside a graph) the same launches issued directly.
+static vb_status launch_step(vb_engine* e) {
+    static const bool direct = [] {
+        const char* v = getenv("VB_STEP_DIRECT");
+        return v && v[0] == '1';
+    }();
+    if (!direct) {
+        VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+        return VB_OK;
+    }
+    return (e->path == 0 && e->mega)    ? mega_enqueue_step(e, e->stream)
+           : (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream)
+                                        : enqueue_step_ops(e, e->stream);
 }
 
 static vb_status ensure_graph(vb_engine* e) {
@@ -536,7 +555,7 @@ vb_status vb_engine_step(vb_engine* e, int token, float* logits_host) {
     e->h_pinned_i[1] = 0;
     VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->h_pinned_i, sizeof(int), cudaMemcpyHostToDevice, e->stream));
     VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
-    VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    if ((st = launch_step(e))) return st;
     VB_CUDA_TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->cfg.vocab * 4,
                                 cudaMemcpyDeviceToHost, e->stream));
     VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -558,7 +577,8 @@ vb_status vb_engine_decode(vb_engine* e, int first_token, int n, int* tokens_hos
     e->h_pinned_i[1] = 0;
     VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->h_pinned_i, sizeof(int), cudaMemcpyHostToDevice, e->stream));
     VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
-    for (int i = 0; i < n; i++) VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    for (int i = 0; i < n; i++)
+        if ((st = launch_step(e))) return st;
     if (tokens_host)
         VB_CUDA_TRY(cudaMemcpyAsync(tokens_host, e->d_hist, (size_t)n * sizeof(int),
                                     cudaMemcpyDeviceToHost, e->stream));
@@ -587,7 +607,7 @@ vb_status vb_engine_prefill(vb_engine* e, const int* tokens_host, int n, float* 
     for (int i = 0; i < n; i++) {
         VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->d_prompt + i, sizeof(int),
                                     cudaMemcpyDeviceToDevice, e->stream));
-        VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+        if ((st = launch_step(e))) return st;
     }
     if (logits_host)
         VB_CUDA_TRY(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->cfg.vocab * 4,

@@ -45,6 +45,7 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -67,9 +68,9 @@ constexpr int kPer = kXs / kCT;     // 4
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kXs * sizeof(float);
 
 struct M2Layer {
-    const void* wqkv;  // [KVH][512][hidden]
+    const void* wqkv;  // [KVH][512][hidden]: kv block k rows = q head 2k, 2k+1, k head k, v head k
     const float* sqkv; // [KVH][512]
-    const void* wo;    // [KVH][hidden][256]
+    const void* wo;    // [KVH][hidden][256]: Wo columns 256k..256k+255
     const float* so;   // [hidden]
     const void* wgu;   // [2*ffn][hidden], gate/up rows interleaved
     const float* sgu;  // [2*ffn]
@@ -178,6 +179,9 @@ struct __align__(16) S2 {
 // whole per-layer code path has to stay small enough for the instruction
 // caches, since every layer runs all of it once.
 #define VB_SHARED(ptr) __builtin_assume(__isShared(ptr))
+
+// One out-of-line copy of the double-precision norm scale (three call sites).
+__device__ __noinline__ float rms_scale_ool(double sumsq, int dim, float eps) { return rms_scale(sumsq, dim, eps); }
 
 __device__ __forceinline__ unsigned cluster_rank() {
     unsigned r;
@@ -353,6 +357,48 @@ __device__ __forceinline__ int perm_index(int i) {
     return (c << 9) + (((r >> 2) & 3) << 7) + ((r >> 4) << 2) + (r & 3);
 }
 
+// Packed f32x2 arithmetic (sm_100): two lanes of f32 math per instruction,
+// each lane rounded exactly like the scalar operation.
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 f2pack(float lo, float hi) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float f2sum(f2 v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo + hi;
+}
+__device__ __forceinline__ void f2unpack(f2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2 f2fma(f2 a, f2 b, f2 c) {
+    f2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f2 f2sub(f2 a, f2 b) {
+    f2 d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2 f2mul(f2 a, f2 b) {
+    f2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// 4 int8 -> two exact f32 pairs (q0, q1), (q2, q3): each byte is placed in
+// the mantissa of 2^23 (after a bias of 128) and the offset subtracted.
+__device__ __forceinline__ void i8x4_to_f2(uint32_t w, f2& lo, f2& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const f2 bias = f2pack(8388736.0f, 8388736.0f);  // 2^23 + 128
+    lo = f2sub(f2pack(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), bias);
+    hi = f2sub(f2pack(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), bias);
+}
+
 // Stage wait shared by all consumer modes.  in_order: every warp takes every
 // stage (no slot-order gate needed); otherwise warps take stages out of order
 // and wait for the slot's previous round first.
@@ -391,48 +437,52 @@ struct Epi {
     float* logits;
 };
 
-// Dot products of up to NR rows of one stage with xs, all rows in flight at
-// once.  f32: every lane takes float4 columns lane, lane+32, ...
+// Dot products of NR rows of one stage with xs, all rows in flight at once
+// (rows past the stage's valid ones read stale shared memory; their results
+// are never used).  f32: every lane takes float4 columns lane, lane+32, ...
 template <int NR, int K>
 __device__ __forceinline__ void dot_rows_f32(const char* st, int row_bytes, int cnt, const float* xs,
                                              int lane, float (&acc)[NR]) {
     static_assert(K % 128 == 0, "f32 rows: K multiple of 128");
     const float4* x4 = reinterpret_cast<const float4*>(xs);
+    f2 a[NR], b[NR];
 #pragma unroll
-    for (int r = 0; r < NR; r++) acc[r] = 0.f;
+    for (int r = 0; r < NR; r++) a[r] = b[r] = 0ull;
 #pragma unroll 2
     for (int it = 0; it < K / 128; it++) {
         const int k = lane + 32 * it;
         const float4 x = x4[k];
+        const f2 xlo = f2pack(x.x, x.y), xhi = f2pack(x.z, x.w);
 #pragma unroll
         for (int r = 0; r < NR; r++) {
-            if (r < cnt) {
-                const float4 w = reinterpret_cast<const float4*>(st + (size_t)r * row_bytes)[k];
-                acc[r] = fmaf(w.x, x.x, acc[r]);
-                acc[r] = fmaf(w.y, x.y, acc[r]);
-                acc[r] = fmaf(w.z, x.z, acc[r]);
-                acc[r] = fmaf(w.w, x.w, acc[r]);
-            }
+            const float4 w = reinterpret_cast<const float4*>(st + (size_t)r * row_bytes)[k];
+            a[r] = f2fma(f2pack(w.x, w.y), xlo, a[r]);
+            b[r] = f2fma(f2pack(w.z, w.w), xhi, b[r]);
         }
     }
+#pragma unroll
+    for (int r = 0; r < NR; r++) acc[r] = f2sum(a[r]) + f2sum(b[r]);
 #pragma unroll
     for (int off = 16; off; off >>= 1)
 #pragma unroll
         for (int r = 0; r < NR; r++) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
 }
 
-__device__ __forceinline__ float dot16_i8(uint4 w, float4 x0, float4 x1, float4 x2, float4 x3, float a) {
-    const f4 b0 = i8x4_to_f32(w.x), b1 = i8x4_to_f32(w.y);
-    const f4 b2 = i8x4_to_f32(w.z), b3 = i8x4_to_f32(w.w);
-    a = fmaf(b0.v[0], x0.x, a); a = fmaf(b0.v[1], x0.y, a);
-    a = fmaf(b0.v[2], x0.z, a); a = fmaf(b0.v[3], x0.w, a);
-    a = fmaf(b1.v[0], x1.x, a); a = fmaf(b1.v[1], x1.y, a);
-    a = fmaf(b1.v[2], x1.z, a); a = fmaf(b1.v[3], x1.w, a);
-    a = fmaf(b2.v[0], x2.x, a); a = fmaf(b2.v[1], x2.y, a);
-    a = fmaf(b2.v[2], x2.z, a); a = fmaf(b2.v[3], x2.w, a);
-    a = fmaf(b3.v[0], x3.x, a); a = fmaf(b3.v[1], x3.y, a);
-    a = fmaf(b3.v[2], x3.z, a); a = fmaf(b3.v[3], x3.w, a);
-    return a;
+// 16 int8 of one row against 16 x values: two pair accumulators.
+__device__ __forceinline__ void dot16_i8(uint4 w, float4 x0, float4 x1, float4 x2, float4 x3, f2& a, f2& b) {
+    f2 lo, hi;
+    i8x4_to_f2(w.x, lo, hi);
+    a = f2fma(lo, f2pack(x0.x, x0.y), a);
+    b = f2fma(hi, f2pack(x0.z, x0.w), b);
+    i8x4_to_f2(w.y, lo, hi);
+    a = f2fma(lo, f2pack(x1.x, x1.y), a);
+    b = f2fma(hi, f2pack(x1.z, x1.w), b);
+    i8x4_to_f2(w.z, lo, hi);
+    a = f2fma(lo, f2pack(x2.x, x2.y), a);
+    b = f2fma(hi, f2pack(x2.z, x2.w), b);
+    i8x4_to_f2(w.w, lo, hi);
+    a = f2fma(lo, f2pack(x3.x, x3.y), a);
+    b = f2fma(hi, f2pack(x3.z, x3.w), b);
 }
 
 // INT8 rows against the lane-interleaved xs.  K % 512 == 0: the whole warp on
@@ -441,9 +491,10 @@ template <int NR, int K>
 __device__ __forceinline__ void dot_rows_i8(const char* st, int row_bytes, int cnt, const float* xs,
                                             int lane, float (&acc)[NR]) {
     static_assert(K % 512 == 0 || K == 256, "INT8 rows: K multiple of 512, or 256");
-#pragma unroll
-    for (int r = 0; r < NR; r++) acc[r] = 0.f;
     if constexpr (K >= 512) {
+        f2 a[NR], b[NR];
+#pragma unroll
+        for (int r = 0; r < NR; r++) a[r] = b[r] = 0ull;
 #pragma unroll 1
         for (int it = 0; it < K / 512; it++) {
             const int gi = lane + 32 * it;
@@ -454,10 +505,11 @@ __device__ __forceinline__ void dot_rows_i8(const char* st, int row_bytes, int c
             const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
 #pragma unroll
             for (int r = 0; r < NR; r++)
-                if (r < cnt)
-                    acc[r] = dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi),
-                                      x0, x1, x2, x3, acc[r]);
+                dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi), x0, x1, x2, x3,
+                         a[r], b[r]);
         }
+#pragma unroll
+        for (int r = 0; r < NR; r++) acc[r] = f2sum(a[r]) + f2sum(b[r]);
 #pragma unroll
         for (int off = 16; off; off >>= 1)
 #pragma unroll
@@ -473,9 +525,9 @@ __device__ __forceinline__ void dot_rows_i8(const char* st, int row_bytes, int c
 #pragma unroll
         for (int q = 0; q < (NR + 1) / 2; q++) {
             const int r = 2 * q + h;
-            ap[q] = r < cnt ? dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi),
-                                       x0, x1, x2, x3, 0.f)
-                            : 0.f;
+            f2 a = 0ull, b = 0ull;
+            dot16_i8(*reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes + 16 * gi), x0, x1, x2, x3, a, b);
+            ap[q] = f2sum(a) + f2sum(b);
         }
 #pragma unroll
         for (int off = 8; off; off >>= 1)
@@ -486,6 +538,32 @@ __device__ __forceinline__ void dot_rows_i8(const char* st, int row_bytes, int c
             acc[2 * q] = __shfl_sync(0xffffffffu, ap[q], 0);
             if (2 * q + 1 < NR) acc[2 * q + 1] = __shfl_sync(0xffffffffu, ap[q], 16);
         }
+    }
+}
+
+// The epilogue for one row (or gate/up pair), run by the lane that owns it.
+// Logits also fold the row into this lane's running best.
+__device__ __noinline__ void epi_apply(const Epi& epi, int row, float a, float bval, float& best_v, int& best_i) {
+    switch (epi.kind) {
+    case kEpiQkvPush: {
+        const unsigned long long w = xpack(a, epi.tag);
+#pragma unroll 1
+        for (unsigned q = 0; q < kCS; q++) st_peer(mapa(epi.base + 8u * (unsigned)row, q), w);
+        break;
+    }
+    case kEpiStoreTagged:
+        st_gpu(epi.dst + row, xpack(a, epi.tag));
+        break;
+    case kEpiSwiGLU:
+        epi.h[(row >> 1) - epi.p0] = silu_f(a) * bval;
+        break;
+    default:
+        epi.logits[row] = a;
+        if (better(a, row, best_v, best_i)) {
+            best_v = a;
+            best_i = row;
+        }
+        break;
     }
 }
 
@@ -500,34 +578,38 @@ __device__ __forceinline__ float pick(const float (&v)[NR], int i) {
 
 // Row-dot GEMV phase: the value of row r (absolute) goes to the epilogue,
 // scaled by scl[r - g.r0] (shared memory, INT8) when scl is set.
-// warp mode (f32 rows of 4 KB): warp w takes stages w, w+8, ... (all rows).
-// coop mode: every warp takes every stage, rows split evenly across warps.
-// pair: rows come in gate/up pairs.  Logits: the best (value, row) of this
-// warp lands in S.bv / S.bi.
+// Work items: each stage is cut into rps / NR parts of NR rows; warp w takes
+// items w, w + 8, ... (item i: stage i / parts, part i % parts), so every
+// warp has NR independent rows in flight and one interleaved reduction per
+// item.  pair: rows come in gate/up pairs.  Logits: the best (value, row) of
+// this warp lands in S.bv / S.bi.
 template <bool Q8, int NR, int K>
 __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbase, const char* ring, S2& S,
-                                       const float* xs, const float* scl, bool coop, bool pair, const Epi epi,
+                                       const float* xs, const float* scl, bool pair, const Epi epi,
                                        long long* prof, long long* prof2) {
     VB_SHARED(ring);
     VB_SHARED(&S);
     VB_SHARED(xs);
     if (scl) VB_SHARED(scl);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rpw = coop ? g.rps / kCW : g.rps;
+    const int parts = g.rps / NR;                 // 1, 2, 4 or 8
+    const unsigned share = (unsigned)(kCW / parts);  // empty-barrier arrivals per item
     float best_v = -INFINITY;
     int best_i = INT_MAX;
     long long t_wait = 0, t_dot = 0, t_epi = 0, t_first = -1;
     const long long t_start = clock64();
-    for (int j = coop ? 0 : warp; j < g.nstages; j += coop ? 1 : kCW) {
+    const int items = g.nstages * parts;
+    for (int it = warp; it < items; it += kCW) {
+        const int j = it / parts, part = it - j * parts;
         const int gs = gbase + j;
         const long long tw = clock64();
-        if (!stage_wait(p, S, gs, coop)) return false;
+        if (!stage_wait(p, S, gs, false)) return false;
         t_wait += clock64() - tw;
         const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
         const int rA = g.r0 + j * g.rps;
         const int nr = min(g.rps, g.r1 - rA);
-        const int lo = coop ? warp * rpw : 0;
-        const int cnt = max(0, min(rpw, nr - lo));
+        const int lo = part * NR;
+        const int cnt = max(0, min(NR, nr - lo));
         float acc[NR];
         const long long td = clock64();
         if constexpr (Q8) dot_rows_i8<NR, K>(st + (size_t)lo * g.row_bytes, g.row_bytes, cnt, xs, lane, acc);
@@ -535,7 +617,7 @@ __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbas
         if (prof2) asm volatile("" : "+f"(acc[0]));
         const long long te = clock64();
         t_dot += te - td;
-        stage_release(S, gs, coop ? 1u : (unsigned)kCW);
+        stage_release(S, gs, share);
         const int row0 = rA + lo;
         const int mine = pair ? 2 * lane : lane;
         if (mine + (pair ? 1 : 0) < cnt) {
@@ -545,27 +627,7 @@ __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbas
                 a *= scl[row - g.r0];
                 if (pair) bval *= scl[row + 1 - g.r0];
             }
-            switch (epi.kind) {
-            case kEpiQkvPush: {
-                const unsigned long long w = xpack(a, epi.tag);
-#pragma unroll 1
-                for (unsigned q = 0; q < kCS; q++) st_peer(mapa(epi.base + 8u * (unsigned)row, q), w);
-                break;
-            }
-            case kEpiStoreTagged:
-                st_gpu(epi.dst + row, xpack(a, epi.tag));
-                break;
-            case kEpiSwiGLU:
-                epi.h[(row >> 1) - epi.p0] = silu_f(a) * bval;
-                break;
-            default:
-                epi.logits[row] = a;
-                if (better(a, row, best_v, best_i)) {
-                    best_v = a;
-                    best_i = row;
-                }
-                break;
-            }
+            epi_apply(epi, row, a, bval, best_v, best_i);
         }
         const long long tf = clock64();
         t_epi += tf - te;
@@ -630,7 +692,7 @@ __device__ __noinline__ bool residual_norm(const M2Params& p, S2& S, float* xs, 
     double tot = 0.0;
 #pragma unroll
     for (int w = 0; w < kCW; w++) tot += S.red[w];
-    const float sc = rms_scale(tot, p.hidden, p.eps);
+    const float sc = rms_scale_ool(tot, p.hidden, p.eps);
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int i = t + k * kCT;
@@ -696,10 +758,10 @@ __device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, 
     }
     consumers_sync<kCT>();
     const double tq = S.red[hs * 4] + S.red[hs * 4 + 1] + S.red[hs * 4 + 2] + S.red[hs * 4 + 3];
-    S.tq[hs][d] = __fmul_rn(__fmul_rn(qv, rms_scale(tq, 128, p.eps)), L.q_norm[d]);
+    S.tq[hs][d] = __fmul_rn(__fmul_rn(qv, rms_scale_ool(tq, 128, p.eps)), L.q_norm[d]);
     if (t < 128) {
         const double tk = S.red[8] + S.red[9] + S.red[10] + S.red[11];
-        S.tk[d] = __fmul_rn(__fmul_rn(kv, rms_scale(tk, 128, p.eps)), L.k_norm[d]);
+        S.tk[d] = __fmul_rn(__fmul_rn(kv, rms_scale_ool(tk, 128, p.eps)), L.k_norm[d]);
         S.vn[d] = S.qkv[384 + d];
     }
     consumers_sync<kCT>();
@@ -730,7 +792,7 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
     const int njl = rank < nchunks ? (nchunks - rank + kCS - 1) / kCS : 0;
     const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    f2 a0lo = 0ull, a0hi = 0ull, a1lo = 0ull, a1hi = 0ull;  // dims 4l..4l+3 of heads 0, 1
     bool ok = true;
     for (int j = warp; j < njl && ok; j += kCW) {
         const int c = rank + kCS * j;
@@ -747,16 +809,20 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         const int p0 = c * kChunk;
         const bool valid = p0 + lane < n;
         const float* krow = (p0 + lane == pos) ? S.kn : Kt + lane * 128;
-        float s0 = 0.f, s1 = 0.f;
+        f2 s0a = 0ull, s0b = 0ull, s1a = 0ull, s1b = 0ull;
 #pragma unroll 4
         for (int i = 0; i < 32; i++) {
             const int c4 = 4 * ((i + lane) & 31);
             const float4 k4 = *reinterpret_cast<const float4*>(krow + c4);
             const float4 qa = *reinterpret_cast<const float4*>(&S.q[0][c4]);
             const float4 qb = *reinterpret_cast<const float4*>(&S.q[1][c4]);
-            s0 = fmaf(qa.x, k4.x, s0); s0 = fmaf(qa.y, k4.y, s0); s0 = fmaf(qa.z, k4.z, s0); s0 = fmaf(qa.w, k4.w, s0);
-            s1 = fmaf(qb.x, k4.x, s1); s1 = fmaf(qb.y, k4.y, s1); s1 = fmaf(qb.z, k4.z, s1); s1 = fmaf(qb.w, k4.w, s1);
+            const f2 klo = f2pack(k4.x, k4.y), khi = f2pack(k4.z, k4.w);
+            s0a = f2fma(f2pack(qa.x, qa.y), klo, s0a);
+            s0b = f2fma(f2pack(qa.z, qa.w), khi, s0b);
+            s1a = f2fma(f2pack(qb.x, qb.y), klo, s1a);
+            s1b = f2fma(f2pack(qb.z, qb.w), khi, s1b);
         }
+        const float s0 = f2sum(s0a) + f2sum(s0b), s1 = f2sum(s1a) + f2sum(s1b);
         const float sc0 = valid ? s0 * inv_sqrt_d : -INFINITY;
         const float sc1 = valid ? s1 * inv_sqrt_d : -INFINITY;
         const float mn0 = fmaxf(m0, warp_max(sc0)), mn1 = fmaxf(m1, warp_max(sc1));
@@ -766,8 +832,11 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         const float e1 = valid ? expf(sc1 - mn1) : 0.f;
         l0 = l0 * f0 + warp_sum(e0);
         l1 = l1 * f1 + warp_sum(e1);
-        a0.x *= f0; a0.y *= f0; a0.z *= f0; a0.w *= f0;
-        a1.x *= f1; a1.y *= f1; a1.z *= f1; a1.w *= f1;
+        const f2 ff0 = f2pack(f0, f0), ff1 = f2pack(f1, f1);
+        a0lo = f2mul(a0lo, ff0);
+        a0hi = f2mul(a0hi, ff0);
+        a1lo = f2mul(a1lo, ff1);
+        a1hi = f2mul(a1hi, ff1);
         m0 = mn0;
         m1 = mn1;
         const int nv = min(kChunk, n - p0);
@@ -777,10 +846,12 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
             float4 v4 = *reinterpret_cast<const float4*>(vrow + 4 * lane);
             if (pp >= nv) v4 = make_float4(0.f, 0.f, 0.f, 0.f);  // stale rows past the context
             const float w0 = __shfl_sync(0xffffffffu, e0, pp), w1 = __shfl_sync(0xffffffffu, e1, pp);
-            a0.x = fmaf(w0, v4.x, a0.x); a0.y = fmaf(w0, v4.y, a0.y);
-            a0.z = fmaf(w0, v4.z, a0.z); a0.w = fmaf(w0, v4.w, a0.w);
-            a1.x = fmaf(w1, v4.x, a1.x); a1.y = fmaf(w1, v4.y, a1.y);
-            a1.z = fmaf(w1, v4.z, a1.z); a1.w = fmaf(w1, v4.w, a1.w);
+            const f2 vlo = f2pack(v4.x, v4.y), vhi = f2pack(v4.z, v4.w);
+            const f2 ww0 = f2pack(w0, w0), ww1 = f2pack(w1, w1);
+            a0lo = f2fma(ww0, vlo, a0lo);
+            a0hi = f2fma(ww0, vhi, a0hi);
+            a1lo = f2fma(ww1, vlo, a1lo);
+            a1hi = f2fma(ww1, vhi, a1hi);
         }
         __syncwarp();
         if (lane == 0) {
@@ -788,8 +859,15 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
             mbar_arrive(smem_addr(&S.empty[gv % kStages]), (unsigned)kCW);
         }
     }
-    *reinterpret_cast<float4*>(&S.wacc[warp][0][4 * lane]) = a0;
-    *reinterpret_cast<float4*>(&S.wacc[warp][1][4 * lane]) = a1;
+    {
+        float4 a0, a1;
+        f2unpack(a0lo, a0.x, a0.y);
+        f2unpack(a0hi, a0.z, a0.w);
+        f2unpack(a1lo, a1.x, a1.y);
+        f2unpack(a1hi, a1.z, a1.w);
+        *reinterpret_cast<float4*>(&S.wacc[warp][0][4 * lane]) = a0;
+        *reinterpret_cast<float4*>(&S.wacc[warp][1][4 * lane]) = a1;
+    }
     if (lane == 0) {
         S.wm[warp][0] = m0;
         S.wm[warp][1] = m1;
@@ -802,7 +880,7 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
 #pragma unroll
     for (int w = 0; w < kCW; w++) M = fmaxf(M, S.wm[w][hs]);
     float Lsum = 0.f, A = 0.f;
-#pragma unroll
+#pragma unroll 1
     for (int w = 0; w < kCW; w++) {
         const float mw = S.wm[w][hs];
         if (mw == -INFINITY) continue;
@@ -879,7 +957,7 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
     VB_SHARED(&S);
     VB_SHARED(ring);
     const int t = threadIdx.x;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    f2 alo = 0ull, ahi = 0ull;  // outputs 4t, 4t+1 | 4t+2, 4t+3
     const long long d0 = clock64();
     long long dw = 0;
     for (int j = 0; j < pl.nstages; j++) {
@@ -893,15 +971,16 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
 #pragma unroll 4
         for (int rr = 0; rr < nr; rr++) {
             const float hv = S.h[rA + rr - pl.r0];
+            const f2 hh = f2pack(hv, hv);
             if constexpr (Q8) {
-                const uint32_t wv = *reinterpret_cast<const uint32_t*>(st + (size_t)rr * pl.row_bytes + 4 * t);
-                const f4 f = i8x4_to_f32(wv);
-                acc.x = fmaf(hv, f.v[0], acc.x); acc.y = fmaf(hv, f.v[1], acc.y);
-                acc.z = fmaf(hv, f.v[2], acc.z); acc.w = fmaf(hv, f.v[3], acc.w);
+                f2 lo, hi;
+                i8x4_to_f2(*reinterpret_cast<const uint32_t*>(st + (size_t)rr * pl.row_bytes + 4 * t), lo, hi);
+                alo = f2fma(hh, lo, alo);
+                ahi = f2fma(hh, hi, ahi);
             } else {
                 const float4 w4 = *reinterpret_cast<const float4*>(st + (size_t)rr * pl.row_bytes + 16 * t);
-                acc.x = fmaf(hv, w4.x, acc.x); acc.y = fmaf(hv, w4.y, acc.y);
-                acc.z = fmaf(hv, w4.z, acc.z); acc.w = fmaf(hv, w4.w, acc.w);
+                alo = f2fma(hh, f2pack(w4.x, w4.y), alo);
+                ahi = f2fma(hh, f2pack(w4.z, w4.w), ahi);
             }
         }
         stage_release(S, gs, 1u);
@@ -914,6 +993,9 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
     const int per = p.hidden / kCS;
     const int q = (4 * t) / per, o = 4 * t - q * per;
     const unsigned dst = mapa(smem_addr(&S.xu.red64[rank][o]), (unsigned)q);
+    float4 acc;
+    f2unpack(alo, acc.x, acc.y);
+    f2unpack(ahi, acc.z, acc.w);
     st_peer(dst, xpack(acc.x, tag));
     st_peer(dst + 8u, xpack(acc.y, tag));
     st_peer(dst + 16u, xpack(acc.z, tag));
@@ -1129,13 +1211,13 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
                 consumers_sync<kCT>();
             }
             tmark(p, l, 1);
-            {
+            {   // this CTA's 64 rows of kv block cid, each pushed to the 8 CTAs
                 const Plan pl = plan_qkv(p, l, Q8, cid, rank);
                 const Epi epi{kEpiQkvPush, smem_addr(&S.qkv64[0]), xtag(ep1, l, kXQkv), nullptr, nullptr, 0, nullptr};
                 bool r;
-                if constexpr (Q8) r = gemv_rows<true, 2, kHid>(p, pl, g, ring, S, xs, S.sc_qkv, true, false, epi, prof,
+                if constexpr (Q8) r = gemv_rows<true, 8, kHid>(p, pl, g, ring, S, xs, S.sc_qkv, false, epi, prof,
                                                              prof ? prof + 16 : nullptr);
-                else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, false, epi, prof,
+                else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, epi, prof,
                                                    prof ? prof + 16 : nullptr);
                 g += pl.nstages;
                 if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
@@ -1152,15 +1234,15 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             }
             if (!merge_ctx(p, S, xs, l, rank, ep1, Q8, prof)) { ok = false; break; }
             tmark(p, l, 5);
-            {
+            {   // split-K o_proj: hidden rows 128r.. of kv head cid's ctx columns
                 const Plan pl = plan_o(p, l, Q8, cid, rank);
                 const Epi epi{kEpiStoreTagged, 0u, xtag(ep1, l, kXGlobal),
                               p.xo + ((size_t)(l & 1) * p.kvh + cid) * p.hidden, nullptr, 0, nullptr};
                 bool r;
-                if constexpr (Q8) r = gemv_rows<true, 8, 256>(p, pl, g, ring, S, xs, S.sc_o, true, false, epi,
-                                                             prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
-                else r = gemv_rows<false, 2, 256>(p, pl, g, ring, S, xs, nullptr, true, false, epi,
-                                                  prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
+                if constexpr (Q8) r = gemv_rows<true, 16, 256>(p, pl, g, ring, S, xs, S.sc_o, false, epi,
+                                                              prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
+                else r = gemv_rows<false, 16, 256>(p, pl, g, ring, S, xs, nullptr, false, epi,
+                                                   prof ? prof + 2 : nullptr, prof ? prof + 19 : nullptr);
                 g += pl.nstages;
                 if (!r) { ok = false; break; }
                 tmark(p, l, 6);
@@ -1184,13 +1266,13 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             consumers_sync<kCT>();
         }
         tmark(p, l, 8);
-        {
+        {   // this CTA's gate/up pairs -> h slice (SwiGLU fused)
             const Plan pl = plan_gu(p, l, Q8, b, G);
             const Epi epi{kEpiSwiGLU, 0u, 0u, nullptr, S.h, pl.r0 >> 1, nullptr};
             bool r;
-            if constexpr (Q8) r = gemv_rows<true, 2, kHid>(p, pl, g, ring, S, xs, S.sc_gu, true, true, epi,
+            if constexpr (Q8) r = gemv_rows<true, 8, kHid>(p, pl, g, ring, S, xs, S.sc_gu, true, epi,
                                                          prof ? prof + 4 : nullptr, prof ? prof + 22 : nullptr);
-            else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, true, epi,
+            else r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, true, epi,
                                                prof ? prof + 4 : nullptr, prof ? prof + 22 : nullptr);
             g += pl.nstages;
             if (!consumers_sync_and<kCT>(r)) { ok = false; break; }
@@ -1216,7 +1298,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     {
         const Plan pl = plan_lm(p, b, G);
         const Epi epi{kEpiLogits, 0u, 0u, nullptr, nullptr, 0, p.logits};
-        const bool r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, false, epi, nullptr, nullptr);
+        const bool r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, epi, nullptr, nullptr);
         if (!consumers_sync_and<kCT>(r)) goto consumer_exit;
     }
     if (threadIdx.x == 0) {
@@ -1329,6 +1411,7 @@ vb_status mega2_prepare(vb_engine* e) {
         m->bufs.push_back(ptr);
         return ptr;
     };
+    const int G = nclusters * kCS;
     std::vector<M2Layer> hl(c.layers);
     cudaError_t ce = cudaSuccess;
     for (int l = 0; l < c.layers && ce == cudaSuccess; l++) {
@@ -1385,7 +1468,6 @@ vb_status mega2_prepare(vb_engine* e) {
         M.q_norm = Ld.q_norm;
         M.k_norm = Ld.k_norm;
     }
-    const int G = nclusters * kCS;
     m->grid = G;
     if (ce == cudaSuccess) {
         m->d_layers = static_cast<M2Layer*>(alloc(sizeof(M2Layer) * c.layers));

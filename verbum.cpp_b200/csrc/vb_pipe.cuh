@@ -58,8 +58,9 @@ __device__ __noinline__ void record_fail(int* err, int* dbg, int code, int site,
 }
 
 // Bounded wait for the phase of parity `parity` of mbarrier `a` to complete.
-__device__ bool mbar_wait(unsigned a, unsigned parity, int* err, int* dbg, int site, int index) {
-    if (mbar_try(a, parity)) return true;
+// The spin loops are kept out of line: the persistent kernels run every wait
+// site once per layer and their code has to stay small.
+__device__ __noinline__ bool mbar_wait_slow(unsigned a, unsigned parity, int* err, int* dbg, int site, int index) {
     const unsigned long long t0 = now_ns();
     for (unsigned it = 1;; it++) {
         if (mbar_try(a, parity)) return true;
@@ -72,14 +73,17 @@ __device__ bool mbar_wait(unsigned a, unsigned parity, int* err, int* dbg, int s
         }
     }
 }
+__device__ __forceinline__ bool mbar_wait(unsigned a, unsigned parity, int* err, int* dbg, int site, int index) {
+    return mbar_try(a, parity) || mbar_wait_slow(a, parity, err, dbg, site, index);
+}
 // Bounded wait until the previous round of `slot` (stage s - kStages) has been
-// observed by its consumer.
-__device__ bool seq_wait(volatile int* seq, int slot, int s, int stages, int* err, int* dbg) {
+// observed by a consumer (or this round already has, by another warp sharing
+// the stage).
+__device__ __noinline__ bool seq_wait_slow(volatile int* seq, int slot, int s, int stages, int* err, int* dbg) {
     const int want = s - stages;
-    if (seq[slot] == want) return true;
     const unsigned long long t0 = now_ns();
     for (unsigned it = 1;; it++) {
-        if (seq[slot] == want) return true;
+        if (seq[slot] >= want) return true;
         if ((it & 255u) == 0) {
             if (err_read(err)) return false;
             if (now_ns() - t0 > kWaitNs) {
@@ -88,6 +92,9 @@ __device__ bool seq_wait(volatile int* seq, int slot, int s, int stages, int* er
             }
         }
     }
+}
+__device__ __forceinline__ bool seq_wait(volatile int* seq, int slot, int s, int stages, int* err, int* dbg) {
+    return seq[slot] >= s - stages || seq_wait_slow(seq, slot, s, stages, err, dbg);
 }
 
 // Warp-uniform wait: lane 0 waits (bounded) and broadcasts the outcome; on
