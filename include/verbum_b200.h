@@ -86,6 +86,15 @@ VB_API vb_status vb_matmul_nt_f32(const float* A, const float* W, float* C, int 
 VB_API vb_status vb_matmul_nt_q8(const float* A, const int8_t* Wq, const float* scales,
                           float* C, int M, int N, int K, void* stream);
 
+/* C[M][N] = A[M][K] . W[N][K]^T on the tensor cores (tcgen05, bf16 operands,
+ * f32 accumulation): the batched form of matmul_nt / matmul_nt_q8 (ops.cpp:42-70,
+ * quant.cpp:43-70) with 1 <= M <= 64 activation rows and K % 64 == 0.  W is
+ * f32 (w_int8 = 0; used as a bf16 hi+lo pair) or INT8 with per-row scales
+ * applied after the sum (w_int8 = 1); A is split into bf16 hi+lo.  Synchronous
+ * on `stream`; scratch comes from a per-device buffer grown on demand. */
+VB_API vb_status vb_matmul_nt_tc(const float* A, const void* W, const float* scales, float* C, int M, int N,
+                                 int K, int w_int8, void* stream);
+
 /* Per-row symmetric absmax INT8 quantisation, bit-exact with quantize_rows
  * (core/src/quant.cpp:9-41): scale = amax>0 ? amax/127 : 1, q = clamp(
  * round-half-even(w * (1/scale)), -127, 127). */

@@ -4,7 +4,15 @@
 // split-K attention over B caches -> o GEMM + residual -> rmsnorm -> gate/up
 // GEMM + SwiGLU -> down GEMM + residual; then final norm -> lm_head GEMM ->
 // per-row argmax.  The step is graph-captured and replayed.
+//
+// The GEMMs run on the tensor cores (vb_tcgemm.cu): the batch keeps bf16
+// copies of the projections (exact for INT8 values; a hi+lo pair for f32
+// weights and the tied lm_head), each GEMM's activations are split into bf16
+// hi+lo, and the split-K partials are summed with the INT8 scales and the
+// epilogue (store, residual add, SwiGLU) by the reduce kernel.
+#include <algorithm>
 #include <string>
+#include <vector>
 
 #include "vb_engine.cuh"
 
@@ -36,6 +44,14 @@ struct vb_batch {
     int graph_nodes = 0;
     int* d_prompt = nullptr;  // [P][B] prefill tokens
     int prompt_cap = 0;
+    // tensor-core operands
+    std::vector<void*> tcw;   // per layer: qkv, o, gu, d -> {hi, lo}
+    void* lm_hi = nullptr;
+    void* lm_lo = nullptr;
+    bool tc_q8 = false;       // which weights tcw holds
+    bool tc_ready = false;
+    void* a_hi = nullptr;     // [64][max K] bf16 activation split
+    void* a_lo = nullptr;
 };
 
 namespace vb {
@@ -54,6 +70,50 @@ void bfree(T*& p) {
     p = nullptr;
 }
 
+void free_tc_weights(vb_batch* b) {
+    for (void*& p : b->tcw)
+        if (p) cudaFree(p), p = nullptr;
+    b->tcw.clear();
+    b->tc_ready = false;
+}
+
+// bf16 tensor-core copies of the current weights (rebuilt when the engine is
+// quantised after the batch was made); the lm_head pair is built once.
+vb_status batch_tc_weights(vb_batch* b) {
+    vb_engine* e = b->e;
+    if (b->tc_ready && b->tc_q8 == e->quantized) return VB_OK;
+    const vb_config& c = e->cfg;
+    cudaStream_t s = e->stream;
+    const bool q8 = e->quantized;
+    free_tc_weights(b);
+    b->tcw.assign((size_t)c.layers * 8, nullptr);
+    const int Ns[4] = {e->qkv_rows, c.hidden, 2 * c.ffn, c.hidden};
+    const int Ks[4] = {c.hidden, e->q_width, c.hidden, c.ffn};
+    vb_status st;
+    for (int l = 0; l < c.layers; l++) {
+        const vb_layer_dev& L = e->L[l];
+        const void* src[4] = {q8 ? (const void*)L.qqkv : (const void*)L.wqkv, q8 ? (const void*)L.qo : (const void*)L.wo,
+                              q8 ? (const void*)L.qgu : (const void*)L.wgu, q8 ? (const void*)L.qd : (const void*)L.wd};
+        for (int j = 0; j < 4; j++) {
+            const size_t n = (size_t)Ns[j] * Ks[j];
+            void** hl = &b->tcw[(size_t)l * 8 + 2 * j];
+            VB_CUDA_TRY(cudaMalloc(&hl[0], n * 2));
+            if (!q8) VB_CUDA_TRY(cudaMalloc(&hl[1], n * 2));
+            if ((st = launch_weights_bf16(src[j], q8, n, hl[0], hl[1], s))) return st;
+        }
+    }
+    if (!b->lm_hi) {
+        const size_t n = (size_t)c.vocab * c.hidden;
+        VB_CUDA_TRY(cudaMalloc(&b->lm_hi, n * 2));
+        VB_CUDA_TRY(cudaMalloc(&b->lm_lo, n * 2));
+        if ((st = launch_weights_bf16(e->embed, false, n, b->lm_hi, b->lm_lo, s))) return st;
+    }
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    b->tc_q8 = q8;
+    b->tc_ready = true;
+    return VB_OK;
+}
+
 vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     vb_engine* e = b->e;
     const vb_config& c = e->cfg;
@@ -63,11 +123,24 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     if ((st = launch_embed(e->embed, b->d_tok, B, c.hidden, c.vocab, b->x, b->d_err, s))) return st;
     const size_t per_seq = (size_t)c.kv_heads * b->max_seq * c.head_dim;
     const size_t layer_kv = per_seq * B;
-    auto gemm = [&](const float* A, const void* W, const float* sc, float* C, int N, int K,
-                    int ldc, int epi, bool wq8) {
+    // C (epilogue) A . W^T: split A into bf16 hi+lo, tensor-core partials, reduce
+    auto gemm = [&](const float* A, void* const* w, const float* sc, float* C, int N, int K, int ldc, int epi,
+                    bool wq8) {
+        vb_status r;
+        if ((r = launch_split_bf16(A, B, K, K, b->a_hi, b->a_lo, s))) return r;
+        TcGemmArgs t{};
+        t.w_hi = w[0];
+        t.w_lo = wq8 ? nullptr : w[1];
+        t.a_hi = b->a_hi;
+        t.a_lo = b->a_lo;
+        t.M = B;
+        t.N = N;
+        t.K = K;
+        t.ws = b->gemm_ws;
+        t.ws_floats = b->gemm_ws_floats;
+        t.err = b->d_err;
+        if ((r = launch_tc_gemm(t, s))) return r;
         GemmArgs g{};
-        g.A = A;
-        g.W = W;
         g.scales = sc;
         g.C = C;
         g.M = B;
@@ -76,13 +149,13 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         g.ldc = ldc;
         g.ws = b->gemm_ws;
         g.ws_floats = b->gemm_ws_floats;
-        return launch_gemm(g, wq8, epi, s);
+        return launch_gemm_reduce(g, tc_gemm_splits(N, K), wq8, epi, s);
     };
     for (int l = 0; l < c.layers; l++) {
         const vb_layer_dev& L = e->L[l];
+        void* const* tw = &b->tcw[(size_t)l * 8];
         if ((st = launch_rmsnorm_rows(b->x, L.in_norm, b->xn, B, c.hidden, c.eps, s))) return st;
-        if ((st = gemm(b->xn, q8 ? (const void*)L.qqkv : (const void*)L.wqkv, L.sqkv, b->qkv,
-                       e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8)))
+        if ((st = gemm(b->xn, tw + 0, L.sqkv, b->qkv, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8)))
             return st;
         QkNormArgs qa{};
         qa.qkv = b->qkv;
@@ -122,27 +195,23 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         aa.splits = b->attn_splits;
         aa.ws = b->attn_ws;
         if ((st = launch_attention(aa, s))) return st;
-        if ((st = gemm(b->ctx, q8 ? (const void*)L.qo : (const void*)L.wo, L.so, b->x, c.hidden,
-                       e->q_width, c.hidden, kEpiResidual, q8)))
-            return st;
+        if ((st = gemm(b->ctx, tw + 2, L.so, b->x, c.hidden, e->q_width, c.hidden, kEpiResidual, q8))) return st;
         if ((st = launch_rmsnorm_rows(b->x, L.post_norm, b->xn, B, c.hidden, c.eps, s))) return st;
-        if ((st = gemm(b->xn, q8 ? (const void*)L.qgu : (const void*)L.wgu, L.sgu, b->h,
-                       2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8)))
-            return st;
-        if ((st = gemm(b->h, q8 ? (const void*)L.qd : (const void*)L.wd, L.sd, b->x, c.hidden,
-                       c.ffn, c.hidden, kEpiResidual, q8)))
-            return st;
+        if ((st = gemm(b->xn, tw + 4, L.sgu, b->h, 2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8))) return st;
+        if ((st = gemm(b->h, tw + 6, L.sd, b->x, c.hidden, c.ffn, c.hidden, kEpiResidual, q8))) return st;
     }
     if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, c.hidden, c.eps, s))) return st;
-    if ((st = gemm(b->xn, e->embed, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore,
-                   false)))
-        return st;
+    {
+        void* const lm[2] = {b->lm_hi, b->lm_lo};
+        if ((st = gemm(b->xn, lm, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore, false))) return st;
+    }
     if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
     return launch_advance(b->d_pos, b->d_tok, b->d_next, B, s);
 }
 
 vb_status batch_graph(vb_batch* b) {
     if (b->graph && b->graph_q8 == b->e->quantized) return VB_OK;
+    if (vb_status ws = batch_tc_weights(b)) return ws;
     if (b->graph) cudaGraphExecDestroy(b->graph);
     b->graph = nullptr;
     cudaStream_t s = b->e->stream;
@@ -229,20 +298,28 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
     b->attn_splits = attn_splits_for(batch, c.kv_heads, max_seq);
     if ((st = balloc(&b->attn_ws, attn_ws_bytes(batch, c.heads, b->attn_splits) / 4 + 1, "attn ws")))
         return bail(st);
+    if (c.hidden % 64 || e->q_width % 64 || c.ffn % 64)
+        return bail(fail(VB_ERR_UNSUPPORTED, "batch: tensor-core GEMMs need hidden, heads*head_dim, ffn % 64 == 0"));
     size_t ws = 0;
-    auto upd = [&](int N, int K, bool q8) {
-        const size_t w = gemm_ws_floats(batch, N, K, q8);
+    auto upd = [&](int N, int K) {
+        const size_t w = tc_gemm_ws_floats(batch, N, K);
         if (w > ws) ws = w;
     };
-    for (int q8 = 0; q8 < 2; q8++) {
-        upd(e->qkv_rows, c.hidden, q8);
-        upd(c.hidden, e->q_width, q8);
-        upd(2 * c.ffn, c.hidden, q8);
-        upd(c.hidden, c.ffn, q8);
-    }
-    upd(c.vocab, c.hidden, false);
+    upd(e->qkv_rows, c.hidden);
+    upd(c.hidden, e->q_width);
+    upd(2 * c.ffn, c.hidden);
+    upd(c.hidden, c.ffn);
+    upd(c.vocab, c.hidden);
     b->gemm_ws_floats = ws;
     if ((st = balloc(&b->gemm_ws, ws, "gemm ws"))) return bail(st);
+    {
+        const int kmax = std::max(c.hidden, std::max(e->q_width, c.ffn));
+        unsigned short *ah = nullptr, *al = nullptr;
+        if ((st = balloc(&ah, (size_t)64 * kmax, "activation split"))) return bail(st);
+        b->a_hi = ah;
+        if ((st = balloc(&al, (size_t)64 * kmax, "activation split"))) return bail(st);
+        b->a_lo = al;
+    }
     if ((st = balloc(&b->d_tok, batch, "tok"))) return bail(st);
     if ((st = balloc(&b->d_pos, batch, "pos"))) return bail(st);
     if ((st = balloc(&b->d_next, batch, "next"))) return bail(st);
@@ -265,6 +342,8 @@ vb_status vb_batch_destroy(vb_batch* b) {
     bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->qkv); bfree(b->q);
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
     bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err); bfree(b->d_prompt);
+    free_tc_weights(b);
+    bfree(b->lm_hi); bfree(b->lm_lo); bfree(b->a_hi); bfree(b->a_lo);
     if (b->h_io) cudaFreeHost(b->h_io);
     delete b;
     return VB_OK;

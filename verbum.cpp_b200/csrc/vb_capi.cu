@@ -217,6 +217,49 @@ vb_status vb_matmul_nt_q8(const float* A, const int8_t* Wq, const float* scales,
     return VB_OK;
 }
 
+vb_status vb_matmul_nt_tc(const float* A, const void* W, const float* scales, float* C, int M, int N, int K,
+                          int w_int8, void* stream) {
+    if (!A || !W || !C || (w_int8 && !scales)) return fail(VB_ERR_ARG, "null pointer");
+    if (M <= 0 || M > 64 || N <= 0 || K <= 0 || K % 64)
+        return fail(VB_ERR_UNSUPPORTED, "matmul_nt_tc: needs 1 <= M <= 64 and K % 64 == 0");
+    cudaStream_t s = as_stream(stream);
+    const size_t wf = tc_gemm_ws_floats(M, N, K);
+    const size_t a_bytes = (size_t)64 * K * 2, w_bytes = (size_t)N * K * 2;
+    const size_t off_ahi = 256, off_alo = off_ahi + a_bytes, off_whi = off_alo + a_bytes;
+    const size_t off_wlo = off_whi + w_bytes, off_ws = off_wlo + (w_int8 ? 0 : w_bytes);
+    void* base = nullptr;
+    vb_status st = scratch_for(off_ws + wf * 4, &base);
+    if (st) return st;
+    char* b = static_cast<char*>(base);
+    int* err = reinterpret_cast<int*>(b);
+    VB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+    if ((st = launch_split_bf16(A, M, K, K, b + off_ahi, b + off_alo, s))) return st;
+    if ((st = launch_weights_bf16(W, w_int8 != 0, (size_t)N * K, b + off_whi, w_int8 ? nullptr : b + off_wlo, s)))
+        return st;
+    TcGemmArgs t{};
+    t.w_hi = b + off_whi;
+    t.w_lo = w_int8 ? nullptr : b + off_wlo;
+    t.a_hi = b + off_ahi;
+    t.a_lo = b + off_alo;
+    t.M = M;
+    t.N = N;
+    t.K = K;
+    t.ws = reinterpret_cast<float*>(b + off_ws);
+    t.ws_floats = wf;
+    t.err = err;
+    if ((st = launch_tc_gemm(t, s))) return st;
+    GemmArgs g{};
+    g.A = A; g.W = W; g.scales = scales; g.C = C; g.M = M; g.N = N; g.K = K; g.ldc = N;
+    g.ws = t.ws;
+    g.ws_floats = wf;
+    if ((st = launch_gemm_reduce(g, tc_gemm_splits(N, K), w_int8 != 0, kEpiStore, s))) return st;
+    int h_err = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    if (h_err) return fail(VB_ERR_TIMEOUT, "matmul_nt_tc: a bounded wait in the kernel gave up");
+    return VB_OK;
+}
+
 vb_status vb_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_t* q, float* scales,
                            void* stream) {
     if (!W || !q || !scales) return fail(VB_ERR_ARG, "null pointer");

@@ -851,6 +851,11 @@ vb_status launch_gemm(const GemmArgs& a, bool q8, int epi, cudaStream_t s) {
     if (q8) gemm_partial_kernel<true><<<grid, 256, 0, s>>>(a, kper);
     else gemm_partial_kernel<false><<<grid, 256, 0, s>>>(a, kper);
     VB_LAUNCH_CHECK("gemm_partial_kernel");
+    return launch_gemm_reduce(a, splits, q8, epi, s);
+}
+
+vb_status launch_gemm_reduce(const GemmArgs& a, int splits, bool q8, int epi, cudaStream_t s) {
+    if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemm: swiglu needs even N");
     const int outN = epi == kEpiSwiGLU ? a.N / 2 : a.N;
     const size_t total = (size_t)a.M * outN;
     int rb = (int)((total + 255) / 256);

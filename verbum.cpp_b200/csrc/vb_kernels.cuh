@@ -106,5 +106,27 @@ struct GemmArgs {
 };
 size_t gemm_ws_floats(int M, int N, int K, bool q8);
 vb_status launch_gemm(const GemmArgs& a, bool q8, int epi, cudaStream_t s);
+// Sums `splits` partials P[s][M][N] (a.ws) in fixed order, applies the INT8
+// row scales (q8) and the epilogue into a.C.
+vb_status launch_gemm_reduce(const GemmArgs& a, int splits, bool q8, int epi, cudaStream_t s);
+
+// Tensor-core projection (vb_tcgemm.cu): partial sums of A . W^T over K
+// splits into ws [splits][M][N], from bf16 operands: W_hi (+ W_lo for f32
+// weights, null for INT8), A_hi + A_lo ([64][K], rows >= M zero).
+struct TcGemmArgs {
+    const void* w_hi;
+    const void* w_lo;
+    const void* a_hi;
+    const void* a_lo;
+    int M, N, K;
+    float* ws;
+    size_t ws_floats;
+    int* err;
+};
+int tc_gemm_splits(int N, int K);
+size_t tc_gemm_ws_floats(int M, int N, int K);
+vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
+vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s);
+vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, void* lo, cudaStream_t s);
 
 }  // namespace vb

@@ -1,0 +1,351 @@
+// vb_tcgemm.cu -- projections of the batched decode step on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory, operands staged in
+// shared memory by TMA).
+//
+// C[m][n] = sum_k A[m][k] W[n][k] for the M <= 64 activation rows of a batched
+// step against a weight matrix W [N][K] (the reference's matmul_nt,
+// core/src/ops.cpp:42-70, and matmul_nt_q8, core/src/quant.cpp:43-70, with
+// x holding M rows).  The MMA runs on bf16 operands with f32 accumulation:
+//   * INT8 weights are stored once as bf16 (every value in [-127, 127] is exact
+//     in bf16), the per-row scale is applied after the sum as the reference
+//     does;
+//   * f32 weights (the tied lm_head, and the f32 model) are stored as a bf16
+//     pair W = W_hi + W_lo;
+//   * the f32 activations are split the same way, A = A_hi + A_lo.
+// The sum takes A_hi W + A_lo W (INT8) or A_hi W_hi + A_lo W_hi + A_hi W_lo
+// (f32): products of bf16 values are exact in f32, and the dropped terms are
+// ~2^-16 relative, so the result tracks the f32 reference closely.
+//
+// One CTA computes a 128-row weight tile (the MMA's M) against all 64
+// activation rows (the MMA's N) over one K range (split-K); partial sums
+// P[split][m][n] go to global memory and the existing reduce kernels sum the
+// splits in fixed order and apply the scales and epilogues.
+//
+// Warp 0 lane 0 issues TMA copies into a 4-stage ring, warp 1 lane 0 issues the
+// MMAs (tcgen05.commit frees a stage when its MMAs are done), and all four warps
+// read the 128 x 64 f32 accumulator tile out of tensor memory.  Every wait is
+// bounded; on a timeout the error word is set, in-flight copies and MMAs are
+// waited for (bounded), tensor memory is freed and the kernel returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "vb_engine.cuh"
+#include "vb_pipe.cuh"
+
+namespace vb {
+namespace {
+
+constexpr int kTSMs = 148;        // B200 SM count (split-K sizing)
+constexpr int kTM = 128;         // weight rows per tile (MMA M)
+constexpr int kTN = 64;          // activation rows (MMA N)
+constexpr int kTK = 64;          // K per stage: one 128-byte swizzle row of bf16
+constexpr int kTStages = 4;
+constexpr int kTThreads = 128;
+constexpr int kWTile = kTM * kTK * 2;   // 16 KB
+constexpr int kATile = kTN * kTK * 2;   // 8 KB
+constexpr int kTStage = 2 * kWTile + 2 * kATile;  // W_hi, W_lo, A_hi, A_lo
+constexpr size_t kTSmem = (size_t)kTStages * kTStage + 1024;  // + alignment slack
+
+struct TcParams {
+    int M, N;       // activation rows, weight rows
+    int chunks;     // K / kTK
+    int per_split;  // chunks per split
+    float* P;       // [splits][M][N]
+    int* err;
+};
+
+__device__ __forceinline__ void tma_load_2d(unsigned dst, const CUtensorMap* map, int x, int y, unsigned mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 bytes,
+// 8-row groups 1024 bytes apart (the canonical layout TMA's 128-byte swizzle
+// writes).  Fields: start >> 4 [0,14), leading offset [16,30) (unused for
+// swizzled K-major, 1), stride offset >> 4 [32,46), version 1 [46,48),
+// layout type 2 = 128-byte swizzle [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(unsigned saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator [4,6) = 1, A bf16 [7,10) = 1,
+// B bf16 [10,13) = 1, both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
+                            ((uint32_t)(kTM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(unsigned tmem, uint64_t adesc, uint64_t bdesc, bool acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.u32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"((unsigned)acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(unsigned mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+
+template <int WP>
+__global__ void __launch_bounds__(kTThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
+                   const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                   const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) unsigned long long full[kTStages], empty[kTStages], done;
+    __shared__ unsigned tmem_slot;
+    __shared__ int fail;
+    const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kTM;
+    const int split = blockIdx.y;
+    const int c0 = split * p.per_split;
+    const int nch = min(p.per_split, p.chunks - c0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTStages; s++) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        mbar_init(smem_addr(&done), 1);
+        fail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(kTN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = tmem_slot;
+
+    if (warp == 0 && lane == 0 && nch > 0) {
+        // ------------------------------------------------------ TMA producer
+        int issued = 0;
+        for (int i = 0; i < nch; i++) {
+            const int s = i % kTStages;
+            if (!mbar_wait(smem_addr(&empty[s]), ((unsigned)(i / kTStages) & 1u) ^ 1u, p.err, nullptr, kSiteEmpty, i)) {
+                fail = 1;
+                break;
+            }
+            const unsigned st = sbase + (unsigned)s * kTStage;
+            const unsigned fb = smem_addr(&full[s]);
+            mbar_expect_tx(fb, (unsigned)(WP * kWTile + 2 * kATile));
+            const int x = (c0 + i) * kTK;
+            tma_load_2d(st, &tw_hi, x, n0, fb);
+            if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
+            tma_load_2d(st + 2 * kWTile, &ta_hi, x, 0, fb);
+            tma_load_2d(st + 2 * kWTile + kATile, &ta_lo, x, 0, fb);
+            issued = i + 1;
+        }
+        // never leave with copies in flight
+        for (int i = issued > kTStages ? issued - kTStages : 0; i < issued; i++)
+            mbar_wait(smem_addr(&full[i % kTStages]), (unsigned)(i / kTStages) & 1u, p.err, nullptr, kSiteFull, i);
+    } else if (warp == 1 && lane == 0 && nch > 0) {
+        // ------------------------------------------------------- MMA issuer
+        int committed = 0;
+        for (int i = 0; i < nch && !fail; i++) {
+            const int s = i % kTStages;
+            if (!mbar_wait(smem_addr(&full[s]), (unsigned)(i / kTStages) & 1u, p.err, nullptr, kSiteFull, i)) {
+                fail = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const unsigned st = sbase + (unsigned)s * kTStage;
+#pragma unroll
+            for (int kk = 0; kk < kTK / 16; kk++) {
+                const uint64_t wh = sw128_desc(st + 32u * kk);
+                const uint64_t ah = sw128_desc(st + 2 * kWTile + 32u * kk);
+                const uint64_t al = sw128_desc(st + 2 * kWTile + kATile + 32u * kk);
+                mma_bf16(tmem, wh, ah, i > 0 || kk > 0);
+                mma_bf16(tmem, wh, al, true);
+                if (WP == 2) mma_bf16(tmem, sw128_desc(st + kWTile + 32u * kk), ah, true);
+            }
+            mma_commit(smem_addr(&empty[s]));
+            committed = i + 1;
+        }
+        (void)committed;
+        mma_commit(smem_addr(&done));
+    }
+    // -------------------------------------------------------------- epilogue
+    __syncwarp();
+    bool ok = nch > 0;
+    if (ok) {
+        ok = mbar_wait(smem_addr(&done), 0u, p.err, nullptr, kSiteFull, -1);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    }
+    ok = __syncthreads_and(ok && !fail);
+    if (ok) {
+        float v[kTN];
+        const unsigned taddr = tmem + ((unsigned)(32 * warp) << 16);
+        unsigned* r = reinterpret_cast<unsigned*>(v);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+            "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+            "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+            "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+            "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+              "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+              "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+              "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
+              "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]),
+              "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
+              "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
+              "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int n = n0 + 32 * warp + lane;
+        if (n < p.N) {
+            float* P = p.P + (size_t)split * p.M * p.N + n;
+#pragma unroll
+            for (int m = 0; m < kTN; m++)
+                if (m < p.M) P[(size_t)m * p.N] = v[m];
+        }
+    } else if (threadIdx.x == 0 && nch > 0) {
+        atomicCAS(p.err, 0, kErrPipeTimeout);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN) : "memory");
+}
+
+// A [M][lda] f32 -> A_hi, A_lo [64][K] bf16 with A = A_hi + A_lo (rows >= M zero).
+__global__ void split_bf16_kernel(const float* A, int M, int K, int lda, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const size_t total = (size_t)kTN * K;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / K), k = (int)(i % K);
+        const float x = m < M ? A[(size_t)m * lda + k] : 0.f;
+        const __nv_bfloat16 h = __float2bfloat16_rn(x);
+        hi[i] = h;
+        lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+    }
+}
+
+// W [N][K] (f32, or int8 when q8) -> bf16 copies: W_hi (= W exactly for int8)
+// and, for f32, W_lo = W - W_hi.
+__global__ void weights_bf16_kernel(const void* W, bool q8, size_t total, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        if (q8) {
+            hi[i] = __float2bfloat16_rn((float)static_cast<const int8_t*>(W)[i]);
+        } else {
+            const float x = static_cast<const float*>(W)[i];
+            const __nv_bfloat16 h = __float2bfloat16_rn(x);
+            hi[i] = h;
+            lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+        }
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over [rows][K], boxes of 64 (K) x box_rows, 128-byte swizzle.
+vb_status make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VB_ERR_CUDA, "tensor-core gemm: cuTensorMapEncodeTiled failed");
+    return VB_OK;
+}
+
+}  // namespace
+
+int tc_gemm_splits(int N, int K) {
+    const int tiles = (N + kTM - 1) / kTM;
+    const int chunks = K / kTK;
+    int s = (kTSMs + tiles - 1) / tiles;
+    if (s > chunks) s = chunks;
+    if (s < 1) s = 1;
+    // every split gets at least one chunk
+    const int per = (chunks + s - 1) / s;
+    return (chunks + per - 1) / per;
+}
+
+size_t tc_gemm_ws_floats(int M, int N, int K) { return (size_t)tc_gemm_splits(N, K) * M * N; }
+
+vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s) {
+    if (M < 1 || M > kTN || K <= 0) return fail(VB_ERR_ARG, "split_bf16: bad shape");
+    const size_t total = (size_t)kTN * K;
+    int blocks = (int)((total + 255) / 256);
+    if (blocks > kTSMs * 4) blocks = kTSMs * 4;
+    split_bf16_kernel<<<blocks, 256, 0, s>>>(A, M, K, lda, static_cast<__nv_bfloat16*>(hi),
+                                             static_cast<__nv_bfloat16*>(lo));
+    VB_LAUNCH_CHECK("split_bf16_kernel");
+    return VB_OK;
+}
+
+vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, void* lo, cudaStream_t s) {
+    int blocks = (int)((count + 255) / 256);
+    if (blocks > kTSMs * 16) blocks = kTSMs * 16;
+    weights_bf16_kernel<<<blocks, 256, 0, s>>>(W, q8, count, static_cast<__nv_bfloat16*>(hi),
+                                               static_cast<__nv_bfloat16*>(lo));
+    VB_LAUNCH_CHECK("weights_bf16_kernel");
+    return VB_OK;
+}
+
+vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
+    if (a.M < 1 || a.M > kTN) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M must be 1..64");
+    if (a.K % kTK || a.K <= 0) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: K must be a multiple of 64");
+    if (a.N <= 0) return fail(VB_ERR_ARG, "tensor-core gemm: N <= 0");
+    const int splits = tc_gemm_splits(a.N, a.K);
+    if ((size_t)splits * a.M * a.N > a.ws_floats) return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
+    static bool attr_done[2] = {false, false};
+    const int wp = a.w_lo ? 2 : 1;
+    if (!attr_done[wp - 1]) {
+        cudaError_t ce = wp == 2 ? cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)kTSmem)
+                                 : cudaFuncSetAttribute(tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)kTSmem);
+        if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
+        attr_done[wp - 1] = true;
+    }
+    CUtensorMap mwh, mwl, mah, mal;
+    vb_status st;
+    if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kTM))) return st;
+    if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kTM))) return st;
+    if ((st = make_map(&mah, a.a_hi, kTN, a.K, kTN))) return st;
+    if ((st = make_map(&mal, a.a_lo, kTN, a.K, kTN))) return st;
+    TcParams p;
+    p.M = a.M;
+    p.N = a.N;
+    p.chunks = a.K / kTK;
+    p.per_split = (p.chunks + splits - 1) / splits;
+    p.P = a.ws;
+    p.err = a.err;
+    const dim3 grid((a.N + kTM - 1) / kTM, splits);
+    if (wp == 2) tc_gemm_kernel<2><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
+    else tc_gemm_kernel<1><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
+    VB_LAUNCH_CHECK("tc_gemm_kernel");
+    return VB_OK;
+}
+
+}  // namespace vb

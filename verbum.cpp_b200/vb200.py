@@ -65,6 +65,7 @@ _SIGS = {
     "vb_sync": (_I, [_P]),
     "vb_matmul_nt_f32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vb_matmul_nt_q8": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "vb_matmul_nt_tc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_quantize_rows": (_I, [_P, _L, _L, _P, _P, _P]),
     "vb_rmsnorm": (_I, [_P, _P, _P, _I, _I, _F, _P]),
     "vb_rope": (_I, [_P, _P, _P, _I, _I, _I, _P]),
@@ -343,6 +344,15 @@ def matmul_nt_q8(A, Wq, scales, C_out, stream=None):
     M, K = A.shape
     N = Wq.shape[0]
     check(lib().vb_matmul_nt_q8(_tp(A), _tp(Wq), _tp(scales), _tp(C_out), M, N, K, _stream(stream)))
+
+
+def matmul_nt_tc(A, W, C_out, scales=None, stream=None):
+    """C = A . W^T on the tensor cores; W f32, or int8 with per-row scales."""
+    M, K = A.shape
+    N = W.shape[0]
+    q8 = scales is not None
+    check(lib().vb_matmul_nt_tc(_tp(A), _tp(W), _tp(scales) if q8 else None, _tp(C_out), M, N, K, int(q8),
+                                _stream(stream)))
 
 
 def quantize_rows(W, q, scales, stream=None):
