@@ -50,8 +50,10 @@ struct vb_batch {
     void* lm_lo = nullptr;
     bool tc_q8 = false;       // which weights tcw holds
     bool tc_ready = false;
-    void* a_hi = nullptr;     // [64][max K] bf16 activation split
+    void* a_hi = nullptr;     // [64][hidden] bf16 split of the normed input (QKV, gate/up, lm_head)
     void* a_lo = nullptr;
+    void* y_hi = nullptr;     // [64][max(H*D, ffn)] bf16 split of ctx (o_proj) or h (down)
+    void* y_lo = nullptr;
 };
 
 namespace vb {
@@ -123,39 +125,34 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     if ((st = launch_embed(e->embed, b->d_tok, B, c.hidden, c.vocab, b->x, b->d_err, s))) return st;
     const size_t per_seq = (size_t)c.kv_heads * b->max_seq * c.head_dim;
     const size_t layer_kv = per_seq * B;
-    // C (epilogue) A . W^T: split A into bf16 hi+lo, tensor-core partials, reduce
-    auto gemm = [&](const float* A, void* const* w, const float* sc, float* C, int N, int K, int ldc, int epi,
-                    bool wq8) {
-        vb_status r;
-        if ((r = launch_split_bf16(A, B, K, K, b->a_hi, b->a_lo, s))) return r;
+    // C (epilogue) A . W^T on the tensor cores from A's bf16 split (ahi, alo)
+    auto gemm = [&](const void* ahi, const void* alo, void* const* w, const float* sc, float* C, int N, int K,
+                    int ldc, int epi, bool wq8, void* ohi, void* olo) {
         TcGemmArgs t{};
         t.w_hi = w[0];
         t.w_lo = wq8 ? nullptr : w[1];
-        t.a_hi = b->a_hi;
-        t.a_lo = b->a_lo;
+        t.a_hi = ahi;
+        t.a_lo = alo;
         t.M = B;
         t.N = N;
         t.K = K;
         t.ws = b->gemm_ws;
         t.ws_floats = b->gemm_ws_floats;
+        t.scales = wq8 ? sc : nullptr;
+        t.C = C;
+        t.ldc = ldc;
+        t.epi = epi;
+        t.out_hi = ohi;
+        t.out_lo = olo;
         t.err = b->d_err;
-        if ((r = launch_tc_gemm(t, s))) return r;
-        GemmArgs g{};
-        g.scales = sc;
-        g.C = C;
-        g.M = B;
-        g.N = N;
-        g.K = K;
-        g.ldc = ldc;
-        g.ws = b->gemm_ws;
-        g.ws_floats = b->gemm_ws_floats;
-        return launch_gemm_reduce(g, tc_gemm_splits(N, K), wq8, epi, s);
+        return launch_tc_gemm(t, s);
     };
     for (int l = 0; l < c.layers; l++) {
         const vb_layer_dev& L = e->L[l];
         void* const* tw = &b->tcw[(size_t)l * 8];
-        if ((st = launch_rmsnorm_rows(b->x, L.in_norm, b->xn, B, c.hidden, c.eps, s))) return st;
-        if ((st = gemm(b->xn, tw + 0, L.sqkv, b->qkv, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8)))
+        if ((st = launch_rmsnorm_rows(b->x, L.in_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo))) return st;
+        if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, b->qkv, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8,
+                       nullptr, nullptr)))
             return st;
         QkNormArgs qa{};
         qa.qkv = b->qkv;
@@ -194,16 +191,27 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         aa.stride_h = qa.stride_h;
         aa.splits = b->attn_splits;
         aa.ws = b->attn_ws;
+        aa.out_hi = b->y_hi;
+        aa.out_lo = b->y_lo;
         if ((st = launch_attention(aa, s))) return st;
-        if ((st = gemm(b->ctx, tw + 2, L.so, b->x, c.hidden, e->q_width, c.hidden, kEpiResidual, q8))) return st;
-        if ((st = launch_rmsnorm_rows(b->x, L.post_norm, b->xn, B, c.hidden, c.eps, s))) return st;
-        if ((st = gemm(b->xn, tw + 4, L.sgu, b->h, 2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8))) return st;
-        if ((st = gemm(b->h, tw + 6, L.sd, b->x, c.hidden, c.ffn, c.hidden, kEpiResidual, q8))) return st;
+        if ((st = gemm(b->y_hi, b->y_lo, tw + 2, L.so, b->x, c.hidden, e->q_width, c.hidden, kEpiResidual, q8,
+                       nullptr, nullptr)))
+            return st;
+        if ((st = launch_rmsnorm_rows(b->x, L.post_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo)))
+            return st;
+        if ((st = gemm(b->a_hi, b->a_lo, tw + 4, L.sgu, b->h, 2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8, b->y_hi,
+                       b->y_lo)))
+            return st;
+        if ((st = gemm(b->y_hi, b->y_lo, tw + 6, L.sd, b->x, c.hidden, c.ffn, c.hidden, kEpiResidual, q8, nullptr,
+                       nullptr)))
+            return st;
     }
-    if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, c.hidden, c.eps, s))) return st;
+    if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo))) return st;
     {
         void* const lm[2] = {b->lm_hi, b->lm_lo};
-        if ((st = gemm(b->xn, lm, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore, false))) return st;
+        if ((st = gemm(b->a_hi, b->a_lo, lm, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore, false,
+                       nullptr, nullptr)))
+            return st;
     }
     if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
     return launch_advance(b->d_pos, b->d_tok, b->d_next, B, s);
@@ -313,12 +321,21 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
     b->gemm_ws_floats = ws;
     if ((st = balloc(&b->gemm_ws, ws, "gemm ws"))) return bail(st);
     {
-        const int kmax = std::max(c.hidden, std::max(e->q_width, c.ffn));
-        unsigned short *ah = nullptr, *al = nullptr;
-        if ((st = balloc(&ah, (size_t)64 * kmax, "activation split"))) return bail(st);
+        const int ky = std::max(e->q_width, c.ffn);
+        unsigned short *ah = nullptr, *al = nullptr, *yh = nullptr, *yl = nullptr;
+        if ((st = balloc(&ah, (size_t)64 * c.hidden, "activation split"))) return bail(st);
         b->a_hi = ah;
-        if ((st = balloc(&al, (size_t)64 * kmax, "activation split"))) return bail(st);
+        if ((st = balloc(&al, (size_t)64 * c.hidden, "activation split"))) return bail(st);
         b->a_lo = al;
+        if ((st = balloc(&yh, (size_t)64 * ky, "activation split"))) return bail(st);
+        b->y_hi = yh;
+        if ((st = balloc(&yl, (size_t)64 * ky, "activation split"))) return bail(st);
+        b->y_lo = yl;
+        // rows >= batch are read by the MMA (their outputs are dropped): keep them finite
+        if (cudaMemsetAsync(ah, 0, (size_t)128 * c.hidden, es) || cudaMemsetAsync(al, 0, (size_t)128 * c.hidden, es) ||
+            cudaMemsetAsync(yh, 0, (size_t)128 * ky, es) || cudaMemsetAsync(yl, 0, (size_t)128 * ky, es))
+            return bail(fail(VB_ERR_CUDA, "activation split memset failed"));
+
     }
     if ((st = balloc(&b->d_tok, batch, "tok"))) return bail(st);
     if ((st = balloc(&b->d_pos, batch, "pos"))) return bail(st);
@@ -343,7 +360,7 @@ vb_status vb_batch_destroy(vb_batch* b) {
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
     bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err); bfree(b->d_prompt);
     free_tc_weights(b);
-    bfree(b->lm_hi); bfree(b->lm_lo); bfree(b->a_hi); bfree(b->a_lo);
+    bfree(b->lm_hi); bfree(b->lm_lo); bfree(b->a_hi); bfree(b->a_lo); bfree(b->y_hi); bfree(b->y_lo);
     if (b->h_io) cudaFreeHost(b->h_io);
     delete b;
     return VB_OK;

@@ -225,14 +225,15 @@ vb_status vb_matmul_nt_tc(const float* A, const void* W, const float* scales, fl
     cudaStream_t s = as_stream(stream);
     const size_t wf = tc_gemm_ws_floats(M, N, K);
     const size_t a_bytes = (size_t)64 * K * 2, w_bytes = (size_t)N * K * 2;
-    const size_t off_ahi = 256, off_alo = off_ahi + a_bytes, off_whi = off_alo + a_bytes;
+    const size_t off_ahi = 256;
+    const size_t off_alo = off_ahi + a_bytes, off_whi = off_alo + a_bytes;
     const size_t off_wlo = off_whi + w_bytes, off_ws = off_wlo + (w_int8 ? 0 : w_bytes);
     void* base = nullptr;
     vb_status st = scratch_for(off_ws + wf * 4, &base);
     if (st) return st;
     char* b = static_cast<char*>(base);
     int* err = reinterpret_cast<int*>(b);
-    VB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+    VB_CUDA_TRY(cudaMemsetAsync(b, 0, sizeof(int), s));  // error word
     if ((st = launch_split_bf16(A, M, K, K, b + off_ahi, b + off_alo, s))) return st;
     if ((st = launch_weights_bf16(W, w_int8 != 0, (size_t)N * K, b + off_whi, w_int8 ? nullptr : b + off_wlo, s)))
         return st;
@@ -246,13 +247,12 @@ vb_status vb_matmul_nt_tc(const float* A, const void* W, const float* scales, fl
     t.K = K;
     t.ws = reinterpret_cast<float*>(b + off_ws);
     t.ws_floats = wf;
+    t.scales = w_int8 ? scales : nullptr;
+    t.C = C;
+    t.ldc = N;
+    t.epi = kEpiStore;
     t.err = err;
     if ((st = launch_tc_gemm(t, s))) return st;
-    GemmArgs g{};
-    g.A = A; g.W = W; g.scales = scales; g.C = C; g.M = M; g.N = N; g.K = K; g.ldc = N;
-    g.ws = t.ws;
-    g.ws_floats = wf;
-    if ((st = launch_gemm_reduce(g, tc_gemm_splits(N, K), w_int8 != 0, kEpiStore, s))) return st;
     int h_err = 0;
     VB_CUDA_TRY(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, s));
     VB_CUDA_TRY(cudaStreamSynchronize(s));

@@ -10,6 +10,8 @@
 #include <limits.h>
 #include <math.h>
 
+#include <cuda_bf16.h>
+
 #include "vb_kernels.cuh"
 
 namespace vb {
@@ -298,8 +300,10 @@ __global__ void quantize_rows_kernel(const float* W, int64_t rows, int64_t cols,
 }
 
 // nn.cpp:8-42, one block per row.
-__global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int dim,
-                                    float eps) {
+// Also writes the bf16 split of the output (hi + lo = out) when hi is set:
+// the tensor-core GEMM's activation operand, rows of `dim`.
+__global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int dim, float eps,
+                                    __nv_bfloat16* hi, __nv_bfloat16* lo) {
     __shared__ double red[8];
     const float* xr = x + (size_t)blockIdx.x * dim;
     float* orow = out + (size_t)blockIdx.x * dim;
@@ -309,7 +313,15 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
         ss += (double)v * (double)v;
     }
     const float sc = rms_scale(block_sum_d<256>(ss, red), dim, eps);
-    for (int i = threadIdx.x; i < dim; i += 256) orow[i] = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        const float y = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+        orow[i] = y;
+        if (hi) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(y);
+            hi[(size_t)blockIdx.x * dim + i] = h;
+            lo[(size_t)blockIdx.x * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+        }
+    }
 }
 
 // generate.cpp:52-71 for B sequences: per-head RMSNorm (q_norm / k_norm),
@@ -483,7 +495,14 @@ __global__ void attn_merge_kernel(AttnArgs a) {
         L = fmaf(base[s * 130 + 1], f, L);
         A = fmaf(base[s * 130 + 2 + d], f, A);
     }
-    a.out[((size_t)b * a.H + h) * 128 + d] = (L > 0.0f) ? A / L : 0.0f;
+    const float c = (L > 0.0f) ? A / L : 0.0f;
+    const size_t o = ((size_t)b * a.H + h) * 128 + d;
+    a.out[o] = c;
+    if (a.out_hi) {
+        const __nv_bfloat16 hv = __float2bfloat16_rn(c);
+        static_cast<__nv_bfloat16*>(a.out_hi)[o] = hv;
+        static_cast<__nv_bfloat16*>(a.out_lo)[o] = __float2bfloat16_rn(c - __bfloat162float(hv));
+    }
 }
 
 __global__ void embed_kernel(const float* E, const int* tokens, int dim, int vocab, float* out,
@@ -636,7 +655,13 @@ __global__ void gemm_reduce_kernel(GemmArgs a, int splits) {
                 usum += P[2 * j + 1];
             }
             if (Q8) { gsum *= a.scales[2 * j]; usum *= a.scales[2 * j + 1]; }
-            a.C[(size_t)m * a.ldc + j] = silu_f(gsum) * usum;
+            const float hv = silu_f(gsum) * usum;
+            a.C[(size_t)m * a.ldc + j] = hv;
+            if (a.out_hi) {
+                const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
+                static_cast<__nv_bfloat16*>(a.out_hi)[(size_t)m * a.ldc + j] = hb;
+                static_cast<__nv_bfloat16*>(a.out_lo)[(size_t)m * a.ldc + j] = __float2bfloat16_rn(hv - __bfloat162float(hb));
+            }
         } else {
             float v = 0.f;
             for (int s = 0; s < splits; s++) v += a.ws[(size_t)s * M * N + (size_t)m * N + j];
@@ -745,9 +770,10 @@ vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_
 }
 
 vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows, int dim,
-                              float eps, cudaStream_t s) {
+                              float eps, cudaStream_t s, void* hi, void* lo) {
     if (rows <= 0 || dim <= 0) return fail(VB_ERR_ARG, "rmsnorm: empty shape");
-    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, dim, eps);
+    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
+                                              static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("rmsnorm_rows_kernel");
     return VB_OK;
 }

@@ -41,7 +41,8 @@ vb_status launch_argmax_parts(const float* part_val, const int* part_idx, int pa
 vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_t* q,
                                float* scales, cudaStream_t s);
 vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows,
-                              int dim, float eps, cudaStream_t s);
+                              int dim, float eps, cudaStream_t s,
+                              void* hi = nullptr, void* lo = nullptr);
 
 // Per-head q/k RMSNorm + RoPE for B sequences, writing rotated q to q_out
 // [B, H, D] and k / v rows into the caches at each sequence's position.
@@ -74,6 +75,8 @@ struct AttnArgs {
     int64_t stride_b, stride_pos, stride_h;
     int splits;            // splits per (b, kvh)
     float* ws;             // partials
+    void* out_hi;          // optional bf16 split of out (tensor-core GEMM operand)
+    void* out_lo;
 };
 int attn_splits_for(int B, int KVH, int n_max);
 size_t attn_ws_bytes(int B, int H, int splits);
@@ -103,6 +106,8 @@ struct GemmArgs {
     int ldc;               // row stride of C in floats
     float* ws;             // split-K partial workspace
     size_t ws_floats;
+    void* out_hi;          // kEpiSwiGLU: optional bf16 split of the output
+    void* out_lo;
 };
 size_t gemm_ws_floats(int M, int N, int K, bool q8);
 vb_status launch_gemm(const GemmArgs& a, bool q8, int epi, cudaStream_t s);
@@ -113,18 +118,30 @@ vb_status launch_gemm_reduce(const GemmArgs& a, int splits, bool q8, int epi, cu
 // Tensor-core projection (vb_tcgemm.cu): partial sums of A . W^T over K
 // splits into ws [splits][M][N], from bf16 operands: W_hi (+ W_lo for f32
 // weights, null for INT8), A_hi + A_lo ([64][K], rows >= M zero).
+// The K splits are summed in fixed order, the INT8 row scales applied (when
+// `scales` is set) and the epilogue written into C: kEpiStore C[m][n] = v,
+// kEpiResidual C[m][n] += v, kEpiSwiGLU (rows interleaved gate/up)
+// C[m][n/2] = silu(v_n) * v_n+1, also written as a bf16 split to
+// out_hi/out_lo when set (the next GEMM's operand).
 struct TcGemmArgs {
     const void* w_hi;
     const void* w_lo;
     const void* a_hi;
     const void* a_lo;
     int M, N, K;
-    float* ws;
+    float* ws;             // split partials
     size_t ws_floats;
+    const float* scales;
+    float* C;
+    int ldc;
+    int epi;
+    void* out_hi;
+    void* out_lo;
     int* err;
 };
 int tc_gemm_splits(int N, int K);
 size_t tc_gemm_ws_floats(int M, int N, int K);
+int tc_gemm_tiles(int N);
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
 vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s);
 vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, void* lo, cudaStream_t s);

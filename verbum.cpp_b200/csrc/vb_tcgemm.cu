@@ -17,9 +17,13 @@
 // ~2^-16 relative, so the result tracks the f32 reference closely.
 //
 // One CTA computes a 128-row weight tile (the MMA's M) against all 64
-// activation rows (the MMA's N) over one K range (split-K); partial sums
-// P[split][m][n] go to global memory and the existing reduce kernels sum the
-// splits in fixed order and apply the scales and epilogues.
+// activation rows (the MMA's N) over one K range (split-K).  With several
+// splits each CTA stores its partial P[split][m][n] and the reduce kernel sums
+// them in split order across the whole GPU (one CTA per tile summing 16
+// splits was measured slower); a single split applies the epilogue itself.
+// Either way the INT8 row scales are applied after the sum, as the reference
+// does, then the epilogue (store, residual add, or SwiGLU with its bf16 split
+// for the next GEMM).
 //
 // Warp 0 lane 0 issues TMA copies into a 4-stage ring, warp 1 lane 0 issues the
 // MMAs (tcgen05.commit frees a stage when its MMAs are done), and all four warps
@@ -53,7 +57,14 @@ struct TcParams {
     int M, N;       // activation rows, weight rows
     int chunks;     // K / kTK
     int per_split;  // chunks per split
+    int splits;
     float* P;       // [splits][M][N]
+    const float* scales;
+    float* C;
+    int ldc;
+    int epi;
+    __nv_bfloat16* out_hi;
+    __nv_bfloat16* out_lo;
     int* err;
 };
 
@@ -206,11 +217,48 @@ __global__ void __launch_bounds__(kTThreads, 1)
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int n = n0 + 32 * warp + lane;
-        if (n < p.N) {
+        bool mine = true;  // a single split applies the epilogue itself
+        if (p.splits > 1) {
+            mine = false;
             float* P = p.P + (size_t)split * p.M * p.N + n;
+            if (n < p.N)
 #pragma unroll
-            for (int m = 0; m < kTN; m++)
-                if (m < p.M) P[(size_t)m * p.N] = v[m];
+                for (int m = 0; m < kTN; m++)
+                    if (m < p.M) P[(size_t)m * p.N] = v[m];
+        }
+        if (mine) {
+            const float sc = (p.scales && n < p.N) ? p.scales[n] : 1.f;
+            if (p.epi == kEpiSwiGLU) {
+                // gate row n (even) and up row n + 1 sit in adjacent lanes
+#pragma unroll
+                for (int m = 0; m < kTN; m++) {
+                    const float val = v[m] * sc;
+                    const float up = __shfl_down_sync(0xffffffffu, val, 1);
+                    if (m < p.M && (lane & 1) == 0 && n + 1 < p.N) {
+                        const float h = silu_f(val) * up;
+                        const size_t o = (size_t)m * p.ldc + (n >> 1);
+                        p.C[o] = h;
+                        if (p.out_hi) {
+                            const __nv_bfloat16 hb = __float2bfloat16_rn(h);
+                            p.out_hi[o] = hb;
+                            p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
+                        }
+                    }
+                }
+            } else if (n < p.N) {
+                float* c = p.C + n;
+                if (p.epi == kEpiResidual) {
+#pragma unroll
+                    for (int m = 0; m < kTN; m++) v[m] = (m < p.M ? c[(size_t)m * p.ldc] : 0.f) + v[m] * sc;
+#pragma unroll
+                    for (int m = 0; m < kTN; m++)
+                        if (m < p.M) c[(size_t)m * p.ldc] = v[m];
+                } else {
+#pragma unroll
+                    for (int m = 0; m < kTN; m++)
+                        if (m < p.M) c[(size_t)m * p.ldc] = v[m] * sc;
+                }
+            }
         }
     } else if (threadIdx.x == 0 && nch > 0) {
         atomicCAS(p.err, 0, kErrPipeTimeout);
@@ -279,6 +327,8 @@ vb_status make_map(CUtensorMap* map, const void* base, int rows, int K, int box_
 
 }  // namespace
 
+int tc_gemm_tiles(int N) { return (N + kTM - 1) / kTM; }
+
 int tc_gemm_splits(int N, int K) {
     const int tiles = (N + kTM - 1) / kTM;
     const int chunks = K / kTK;
@@ -334,18 +384,39 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kTM))) return st;
     if ((st = make_map(&mah, a.a_hi, kTN, a.K, kTN))) return st;
     if ((st = make_map(&mal, a.a_lo, kTN, a.K, kTN))) return st;
+    if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
+    if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
     TcParams p;
     p.M = a.M;
     p.N = a.N;
     p.chunks = a.K / kTK;
     p.per_split = (p.chunks + splits - 1) / splits;
+    p.splits = splits;
     p.P = a.ws;
+    p.scales = a.scales;
+    p.C = a.C;
+    p.ldc = a.ldc;
+    p.epi = a.epi;
+    p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
+    p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
     const dim3 grid((a.N + kTM - 1) / kTM, splits);
     if (wp == 2) tc_gemm_kernel<2><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
     else tc_gemm_kernel<1><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
     VB_LAUNCH_CHECK("tc_gemm_kernel");
-    return VB_OK;
+    if (splits == 1) return VB_OK;
+    GemmArgs g{};
+    g.scales = a.scales;
+    g.C = a.C;
+    g.M = a.M;
+    g.N = a.N;
+    g.K = a.K;
+    g.ldc = a.ldc;
+    g.ws = a.ws;
+    g.ws_floats = a.ws_floats;
+    g.out_hi = a.out_hi;
+    g.out_lo = a.out_lo;
+    return launch_gemm_reduce(g, splits, a.scales != nullptr, a.epi, s);
 }
 
 }  // namespace vb
