@@ -254,9 +254,11 @@ VB_API int vb_engine_graph_nodes(const vb_engine* e);
  * memory as [len, KVH*D] (the reference KVCache layout). */
 VB_API vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host);
 /* Selects the bs1 step implementation: 0 = persistent fused kernel with five
- * grid barriers per layer, 1 = one kernel per op in a CUDA graph (default),
- * 2 = persistent kernel on KV-head clusters with two grid barriers per layer.
- * A fused path whose shape requirements are not met falls back to 1. */
+ * grid barriers per layer, 1 = one kernel per op in a CUDA graph, 2 =
+ * persistent kernel on KV-head thread-block clusters exchanging tagged data
+ * words (no barriers), -1 = automatic (default: 2 for INT8 weights, 0 for
+ * f32, the faster of each on B200).  A fused path whose shape requirements
+ * are not met falls back to 1. */
 VB_API vb_status vb_engine_set_path(vb_engine* e, int path);
 /* The stream the engine runs on (a cudaStream_t). */
 VB_API void* vb_engine_stream(vb_engine* e);

@@ -25,11 +25,13 @@ pytestmark = pytest.mark.gpu
 TOL = {"f32": 1e-3, "int8": 1e-2}
 
 
-def make_engine(cfg, w, mode, max_seq):
+def make_engine(cfg, w, mode, max_seq, path=-1):
+    """path -1 = the engine's automatic choice; 1 = the per-op CUDA graph."""
     e = vb200.Engine(cfg).load(w)
     if mode == "int8":
         e.quantize()
     e.reset_cache(max_seq)
+    e.set_path(path)
     return e
 
 
@@ -41,11 +43,12 @@ def mini():
     return meta, fx, w
 
 
+@pytest.mark.parametrize("path", [-1, 1])
 @pytest.mark.parametrize("mode", ["f32", "int8"])
-def test_mini_model_matches_reference_fixture(mini, mode):
+def test_mini_model_matches_reference_fixture(mini, mode, path):
     meta, fx, w = mini
     cfg = meta["config"]
-    e = make_engine(cfg, w, mode, meta["prompt_len"] + meta["greedy"] + 8)
+    e = make_engine(cfg, w, mode, meta["prompt_len"] + meta["greedy"] + 8, path)
     assert e.weight_bytes() == int(fx[f"weight_bytes_{mode}"])
     steps = [int(t) for t in fx["prompt"]] + [int(t) for t in fx[f"tokens_{mode}"][:-1]]
     for i, t in enumerate(steps):
@@ -56,8 +59,9 @@ def test_mini_model_matches_reference_fixture(mini, mode):
     e.close()
 
 
+@pytest.mark.parametrize("path", [-1, 1])
 @pytest.mark.parametrize("mode", ["f32", "int8"])
-def test_decode_equals_step_loop_and_oracle(mode):
+def test_decode_equals_step_loop_and_oracle(mode, path):
     cfg = mini_config()
     w = vbsynth.make_weights(cfg, seed=31)
     prompt = vbsynth.prompt_ids(6, 3, cfg["vocab_size"])
@@ -73,7 +77,7 @@ def test_decode_equals_step_loop_and_oracle(mode):
         ref_toks.append(nxt)
         lg = orc.step(nxt)
     # step() loop
-    e = make_engine(cfg, w, mode, 64)
+    e = make_engine(cfg, w, mode, 64, path)
     for t in prompt:
         glg = e.step(int(t))
     toks = []

@@ -128,4 +128,30 @@ enum : int {
     kErrCacheFull = 4,
 };
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch: kernels on the decode paths are launched so
+// that the next kernel can start (be scheduled, run its prologue) while its
+// predecessor drains.  Each such kernel calls pdl_trigger() (lets its own
+// successor launch once every CTA got here) and pdl_wait() before it touches
+// anything an earlier kernel wrote; launched the ordinary way, both are
+// no-ops.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace vb

@@ -38,7 +38,8 @@ struct vb_engine {
     int device = 0;
     cudaStream_t stream = nullptr;
     bool quantized = false;
-    int path = 1;
+    int path = 1;          // effective step path (0, 1, 2)
+    bool path_auto = true; // pick the path per weight format at graph build
 
     // sizes
     int qkv_rows = 0;    // (H + 2 KVH) * D

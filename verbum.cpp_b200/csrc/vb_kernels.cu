@@ -49,6 +49,8 @@ __device__ __forceinline__ int xs_index(int i) {
 // ---------------------------------------------------------------------------
 template <bool Q8, int R, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) float xs[];
     __shared__ double red[kGemvWarps];
     __shared__ float sbv[kGemvWarps];
@@ -214,6 +216,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
 }
 
 __global__ void argmax_parts_kernel(const float* pv, const int* pi, int parts, int* out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     float bv = -INFINITY;
@@ -240,6 +244,8 @@ __global__ void argmax_parts_kernel(const float* pv, const int* pi, int parts, i
 
 // One block per row of logits.
 __global__ void argmax_rows_kernel(const float* logits, int64_t n, int* out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float* row = logits + (size_t)blockIdx.x * (size_t)n;
@@ -304,6 +310,8 @@ __global__ void quantize_rows_kernel(const float* W, int64_t rows, int64_t cols,
 // the tensor-core GEMM's activation operand, rows of `dim`.
 __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, int dim, float eps,
                                     __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ double red[8];
     const float* xr = x + (size_t)blockIdx.x * dim;
     float* orow = out + (size_t)blockIdx.x * dim;
@@ -328,6 +336,8 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
 // split-half RoPE from the host table, k and v rows written at pos[b].
 // grid (H + KVH, B), block D (= 128).
 __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const float eps = a.eps;
     __shared__ double red[4];
     __shared__ float ys[128];
@@ -379,6 +389,8 @@ constexpr int kAttnPB = 4;  // positions per warp iteration
 
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int n = a.lens ? a.lens[b] : a.pos[b] + 1;
@@ -482,6 +494,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
 
 // grid (H, B), block 128: merges the splits of one (b, h).
 __global__ void attn_merge_kernel(AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int S = a.splits;
     const float* base = a.ws + ((size_t)b * a.H + h) * S * (128 + 2);
@@ -507,6 +521,8 @@ __global__ void attn_merge_kernel(AttnArgs a) {
 
 __global__ void embed_kernel(const float* E, const int* tokens, int dim, int vocab, float* out,
                              int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x;
     int tok = tokens[b];
     if (tok < 0 || tok >= vocab) {
@@ -519,6 +535,8 @@ __global__ void embed_kernel(const float* E, const int* tokens, int dim, int voc
 }
 
 __global__ void advance_kernel(int* pos, int* tokens, const int* next, int B) {
+    pdl_trigger();
+    pdl_wait();
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
         pos[b] += 1;
         if (tokens && next) tokens[b] = next[b];
@@ -641,6 +659,8 @@ __global__ void __launch_bounds__(256) gemm_partial_kernel(GemmArgs a, int kper)
 // Sums the split partials in fixed order and applies the epilogue.
 template <bool Q8, int EPI>
 __global__ void gemm_reduce_kernel(GemmArgs a, int splits) {
+    pdl_trigger();
+    pdl_wait();
     const int M = a.M, N = a.N;
     const int outN = (EPI == kEpiSwiGLU) ? N / 2 : N;
     const size_t total = (size_t)M * outN;
@@ -708,12 +728,12 @@ template <bool Q8, int R, int PRO>
 static void gemv_dispatch_epi(const GemvArgs& a, int epi, int grid, size_t smem,
                               cudaStream_t s) {
     switch (epi) {
-        case kEpiStore: gemv_kernel<Q8, R, PRO, kEpiStore><<<grid, kGemvThreads, smem, s>>>(a); break;
-        case kEpiResidual: gemv_kernel<Q8, R, PRO, kEpiResidual><<<grid, kGemvThreads, smem, s>>>(a); break;
+        case kEpiStore: launch_pdl(gemv_kernel<Q8, R, PRO, kEpiStore>, grid, kGemvThreads, smem, s, a); break;
+        case kEpiResidual: launch_pdl(gemv_kernel<Q8, R, PRO, kEpiResidual>, grid, kGemvThreads, smem, s, a); break;
         case kEpiSwiGLU:  // launch_gemv only picks even R for this epilogue
-            gemv_kernel<Q8, (R % 2 == 0 ? R : 2), PRO, kEpiSwiGLU><<<grid, kGemvThreads, smem, s>>>(a);
+            launch_pdl(gemv_kernel<Q8, (R % 2 == 0 ? R : 2), PRO, kEpiSwiGLU>, grid, kGemvThreads, smem, s, a);
             break;
-        default: gemv_kernel<Q8, R, PRO, kEpiArgmax><<<grid, kGemvThreads, smem, s>>>(a); break;
+        default: launch_pdl(gemv_kernel<Q8, R, PRO, kEpiArgmax>, grid, kGemvThreads, smem, s, a); break;
     }
 }
 
@@ -747,7 +767,7 @@ vb_status launch_gemv(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t
 
 vb_status launch_argmax_parts(const float* pv, const int* pi, int parts, int* out,
                               cudaStream_t s) {
-    argmax_parts_kernel<<<1, 1024, 0, s>>>(pv, pi, parts, out);
+    launch_pdl(argmax_parts_kernel, 1, 1024, 0, s, pv, pi, parts, out);
     VB_LAUNCH_CHECK("argmax_parts_kernel");
     return VB_OK;
 }
@@ -755,7 +775,7 @@ vb_status launch_argmax_parts(const float* pv, const int* pi, int parts, int* ou
 vb_status launch_argmax_rows(const float* logits, int rows, int64_t n, int* out,
                              cudaStream_t s) {
     if (rows <= 0 || n <= 0) return fail(VB_ERR_ARG, "argmax: empty input");
-    argmax_rows_kernel<<<rows, 1024, 0, s>>>(logits, n, out);
+    launch_pdl(argmax_rows_kernel, rows, 1024, 0, s, logits, n, out);
     VB_LAUNCH_CHECK("argmax_rows_kernel");
     return VB_OK;
 }
@@ -772,8 +792,8 @@ vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_
 vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows, int dim,
                               float eps, cudaStream_t s, void* hi, void* lo) {
     if (rows <= 0 || dim <= 0) return fail(VB_ERR_ARG, "rmsnorm: empty shape");
-    rmsnorm_rows_kernel<<<rows, 256, 0, s>>>(x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
-                                              static_cast<__nv_bfloat16*>(lo));
+    launch_pdl(rmsnorm_rows_kernel, rows, 256, 0, s, x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
+               static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("rmsnorm_rows_kernel");
     return VB_OK;
 }
@@ -781,7 +801,7 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
 vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
     dim3 grid(a.H + a.KVH, a.B);
-    qk_norm_rope_kernel<<<grid, 128, 0, s>>>(a);
+    launch_pdl(qk_norm_rope_kernel, grid, 128, 0, s, a);
     VB_LAUNCH_CHECK("qk_norm_rope_kernel");
     return VB_OK;
 }
@@ -807,13 +827,13 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
     const int G = a.H / a.KVH;
     dim3 grid(a.splits, a.KVH, a.B);
     switch (G) {
-        case 1: attn_split_kernel<1><<<grid, kAttnThreads, 0, s>>>(a); break;
-        case 2: attn_split_kernel<2><<<grid, kAttnThreads, 0, s>>>(a); break;
-        case 4: attn_split_kernel<4><<<grid, kAttnThreads, 0, s>>>(a); break;
+        case 1: launch_pdl(attn_split_kernel<1>, grid, kAttnThreads, 0, s, a); break;
+        case 2: launch_pdl(attn_split_kernel<2>, grid, kAttnThreads, 0, s, a); break;
+        case 4: launch_pdl(attn_split_kernel<4>, grid, kAttnThreads, 0, s, a); break;
         default: return fail(VB_ERR_UNSUPPORTED, "attention: GQA group must be 1, 2 or 4");
     }
     VB_LAUNCH_CHECK("attn_split_kernel");
-    attn_merge_kernel<<<dim3(a.H, a.B), 128, 0, s>>>(a);
+    launch_pdl(attn_merge_kernel, dim3(a.H, a.B), 128, 0, s, a);
     VB_LAUNCH_CHECK("attn_merge_kernel");
     return VB_OK;
 }
@@ -821,13 +841,13 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
 vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
                        float* out, int* err, cudaStream_t s) {
     if (dim % 4) return fail(VB_ERR_UNSUPPORTED, "embed: dim % 4");
-    embed_kernel<<<B, 256, 0, s>>>(E, tokens, dim, vocab, out, err);
+    launch_pdl(embed_kernel, B, 256, 0, s, E, tokens, dim, vocab, out, err);
     VB_LAUNCH_CHECK("embed_kernel");
     return VB_OK;
 }
 
 vb_status launch_advance(int* pos, int* tokens, const int* next, int B, cudaStream_t s) {
-    advance_kernel<<<1, 128, 0, s>>>(pos, tokens, next, B);
+    launch_pdl(advance_kernel, 1, 128, 0, s, pos, tokens, next, B);
     VB_LAUNCH_CHECK("advance_kernel");
     return VB_OK;
 }
@@ -889,7 +909,7 @@ vb_status launch_gemm_reduce(const GemmArgs& a, int splits, bool q8, int epi, cu
     const size_t total = (size_t)a.M * outN;
     int rb = (int)((total + 255) / 256);
     if (rb > kNumSMs * 8) rb = kNumSMs * 8;
-#define VB_RED(Q, E) gemm_reduce_kernel<Q, E><<<rb, 256, 0, s>>>(a, splits)
+#define VB_RED(Q, E) launch_pdl(gemm_reduce_kernel<Q, E>, rb, 256, 0, s, a, splits)
     if (q8) {
         if (epi == kEpiResidual) VB_RED(true, kEpiResidual);
         else if (epi == kEpiSwiGLU) VB_RED(true, kEpiSwiGLU);

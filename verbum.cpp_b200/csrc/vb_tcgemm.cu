@@ -138,26 +138,45 @@ __global__ void __launch_bounds__(kTThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const unsigned tmem = tmem_slot;
+    pdl_trigger();
 
     if (warp == 0 && lane == 0 && nch > 0) {
         // ------------------------------------------------------ TMA producer
-        int issued = 0;
-        for (int i = 0; i < nch; i++) {
-            const int s = i % kTStages;
-            if (!mbar_wait(smem_addr(&empty[s]), ((unsigned)(i / kTStages) & 1u) ^ 1u, p.err, nullptr, kSiteEmpty, i)) {
-                fail = 1;
-                break;
-            }
-            const unsigned st = sbase + (unsigned)s * kTStage;
-            const unsigned fb = smem_addr(&full[s]);
+        // The weights do not depend on the previous kernel: the first stages'
+        // weight tiles are requested before waiting for it, the activation
+        // tiles after.
+        const int pre = min(nch, kTStages);
+        for (int i = 0; i < pre; i++) {
+            const unsigned st = sbase + (unsigned)i * kTStage;
+            const unsigned fb = smem_addr(&full[i]);
             mbar_expect_tx(fb, (unsigned)(WP * kWTile + 2 * kATile));
             const int x = (c0 + i) * kTK;
             tma_load_2d(st, &tw_hi, x, n0, fb);
             if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
+        }
+        pdl_wait();
+        int issued = 0;
+        for (int i = 0; i < nch; i++) {
+            const int s = i % kTStages;
+            const unsigned st = sbase + (unsigned)s * kTStage;
+            const unsigned fb = smem_addr(&full[s]);
+            const int x = (c0 + i) * kTK;
+            if (i >= pre) {
+                if (!mbar_wait(smem_addr(&empty[s]), ((unsigned)(i / kTStages) & 1u) ^ 1u, p.err, nullptr, kSiteEmpty,
+                               i)) {
+                    fail = 1;
+                    break;
+                }
+                mbar_expect_tx(fb, (unsigned)(WP * kWTile + 2 * kATile));
+                tma_load_2d(st, &tw_hi, x, n0, fb);
+                if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
+            }
             tma_load_2d(st + 2 * kWTile, &ta_hi, x, 0, fb);
             tma_load_2d(st + 2 * kWTile + kATile, &ta_lo, x, 0, fb);
             issued = i + 1;
         }
+        // a stage whose weights went out before a failure still has its copies in flight
+        if (issued < pre) issued = pre;
         // never leave with copies in flight
         for (int i = issued > kTStages ? issued - kTStages : 0; i < issued; i++)
             mbar_wait(smem_addr(&full[i % kTStages]), (unsigned)(i / kTStages) & 1u, p.err, nullptr, kSiteFull, i);
@@ -189,6 +208,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
     // -------------------------------------------------------------- epilogue
     __syncwarp();
+    pdl_wait();  // partials and outputs are read / written by neighbouring kernels
     bool ok = nch > 0;
     if (ok) {
         ok = mbar_wait(smem_addr(&done), 0u, p.err, nullptr, kSiteFull, -1);
@@ -401,9 +421,9 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
     const dim3 grid((a.N + kTM - 1) / kTM, splits);
-    if (wp == 2) tc_gemm_kernel<2><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
-    else tc_gemm_kernel<1><<<grid, kTThreads, kTSmem, s>>>(mwh, mwl, mah, mal, p);
-    VB_LAUNCH_CHECK("tc_gemm_kernel");
+    const cudaError_t ce = wp == 2 ? launch_pdl(tc_gemm_kernel<2>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p)
+                                   : launch_pdl(tc_gemm_kernel<1>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p);
+    if (ce != cudaSuccess) return cuda_fail(ce, "tc_gemm_kernel launch");
     if (splits == 1) return VB_OK;
     GemmArgs g{};
     g.scales = a.scales;
