@@ -50,6 +50,17 @@ __device__ __forceinline__ int xs_index(int i) {
 template <bool Q8, int R, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     pdl_trigger();
+    {
+        // The weights do not depend on the previous kernel: while it drains,
+        // pull this warp's first row group into L2 (one bulk prefetch per row).
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int g0 = blockIdx.x * kGemvWarps + warp;
+        const size_t row_bytes = (size_t)a.K * (Q8 ? 1 : 4);
+        if (lane < R && g0 * R + lane < a.N && (row_bytes & 15) == 0) {
+            const char* row = static_cast<const char*>(a.W) + (size_t)(g0 * R + lane) * row_bytes;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row), "r"((unsigned)row_bytes) : "memory");
+        }
+    }
     pdl_wait();
     extern __shared__ __align__(16) float xs[];
     __shared__ double red[kGemvWarps];
