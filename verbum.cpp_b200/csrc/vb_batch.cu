@@ -127,7 +127,7 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     const size_t layer_kv = per_seq * B;
     // C (epilogue) A . W^T on the tensor cores from A's bf16 split (ahi, alo)
     auto gemm = [&](const void* ahi, const void* alo, void* const* w, const float* sc, float* C, int N, int K,
-                    int ldc, int epi, bool wq8, void* ohi, void* olo) {
+                    int ldc, int epi, bool wq8, void* ohi, void* olo, bool partials = false) {
         TcGemmArgs t{};
         t.w_hi = w[0];
         t.w_lo = wq8 ? nullptr : w[1];
@@ -144,18 +144,26 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         t.epi = epi;
         t.out_hi = ohi;
         t.out_lo = olo;
+        t.partials_only = partials;
         t.err = b->d_err;
         return launch_tc_gemm(t, s);
     };
+    // Split-K partials of the q|k|v, o and down projections are left in the
+    // GEMM workspace and summed by their consumer: q/k-norm + RoPE + append,
+    // and residual add + the next RMSNorm (nn.cpp:8-42) + bf16 split.
+    const float* parts = b->gemm_ws;
+    if ((st = launch_rmsnorm_rows(b->x, e->L[0].in_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo)))
+        return st;
     for (int l = 0; l < c.layers; l++) {
         const vb_layer_dev& L = e->L[l];
         void* const* tw = &b->tcw[(size_t)l * 8];
-        if ((st = launch_rmsnorm_rows(b->x, L.in_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo))) return st;
-        if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, b->qkv, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8,
-                       nullptr, nullptr)))
+        if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, nullptr, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8,
+                       nullptr, nullptr, true)))
             return st;
         QkNormArgs qa{};
-        qa.qkv = b->qkv;
+        qa.parts = parts;
+        qa.splits = tc_gemm_splits(e->qkv_rows, c.hidden);
+        qa.scales = q8 ? L.sqkv : nullptr;
         qa.q_norm = L.q_norm;
         qa.k_norm = L.k_norm;
         qa.cos_tab = e->rope_cos;
@@ -194,19 +202,23 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         aa.out_hi = b->y_hi;
         aa.out_lo = b->y_lo;
         if ((st = launch_attention(aa, s))) return st;
-        if ((st = gemm(b->y_hi, b->y_lo, tw + 2, L.so, b->x, c.hidden, e->q_width, c.hidden, kEpiResidual, q8,
-                       nullptr, nullptr)))
+        if ((st = gemm(b->y_hi, b->y_lo, tw + 2, L.so, nullptr, c.hidden, e->q_width, c.hidden, kEpiResidual, q8,
+                       nullptr, nullptr, true)))
             return st;
-        if ((st = launch_rmsnorm_rows(b->x, L.post_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo)))
+        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, e->q_width), q8 ? L.so : nullptr,
+                                              L.post_norm, b->xn, b->a_hi, b->a_lo, B, c.hidden, c.eps, s)))
             return st;
         if ((st = gemm(b->a_hi, b->a_lo, tw + 4, L.sgu, b->h, 2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8, b->y_hi,
                        b->y_lo)))
             return st;
-        if ((st = gemm(b->y_hi, b->y_lo, tw + 6, L.sd, b->x, c.hidden, c.ffn, c.hidden, kEpiResidual, q8, nullptr,
-                       nullptr)))
+        if ((st = gemm(b->y_hi, b->y_lo, tw + 6, L.sd, nullptr, c.hidden, c.ffn, c.hidden, kEpiResidual, q8, nullptr,
+                       nullptr, true)))
+            return st;
+        const float* next_norm = l + 1 < c.layers ? e->L[l + 1].in_norm : e->final_norm;
+        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, c.ffn), q8 ? L.sd : nullptr,
+                                              next_norm, b->xn, b->a_hi, b->a_lo, B, c.hidden, c.eps, s)))
             return st;
     }
-    if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo))) return st;
     {
         void* const lm[2] = {b->lm_hi, b->lm_lo};
         if ((st = gemm(b->a_hi, b->a_lo, lm, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore, false,

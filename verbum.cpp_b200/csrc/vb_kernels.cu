@@ -343,6 +343,38 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
     }
 }
 
+// Split-K reduce of a residual projection fused with the following RMSNorm
+// (nn.cpp:8-42): x[b][i] += (sum_s parts[s][b][i]) * scale[i], then the normed
+// row and its bf16 split.  grid rows, block 256.
+__global__ void reduce_residual_norm_kernel(float* x, const float* parts, int splits, const float* scales,
+                                            const float* w, float* out, int rows, int dim, float eps,
+                                            __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ double red[8];
+    const int b = blockIdx.x;
+    float* xr = x + (size_t)b * dim;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        float v = 0.f;
+        for (int q = 0; q < splits; q++) v += parts[((size_t)q * rows + b) * dim + i];
+        if (scales) v *= scales[i];
+        const float xv = xr[i] + v;
+        xr[i] = xv;
+        ss += (double)xv * (double)xv;
+    }
+    const float sc = rms_scale(block_sum_d<256>(ss, red), dim, eps);
+    for (int i = threadIdx.x; i < dim; i += 256) {
+        const float y = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
+        out[(size_t)b * dim + i] = y;
+        if (hi) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(y);
+            hi[(size_t)b * dim + i] = h;
+            lo[(size_t)b * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+        }
+    }
+}
+
 // generate.cpp:52-71 for B sequences: per-head RMSNorm (q_norm / k_norm),
 // split-half RoPE from the host table, k and v rows written at pos[b].
 // grid (H + KVH, B), block D (= 128).
@@ -359,13 +391,29 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
         if (d == 0 && a.err) atomicExch(a.err, kErrCacheFull);
         return;
     }
-    const int QW = a.H * D, KW = a.KVH * D;
-    const float* row = a.qkv + (size_t)b * (QW + 2 * KW);
+    const int QW = a.H * D, KW = a.KVH * D, RW = QW + 2 * KW;
     const bool isq = hd < a.H;
     const int h = isq ? hd : hd - a.H;
-    const float* src = isq ? row + h * D : row + QW + h * D;
+    const int col = isq ? h * D + d : QW + h * D + d;
+    // the q or k value of this thread, and (k heads) the v value of the same head
+    float xv, vv = 0.f;
+    if (a.parts) {
+        xv = 0.f;
+        for (int q = 0; q < a.splits; q++) {
+            const float* pr = a.parts + ((size_t)q * a.B + b) * RW;
+            xv += pr[col];
+            if (!isq) vv += pr[QW + KW + h * D + d];
+        }
+        if (a.scales) {
+            xv *= a.scales[col];
+            vv *= a.scales[QW + KW + h * D + d];
+        }
+    } else {
+        const float* row = a.qkv + (size_t)b * RW;
+        xv = row[col];
+        if (!isq) vv = row[QW + KW + h * D + d];
+    }
     const float* nw = isq ? a.q_norm : a.k_norm;
-    const float xv = src[d];
     const float sc = rms_scale(block_sum_d<128>((double)xv * (double)xv, red), D, eps);
     ys[d] = __fmul_rn(__fmul_rn(xv, sc), nw[d]);
     __syncthreads();
@@ -383,7 +431,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
         const size_t off = (size_t)b * a.stride_b + (size_t)pos * a.stride_pos +
                            (size_t)h * a.stride_h + d;
         a.kc[off] = o;
-        a.vc[off] = row[QW + KW + h * D + d];
+        a.vc[off] = vv;
     }
 }
 
@@ -806,6 +854,16 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
     launch_pdl(rmsnorm_rows_kernel, rows, 256, 0, s, x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
                static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("rmsnorm_rows_kernel");
+    return VB_OK;
+}
+
+vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, const float* scales,
+                                      const float* w, float* out, void* hi, void* lo, int rows, int dim,
+                                      float eps, cudaStream_t s) {
+    if (rows <= 0 || dim <= 0 || splits <= 0) return fail(VB_ERR_ARG, "reduce_residual_norm: bad shape");
+    const cudaError_t ce = launch_pdl(reduce_residual_norm_kernel, rows, 256, 0, s, x, parts, splits, scales, w, out,
+                                      rows, dim, eps, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+    if (ce != cudaSuccess) return cuda_fail(ce, "reduce_residual_norm_kernel launch");
     return VB_OK;
 }
 

@@ -48,6 +48,9 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
 // [B, H, D] and k / v rows into the caches at each sequence's position.
 struct QkNormArgs {
     const float* qkv;       // [B, (H + 2*KVH) * D]  (q | k | v)
+    const float* parts;     // or, when set: split-K partials [splits][B][(H + 2*KVH) * D]
+    int splits;             //   summed in split order,
+    const float* scales;    //   times these INT8 row scales when set
     const float* q_norm;    // [D]
     const float* k_norm;    // [D]
     const float* cos_tab;   // [rope_positions, D]
@@ -62,6 +65,13 @@ struct QkNormArgs {
     int* err;               // device error word (may be null)
 };
 vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s);
+
+// x[b] += sum_s parts[s][b] (x scales), then out[b] = RMSNorm(x[b]) . w and its
+// bf16 split (hi, lo) -- the split-K reduce of a residual projection fused
+// with the next RMSNorm.  One block per row.
+vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, const float* scales,
+                                      const float* w, float* out, void* hi, void* lo, int rows, int dim,
+                                      float eps, cudaStream_t s);
 
 // Split-K decode attention.  lens[b] = number of valid cache rows.
 struct AttnArgs {
@@ -137,6 +147,7 @@ struct TcGemmArgs {
     int epi;
     void* out_hi;
     void* out_lo;
+    bool partials_only;    // leave the split partials in ws for a fused consumer
     int* err;
 };
 int tc_gemm_splits(int N, int K);

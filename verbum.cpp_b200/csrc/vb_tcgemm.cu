@@ -58,6 +58,7 @@ struct TcParams {
     int chunks;     // K / kTK
     int per_split;  // chunks per split
     int splits;
+    int partials;   // write P even for one split (a fused consumer reads it)
     float* P;       // [splits][M][N]
     const float* scales;
     float* C;
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int n = n0 + 32 * warp + lane;
         bool mine = true;  // a single split applies the epilogue itself
-        if (p.splits > 1) {
+        if (p.splits > 1 || p.partials) {
             mine = false;
             float* P = p.P + (size_t)split * p.M * p.N + n;
             if (n < p.N)
@@ -404,7 +405,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kTM))) return st;
     if ((st = make_map(&mah, a.a_hi, kTN, a.K, kTN))) return st;
     if ((st = make_map(&mal, a.a_lo, kTN, a.K, kTN))) return st;
-    if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
+    if (!a.C && !a.partials_only) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
     if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
     TcParams p;
     p.M = a.M;
@@ -412,6 +413,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.chunks = a.K / kTK;
     p.per_split = (p.chunks + splits - 1) / splits;
     p.splits = splits;
+    p.partials = a.partials_only ? 1 : 0;
     p.P = a.ws;
     p.scales = a.scales;
     p.C = a.C;
@@ -424,7 +426,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     const cudaError_t ce = wp == 2 ? launch_pdl(tc_gemm_kernel<2>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p)
                                    : launch_pdl(tc_gemm_kernel<1>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p);
     if (ce != cudaSuccess) return cuda_fail(ce, "tc_gemm_kernel launch");
-    if (splits == 1) return VB_OK;
+    if (splits == 1 || a.partials_only) return VB_OK;
     GemmArgs g{};
     g.scales = a.scales;
     g.C = a.C;
