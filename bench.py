@@ -220,6 +220,7 @@ def run_batched(args, grp, weights, cfg):
         if grp.rank == 0 else None
     grp.barrier()
     torch.cuda.synchronize()
+    nx0, len0 = nx.copy(), bt.cache_len()
     ev0.record(stream)
     nx = bt.decode(nx, K)
     ev1.record(stream)
@@ -227,13 +228,20 @@ def run_batched(args, grp, weights, cfg):
     torch.cuda.synchronize()
     grp.barrier()
     ms = ev0.elapsed_time(ev1)
-    # end to end through the C ABI with host buffers: tokens in, next tokens out
+    nx_dev = nx.copy()
+    # end to end through the C ABI with host buffers (tokens in, next tokens
+    # out, one call per step) over the same K steps: the caches are rolled
+    # back to where the device-timed run started
+    bt.truncate(len0)
+    nx = nx0
     grp.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(K):
         _, nx = bt.step(nx, want_logits=False, want_next=True)
     e2e_s = time.perf_counter() - t0
+    if not np.array_equal(nx, nx_dev):
+        raise SystemExit("batched decode: per-step API and device loop disagree")
     grp.barrier()
     clocks = clk.stop() if clk else None
     ms_max = grp.reduce_max(ms)

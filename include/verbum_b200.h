@@ -293,6 +293,10 @@ VB_API vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, in
 VB_API int vb_batch_graph_nodes(const vb_batch* b);
 VB_API int vb_batch_cache_len(const vb_batch* b);
 VB_API vb_status vb_batch_reset(vb_batch* b);
+/* Roll every sequence back to len cached positions (0 <= len <= cache length):
+ * the next step writes position len.  Cached entries past len are left in
+ * place and overwritten before they are read again. */
+VB_API vb_status vb_batch_truncate(vb_batch* b, int len);
 
 #ifdef __cplusplus
 }

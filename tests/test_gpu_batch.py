@@ -54,6 +54,13 @@ def test_batch_matches_per_sequence_oracle(mode):
     nx2 = bt.prefill(prompts.T.copy())
     assert np.array_equal(nx2, nx)
     assert bt.cache_len() == P
+    # rolled back to P positions, the same continuation comes out again
+    bt.decode(nx, 3)
+    bt.truncate(P)
+    assert bt.cache_len() == P
+    assert np.array_equal(bt.decode(nx, G), nxt)
+    with pytest.raises(vb200.VBError):
+        bt.truncate(P + G + 1)
     bt.close()
     eng.close()
 

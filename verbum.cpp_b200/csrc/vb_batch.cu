@@ -38,7 +38,7 @@ struct vb_batch {
     int* d_pos = nullptr;
     int* d_next = nullptr;
     int* d_err = nullptr;
-    int* h_io = nullptr;  // pinned [2*B]
+    int* h_io = nullptr;  // pinned [2*B + 1]: tokens in, next tokens out, error word
     cudaGraphExec_t graph = nullptr;
     bool graph_q8 = false;
     int graph_nodes = 0;
@@ -162,7 +162,7 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
             return st;
         QkNormArgs qa{};
         qa.parts = parts;
-        qa.splits = tc_gemm_splits(e->qkv_rows, c.hidden);
+        qa.splits = tc_gemm_splits(e->qkv_rows, c.hidden, !q8);
         qa.scales = q8 ? L.sqkv : nullptr;
         qa.q_norm = L.q_norm;
         qa.k_norm = L.k_norm;
@@ -205,7 +205,7 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         if ((st = gemm(b->y_hi, b->y_lo, tw + 2, L.so, nullptr, c.hidden, e->q_width, c.hidden, kEpiResidual, q8,
                        nullptr, nullptr, true)))
             return st;
-        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, e->q_width), q8 ? L.so : nullptr,
+        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, e->q_width, !q8), q8 ? L.so : nullptr,
                                               L.post_norm, b->xn, b->a_hi, b->a_lo, B, c.hidden, c.eps, s)))
             return st;
         if ((st = gemm(b->a_hi, b->a_lo, tw + 4, L.sgu, b->h, 2 * c.ffn, c.hidden, c.ffn, kEpiSwiGLU, q8, b->y_hi,
@@ -215,7 +215,7 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
                        nullptr, true)))
             return st;
         const float* next_norm = l + 1 < c.layers ? e->L[l + 1].in_norm : e->final_norm;
-        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, c.ffn), q8 ? L.sd : nullptr,
+        if ((st = launch_reduce_residual_norm(b->x, parts, tc_gemm_splits(c.hidden, c.ffn, !q8), q8 ? L.sd : nullptr,
                                               next_norm, b->xn, b->a_hi, b->a_lo, B, c.hidden, c.eps, s)))
             return st;
     }
@@ -254,12 +254,14 @@ vb_status batch_graph(vb_batch* b) {
         return cuda_fail(ce, "cudaGraphInstantiate");
     }
     b->graph_q8 = b->e->quantized;
+    // upload now so the first launch does not pay for it
+    ce = cudaGraphUpload(b->graph, s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphUpload");
     return VB_OK;
 }
 
-vb_status batch_check_err(vb_batch* b) {
-    int err = 0;
-    VB_CUDA_TRY(cudaMemcpy(&err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+// Maps the device error word (read by the caller after its stream sync) to a status.
+vb_status batch_err_status(vb_batch* b, int err) {
     if (!err) return VB_OK;
     cudaMemsetAsync(b->d_err, 0, sizeof(int), b->e->stream);
     cudaStreamSynchronize(b->e->stream);
@@ -357,7 +359,7 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
         cudaMemsetAsync(b->d_tok, 0, sizeof(int) * batch, es) ||
         cudaMemsetAsync(b->d_err, 0, sizeof(int), es) || cudaStreamSynchronize(es))
         return bail(fail(VB_ERR_CUDA, "batch state init failed"));
-    if (cudaMallocHost(&b->h_io, sizeof(int) * 2 * batch) != cudaSuccess)
+    if (cudaMallocHost(&b->h_io, sizeof(int) * (2 * batch + 1)) != cudaSuccess)
         return bail(fail(VB_ERR_CUDA, "cudaMallocHost failed"));
     *out = b;
     return VB_OK;
@@ -408,8 +410,9 @@ vb_status vb_batch_step(vb_batch* b, const int* tokens_host, float* logits_host,
     if (next_host)
         VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
                                     cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + 2 * b->B, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     VB_CUDA_TRY(cudaStreamSynchronize(s));
-    if ((st = batch_check_err(b))) return st;
+    if ((st = batch_err_status(b, b->h_io[2 * b->B]))) return st;
     if (next_host)
         for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
     b->len += 1;
@@ -435,8 +438,9 @@ vb_status vb_batch_decode(vb_batch* b, const int* tokens_host, int n, int* next_
     if (next_host)
         VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
                                     cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + 2 * b->B, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     VB_CUDA_TRY(cudaStreamSynchronize(s));
-    if ((st = batch_check_err(b))) return st;
+    if ((st = batch_err_status(b, b->h_io[2 * b->B]))) return st;
     if (next_host)
         for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
     b->len += n;
@@ -468,8 +472,9 @@ vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, int* next
     if (next_host)
         VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
                                     cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + 2 * b->B, b->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     VB_CUDA_TRY(cudaStreamSynchronize(s));
-    if ((st = batch_check_err(b))) return st;
+    if ((st = batch_err_status(b, b->h_io[2 * b->B]))) return st;
     if (next_host)
         for (int i = 0; i < b->B; i++) next_host[i] = b->h_io[b->B + i];
     b->len += P;
@@ -491,6 +496,20 @@ vb_status vb_batch_reset(vb_batch* b) {
     VB_CUDA_TRY(cudaMemsetAsync(b->d_pos, 0, sizeof(int) * b->B, b->e->stream));
     VB_CUDA_TRY(cudaStreamSynchronize(b->e->stream));
     b->len = 0;
+    return VB_OK;
+}
+
+vb_status vb_batch_truncate(vb_batch* b, int len) {
+    if (!b) return fail(VB_ERR_ARG, "null batch");
+    if (len < 0 || len > b->len) return fail(VB_ERR_ARG, "truncate: length outside [0, cache length]");
+    Dev dg(b->e->device);
+    cudaStream_t s = b->e->stream;
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    // positions >= len are overwritten before attention reads them again
+    for (int i = 0; i < b->B; i++) b->h_io[i] = len;
+    VB_CUDA_TRY(cudaMemcpyAsync(b->d_pos, b->h_io, sizeof(int) * b->B, cudaMemcpyHostToDevice, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    b->len = len;
     return VB_OK;
 }
 

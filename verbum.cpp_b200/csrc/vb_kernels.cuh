@@ -150,7 +150,8 @@ struct TcGemmArgs {
     bool partials_only;    // leave the split partials in ws for a fused consumer
     int* err;
 };
-int tc_gemm_splits(int N, int K);
+// split-K factor of a tensor-core GEMM (pair: f32 weights as a bf16 pair)
+int tc_gemm_splits(int N, int K, bool pair);
 size_t tc_gemm_ws_floats(int M, int N, int K);
 int tc_gemm_tiles(int N);
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);

@@ -25,7 +25,7 @@
 // does, then the epilogue (store, residual add, or SwiGLU with its bf16 split
 // for the next GEMM).
 //
-// Warp 0 lane 0 issues TMA copies into a 4-stage ring, warp 1 lane 0 issues the
+// Warp 0 lane 0 issues TMA copies into a 3- or 4-stage ring, warp 1 lane 0 issues the
 // MMAs (tcgen05.commit frees a stage when its MMAs are done), and all four warps
 // read the 128 x 64 f32 accumulator tile out of tensor memory.  Every wait is
 // bounded; on a timeout the error word is set, in-flight copies and MMAs are
@@ -34,6 +34,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "vb_engine.cuh"
@@ -46,12 +47,17 @@ constexpr int kTSMs = 148;        // B200 SM count (split-K sizing)
 constexpr int kTM = 128;         // weight rows per tile (MMA M)
 constexpr int kTN = 64;          // activation rows (MMA N)
 constexpr int kTK = 64;          // K per stage: one 128-byte swizzle row of bf16
-constexpr int kTStages = 4;
 constexpr int kTThreads = 128;
 constexpr int kWTile = kTM * kTK * 2;   // 16 KB
 constexpr int kATile = kTN * kTK * 2;   // 8 KB
-constexpr int kTStage = 2 * kWTile + 2 * kATile;  // W_hi, W_lo, A_hi, A_lo
-constexpr size_t kTSmem = (size_t)kTStages * kTStage + 1024;  // + alignment slack
+// one stage: W_hi [, W_lo], A_hi, A_lo
+__host__ __device__ constexpr int stage_bytes(int wp) { return wp * kWTile + 2 * kATile; }
+__host__ __device__ constexpr size_t tc_smem(int wp, int ns) { return (size_t)ns * stage_bytes(wp) + 1024; }  // + alignment slack
+// Ring depth and CTAs per SM: a weight pair (f32) keeps 4 stages of 48 KB, one
+// CTA per SM; single bf16 weights (INT8) keep kQStages stages of 32 KB.
+constexpr int kPStages = 4;
+constexpr int kQStages = 4;
+__host__ __device__ constexpr int ctas_per_sm(int wp) { return wp == 2 ? 1 : (2 * tc_smem(1, kQStages) + 2048 <= 228 * 1024 ? 2 : 1); }
 
 struct TcParams {
     int M, N;       // activation rows, weight rows
@@ -104,12 +110,15 @@ __device__ __forceinline__ void mma_commit(unsigned mbar) {
                  : "memory");
 }
 
-template <int WP>
-__global__ void __launch_bounds__(kTThreads, 1)
+template <int WP, int NS>
+__global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
                    const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                    const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
+    constexpr int kTStages = NS;
+    constexpr int kTStage = stage_bytes(WP);
+    constexpr int kAOff = WP * kWTile;
     __shared__ __align__(8) unsigned long long full[kTStages], empty[kTStages], done;
     __shared__ unsigned tmem_slot;
     __shared__ int fail;
@@ -172,8 +181,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 tma_load_2d(st, &tw_hi, x, n0, fb);
                 if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
             }
-            tma_load_2d(st + 2 * kWTile, &ta_hi, x, 0, fb);
-            tma_load_2d(st + 2 * kWTile + kATile, &ta_lo, x, 0, fb);
+            tma_load_2d(st + kAOff, &ta_hi, x, 0, fb);
+            tma_load_2d(st + kAOff + kATile, &ta_lo, x, 0, fb);
             issued = i + 1;
         }
         // a stage whose weights went out before a failure still has its copies in flight
@@ -195,8 +204,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kTK / 16; kk++) {
                 const uint64_t wh = sw128_desc(st + 32u * kk);
-                const uint64_t ah = sw128_desc(st + 2 * kWTile + 32u * kk);
-                const uint64_t al = sw128_desc(st + 2 * kWTile + kATile + 32u * kk);
+                const uint64_t ah = sw128_desc(st + kAOff + 32u * kk);
+                const uint64_t al = sw128_desc(st + kAOff + kATile + 32u * kk);
                 mma_bf16(tmem, wh, ah, i > 0 || kk > 0);
                 mma_bf16(tmem, wh, al, true);
                 if (WP == 2) mma_bf16(tmem, sw128_desc(st + kWTile + 32u * kk), ah, true);
@@ -350,10 +359,17 @@ vb_status make_map(CUtensorMap* map, const void* base, int rows, int K, int box_
 
 int tc_gemm_tiles(int N) { return (N + kTM - 1) / kTM; }
 
-int tc_gemm_splits(int N, int K) {
+int tc_gemm_splits(int N, int K, bool pair) {
+    // as many (tile, split) CTAs as fit in one wave
     const int tiles = (N + kTM - 1) / kTM;
     const int chunks = K / kTK;
-    int s = (kTSMs + tiles - 1) / tiles;
+    // VB_TC_MAX_SPLITS caps the split-K factor (more splits: more partials to sum)
+    static const int max_splits = [] {
+        const char* v = getenv("VB_TC_MAX_SPLITS");
+        const int m = v ? atoi(v) : 0;
+        return m > 0 ? m : 1 << 20;
+    }();
+    int s = std::min(kTSMs * ctas_per_sm(pair ? 2 : 1) / tiles, max_splits);
     if (s > chunks) s = chunks;
     if (s < 1) s = 1;
     // every split gets at least one chunk
@@ -361,7 +377,10 @@ int tc_gemm_splits(int N, int K) {
     return (chunks + per - 1) / per;
 }
 
-size_t tc_gemm_ws_floats(int M, int N, int K) { return (size_t)tc_gemm_splits(N, K) * M * N; }
+size_t tc_gemm_ws_floats(int M, int N, int K) {
+    const int s = std::max(tc_gemm_splits(N, K, false), tc_gemm_splits(N, K, true));
+    return (size_t)s * M * N;
+}
 
 vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s) {
     if (M < 1 || M > kTN || K <= 0) return fail(VB_ERR_ARG, "split_bf16: bad shape");
@@ -387,15 +406,17 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if (a.M < 1 || a.M > kTN) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M must be 1..64");
     if (a.K % kTK || a.K <= 0) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: K must be a multiple of 64");
     if (a.N <= 0) return fail(VB_ERR_ARG, "tensor-core gemm: N <= 0");
-    const int splits = tc_gemm_splits(a.N, a.K);
+    const int wp = a.w_lo ? 2 : 1;
+    const int splits = tc_gemm_splits(a.N, a.K, wp == 2);
     if ((size_t)splits * a.M * a.N > a.ws_floats) return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
     static bool attr_done[2] = {false, false};
-    const int wp = a.w_lo ? 2 : 1;
     if (!attr_done[wp - 1]) {
-        cudaError_t ce = wp == 2 ? cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)kTSmem)
-                                 : cudaFuncSetAttribute(tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)kTSmem);
+        cudaError_t ce = wp == 2 ? cudaFuncSetAttribute(tc_gemm_kernel<2, kPStages>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)tc_smem(2, kPStages))
+                                 : cudaFuncSetAttribute(tc_gemm_kernel<1, kQStages>,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                        (int)tc_smem(1, kQStages));
         if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
         attr_done[wp - 1] = true;
     }
@@ -423,8 +444,11 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
     const dim3 grid((a.N + kTM - 1) / kTM, splits);
-    const cudaError_t ce = wp == 2 ? launch_pdl(tc_gemm_kernel<2>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p)
-                                   : launch_pdl(tc_gemm_kernel<1>, grid, kTThreads, kTSmem, s, mwh, mwl, mah, mal, p);
+    const cudaError_t ce =
+        wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages>, grid, kTThreads, tc_smem(2, kPStages), s, mwh, mwl, mah,
+                             mal, p)
+                : launch_pdl(tc_gemm_kernel<1, kQStages>, grid, kTThreads, tc_smem(1, kQStages), s, mwh, mwl, mah,
+                             mal, p);
     if (ce != cudaSuccess) return cuda_fail(ce, "tc_gemm_kernel launch");
     if (splits == 1 || a.partials_only) return VB_OK;
     GemmArgs g{};

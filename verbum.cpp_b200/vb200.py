@@ -104,6 +104,7 @@ _SIGS = {
     "vb_batch_prefill": (_I, [_P, _P, _I, _P]),
     "vb_batch_graph_nodes": (_I, [_P]),
     "vb_batch_reset": (_I, [_P]),
+    "vb_batch_truncate": (_I, [_P, _I]),
 }
 
 
@@ -308,6 +309,9 @@ class Batch:
 
     def reset(self):
         check(lib().vb_batch_reset(self.h))
+
+    def truncate(self, length: int):
+        check(lib().vb_batch_truncate(self.h, int(length)))
 
     def close(self):
         if getattr(self, "h", None):
