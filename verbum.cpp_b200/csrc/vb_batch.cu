@@ -25,7 +25,6 @@ struct vb_batch {
     float* vc = nullptr;
     float* x = nullptr;
     float* xn = nullptr;
-    float* qkv = nullptr;
     float* q = nullptr;
     float* ctx = nullptr;
     float* h = nullptr;
@@ -312,7 +311,6 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
         return bail(fail(VB_ERR_CUDA, "kv cache memset failed"));
     if ((st = balloc(&b->x, (size_t)batch * c.hidden, "x"))) return bail(st);
     if ((st = balloc(&b->xn, (size_t)batch * c.hidden, "xn"))) return bail(st);
-    if ((st = balloc(&b->qkv, (size_t)batch * e->qkv_rows, "qkv"))) return bail(st);
     if ((st = balloc(&b->q, (size_t)batch * e->q_width, "q"))) return bail(st);
     if ((st = balloc(&b->ctx, (size_t)batch * e->q_width, "ctx"))) return bail(st);
     if ((st = balloc(&b->h, (size_t)batch * c.ffn, "h"))) return bail(st);
@@ -370,7 +368,7 @@ vb_status vb_batch_destroy(vb_batch* b) {
     Dev dg(b->e->device);
     cudaStreamSynchronize(b->e->stream);
     if (b->graph) cudaGraphExecDestroy(b->graph);
-    bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->qkv); bfree(b->q);
+    bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->q);
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
     bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err); bfree(b->d_prompt);
     free_tc_weights(b);
