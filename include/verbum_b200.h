@@ -88,7 +88,8 @@ VB_API vb_status vb_matmul_nt_q8(const float* A, const int8_t* Wq, const float* 
 
 /* C[M][N] = A[M][K] . W[N][K]^T on the tensor cores (tcgen05, bf16 operands,
  * f32 accumulation): the batched form of matmul_nt / matmul_nt_q8 (ops.cpp:42-70,
- * quant.cpp:43-70) with 1 <= M <= 64 activation rows and K % 64 == 0.  W is
+ * quant.cpp:43-70) for M >= 1 activation rows (64-row tiles; split-K when
+ * M <= 64) and K % 64 == 0.  W is
  * f32 (w_int8 = 0; used as a bf16 hi+lo pair) or INT8 with per-row scales
  * applied after the sum (w_int8 = 1); A is split into bf16 hi+lo.  Synchronous
  * on `stream`; scratch comes from a per-device buffer grown on demand. */
@@ -160,6 +161,14 @@ VB_API vb_status vb_attn_decode_noalloc(const float* q, const float* kcache,
  * out [B, H, D].  No reference counterpart beyond generate.cpp:73-105 applied
  * per sequence. */
 VB_API size_t vb_attn_workspace_bytes(int B, int H, int n_max);
+/* Causal attention of a prompt chunk (prefill), the decode attention of
+ * generate.cpp:73-105 applied at every position p0 + c (c < C) of B sequences:
+ * q and out [B*C][H*D] (row b*C + c); element (b, kvh, pos, d) of K/V at
+ * base + b*stride_b + kvh*stride_h + pos*D (floats), positions 0 .. p0 + C - 1
+ * filled.  H == 2*KVH, D == 128.  No workspace. */
+VB_API vb_status vb_attn_prefill(const float* q, const float* k, const float* v, float* out,
+                                 int B, int C, int p0, int H, int KVH, int D,
+                                 int64_t stride_b, int64_t stride_h, void* stream);
 VB_API vb_status vb_attn_decode_batched(const float* q, const float* k, const float* v,
                                  float* out, const int* lens, int B, int H, int KVH,
                                  int D, int n_max, int64_t stride_b,

@@ -228,6 +228,186 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     return launch_advance(b->d_pos, b->d_tok, b->d_next, B, s);
 }
 
+// Device buffers of one prompt chunk of R = B * C rows (row b*C + c is
+// position p0 + c of sequence b).
+struct PrefillBufs {
+    float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *ctx = nullptr, *h = nullptr, *ws = nullptr;
+    size_t ws_floats = 0;
+    void *a_hi = nullptr, *a_lo = nullptr, *y_hi = nullptr, *y_lo = nullptr;
+    int *tok = nullptr, *pos = nullptr;
+    ~PrefillBufs() {
+        for (void* p : {(void*)x, (void*)xn, (void*)qkv, (void*)q, (void*)ctx, (void*)h, (void*)ws, a_hi, a_lo,
+                        y_hi, y_lo,
+                        (void*)tok, (void*)pos})
+            if (p) cudaFree(p);
+    }
+};
+
+// Prefill of P positions for all B sequences (tokens_host [P][B]) as whole
+// chunks: the projections of all chunk rows run as tensor-core GEMMs (weights
+// read once per chunk instead of once per position), the q/k norm + RoPE +
+// append over all rows, then causal flash attention over the cache.  The same
+// layer arithmetic as the decode step (model.cpp:240-254, generate.cpp:42-107)
+// in a different summation order.  Afterwards the decode state is what P
+// decode steps leave: logits and greedy picks of the last position, tokens =
+// picks, positions advanced by P.
+vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
+    vb_engine* e = b->e;
+    const vb_config& c = e->cfg;
+    const bool q8 = e->quantized;
+    const int B = b->B, H = c.hidden;
+    // positions per chunk: ~16k rows (VB_PREFILL_ROWS overrides the row budget)
+    int rows = 16384;
+    if (const char* v = getenv("VB_PREFILL_ROWS"))
+        if (atoi(v) > 0) rows = atoi(v);
+    const int C = std::min(P, std::max(1, rows / B));
+    const int R = B * C, R64 = std::max(R, 64);
+    const int ky = std::max(e->q_width, c.ffn);
+    cudaStream_t s = e->stream;
+    PrefillBufs pb;
+    vb_status st;
+    if ((st = balloc(&pb.x, (size_t)R * H, "prefill x")) || (st = balloc(&pb.xn, (size_t)R * H, "prefill xn")) ||
+        (st = balloc(&pb.qkv, (size_t)R * e->qkv_rows, "prefill qkv")) ||
+        (st = balloc(&pb.q, (size_t)R * e->q_width, "prefill q")) ||
+        (st = balloc(&pb.ctx, (size_t)R * e->q_width, "prefill ctx")) ||
+        (st = balloc(&pb.h, (size_t)R * c.ffn, "prefill h")) || (st = balloc(&pb.tok, R, "prefill tokens")) ||
+        (st = balloc(&pb.pos, R, "prefill positions")))
+        return st;
+    // split-K partials (GEMMs of at most 64 rows use split-K)
+    {
+        const int nk[4][2] = {{e->qkv_rows, H}, {H, e->q_width}, {2 * c.ffn, H}, {H, c.ffn}};
+        for (const auto& g : nk)
+            pb.ws_floats = std::max(pb.ws_floats, tc_gemm_ws_floats(std::min(R, 64), g[0], g[1]));
+        if ((st = balloc(&pb.ws, pb.ws_floats, "prefill gemm ws"))) return st;
+    }
+    {
+        uint16_t *ah, *al, *yh, *yl;
+        if ((st = balloc(&ah, (size_t)R64 * H, "prefill split"))) return st;
+        pb.a_hi = ah;
+        if ((st = balloc(&al, (size_t)R64 * H, "prefill split"))) return st;
+        pb.a_lo = al;
+        if ((st = balloc(&yh, (size_t)R64 * ky, "prefill split"))) return st;
+        pb.y_hi = yh;
+        if ((st = balloc(&yl, (size_t)R64 * ky, "prefill split"))) return st;
+        pb.y_lo = yl;
+        // rows past R of a single 64-row tile are read by the MMA: keep them finite
+        VB_CUDA_TRY(cudaMemsetAsync(ah, 0, (size_t)R64 * H * 2, s));
+        VB_CUDA_TRY(cudaMemsetAsync(al, 0, (size_t)R64 * H * 2, s));
+        VB_CUDA_TRY(cudaMemsetAsync(yh, 0, (size_t)R64 * ky * 2, s));
+        VB_CUDA_TRY(cudaMemsetAsync(yl, 0, (size_t)R64 * ky * 2, s));
+    }
+    auto gemm = [&](int M, const void* ahi, const void* alo, void* const* w, const float* sc, float* Cm, int N, int K,
+                    int ldc, int epi, bool wq8, void* ohi, void* olo) {
+        TcGemmArgs t{};
+        t.w_hi = w[0];
+        t.w_lo = wq8 ? nullptr : w[1];
+        t.a_hi = ahi;
+        t.a_lo = alo;
+        t.M = M;
+        t.N = N;
+        t.K = K;
+        t.ws = pb.ws;
+        t.ws_floats = pb.ws_floats;
+        t.scales = wq8 ? sc : nullptr;
+        t.C = Cm;
+        t.ldc = ldc;
+        t.epi = epi;
+        t.out_hi = ohi;
+        t.out_lo = olo;
+        t.err = b->d_err;
+        return launch_tc_gemm(t, s);
+    };
+    const size_t per_seq = (size_t)c.kv_heads * b->max_seq * c.head_dim;
+    const size_t layer_kv = per_seq * B;
+    std::vector<int> htok(R), hpos(R);
+    int Cn = 0;
+    for (int p0 = 0; p0 < P; p0 += C) {
+        Cn = std::min(C, P - p0);
+        const int Rn = B * Cn, start = b->len + p0;
+        for (int sq = 0; sq < B; sq++)
+            for (int i = 0; i < Cn; i++) {
+                htok[(size_t)sq * Cn + i] = tokens_host[(size_t)(p0 + i) * B + sq];
+                hpos[(size_t)sq * Cn + i] = start + i;
+            }
+        VB_CUDA_TRY(cudaMemcpyAsync(pb.tok, htok.data(), sizeof(int) * Rn, cudaMemcpyHostToDevice, s));
+        VB_CUDA_TRY(cudaMemcpyAsync(pb.pos, hpos.data(), sizeof(int) * Rn, cudaMemcpyHostToDevice, s));
+        // the host arrays are rewritten for the next chunk: wait for the copies
+        VB_CUDA_TRY(cudaStreamSynchronize(s));
+        if ((st = launch_embed(e->embed, pb.tok, Rn, H, c.vocab, pb.x, b->d_err, s))) return st;
+        for (int l = 0; l < c.layers; l++) {
+            const vb_layer_dev& L = e->L[l];
+            void* const* tw = &b->tcw[(size_t)l * 8];
+            if ((st = launch_rmsnorm_rows(pb.x, L.in_norm, pb.xn, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
+            if ((st = gemm(Rn, pb.a_hi, pb.a_lo, tw + 0, L.sqkv, pb.qkv, e->qkv_rows, H, e->qkv_rows, kEpiStore, q8,
+                           nullptr, nullptr)))
+                return st;
+            QkNormArgs qa{};
+            qa.qkv = pb.qkv;
+            qa.rows_per_seq = Cn;
+            qa.q_norm = L.q_norm;
+            qa.k_norm = L.k_norm;
+            qa.cos_tab = e->rope_cos;
+            qa.sin_tab = e->rope_sin;
+            qa.pos = pb.pos;
+            qa.q_out = pb.q;
+            qa.kc = b->kc + l * layer_kv;
+            qa.vc = b->vc + l * layer_kv;
+            qa.stride_b = (int64_t)per_seq;
+            qa.stride_pos = c.head_dim;
+            qa.stride_h = (int64_t)b->max_seq * c.head_dim;
+            qa.B = Rn;
+            qa.H = c.heads;
+            qa.KVH = c.kv_heads;
+            qa.D = c.head_dim;
+            qa.rope_positions = c.rope_positions < b->max_seq ? c.rope_positions : b->max_seq;
+            qa.eps = c.eps;
+            qa.err = b->d_err;
+            if ((st = launch_qk_norm_rope_append(qa, s))) return st;
+            PrefillAttnArgs pa{};
+            pa.q = pb.q;
+            pa.k = qa.kc;
+            pa.v = qa.vc;
+            pa.stride_b = qa.stride_b;
+            pa.stride_h = qa.stride_h;
+            pa.B = B;
+            pa.C = Cn;
+            pa.p0 = start;
+            pa.H = c.heads;
+            pa.KVH = c.kv_heads;
+            pa.D = c.head_dim;
+            pa.out = pb.ctx;
+            pa.out_hi = pb.y_hi;
+            pa.out_lo = pb.y_lo;
+            if ((st = launch_prefill_attention(pa, s))) return st;
+            if ((st = gemm(Rn, pb.y_hi, pb.y_lo, tw + 2, L.so, pb.x, H, e->q_width, H, kEpiResidual, q8, nullptr,
+                           nullptr)))
+                return st;
+            if ((st = launch_rmsnorm_rows(pb.x, L.post_norm, pb.xn, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
+            if ((st = gemm(Rn, pb.a_hi, pb.a_lo, tw + 4, L.sgu, pb.h, 2 * c.ffn, H, c.ffn, kEpiSwiGLU, q8, pb.y_hi,
+                           pb.y_lo)))
+                return st;
+            if ((st = gemm(Rn, pb.y_hi, pb.y_lo, tw + 6, L.sd, pb.x, H, c.ffn, H, kEpiResidual, q8, nullptr,
+                           nullptr)))
+                return st;
+        }
+    }
+    // the last position of every sequence: final norm, lm_head, greedy pick
+    VB_CUDA_TRY(cudaMemcpy2DAsync(b->x, sizeof(float) * H, pb.x + (size_t)(Cn - 1) * H, sizeof(float) * H * Cn,
+                                  sizeof(float) * H, B, cudaMemcpyDeviceToDevice, s));
+    if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, H, c.eps, s, b->a_hi, b->a_lo))) return st;
+    void* const lm[2] = {b->lm_hi, b->lm_lo};
+    if ((st = gemm(B, b->a_hi, b->a_lo, lm, nullptr, b->logits, c.vocab, H, c.vocab, kEpiStore, false, nullptr,
+                   nullptr)))
+        return st;
+    if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
+    // decode state after P steps: tokens = picks, positions += P
+    for (int sq = 0; sq < B; sq++) htok[sq] = b->len + P;
+    VB_CUDA_TRY(cudaMemcpyAsync(b->d_pos, htok.data(), sizeof(int) * B, cudaMemcpyHostToDevice, s));
+    VB_CUDA_TRY(cudaMemcpyAsync(b->d_tok, b->d_next, sizeof(int) * B, cudaMemcpyDeviceToDevice, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    return VB_OK;
+}
+
 vb_status batch_graph(vb_batch* b) {
     if (b->graph && b->graph_q8 == b->e->quantized) return VB_OK;
     if (vb_status ws = batch_tc_weights(b)) return ws;
@@ -455,18 +635,8 @@ vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, int* next
     for (size_t i = 0; i < n; i++)
         if (tokens_host[i] < 0 || tokens_host[i] >= b->e->cfg.vocab)
             return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
-    if (b->prompt_cap < (int)n) {
-        bfree(b->d_prompt);
-        if ((st = balloc(&b->d_prompt, n, "prompt"))) return st;
-        b->prompt_cap = (int)n;
-    }
+    if ((st = batch_prefill_chunks(b, tokens_host, P))) return st;
     cudaStream_t s = b->e->stream;
-    VB_CUDA_TRY(cudaMemcpyAsync(b->d_prompt, tokens_host, sizeof(int) * n, cudaMemcpyHostToDevice, s));
-    for (int t = 0; t < P; t++) {
-        VB_CUDA_TRY(cudaMemcpyAsync(b->d_tok, b->d_prompt + (size_t)t * b->B, sizeof(int) * b->B,
-                                    cudaMemcpyDeviceToDevice, s));
-        VB_CUDA_TRY(cudaGraphLaunch(b->graph, s));
-    }
     if (next_host)
         VB_CUDA_TRY(cudaMemcpyAsync(b->h_io + b->B, b->d_next, sizeof(int) * b->B,
                                     cudaMemcpyDeviceToHost, s));

@@ -1,5 +1,6 @@
 // vb_capi.cu -- extern "C" kernel entry points, memory helpers and error
 // state of the C ABI declared in include/verbum_b200.h.
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -220,11 +221,11 @@ vb_status vb_matmul_nt_q8(const float* A, const int8_t* Wq, const float* scales,
 vb_status vb_matmul_nt_tc(const float* A, const void* W, const float* scales, float* C, int M, int N, int K,
                           int w_int8, void* stream) {
     if (!A || !W || !C || (w_int8 && !scales)) return fail(VB_ERR_ARG, "null pointer");
-    if (M <= 0 || M > 64 || N <= 0 || K <= 0 || K % 64)
-        return fail(VB_ERR_UNSUPPORTED, "matmul_nt_tc: needs 1 <= M <= 64 and K % 64 == 0");
+    if (M <= 0 || N <= 0 || K <= 0 || K % 64)
+        return fail(VB_ERR_UNSUPPORTED, "matmul_nt_tc: needs M >= 1 and K % 64 == 0");
     cudaStream_t s = as_stream(stream);
-    const size_t wf = tc_gemm_ws_floats(M, N, K);
-    const size_t a_bytes = (size_t)64 * K * 2, w_bytes = (size_t)N * K * 2;
+    const size_t wf = M <= 64 ? tc_gemm_ws_floats(M, N, K) : 0;
+    const size_t a_bytes = (size_t)std::max(M, 64) * K * 2, w_bytes = (size_t)N * K * 2;
     const size_t off_ahi = 256;
     const size_t off_alo = off_ahi + a_bytes, off_whi = off_alo + a_bytes;
     const size_t off_wlo = off_whi + w_bytes, off_ws = off_wlo + (w_int8 ? 0 : w_bytes);
@@ -318,6 +319,18 @@ vb_status vb_attn_decode_batched(const float* q, const float* k, const float* v,
     a.splits = attn_splits_for(B, KVH, n_max);
     a.ws = static_cast<float*>(workspace);
     return launch_attention(a, as_stream(stream));
+}
+
+vb_status vb_attn_prefill(const float* q, const float* k, const float* v, float* out, int B, int C, int p0,
+                          int H, int KVH, int D, int64_t stride_b, int64_t stride_h, void* stream) {
+    if (!q || !k || !v || !out) return fail(VB_ERR_ARG, "null pointer");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || (stride_b | stride_h) & 3)
+        return fail(VB_ERR_UNSUPPORTED, "attention: 16-byte alignment required");
+    PrefillAttnArgs a{};
+    a.q = q; a.k = k; a.v = v; a.out = out;
+    a.stride_b = stride_b; a.stride_h = stride_h;
+    a.B = B; a.C = C; a.p0 = p0; a.H = H; a.KVH = KVH; a.D = D;
+    return launch_prefill_attention(a, as_stream(stream));
 }
 
 vb_status vb_attn_decode(const float* q, const float* kcache, const float* vcache, float* out,

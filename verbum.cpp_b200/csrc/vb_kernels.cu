@@ -375,8 +375,9 @@ __global__ void reduce_residual_norm_kernel(float* x, const float* parts, int sp
     }
 }
 
-// generate.cpp:52-71 for B sequences: per-head RMSNorm (q_norm / k_norm),
-// split-half RoPE from the host table, k and v rows written at pos[b].
+// generate.cpp:52-71 for B rows: per-head RMSNorm (q_norm / k_norm),
+// split-half RoPE from the host table, k and v rows written at pos[b] of the
+// row's sequence (b, or b / rows_per_seq for a prompt chunk).
 // grid (H + KVH, B), block D (= 128).
 __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
     pdl_trigger();
@@ -428,7 +429,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
     if (isq) {
         a.q_out[((size_t)b * a.H + h) * D + d] = o;
     } else {
-        const size_t off = (size_t)b * a.stride_b + (size_t)pos * a.stride_pos +
+        const int seq = a.rows_per_seq > 0 ? b / a.rows_per_seq : b;
+        const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos +
                            (size_t)h * a.stride_h + d;
         a.kc[off] = o;
         a.vc[off] = vv;

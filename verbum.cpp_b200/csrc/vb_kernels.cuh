@@ -48,6 +48,7 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
 // [B, H, D] and k / v rows into the caches at each sequence's position.
 struct QkNormArgs {
     const float* qkv;       // [B, (H + 2*KVH) * D]  (q | k | v)
+    int rows_per_seq;       // > 0: row b belongs to sequence b / rows_per_seq (a prompt chunk)
     const float* parts;     // or, when set: split-K partials [splits][B][(H + 2*KVH) * D]
     int splits;             //   summed in split order,
     const float* scales;    //   times these INT8 row scales when set
@@ -91,6 +92,23 @@ struct AttnArgs {
 int attn_splits_for(int B, int KVH, int n_max);
 size_t attn_ws_bytes(int B, int H, int splits);
 vb_status launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// Causal attention of a prompt chunk (vb_prefill.cu): q / out [B*C][H*D]
+// (row b*C + c = position p0 + c of sequence b), keys 0 .. p0 + c of the
+// cache (already holding the chunk's rows).  H == 2 * KVH, D == 128.
+struct PrefillAttnArgs {
+    const float* q;
+    const float* k;        // cache base of the layer: + b*stride_b + g*stride_h + pos*D
+    const float* v;
+    int64_t stride_b;
+    int64_t stride_h;
+    int B, C, p0, H, KVH, D;
+    float* out;
+    void* out_hi;          // optional bf16 split of out
+    void* out_lo;
+};
+vb_status launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
+size_t prefill_attention_smem();
 
 vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
                        float* out, int* err, cudaStream_t s);

@@ -60,7 +60,7 @@ constexpr int kQStages = 4;
 __host__ __device__ constexpr int ctas_per_sm(int wp) { return wp == 2 ? 1 : (2 * tc_smem(1, kQStages) + 2048 <= 228 * 1024 ? 2 : 1); }
 
 struct TcParams {
-    int M, N;       // activation rows, weight rows
+    int M, N;       // activation rows, weight rows (blockIdx.z: 64-row activation tile)
     int chunks;     // K / kTK
     int per_split;  // chunks per split
     int splits;
@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTM;
     const int split = blockIdx.y;
+    const int m0 = blockIdx.z * kTN;  // first activation row of this tile
+    const int Mt = min(kTN, p.M - m0);
     const int c0 = split * p.per_split;
     const int nch = min(p.per_split, p.chunks - c0);
 
@@ -181,8 +183,8 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
                 tma_load_2d(st, &tw_hi, x, n0, fb);
                 if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
             }
-            tma_load_2d(st + kAOff, &ta_hi, x, 0, fb);
-            tma_load_2d(st + kAOff + kATile, &ta_lo, x, 0, fb);
+            tma_load_2d(st + kAOff, &ta_hi, x, m0, fb);
+            tma_load_2d(st + kAOff + kATile, &ta_lo, x, m0, fb);
             issued = i + 1;
         }
         // a stage whose weights went out before a failure still has its copies in flight
@@ -248,13 +250,13 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int n = n0 + 32 * warp + lane;
         bool mine = true;  // a single split applies the epilogue itself
-        if (p.splits > 1 || p.partials) {
+        if (p.splits > 1 || p.partials) {  // (split-K runs with one activation tile)
             mine = false;
             float* P = p.P + (size_t)split * p.M * p.N + n;
             if (n < p.N)
 #pragma unroll
                 for (int m = 0; m < kTN; m++)
-                    if (m < p.M) P[(size_t)m * p.N] = v[m];
+                    if (m < Mt) P[(size_t)m * p.N] = v[m];
         }
         if (mine) {
             const float sc = (p.scales && n < p.N) ? p.scales[n] : 1.f;
@@ -264,9 +266,9 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
                 for (int m = 0; m < kTN; m++) {
                     const float val = v[m] * sc;
                     const float up = __shfl_down_sync(0xffffffffu, val, 1);
-                    if (m < p.M && (lane & 1) == 0 && n + 1 < p.N) {
+                    if (m < Mt && (lane & 1) == 0 && n + 1 < p.N) {
                         const float h = silu_f(val) * up;
-                        const size_t o = (size_t)m * p.ldc + (n >> 1);
+                        const size_t o = (size_t)(m0 + m) * p.ldc + (n >> 1);
                         p.C[o] = h;
                         if (p.out_hi) {
                             const __nv_bfloat16 hb = __float2bfloat16_rn(h);
@@ -276,17 +278,17 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
                     }
                 }
             } else if (n < p.N) {
-                float* c = p.C + n;
+                float* c = p.C + (size_t)m0 * p.ldc + n;
                 if (p.epi == kEpiResidual) {
 #pragma unroll
-                    for (int m = 0; m < kTN; m++) v[m] = (m < p.M ? c[(size_t)m * p.ldc] : 0.f) + v[m] * sc;
+                    for (int m = 0; m < kTN; m++) v[m] = (m < Mt ? c[(size_t)m * p.ldc] : 0.f) + v[m] * sc;
 #pragma unroll
                     for (int m = 0; m < kTN; m++)
-                        if (m < p.M) c[(size_t)m * p.ldc] = v[m];
+                        if (m < Mt) c[(size_t)m * p.ldc] = v[m];
                 } else {
 #pragma unroll
                     for (int m = 0; m < kTN; m++)
-                        if (m < p.M) c[(size_t)m * p.ldc] = v[m] * sc;
+                        if (m < Mt) c[(size_t)m * p.ldc] = v[m] * sc;
                 }
             }
         }
@@ -299,9 +301,10 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN) : "memory");
 }
 
-// A [M][lda] f32 -> A_hi, A_lo [64][K] bf16 with A = A_hi + A_lo (rows >= M zero).
+// A [M][lda] f32 -> A_hi, A_lo [max(M, 64)][K] bf16 with A = A_hi + A_lo
+// (rows >= M zero).
 __global__ void split_bf16_kernel(const float* A, int M, int K, int lda, __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    const size_t total = (size_t)kTN * K;
+    const size_t total = (size_t)max(M, kTN) * K;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / K), k = (int)(i % K);
         const float x = m < M ? A[(size_t)m * lda + k] : 0.f;
@@ -383,10 +386,10 @@ size_t tc_gemm_ws_floats(int M, int N, int K) {
 }
 
 vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s) {
-    if (M < 1 || M > kTN || K <= 0) return fail(VB_ERR_ARG, "split_bf16: bad shape");
-    const size_t total = (size_t)kTN * K;
+    if (M < 1 || K <= 0) return fail(VB_ERR_ARG, "split_bf16: bad shape");
+    const size_t total = (size_t)std::max(M, kTN) * K;
     int blocks = (int)((total + 255) / 256);
-    if (blocks > kTSMs * 4) blocks = kTSMs * 4;
+    if (blocks > kTSMs * 16) blocks = kTSMs * 16;
     split_bf16_kernel<<<blocks, 256, 0, s>>>(A, M, K, lda, static_cast<__nv_bfloat16*>(hi),
                                              static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("split_bf16_kernel");
@@ -403,12 +406,17 @@ vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, vo
 }
 
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
-    if (a.M < 1 || a.M > kTN) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M must be 1..64");
+    if (a.M < 1) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M must be >= 1");
+    const int mtiles = (a.M + kTN - 1) / kTN;
+    if (mtiles > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
+    if (mtiles > 1 && a.partials_only) return fail(VB_ERR_ARG, "tensor-core gemm: partials need M <= 64");
     if (a.K % kTK || a.K <= 0) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: K must be a multiple of 64");
     if (a.N <= 0) return fail(VB_ERR_ARG, "tensor-core gemm: N <= 0");
     const int wp = a.w_lo ? 2 : 1;
-    const int splits = tc_gemm_splits(a.N, a.K, wp == 2);
-    if ((size_t)splits * a.M * a.N > a.ws_floats) return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
+    // several activation tiles fill the GPU without split-K
+    const int splits = mtiles > 1 ? 1 : tc_gemm_splits(a.N, a.K, wp == 2);
+    if ((splits > 1 || a.partials_only) && (size_t)splits * a.M * a.N > a.ws_floats)
+        return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
     static bool attr_done[2] = {false, false};
     if (!attr_done[wp - 1]) {
         cudaError_t ce = wp == 2 ? cudaFuncSetAttribute(tc_gemm_kernel<2, kPStages>,
@@ -424,8 +432,10 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     vb_status st;
     if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kTM))) return st;
     if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kTM))) return st;
-    if ((st = make_map(&mah, a.a_hi, kTN, a.K, kTN))) return st;
-    if ((st = make_map(&mal, a.a_lo, kTN, a.K, kTN))) return st;
+    // activations: [max(M, 64)][K] (rows past M of a single tile are read and dropped)
+    const int arows = a.M > kTN ? a.M : kTN;
+    if ((st = make_map(&mah, a.a_hi, arows, a.K, kTN))) return st;
+    if ((st = make_map(&mal, a.a_lo, arows, a.K, kTN))) return st;
     if (!a.C && !a.partials_only) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
     if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
     TcParams p;
@@ -443,7 +453,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
-    const dim3 grid((a.N + kTM - 1) / kTM, splits);
+    const dim3 grid((a.N + kTM - 1) / kTM, splits, mtiles);
     const cudaError_t ce =
         wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages>, grid, kTThreads, tc_smem(2, kPStages), s, mwh, mwl, mah,
                              mal, p)

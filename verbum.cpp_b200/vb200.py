@@ -75,6 +75,7 @@ _SIGS = {
     "vb_attn_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_attn_decode_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_attn_workspace_bytes": (_Z, [_I, _I, _I]),
+    "vb_attn_prefill": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _L, _L, _P]),
     "vb_attn_decode_batched": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _L, _L, _L, _P, _P]),
     "vb_argmax_rows": (_I, [_P, _I, _L, _P, _P]),
     "vb_synth_normal": (None, [_P, C.c_uint64, C.c_uint64, _F]),
@@ -407,6 +408,12 @@ def attn_decode_batched(q, k, v, out, lens, B, H, KVH, D, n_max, stride_b, strid
     check(lib().vb_attn_decode_batched(_tp(q), _tp(k), _tp(v), _tp(out), _tp(lens), B, H, KVH, D,
                                        n_max, stride_b, stride_pos, stride_h, _tp(workspace),
                                        _stream(stream)))
+
+
+def attn_prefill(q, k, v, out, B, C, p0, H, KVH, D, stride_b, stride_h, stream=None):
+    """Causal attention of a prompt chunk: q / out [B*C, H*D]; caches [B, KVH, n, D]."""
+    check(lib().vb_attn_prefill(_tp(q), _tp(k), _tp(v), _tp(out), B, C, p0, H, KVH, D, stride_b,
+                                stride_h, _stream(stream)))
 
 
 def argmax_rows(logits, out_idx, stream=None):
