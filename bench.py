@@ -190,6 +190,40 @@ def step_kv_bytes(n_ctx):
     return KV_BYTES_PER_POS * (n_ctx + 1)
 
 
+def run_prefill(args, weights, cfg, dev=0):
+    """The batched prefill alone (B sequences x P prompt positions, INT8 model):
+    device time with CUDA events on the engine stream, prompt tokens/s."""
+    import numpy as np
+    import torch
+
+    import vb200
+    import vbsynth
+
+    B, P = args.batch, args.prompt
+    torch.cuda.set_device(dev)
+    eng = vb200.Engine(cfg, device=dev).load(weights)
+    eng.quantize()
+    bt = vb200.Batch(eng, B, P + 8)
+    prompts = np.stack([vbsynth.prompt_ids(P, 77 + b, cfg["vocab_size"]) for b in range(B)])
+    bt.prefill(prompts[:, :64].T.copy())  # builds the tensor-core weight copies
+    bt.reset()
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    nx = bt.prefill(prompts.T.copy())
+    ev1.record(stream)
+    ev1.synchronize()
+    wall = time.perf_counter() - t0
+    sec = ev0.elapsed_time(ev1) / 1e3
+    out = {"batch": B, "prompt": P, "seconds": round(sec, 4), "wall_s": round(wall, 4),
+           "prompt_tok_s": round(B * P / sec, 1), "first_next": [int(x) for x in nx[:4]]}
+    bt.close()
+    eng.close()
+    return out
+
+
 def run_batched(args, grp, weights, cfg):
     import numpy as np
     import torch
@@ -551,7 +585,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-extras", action="store_true", help="skip the bs1 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--only", choices=["gemv", "attn", "bs1"], help="one workload (for profiling)")
+    ap.add_argument("--only", choices=["gemv", "attn", "bs1", "prefill"], help="one workload (for profiling)")
     ap.add_argument("--mode", choices=["f32", "int8"], default="int8", help="--only bs1: weights")
     ap.add_argument("--path", type=int, default=0, help="--only bs1: 0 fused step, 1 per-op graph")
     ap.add_argument("--trace", action="store_true", help="--only bs1: per-phase trace of the fused step")
@@ -577,6 +611,12 @@ def main():
         r = run_bs1(args.mode, P, min(G, args.steps), w, cfg, dev=local_rank, path=args.path,
                     trace=args.trace)
         print(json.dumps({"bs1": r}), flush=True)
+        return 0
+    if args.only == "prefill":
+        import vbsynth
+        cfg = vbsynth.qwen3_config()
+        w = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+        print(json.dumps({"prefill": run_prefill(args, w, cfg, dev=local_rank)}), flush=True)
         return 0
     if args.only == "attn":
         print(json.dumps({"attn": attn_microbench(local_rank, ns=(args.ctx,), Bs=(args.batch,))}),
