@@ -29,7 +29,9 @@ SHAPES = [  # (M, N, K)
     (1, 384, 512),
     (33, 1000, 1024),
     (65, 1024, 2048),     # two activation tiles, the second of one row
-    (1000, 3072, 1024),   # prefill-sized
+    (1000, 3072, 1024),   # prefill-sized: wide tiles (128 activation x 256 weight rows)
+    (300, 1000, 2048),    # wide tiles with partial activation and weight tiles
+    (128, 256, 64),       # one wide tile, one K step
 ]
 
 

@@ -301,6 +301,198 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTN) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Wide tiles for many activation rows (a prompt chunk): one CTA computes 128
+// activation rows (the MMA's M, tensor-memory lanes) x 256 weight rows (the
+// MMA's N, 256 f32 columns) over all of K, so each SM takes in 64 KB (bf16
+// weights) or 96 KB (a weight pair) per 64-wide K step for 2 M MACs of
+// products -- half the bytes per MAC of the 128 x 64 decode tile.  Same
+// operands and accumulation as above; no split-K.
+constexpr int kWM = 128;                 // activation rows per tile
+constexpr int kWN = 256;                 // weight rows per tile
+constexpr int kWA = kWM * kTK * 2;       // 16 KB per activation half
+constexpr int kWW = kWN * kTK * 2;       // 32 KB per weight half
+__host__ __device__ constexpr int wide_stage(int wp) { return 2 * kWA + wp * kWW; }
+__host__ __device__ constexpr int wide_stages(int wp) { return wp == 1 ? 3 : 2; }
+__host__ __device__ constexpr size_t wide_smem(int wp) { return (size_t)wide_stages(wp) * wide_stage(wp) + 1024; }
+constexpr uint32_t kIdescWide = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kWN >> 3) << 17) |
+                                ((uint32_t)(kWM >> 4) << 24);
+
+__device__ __forceinline__ void mma_wide(unsigned tmem, uint64_t adesc, uint64_t bdesc, bool acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.u32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdescWide), "r"((unsigned)acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld64(unsigned taddr, float* v) {
+    unsigned* r = reinterpret_cast<unsigned*>(v);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+        "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+        "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
+          "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]),
+          "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
+          "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
+          "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// grid (ceil(N / 256), ceil(M / 128)); 128 threads: warp 0 lane 0 issues the
+// TMA copies, warp 1 lane 0 the MMAs, all four warps the epilogue (thread =
+// activation row m0 + 32 w + lane, 256 weight columns read out 64 at a time).
+template <int WP>
+__global__ void __launch_bounds__(kTThreads, 1)
+    tc_gemm_wide_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
+                        const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                        const TcParams p) {
+    constexpr int NS = wide_stages(WP);
+    constexpr int kStage = wide_stage(WP);
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) unsigned long long full[NS], empty[NS], done;
+    __shared__ unsigned tmem_slot;
+    __shared__ int fail;
+    const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kWN, m0 = blockIdx.y * kWM;
+    const int nch = p.chunks;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        mbar_init(smem_addr(&done), 1);
+        fail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(kWN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = tmem_slot;
+    if (warp == 0 && lane == 0) {
+        int issued = 0;
+        for (int i = 0; i < nch; i++) {
+            const int s = i % NS;
+            if (i >= NS &&
+                !mbar_wait(smem_addr(&empty[s]), ((unsigned)(i / NS) & 1u) ^ 1u, p.err, nullptr, kSiteEmpty, i)) {
+                fail = 1;
+                break;
+            }
+            const unsigned st = sbase + (unsigned)s * kStage;
+            const unsigned fb = smem_addr(&full[s]);
+            mbar_expect_tx(fb, (unsigned)kStage);
+            const int x = i * kTK;
+            tma_load_2d(st, &ta_hi, x, m0, fb);
+            tma_load_2d(st + kWA, &ta_lo, x, m0, fb);
+            tma_load_2d(st + 2 * kWA, &tw_hi, x, n0, fb);
+            if (WP == 2) tma_load_2d(st + 2 * kWA + kWW, &tw_lo, x, n0, fb);
+            issued = i + 1;
+        }
+        for (int i = issued > NS ? issued - NS : 0; i < issued; i++)
+            mbar_wait(smem_addr(&full[i % NS]), (unsigned)(i / NS) & 1u, p.err, nullptr, kSiteFull, i);
+    } else if (warp == 1 && lane == 0) {
+        for (int i = 0; i < nch && !fail; i++) {
+            const int s = i % NS;
+            if (!mbar_wait(smem_addr(&full[s]), (unsigned)(i / NS) & 1u, p.err, nullptr, kSiteFull, i)) {
+                fail = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const unsigned st = sbase + (unsigned)s * kStage;
+#pragma unroll
+            for (int kk = 0; kk < kTK / 16; kk++) {
+                const uint64_t ah = sw128_desc(st + 32u * kk);
+                const uint64_t al = sw128_desc(st + kWA + 32u * kk);
+                const uint64_t wh = sw128_desc(st + 2 * kWA + 32u * kk);
+                mma_wide(tmem, ah, wh, i > 0 || kk > 0);
+                mma_wide(tmem, al, wh, true);
+                if (WP == 2) mma_wide(tmem, ah, sw128_desc(st + 2 * kWA + kWW + 32u * kk), true);
+            }
+            mma_commit(smem_addr(&empty[s]));
+        }
+        mma_commit(smem_addr(&done));
+    }
+    __syncwarp();
+    bool ok = mbar_wait(smem_addr(&done), 0u, p.err, nullptr, kSiteFull, -1);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    ok = __syncthreads_and(ok && !fail);
+    if (ok) {
+        // Each warp stages its 32 rows x 64 columns in shared memory (the
+        // pipeline stages are free now), then writes row by row: lane j takes
+        // columns 2j, 2j + 1, so every store instruction covers 256
+        // consecutive bytes of one output row.
+        float* T = reinterpret_cast<float*>(smem_raw + (sbase - smem_addr(smem_raw))) + warp * 32 * 68;
+        for (int cb = 0; cb < kWN; cb += 64) {
+            const int nb = n0 + cb;
+            if (nb >= p.N) break;  // uniform across the CTA
+            float v[64];
+            tmem_ld64(tmem + ((unsigned)(32 * warp) << 16) + (unsigned)cb, v);
+#pragma unroll
+            for (int j = 0; j < 64; j += 4)
+                *reinterpret_cast<float4*>(T + lane * 68 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            __syncwarp();
+            const int n = nb + 2 * lane;
+            const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
+            const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
+            const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
+            const int rows = min(32, p.M - (m0 + 32 * warp));
+            for (int r = 0; r < rows; r++) {
+                const size_t m = (size_t)(m0 + 32 * warp + r);
+                const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
+                const float g = t2.x * s0, u = t2.y * s1;
+                if (p.epi == kEpiSwiGLU) {
+                    if (c1ok) {  // gate row n, up row n + 1 -> output n / 2
+                        const size_t o = m * p.ldc + (n >> 1);
+                        const float h = silu_f(g) * u;
+                        p.C[o] = h;
+                        if (p.out_hi) {
+                            const __nv_bfloat16 hb = __float2bfloat16_rn(h);
+                            p.out_hi[o] = hb;
+                            p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
+                        }
+                    }
+                } else {
+                    float* c = p.C + m * p.ldc + n;
+                    if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                        float2 o2 = make_float2(g, u);
+                        if (p.epi == kEpiResidual) {
+                            const float2 old = *reinterpret_cast<const float2*>(c);
+                            o2.x += old.x;
+                            o2.y += old.y;
+                        }
+                        *reinterpret_cast<float2*>(c) = o2;
+                    } else {
+                        if (c0ok) c[0] = p.epi == kEpiResidual ? c[0] + g : g;
+                        if (c1ok) c[1] = p.epi == kEpiResidual ? c[1] + u : u;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    } else if (threadIdx.x == 0) {
+        atomicCAS(p.err, 0, kErrPipeTimeout);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWN) : "memory");
+}
+
 // A [M][lda] f32 -> A_hi, A_lo [max(M, 64)][K] bf16 with A = A_hi + A_lo
 // (rows >= M zero).
 __global__ void split_bf16_kernel(const float* A, int M, int K, int lda, __nv_bfloat16* hi, __nv_bfloat16* lo) {
@@ -430,6 +622,46 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     }
     CUtensorMap mwh, mwl, mah, mal;
     vb_status st;
+    if (a.M >= kWM && a.N >= kWN && !a.partials_only) {
+        // many activation rows: wide tiles (boxes within the tensors), no split-K
+        if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
+        if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
+        if (a.M / kWM + 1 > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
+        static bool wide_attr[2] = {false, false};
+        if (!wide_attr[wp - 1]) {
+            const cudaError_t ce =
+                wp == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)wide_smem(2))
+                        : cudaFuncSetAttribute(tc_gemm_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)wide_smem(1));
+            if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
+            wide_attr[wp - 1] = true;
+        }
+        if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
+        if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kWN))) return st;
+        if ((st = make_map(&mah, a.a_hi, a.M, a.K, kWM))) return st;
+        if ((st = make_map(&mal, a.a_lo, a.M, a.K, kWM))) return st;
+        TcParams p{};
+        p.M = a.M;
+        p.N = a.N;
+        p.chunks = a.K / kTK;
+        p.per_split = p.chunks;
+        p.splits = 1;
+        p.scales = a.scales;
+        p.C = a.C;
+        p.ldc = a.ldc;
+        p.epi = a.epi;
+        p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
+        p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
+        p.err = a.err;
+        const dim3 grid((a.N + kWN - 1) / kWN, (a.M + kWM - 1) / kWM);
+        if (wp == 2)
+            tc_gemm_wide_kernel<2><<<grid, kTThreads, wide_smem(2), s>>>(mwh, mwl, mah, mal, p);
+        else
+            tc_gemm_wide_kernel<1><<<grid, kTThreads, wide_smem(1), s>>>(mwh, mwl, mah, mal, p);
+        VB_LAUNCH_CHECK("tc_gemm_wide_kernel");
+        return VB_OK;
+    }
     if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kTM))) return st;
     if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kTM))) return st;
     // activations: [max(M, 64)][K] (rows past M of a single tile are read and dropped)
