@@ -165,7 +165,9 @@ VB_API size_t vb_attn_workspace_bytes(int B, int H, int n_max);
  * generate.cpp:73-105 applied at every position p0 + c (c < C) of B sequences:
  * q and out [B*C][H*D] (row b*C + c); element (b, kvh, pos, d) of K/V at
  * base + b*stride_b + kvh*stride_h + pos*D (floats), positions 0 .. p0 + C - 1
- * filled.  H == 2*KVH, D == 128.  No workspace. */
+ * filled.  H == 2*KVH, D == 128.  p0 == 0 runs on the tensor cores (bf16 hi/lo
+ * operands, scratch from the per-device buffer, synchronous on `stream`);
+ * p0 > 0 on the CUDA cores (no scratch, asynchronous). */
 VB_API vb_status vb_attn_prefill(const float* q, const float* k, const float* v, float* out,
                                  int B, int C, int p0, int H, int KVH, int D,
                                  int64_t stride_b, int64_t stride_h, void* stream);

@@ -4,8 +4,9 @@ flash attention) against the oracle.
 The reference prefills one position at a time through Model::step
 (generate.cpp:75-77); the chunked prefill computes the same layers
 (model.cpp:240-254, generate.cpp:42-107) for all positions of a chunk at once,
-so only the summation order differs.  Checked: the causal attention kernel
-against the oracle's decode attention at every query position, and a batch
+so only the summation order differs.  Checked: the causal attention kernels
+(tensor cores for a prompt from position 0, CUDA cores otherwise) against the
+oracle's decode attention at every query position, and a batch
 prefilled in several chunks against per-sequence oracle decoding (greedy pick
 after the prompt, and the logits of the next step within the logits bars).
 """
@@ -23,7 +24,7 @@ torch = pytest.importorskip("torch")
 TOL = {"f32": 1e-3, "int8": 1e-2}
 
 
-@pytest.mark.parametrize("B,C,p0", [(3, 40, 9), (2, 1, 0), (1, 64, 0), (2, 33, 100)])
+@pytest.mark.parametrize("B,C,p0", [(3, 40, 9), (2, 1, 0), (1, 64, 0), (2, 33, 100), (2, 200, 0), (1, 130, 0)])
 def test_attn_prefill_matches_decode_attention(B, C, p0):
     H, KVH, D = 16, 8, 128
     n = p0 + C
@@ -52,11 +53,17 @@ def test_attn_prefill_rejects_bad_shapes():
 
 
 @pytest.mark.parametrize("mode", ["f32", "int8"])
-def test_chunked_prefill_matches_oracle(mode, monkeypatch):
+@pytest.mark.parametrize("rows", ["64", None])
+def test_chunked_prefill_matches_oracle(mode, rows, monkeypatch):
+    """rows 64: 12 positions per chunk (chunks 12, 12, 6; attention on the CUDA
+    cores after the first chunk); default: one chunk, tensor-core attention."""
     cfg = mini_config()
     w = vbsynth.make_weights(cfg, seed=61)
     B, P = 5, 30
-    monkeypatch.setenv("VB_PREFILL_ROWS", "64")  # 12 positions per chunk: chunks 12, 12, 6
+    if rows:
+        monkeypatch.setenv("VB_PREFILL_ROWS", rows)
+    else:
+        monkeypatch.delenv("VB_PREFILL_ROWS", raising=False)
     prompts = np.stack([vbsynth.prompt_ids(P, 300 + b, cfg["vocab_size"]) for b in range(B)])
     eng = vb200.Engine(cfg).load(w)
     if mode == "int8":

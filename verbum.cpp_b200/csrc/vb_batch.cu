@@ -233,10 +233,11 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
 struct PrefillBufs {
     float *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *ctx = nullptr, *h = nullptr, *ws = nullptr;
     size_t ws_floats = 0;
+    void* att = nullptr;  // bf16 copies for the tensor-core prompt attention
     void *a_hi = nullptr, *a_lo = nullptr, *y_hi = nullptr, *y_lo = nullptr;
     int *tok = nullptr, *pos = nullptr;
     ~PrefillBufs() {
-        for (void* p : {(void*)x, (void*)xn, (void*)qkv, (void*)q, (void*)ctx, (void*)h, (void*)ws, a_hi, a_lo,
+        for (void* p : {(void*)x, (void*)xn, (void*)qkv, (void*)q, (void*)ctx, (void*)h, (void*)ws, att, a_hi, a_lo,
                         y_hi, y_lo,
                         (void*)tok, (void*)pos})
             if (p) cudaFree(p);
@@ -256,8 +257,9 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
     const vb_config& c = e->cfg;
     const bool q8 = e->quantized;
     const int B = b->B, H = c.hidden;
-    // positions per chunk: ~16k rows (VB_PREFILL_ROWS overrides the row budget)
-    int rows = 16384;
+    // positions per chunk: up to 128k rows, so a 64 x 2048 prompt is one chunk
+    // (VB_PREFILL_ROWS overrides the row budget)
+    int rows = 131072;
     if (const char* v = getenv("VB_PREFILL_ROWS"))
         if (atoi(v) > 0) rows = atoi(v);
     const int C = std::min(P, std::max(1, rows / B));
@@ -273,6 +275,9 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
         (st = balloc(&pb.h, (size_t)R * c.ffn, "prefill h")) || (st = balloc(&pb.tok, R, "prefill tokens")) ||
         (st = balloc(&pb.pos, R, "prefill positions")))
         return st;
+    // the whole prompt from position 0 in one chunk: attention on the tensor cores
+    const bool tc_att = b->len == 0 && C == P && c.heads == 2 * c.kv_heads && c.head_dim == 128;
+    if (tc_att) VB_CUDA_TRY(cudaMalloc(&pb.att, prompt_attention_tc_bytes(B, P, c.heads, c.kv_heads)));
     // split-K partials (GEMMs of at most 64 rows use split-K)
     {
         const int nk[4][2] = {{e->qkv_rows, H}, {H, e->q_width}, {2 * c.ffn, H}, {H, c.ffn}};
@@ -378,7 +383,13 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
             pa.out = pb.ctx;
             pa.out_hi = pb.y_hi;
             pa.out_lo = pb.y_lo;
-            if ((st = launch_prefill_attention(pa, s))) return st;
+            pa.err = b->d_err;
+            if (tc_att) {
+                pa.out = nullptr;  // the o_proj reads the split only
+                if ((st = launch_prompt_attention_tc(pa, pb.q, pb.att, s))) return st;
+            } else if ((st = launch_prefill_attention(pa, s))) {
+                return st;
+            }
             if ((st = gemm(Rn, pb.y_hi, pb.y_lo, tw + 2, L.so, pb.x, H, e->q_width, H, kEpiResidual, q8, nullptr,
                            nullptr)))
                 return st;

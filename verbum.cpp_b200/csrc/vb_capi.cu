@@ -330,7 +330,26 @@ vb_status vb_attn_prefill(const float* q, const float* k, const float* v, float*
     a.q = q; a.k = k; a.v = v; a.out = out;
     a.stride_b = stride_b; a.stride_h = stride_h;
     a.B = B; a.C = C; a.p0 = p0; a.H = H; a.KVH = KVH; a.D = D;
-    return launch_prefill_attention(a, as_stream(stream));
+    if (p0 != 0 || H != 2 * KVH || D != 128 || B <= 0 || C <= 0) return launch_prefill_attention(a, as_stream(stream));
+    // a prompt from position 0: the tensor-core form (bf16 hi/lo copies in the scratch buffer)
+    cudaStream_t s = as_stream(stream);
+    const size_t split = (size_t)B * C * H * D * 2;
+    const size_t need = 256 + 2 * split + prompt_attention_tc_bytes(B, C, H, KVH);
+    void* base = nullptr;
+    vb_status st = scratch_for(need, &base);
+    if (st) return st;
+    char* sc = static_cast<char*>(base);
+    int* err = reinterpret_cast<int*>(sc);
+    VB_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+    a.err = err;
+    a.out_hi = sc + 256;
+    a.out_lo = sc + 256 + split;
+    if ((st = launch_prompt_attention_tc(a, q, sc + 256 + 2 * split, s))) return st;
+    int h_err = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    VB_CUDA_TRY(cudaStreamSynchronize(s));
+    if (h_err) return fail(VB_ERR_TIMEOUT, "attn_prefill: a bounded wait in the kernel gave up");
+    return VB_OK;
 }
 
 vb_status vb_attn_decode(const float* q, const float* kcache, const float* vcache, float* out,

@@ -377,15 +377,15 @@ __global__ void reduce_residual_norm_kernel(float* x, const float* parts, int sp
 
 // generate.cpp:52-71 for B rows: per-head RMSNorm (q_norm / k_norm),
 // split-half RoPE from the host table, k and v rows written at pos[b] of the
-// row's sequence (b, or b / rows_per_seq for a prompt chunk).
-// grid (H + KVH, B), block D (= 128).
+// row's sequence (b, or b / rows_per_seq for a prompt chunk).  grid (B, H + KVH),
+// block D (= 128).
 __global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
     pdl_trigger();
     pdl_wait();
     const float eps = a.eps;
     __shared__ double red[4];
     __shared__ float ys[128];
-    const int hd = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int b = blockIdx.x, hd = blockIdx.y, d = threadIdx.x;
     const int D = a.D, half = D >> 1;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.rope_positions) {
@@ -871,7 +871,7 @@ vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, 
 
 vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
-    dim3 grid(a.H + a.KVH, a.B);
+    dim3 grid(a.B, a.H + a.KVH);  // rows on x: a prompt chunk has up to 2^31 - 1
     launch_pdl(qk_norm_rope_kernel, grid, 128, 0, s, a);
     VB_LAUNCH_CHECK("qk_norm_rope_kernel");
     return VB_OK;

@@ -106,9 +106,16 @@ struct PrefillAttnArgs {
     float* out;
     void* out_hi;          // optional bf16 split of out
     void* out_lo;
+    int* err;              // device error word (tensor-core form; may be null)
 };
 vb_status launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
 size_t prefill_attention_smem();
+// Tensor-core form for a prompt from position 0 (a.p0 == 0, a.C = prompt
+// length, q given as f32 [B*C][H*D]): bf16 hi/lo copies of q, K and V^T go to
+// `scratch` (prompt_attention_tc_bytes), the split output to a.out_hi/out_lo
+// (and f32 to a.out when set).
+size_t prompt_attention_tc_bytes(int B, int P, int H, int KVH);
+vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s);
 
 vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
                        float* out, int* err, cudaStream_t s);
@@ -173,7 +180,10 @@ int tc_gemm_splits(int N, int K, bool pair);
 size_t tc_gemm_ws_floats(int M, int N, int K);
 int tc_gemm_tiles(int N);
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);
-vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s);
+// A [M][lda] -> bf16 hi/lo [rows][K]: rows = max(M, 64) zero-padded (pad64, the
+// decode GEMM's 64-row operand) or exactly M.
+vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s,
+                            bool pad64 = true);
 vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, void* lo, cudaStream_t s);
 
 }  // namespace vb

@@ -17,6 +17,7 @@
 #include <cuda_bf16.h>
 
 #include "vb_kernels.cuh"
+#include "vb_tc.cuh"
 
 namespace vb {
 namespace {
@@ -160,6 +161,286 @@ __global__ void __launch_bounds__(kPThreads) prefill_attn_kernel(const PrefillAt
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core form for a prompt that starts at position 0 (the whole prompt in
+// one chunk).  Operands are bf16 hi + lo pairs of the f32 values (q, the
+// chunk's K rows, and V transposed so its positions run along K of the P.V
+// product): S = Q_hi K_hi + Q_hi K_lo + Q_lo K_hi and O += P_hi V_hi +
+// P_lo V_hi + P_hi V_lo, products exact in f32, dropped terms ~2^-16.
+//
+// CTA = 64 query positions x the 2 query heads of one KV head = 128 query rows
+// (MMA M, tensor-memory lanes; thread r owns row r).  Per 64-key tile: TMA
+// (double-buffered) -> S MMA into tensor memory (64 columns) -> each thread
+// reads its row of S, applies the causal mask and the online softmax, writes
+// P_hi / P_lo as its own 128-byte swizzled shared-memory row -> P.V MMA into
+// tensor memory (128 columns) -> each thread folds the tile into its 128
+// output registers.
+constexpr int kAQ = 64;                         // query positions per CTA
+constexpr int kAK = 64;                         // keys per tile
+constexpr int kQT = 128 * 128;                  // [128 rows][64 bf16] swizzled tile, 16 KB
+constexpr int kKT = 64 * 128;                   // [64 keys][64 bf16], 8 KB
+constexpr int kVT = 128 * 128;                  // [128 dims][64 keys], 16 KB
+constexpr int kOffQ = 0;                        // [hi/lo][d half] 4 x 16 KB
+constexpr int kOffKV = 4 * kQT;                 // [buf] {K [hi/lo][d half] 4 x 8 KB, Vt [hi/lo] 2 x 16 KB}
+constexpr int kKVBuf = 4 * kKT + 2 * kVT;       // 64 KB
+constexpr int kOffP = kOffKV + 2 * kKVBuf;      // [hi/lo] 2 x 16 KB
+constexpr size_t kTASmem = (size_t)kOffP + 2 * kQT + 1024;
+constexpr uint32_t kIdS = idesc_bf16(128, kAK);
+constexpr uint32_t kIdPV = idesc_bf16(128, 128);
+
+struct TcAttnParams {
+    int P, KVH, QW;          // prompt length, KV heads, H * 128
+    __nv_bfloat16* out_hi;   // [B*P][QW] split of the output
+    __nv_bfloat16* out_lo;
+    float* out;              // optional f32 output
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(128, 1)
+    tc_prefill_attn_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
+                           const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
+                           const __grid_constant__ CUtensorMap mv_hi, const __grid_constant__ CUtensorMap mv_lo,
+                           const TcAttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) unsigned long long q_full, kv_full[2], s_done, pv_done;
+    __shared__ unsigned tmem_slot;
+    const unsigned sb = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    uint8_t* sg = smem_raw + (sb - smem_addr(smem_raw));
+    const int t = threadIdx.x, warp = t >> 5;
+    const int c0 = blockIdx.x * kAQ, kvh = blockIdx.y, b = blockIdx.z;
+    const int nq = min(kAQ, p.P - c0);
+    const int nt = (c0 + nq - 1) / kAK + 1;  // key tiles up to the last query position
+    const int kv_row = (b * p.KVH + kvh);
+    if (t == 0) {
+        mbar_init(smem_addr(&q_full), 1);
+        mbar_init(smem_addr(&kv_full[0]), 1);
+        mbar_init(smem_addr(&kv_full[1]), 1);
+        mbar_init(smem_addr(&s_done), 1);
+        mbar_init(smem_addr(&pv_done), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(256)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tS = tmem_slot, tPV = tmem_slot + 128;
+    auto issue_kv = [&](int tile, int buf) {
+        const unsigned fb = smem_addr(&kv_full[buf]);
+        const unsigned base = sb + kOffKV + (unsigned)buf * kKVBuf;
+        mbar_expect_tx(fb, (unsigned)kKVBuf);
+#pragma unroll
+        for (int hl = 0; hl < 2; hl++)
+#pragma unroll
+            for (int dh = 0; dh < 2; dh++)
+                tma_load_2d(base + (hl * 2 + dh) * kKT, hl ? &mk_lo : &mk_hi, dh * 64, kv_row * p.P + tile * kAK, fb);
+        tma_load_2d(base + 4 * kKT, &mv_hi, tile * kAK, kv_row * 128, fb);
+        tma_load_2d(base + 4 * kKT + kVT, &mv_lo, tile * kAK, kv_row * 128, fb);
+    };
+    if (t == 0) {
+        const unsigned qb = smem_addr(&q_full);
+        mbar_expect_tx(qb, (unsigned)(4 * kQT));
+#pragma unroll
+        for (int hl = 0; hl < 2; hl++)
+#pragma unroll
+            for (int dh = 0; dh < 2; dh++)
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++)
+                    tma_load_2d(sb + kOffQ + (hl * 2 + dh) * kQT + hh * (kQT / 2), hl ? &mq_lo : &mq_hi,
+                                (2 * kvh + hh) * 128 + dh * 64, b * p.P + c0, qb);
+        issue_kv(0, 0);
+        if (nt > 1) issue_kv(1, 1);
+    }
+    const int r = t;  // query row: position c0 + (r & 63) of head 2 kvh + (r >> 6)
+    const int qpos = c0 + (r & 63);
+    const bool rvalid = (r & 63) < nq;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+    const unsigned lane_off = (unsigned)(32 * warp) << 16;
+    float o[128];
+#pragma unroll
+    for (int d = 0; d < 128; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int issued = nt > 1 ? 2 : 1;  // key tiles requested so far
+    for (int it = 0; it < nt; it++) {
+        const int buf = it & 1;
+        if (t == 32) {
+            bool w = (it > 0 || mbar_wait(smem_addr(&q_full), 0u, p.err, nullptr, kSiteFull, -1)) &&
+                     mbar_wait(smem_addr(&kv_full[buf]), (unsigned)(it >> 1) & 1u, p.err, nullptr, kSiteFull, it);
+            if (w) {
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const unsigned kb = sb + kOffKV + (unsigned)buf * kKVBuf;
+#pragma unroll
+                for (int dh = 0; dh < 2; dh++)
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t qh = sw128_desc(sb + kOffQ + dh * kQT + 32u * kk);
+                        const uint64_t ql = sw128_desc(sb + kOffQ + (2 + dh) * kQT + 32u * kk);
+                        const uint64_t kh = sw128_desc(kb + dh * kKT + 32u * kk);
+                        const uint64_t kl = sw128_desc(kb + (2 + dh) * kKT + 32u * kk);
+                        mma_f16(tS, qh, kh, kIdS, dh > 0 || kk > 0);
+                        mma_f16(tS, qh, kl, kIdS, true);
+                        mma_f16(tS, ql, kh, kIdS, true);
+                    }
+            }
+            // commit even after a failed wait so the waiters below are released
+            mma_commit(smem_addr(&s_done));
+        }
+        ok = mbar_wait(smem_addr(&s_done), (unsigned)it & 1u, p.err, nullptr, kSiteFull, it) && ok;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        float sv[64];
+        tmem_ld64(tS + lane_off, sv);
+        const int k0 = it * kAK;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
+            sv[j] = (rvalid && k0 + j <= qpos) ? sv[j] * scale : -INFINITY;
+            mx = fmaxf(mx, sv[j]);
+        }
+        const float mn = fmaxf(m, mx);
+        const float alpha = (m == -INFINITY) ? 0.f : expf(m - mn);
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
+            sv[j] = (sv[j] == -INFINITY) ? 0.f : expf(sv[j] - mn);
+            sum += sv[j];
+        }
+        l = l * alpha + sum;
+        m = mn;
+        // P_hi / P_lo: this thread's row, 8 chunks of 8 keys, 128-byte swizzle
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            uint32_t hv[4], lv[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float a = sv[8 * c + 2 * q], bb = sv[8 * c + 2 * q + 1];
+                const __nv_bfloat16 ah = __float2bfloat16_rn(a), bh = __float2bfloat16_rn(bb);
+                hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
+                lv[q] = pack_bf16(a - __bfloat162float(ah), bb - __bfloat162float(bh));
+            }
+            const int off = r * 128 + ((c ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(sg + kOffP + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(sg + kOffP + kQT + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();
+        if (t == 32) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (ok) {
+                const unsigned vb = sb + kOffKV + (unsigned)buf * kKVBuf + 4 * kKT;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t ph = sw128_desc(sb + kOffP + 32u * kk);
+                    const uint64_t pl = sw128_desc(sb + kOffP + kQT + 32u * kk);
+                    const uint64_t vh = sw128_desc(vb + 32u * kk);
+                    const uint64_t vl = sw128_desc(vb + kVT + 32u * kk);
+                    mma_f16(tPV, ph, vh, kIdPV, kk > 0);
+                    mma_f16(tPV, pl, vh, kIdPV, true);
+                    mma_f16(tPV, ph, vl, kIdPV, true);
+                }
+            }
+            mma_commit(smem_addr(&pv_done));
+        }
+        ok = mbar_wait(smem_addr(&pv_done), (unsigned)it & 1u, p.err, nullptr, kSiteFull, it) && ok;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // buffer `buf` is free again: request key tile it + 2 into it
+        if (t == 0 && it + 2 < nt) {
+            issue_kv(it + 2, buf);
+            issued = it + 3;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float pv[64];
+            tmem_ld64(tPV + lane_off + 64u * h, pv);
+#pragma unroll
+            for (int d = 0; d < 64; d++) o[64 * h + d] = fmaf(o[64 * h + d], alpha, pv[d]);
+        }
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+        }
+    }
+    if (t == 0) {
+        // never leave with copies in flight (the last two requested tiles)
+        for (int i = issued > 2 ? issued - 2 : 0; i < issued; i++)
+            mbar_wait(smem_addr(&kv_full[i & 1]), (unsigned)(i >> 1) & 1u, p.err, nullptr, kSiteFull, i);
+        mbar_wait(smem_addr(&q_full), 0u, p.err, nullptr, kSiteFull, -1);
+    }
+    if (ok && rvalid) {
+        const int hh = r >> 6;
+        const size_t base = (size_t)(b * p.P + qpos) * p.QW + (size_t)(2 * kvh + hh) * 128;
+#pragma unroll
+        for (int d = 0; d < 128; d += 8) {
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) y[e] = o[d + e] / l;
+            uint32_t hv[4], lv[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const __nv_bfloat16 ah = __float2bfloat16_rn(y[2 * q]), bh = __float2bfloat16_rn(y[2 * q + 1]);
+                hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
+                lv[q] = pack_bf16(y[2 * q] - __bfloat162float(ah), y[2 * q + 1] - __bfloat162float(bh));
+            }
+            *reinterpret_cast<uint4*>(p.out_hi + base + d) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(p.out_lo + base + d) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            if (p.out) {
+                *reinterpret_cast<float4*>(p.out + base + d) = make_float4(y[0], y[1], y[2], y[3]);
+                *reinterpret_cast<float4*>(p.out + base + d + 4) = make_float4(y[4], y[5], y[6], y[7]);
+            }
+        }
+    } else if (!ok && t == 0) {
+        atomicCAS(p.err, 0, kErrPipeTimeout);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_slot), "r"(256) : "memory");
+}
+
+// bf16 hi / lo copies of the prompt's K rows ([B*KVH*P][128]) and of V
+// transposed ([B*KVH*128][Ppad], positions along the row).  grid
+// (ceil(P / 32), KVH, B), 256 threads.
+__global__ void __launch_bounds__(256) prompt_kv_split_kernel(const float* k, const float* v, int64_t stride_b,
+                                                              int64_t stride_h, int P, int Ppad, int KVH,
+                                                              __nv_bfloat16* k_hi, __nv_bfloat16* k_lo,
+                                                              __nv_bfloat16* vt_hi, __nv_bfloat16* vt_lo) {
+    __shared__ float vs[32][129];
+    const int p0 = blockIdx.x * 32, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+    const size_t src = (size_t)b * stride_b + (size_t)kvh * stride_h;
+    const size_t krow = (size_t)(b * KVH + kvh) * P;
+    for (int i = t; i < 32 * 128; i += 256) {
+        const int pp = i >> 7, d = i & 127;
+        if (p0 + pp >= P) continue;
+        const float kx = k[src + (size_t)(p0 + pp) * 128 + d];
+        const __nv_bfloat16 kh = __float2bfloat16_rn(kx);
+        k_hi[(krow + p0 + pp) * 128 + d] = kh;
+        k_lo[(krow + p0 + pp) * 128 + d] = __float2bfloat16_rn(kx - __bfloat162float(kh));
+        vs[pp][d] = v[src + (size_t)(p0 + pp) * 128 + d];
+    }
+    __syncthreads();
+    // thread: dim d = t / 2, positions 16 * (t & 1) .. + 15 of the tile
+    const int d = t >> 1, q0 = 16 * (t & 1);
+    const size_t vrow = ((size_t)(b * KVH + kvh) * 128 + d) * Ppad + p0 + q0;
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+        if (p0 + q0 + q >= P) break;
+        const float vx = vs[q0 + q][d];
+        const __nv_bfloat16 vh = __float2bfloat16_rn(vx);
+        vt_hi[vrow + q] = vh;
+        vt_lo[vrow + q] = __float2bfloat16_rn(vx - __bfloat162float(vh));
+    }
+}
+
 }  // namespace
 
 size_t prefill_attention_smem() { return kPSmem; }
@@ -178,6 +459,61 @@ vb_status launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     const dim3 grid((a.C + kPQ - 1) / kPQ, a.KVH, a.B);
     prefill_attn_kernel<<<grid, kPThreads, kPSmem, s>>>(a);
     VB_LAUNCH_CHECK("prefill_attn_kernel");
+    return VB_OK;
+}
+
+size_t prompt_attention_tc_bytes(int B, int P, int H, int KVH) {
+    const size_t Ppad = (size_t)(P + 63) / 64 * 64;
+    return 2 * ((size_t)B * P * H * 128 + (size_t)B * KVH * P * 128 + (size_t)B * KVH * 128 * Ppad) * 2;
+}
+
+vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s) {
+    if (a.D != 128 || a.H != 2 * a.KVH || a.p0 != 0 || a.C <= 0 || a.B <= 0)
+        return fail(VB_ERR_UNSUPPORTED, "prompt attention (tensor cores): needs D 128, H 2*KVH, a prompt from 0");
+    if (!a.out_hi || !a.out_lo) return fail(VB_ERR_ARG, "prompt attention (tensor cores): split output missing");
+    const int B = a.B, P = a.C, KVH = a.KVH, QW = a.H * 128;
+    const int Ppad = (P + 63) / 64 * 64;
+    if ((size_t)B * P > (size_t)1 << 30 || (size_t)B * KVH * 128 > (size_t)1 << 30)
+        return fail(VB_ERR_UNSUPPORTED, "prompt attention (tensor cores): too many rows");
+    __nv_bfloat16* base = static_cast<__nv_bfloat16*>(scratch);
+    __nv_bfloat16* q_hi = base;
+    __nv_bfloat16* q_lo = q_hi + (size_t)B * P * QW;
+    __nv_bfloat16* k_hi = q_lo + (size_t)B * P * QW;
+    __nv_bfloat16* k_lo = k_hi + (size_t)B * KVH * P * 128;
+    __nv_bfloat16* vt_hi = k_lo + (size_t)B * KVH * P * 128;
+    __nv_bfloat16* vt_lo = vt_hi + (size_t)B * KVH * 128 * Ppad;
+    vb_status st;
+    if (Ppad != P) {
+        // padding columns of V^T are read by the last key tile (with zero weights): keep them finite
+        VB_CUDA_TRY(cudaMemsetAsync(vt_hi, 0, (size_t)B * KVH * 128 * Ppad * 2 * 2, s));
+    }
+    if ((st = launch_split_bf16(q, B * P, QW, QW, q_hi, q_lo, s, false))) return st;
+    prompt_kv_split_kernel<<<dim3((P + 31) / 32, KVH, B), 256, 0, s>>>(a.k, a.v, a.stride_b, a.stride_h, P, Ppad, KVH,
+                                                                      k_hi, k_lo, vt_hi, vt_lo);
+    VB_LAUNCH_CHECK("prompt_kv_split_kernel");
+    CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+    if ((st = tc_make_map(&mqh, q_hi, B * P, QW, 64)) || (st = tc_make_map(&mql, q_lo, B * P, QW, 64)) ||
+        (st = tc_make_map(&mkh, k_hi, B * KVH * P, 128, 64)) || (st = tc_make_map(&mkl, k_lo, B * KVH * P, 128, 64)) ||
+        (st = tc_make_map(&mvh, vt_hi, B * KVH * 128, Ppad, 128)) ||
+        (st = tc_make_map(&mvl, vt_lo, B * KVH * 128, Ppad, 128)))
+        return st;
+    static bool attr_done = false;
+    if (!attr_done) {
+        const cudaError_t ce =
+            cudaFuncSetAttribute(tc_prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTASmem);
+        if (ce != cudaSuccess) return cuda_fail(ce, "prompt attention: shared memory attribute");
+        attr_done = true;
+    }
+    TcAttnParams p{};
+    p.P = P;
+    p.KVH = KVH;
+    p.QW = QW;
+    p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
+    p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
+    p.out = a.out;
+    p.err = a.err;
+    tc_prefill_attn_kernel<<<dim3((P + kAQ - 1) / kAQ, KVH, B), 128, kTASmem, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
+    VB_LAUNCH_CHECK("tc_prefill_attn_kernel");
     return VB_OK;
 }
 

@@ -39,6 +39,7 @@
 
 #include "vb_engine.cuh"
 #include "vb_pipe.cuh"
+#include "vb_tc.cuh"
 
 namespace vb {
 namespace {
@@ -75,23 +76,7 @@ struct TcParams {
     int* err;
 };
 
-__device__ __forceinline__ void tma_load_2d(unsigned dst, const CUtensorMap* map, int x, int y, unsigned mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
-        : "memory");
-}
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 bytes,
-// 8-row groups 1024 bytes apart (the canonical layout TMA's 128-byte swizzle
-// writes).  Fields: start >> 4 [0,14), leading offset [16,30) (unused for
-// swizzled K-major, 1), stride offset >> 4 [32,46), version 1 [46,48),
-// layout type 2 = 128-byte swizzle [61,64).
-__device__ __forceinline__ uint64_t sw128_desc(unsigned saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
 
 // Instruction descriptor, kind::f16: f32 accumulator [4,6) = 1, A bf16 [7,10) = 1,
 // B bf16 [10,13) = 1, both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
@@ -104,10 +89,6 @@ __device__ __forceinline__ void mma_bf16(unsigned tmem, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem),
         "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"((unsigned)acc)
         : "memory");
-}
-__device__ __forceinline__ void mma_commit(unsigned mbar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
-                 : "memory");
 }
 
 template <int WP, int NS>
@@ -326,26 +307,6 @@ __device__ __forceinline__ void mma_wide(unsigned tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld64(unsigned taddr, float* v) {
-    unsigned* r = reinterpret_cast<unsigned*>(v);
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
-        "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-        "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-          "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]),
-          "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]),
-          "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
-          "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
-          "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
 
 // grid (ceil(N / 256), ceil(M / 128)); 128 threads: warp 0 lane 0 issues the
 // TMA copies, warp 1 lane 0 the MMAs, all four warps the epilogue (thread =
@@ -493,10 +454,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWN) : "memory");
 }
 
-// A [M][lda] f32 -> A_hi, A_lo [max(M, 64)][K] bf16 with A = A_hi + A_lo
-// (rows >= M zero).
-__global__ void split_bf16_kernel(const float* A, int M, int K, int lda, __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    const size_t total = (size_t)max(M, kTN) * K;
+// A [M][lda] f32 -> A_hi, A_lo [rows][K] bf16 with A = A_hi + A_lo (rows >= M
+// zero).
+__global__ void split_bf16_kernel(const float* A, int M, int K, int lda, int rows, __nv_bfloat16* hi,
+                                  __nv_bfloat16* lo) {
+    const size_t total = (size_t)rows * K;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / K), k = (int)(i % K);
         const float x = m < M ? A[(size_t)m * lda + k] : 0.f;
@@ -535,8 +497,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D bf16 tensor map over [rows][K], boxes of 64 (K) x box_rows, 128-byte swizzle.
 vb_status make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    return tc_make_map(map, base, rows, K, box_rows);
+}
+
+}  // namespace
+
+// 2-D bf16 tensor map over [rows][K], boxes of 64 (K) x box_rows, 128-byte swizzle.
+vb_status tc_make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
@@ -549,8 +517,6 @@ vb_status make_map(CUtensorMap* map, const void* base, int rows, int K, int box_
     if (r != CUDA_SUCCESS) return fail(VB_ERR_CUDA, "tensor-core gemm: cuTensorMapEncodeTiled failed");
     return VB_OK;
 }
-
-}  // namespace
 
 int tc_gemm_tiles(int N) { return (N + kTM - 1) / kTM; }
 
@@ -577,12 +543,14 @@ size_t tc_gemm_ws_floats(int M, int N, int K) {
     return (size_t)s * M * N;
 }
 
-vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s) {
+vb_status launch_split_bf16(const float* A, int M, int K, int lda, void* hi, void* lo, cudaStream_t s,
+                            bool pad64) {
     if (M < 1 || K <= 0) return fail(VB_ERR_ARG, "split_bf16: bad shape");
-    const size_t total = (size_t)std::max(M, kTN) * K;
+    const int rows = pad64 ? std::max(M, kTN) : M;
+    const size_t total = (size_t)rows * K;
     int blocks = (int)((total + 255) / 256);
     if (blocks > kTSMs * 16) blocks = kTSMs * 16;
-    split_bf16_kernel<<<blocks, 256, 0, s>>>(A, M, K, lda, static_cast<__nv_bfloat16*>(hi),
+    split_bf16_kernel<<<blocks, 256, 0, s>>>(A, M, K, lda, rows, static_cast<__nv_bfloat16*>(hi),
                                              static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("split_bf16_kernel");
     return VB_OK;
