@@ -41,8 +41,8 @@ struct vb_batch {
     cudaGraphExec_t graph = nullptr;
     bool graph_q8 = false;
     int graph_nodes = 0;
-    int* d_prompt = nullptr;  // [P][B] prefill tokens
-    int prompt_cap = 0;
+    void* arena = nullptr;    // prefill buffers, kept for the next prefill
+    size_t arena_bytes = 0;
     // tensor-core operands
     std::vector<void*> tcw;   // per layer: qkv, o, gu, d -> {hi, lo}
     void* lm_hi = nullptr;
@@ -236,12 +236,6 @@ struct PrefillBufs {
     void* att = nullptr;  // bf16 copies for the tensor-core prompt attention
     void *a_hi = nullptr, *a_lo = nullptr, *y_hi = nullptr, *y_lo = nullptr;
     int *tok = nullptr, *pos = nullptr;
-    ~PrefillBufs() {
-        for (void* p : {(void*)x, (void*)xn, (void*)qkv, (void*)q, (void*)ctx, (void*)h, (void*)ws, att, a_hi, a_lo,
-                        y_hi, y_lo,
-                        (void*)tok, (void*)pos})
-            if (p) cudaFree(p);
-    }
 };
 
 // Prefill of P positions for all B sequences (tokens_host [P][B]) as whole
@@ -266,40 +260,69 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
     const int R = B * C, R64 = std::max(R, 64);
     const int ky = std::max(e->q_width, c.ffn);
     cudaStream_t s = e->stream;
-    PrefillBufs pb;
-    vb_status st;
-    if ((st = balloc(&pb.x, (size_t)R * H, "prefill x")) || (st = balloc(&pb.xn, (size_t)R * H, "prefill xn")) ||
-        (st = balloc(&pb.qkv, (size_t)R * e->qkv_rows, "prefill qkv")) ||
-        (st = balloc(&pb.q, (size_t)R * e->q_width, "prefill q")) ||
-        (st = balloc(&pb.ctx, (size_t)R * e->q_width, "prefill ctx")) ||
-        (st = balloc(&pb.h, (size_t)R * c.ffn, "prefill h")) || (st = balloc(&pb.tok, R, "prefill tokens")) ||
-        (st = balloc(&pb.pos, R, "prefill positions")))
-        return st;
     // the whole prompt from position 0 in one chunk: attention on the tensor cores
     const bool tc_att = b->len == 0 && C == P && c.heads == 2 * c.kv_heads && c.head_dim == 128;
-    if (tc_att) VB_CUDA_TRY(cudaMalloc(&pb.att, prompt_attention_tc_bytes(B, P, c.heads, c.kv_heads)));
-    // split-K partials (GEMMs of at most 64 rows use split-K)
+    // one arena for every buffer (kept in the batch and reused by the next prefill)
+    PrefillBufs pb;
     {
         const int nk[4][2] = {{e->qkv_rows, H}, {H, e->q_width}, {2 * c.ffn, H}, {H, c.ffn}};
-        for (const auto& g : nk)
+        for (const auto& g : nk)  // split-K partials: GEMMs of at most 64 rows use split-K
             pb.ws_floats = std::max(pb.ws_floats, tc_gemm_ws_floats(std::min(R, 64), g[0], g[1]));
-        if ((st = balloc(&pb.ws, pb.ws_floats, "prefill gemm ws"))) return st;
+    }
+    const size_t sz[] = {
+        (size_t)R * H * 4,              // x
+        (size_t)R * H * 4,              // xn
+        (size_t)R * e->qkv_rows * 4,    // qkv
+        (size_t)R * e->q_width * 4,     // q
+        tc_att ? 0 : (size_t)R * e->q_width * 4,  // ctx (f32 attention output, CUDA-core form only)
+        (size_t)R * c.ffn * 4,          // h
+        pb.ws_floats * 4,               // ws
+        tc_att ? prompt_attention_tc_bytes(B, P, c.heads, c.kv_heads) : 0,  // att
+        (size_t)R64 * H * 2,            // a_hi
+        (size_t)R64 * H * 2,            // a_lo
+        (size_t)R64 * ky * 2,           // y_hi
+        (size_t)R64 * ky * 2,           // y_lo
+        (size_t)R * 4,                  // tok
+        (size_t)R * 4,                  // pos
+    };
+    constexpr int kN = sizeof(sz) / sizeof(sz[0]);
+    size_t total = 0;
+    for (size_t z : sz) total += (z + 255) / 256 * 256;
+    if (b->arena_bytes < total) {
+        if (b->arena) cudaFree(b->arena);
+        b->arena = nullptr;
+        b->arena_bytes = 0;
+        const cudaError_t ce = cudaMalloc(&b->arena, total);
+        if (ce != cudaSuccess) return cuda_fail(ce, "prefill buffers");
+        b->arena_bytes = total;
     }
     {
-        uint16_t *ah, *al, *yh, *yl;
-        if ((st = balloc(&ah, (size_t)R64 * H, "prefill split"))) return st;
-        pb.a_hi = ah;
-        if ((st = balloc(&al, (size_t)R64 * H, "prefill split"))) return st;
-        pb.a_lo = al;
-        if ((st = balloc(&yh, (size_t)R64 * ky, "prefill split"))) return st;
-        pb.y_hi = yh;
-        if ((st = balloc(&yl, (size_t)R64 * ky, "prefill split"))) return st;
-        pb.y_lo = yl;
+        void* ptr[kN];
+        char* cur = static_cast<char*>(b->arena);
+        for (int i = 0; i < kN; i++) {
+            ptr[i] = sz[i] ? cur : nullptr;
+            cur += (sz[i] + 255) / 256 * 256;
+        }
+        pb.x = static_cast<float*>(ptr[0]);
+        pb.xn = static_cast<float*>(ptr[1]);
+        pb.qkv = static_cast<float*>(ptr[2]);
+        pb.q = static_cast<float*>(ptr[3]);
+        pb.ctx = static_cast<float*>(ptr[4]);
+        pb.h = static_cast<float*>(ptr[5]);
+        pb.ws = static_cast<float*>(ptr[6]);
+        pb.att = ptr[7];
+        pb.a_hi = ptr[8];
+        pb.a_lo = ptr[9];
+        pb.y_hi = ptr[10];
+        pb.y_lo = ptr[11];
+        pb.tok = static_cast<int*>(ptr[12]);
+        pb.pos = static_cast<int*>(ptr[13]);
+    }
+    vb_status st;
+    if (R < 64) {
         // rows past R of a single 64-row tile are read by the MMA: keep them finite
-        VB_CUDA_TRY(cudaMemsetAsync(ah, 0, (size_t)R64 * H * 2, s));
-        VB_CUDA_TRY(cudaMemsetAsync(al, 0, (size_t)R64 * H * 2, s));
-        VB_CUDA_TRY(cudaMemsetAsync(yh, 0, (size_t)R64 * ky * 2, s));
-        VB_CUDA_TRY(cudaMemsetAsync(yl, 0, (size_t)R64 * ky * 2, s));
+        for (void* p : {pb.a_hi, pb.a_lo}) VB_CUDA_TRY(cudaMemsetAsync(p, 0, (size_t)R64 * H * 2, s));
+        for (void* p : {pb.y_hi, pb.y_lo}) VB_CUDA_TRY(cudaMemsetAsync(p, 0, (size_t)R64 * ky * 2, s));
     }
     auto gemm = [&](int M, const void* ahi, const void* alo, void* const* w, const float* sc, float* Cm, int N, int K,
                     int ldc, int epi, bool wq8, void* ohi, void* olo) {
@@ -367,6 +390,14 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
             qa.rope_positions = c.rope_positions < b->max_seq ? c.rope_positions : b->max_seq;
             qa.eps = c.eps;
             qa.err = b->d_err;
+            if (tc_att) {
+                const PromptCopies cp = prompt_attention_copies(pb.att, B, P, c.heads, c.kv_heads);
+                qa.q_hi = cp.q_hi;
+                qa.q_lo = cp.q_lo;
+                qa.k_hi = cp.k_hi;
+                qa.k_lo = cp.k_lo;
+                qa.kbf_rows = P;
+            }
             if ((st = launch_qk_norm_rope_append(qa, s))) return st;
             PrefillAttnArgs pa{};
             pa.q = pb.q;
@@ -386,7 +417,7 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
             pa.err = b->d_err;
             if (tc_att) {
                 pa.out = nullptr;  // the o_proj reads the split only
-                if ((st = launch_prompt_attention_tc(pa, pb.q, pb.att, s))) return st;
+                if ((st = launch_prompt_attention_tc(pa, pb.q, pb.att, s, true))) return st;
             } else if ((st = launch_prefill_attention(pa, s))) {
                 return st;
             }
@@ -561,7 +592,8 @@ vb_status vb_batch_destroy(vb_batch* b) {
     if (b->graph) cudaGraphExecDestroy(b->graph);
     bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->q);
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
-    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err); bfree(b->d_prompt);
+    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err);
+    if (b->arena) cudaFree(b->arena);
     free_tc_weights(b);
     bfree(b->lm_hi); bfree(b->lm_lo); bfree(b->a_hi); bfree(b->a_lo); bfree(b->y_hi); bfree(b->y_lo);
     if (b->h_io) cudaFreeHost(b->h_io);

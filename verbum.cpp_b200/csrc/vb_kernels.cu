@@ -377,63 +377,99 @@ __global__ void reduce_residual_norm_kernel(float* x, const float* parts, int sp
 
 // generate.cpp:52-71 for B rows: per-head RMSNorm (q_norm / k_norm),
 // split-half RoPE from the host table, k and v rows written at pos[b] of the
-// row's sequence (b, or b / rows_per_seq for a prompt chunk).  grid (B, H + KVH),
-// block D (= 128).
-__global__ void __launch_bounds__(128) qk_norm_rope_kernel(QkNormArgs a) {
+// row's sequence (b, or b / rows_per_seq for a prompt chunk).  One warp per
+// (row, head): lane l holds dims l, l + 32, l + 64, l + 96, so the RoPE pairs
+// (d, d + 64) sit in one lane.  grid (B, ceil((H + KVH) / 8)), 256 threads.
+// Optionally also writes bf16 hi/lo copies of q ([B][H*D]) and k
+// ([(seq*KVH + h) * kbf_rows + pos][D]) for the tensor-core prompt attention.
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkNormArgs a) {
     pdl_trigger();
     pdl_wait();
-    const float eps = a.eps;
-    __shared__ double red[4];
-    __shared__ float ys[128];
-    const int b = blockIdx.x, hd = blockIdx.y, d = threadIdx.x;
-    const int D = a.D, half = D >> 1;
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x, hd = blockIdx.y * 8 + (threadIdx.x >> 5);
+    if (hd >= a.H + a.KVH) return;
+    const int D = 128;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.rope_positions) {
-        if (d == 0 && a.err) atomicExch(a.err, kErrCacheFull);
+        if (lane == 0 && a.err) atomicExch(a.err, kErrCacheFull);
         return;
     }
     const int QW = a.H * D, KW = a.KVH * D, RW = QW + 2 * KW;
     const bool isq = hd < a.H;
     const int h = isq ? hd : hd - a.H;
-    const int col = isq ? h * D + d : QW + h * D + d;
-    // the q or k value of this thread, and (k heads) the v value of the same head
-    float xv, vv = 0.f;
+    const int col0 = isq ? h * D : QW + h * D;  // first column of this head's q or k
+    const int vcol0 = QW + KW + h * D;
+    float x[4], v[4] = {0.f, 0.f, 0.f, 0.f};
     if (a.parts) {
-        xv = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) x[e] = 0.f;
         for (int q = 0; q < a.splits; q++) {
             const float* pr = a.parts + ((size_t)q * a.B + b) * RW;
-            xv += pr[col];
-            if (!isq) vv += pr[QW + KW + h * D + d];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                x[e] += pr[col0 + lane + 32 * e];
+                if (!isq) v[e] += pr[vcol0 + lane + 32 * e];
+            }
         }
         if (a.scales) {
-            xv *= a.scales[col];
-            vv *= a.scales[QW + KW + h * D + d];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                x[e] *= a.scales[col0 + lane + 32 * e];
+                if (!isq) v[e] *= a.scales[vcol0 + lane + 32 * e];
+            }
         }
     } else {
         const float* row = a.qkv + (size_t)b * RW;
-        xv = row[col];
-        if (!isq) vv = row[QW + KW + h * D + d];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            x[e] = row[col0 + lane + 32 * e];
+            if (!isq) v[e] = row[vcol0 + lane + 32 * e];
+        }
     }
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) ss += (double)x[e] * (double)x[e];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float sc = rms_scale(ss, D, a.eps);
     const float* nw = isq ? a.q_norm : a.k_norm;
-    const float sc = rms_scale(block_sum_d<128>((double)xv * (double)xv, red), D, eps);
-    ys[d] = __fmul_rn(__fmul_rn(xv, sc), nw[d]);
-    __syncthreads();
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
     const float* c = a.cos_tab + (size_t)pos * D;
     const float* s = a.sin_tab + (size_t)pos * D;
-    float o;
-    if (d < half) {
-        o = __fsub_rn(__fmul_rn(ys[d], c[d]), __fmul_rn(ys[d + half], s[d]));
-    } else {
-        o = __fadd_rn(__fmul_rn(ys[d], c[d]), __fmul_rn(ys[d - half], s[d]));
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int d = lane + 32 * e;
+        o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
+                     : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
     }
+    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(isq ? a.q_hi : a.k_hi);
+    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(isq ? a.q_lo : a.k_lo);
+    size_t bf = 0;
     if (isq) {
-        a.q_out[((size_t)b * a.H + h) * D + d] = o;
+        const size_t qo = ((size_t)b * a.H + h) * D;
+        bf = qo;
+#pragma unroll
+        for (int e = 0; e < 4; e++) a.q_out[qo + lane + 32 * e] = o[e];
     } else {
         const int seq = a.rows_per_seq > 0 ? b / a.rows_per_seq : b;
-        const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos +
-                           (size_t)h * a.stride_h + d;
-        a.kc[off] = o;
-        a.vc[off] = vv;
+        const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos + (size_t)h * a.stride_h;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            a.kc[off + lane + 32 * e] = o[e];
+            a.vc[off + lane + 32 * e] = v[e];
+        }
+        bf = ((size_t)(seq * a.KVH + h) * a.kbf_rows + pos) * D;
+    }
+    if (hi) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const __nv_bfloat16 oh = __float2bfloat16_rn(o[e]);
+            hi[bf + lane + 32 * e] = oh;
+            lo[bf + lane + 32 * e] = __float2bfloat16_rn(o[e] - __bfloat162float(oh));
+        }
     }
 }
 
@@ -871,8 +907,8 @@ vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, 
 
 vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
-    dim3 grid(a.B, a.H + a.KVH);  // rows on x: a prompt chunk has up to 2^31 - 1
-    launch_pdl(qk_norm_rope_kernel, grid, 128, 0, s, a);
+    dim3 grid(a.B, (a.H + a.KVH + 7) / 8);  // rows on x: a prompt chunk has up to 2^31 - 1
+    launch_pdl(qk_norm_rope_kernel, grid, 256, 0, s, a);
     VB_LAUNCH_CHECK("qk_norm_rope_kernel");
     return VB_OK;
 }

@@ -49,6 +49,11 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
 struct QkNormArgs {
     const float* qkv;       // [B, (H + 2*KVH) * D]  (q | k | v)
     int rows_per_seq;       // > 0: row b belongs to sequence b / rows_per_seq (a prompt chunk)
+    void* q_hi;             // optional bf16 hi/lo copies of the q rows [B][H*D]
+    void* q_lo;
+    void* k_hi;             // and of the k rows [(seq*KVH + h) * kbf_rows + pos][D]
+    void* k_lo;
+    int kbf_rows;
     const float* parts;     // or, when set: split-K partials [splits][B][(H + 2*KVH) * D]
     int splits;             //   summed in split order,
     const float* scales;    //   times these INT8 row scales when set
@@ -115,7 +120,14 @@ size_t prefill_attention_smem();
 // `scratch` (prompt_attention_tc_bytes), the split output to a.out_hi/out_lo
 // (and f32 to a.out when set).
 size_t prompt_attention_tc_bytes(int B, int P, int H, int KVH);
-vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s);
+struct PromptCopies {  // where the bf16 copies sit in that scratch
+    void *q_hi, *q_lo, *k_hi, *k_lo, *vt_hi, *vt_lo;
+};
+PromptCopies prompt_attention_copies(void* scratch, int B, int P, int H, int KVH);
+// qk_ready: the q and K copies are already in the scratch (written by the
+// q/k-norm kernel); only V^T is built here.
+vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s,
+                                     bool qk_ready = false);
 
 vb_status launch_embed(const float* E, const int* tokens, int B, int dim, int vocab,
                        float* out, int* err, cudaStream_t s);

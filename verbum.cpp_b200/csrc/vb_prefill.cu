@@ -441,6 +441,44 @@ __global__ void __launch_bounds__(256) prompt_kv_split_kernel(const float* k, co
     }
 }
 
+// bf16 hi / lo copies of V transposed ([B*KVH*128][Ppad], positions along the
+// row) for 64 positions per CTA: coalesced float4 reads, a padded
+// shared-memory transpose, 16-byte stores of 8 positions.  grid
+// (ceil(P / 64), KVH, B), 256 threads.
+__global__ void __launch_bounds__(256) prompt_vt_kernel(const float* v, int64_t stride_b, int64_t stride_h, int P,
+                                                        int Ppad, int KVH, __nv_bfloat16* vt_hi,
+                                                        __nv_bfloat16* vt_lo) {
+    __shared__ float vs[128][65];
+    const int p0 = blockIdx.x * 64, kvh = blockIdx.y, b = blockIdx.z, t = threadIdx.x;
+    const float* src = v + (size_t)b * stride_b + (size_t)kvh * stride_h;
+    for (int i = t; i < 64 * 32; i += 256) {
+        const int pp = i >> 5, d4 = (i & 31) * 4;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p0 + pp < P) x = __ldg(reinterpret_cast<const float4*>(src + (size_t)(p0 + pp) * 128 + d4));
+        vs[d4][pp] = x.x;
+        vs[d4 + 1][pp] = x.y;
+        vs[d4 + 2][pp] = x.z;
+        vs[d4 + 3][pp] = x.w;
+    }
+    __syncthreads();
+    const size_t row0 = (size_t)(b * KVH + kvh) * 128;
+    for (int i = t; i < 128 * 8; i += 256) {
+        const int d = i >> 3, c = i & 7;
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float a = vs[d][8 * c + 2 * q], bb = vs[d][8 * c + 2 * q + 1];
+            const __nv_bfloat16 ah = __float2bfloat16_rn(a), bh = __float2bfloat16_rn(bb);
+            hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
+            lv[q] = pack_bf16(a - __bfloat162float(ah), bb - __bfloat162float(bh));
+        }
+        // positions past P are written as zeros (the padding of the last tile)
+        const size_t o = (row0 + d) * Ppad + p0 + 8 * c;
+        *reinterpret_cast<uint4*>(vt_hi + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(vt_lo + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
 }  // namespace
 
 size_t prefill_attention_smem() { return kPSmem; }
@@ -467,7 +505,21 @@ size_t prompt_attention_tc_bytes(int B, int P, int H, int KVH) {
     return 2 * ((size_t)B * P * H * 128 + (size_t)B * KVH * P * 128 + (size_t)B * KVH * 128 * Ppad) * 2;
 }
 
-vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s) {
+PromptCopies prompt_attention_copies(void* scratch, int B, int P, int H, int KVH) {
+    const int QW = H * 128, Ppad = (P + 63) / 64 * 64;
+    PromptCopies c;
+    __nv_bfloat16* base = static_cast<__nv_bfloat16*>(scratch);
+    c.q_hi = base;
+    c.q_lo = base + (size_t)B * P * QW;
+    c.k_hi = base + 2 * (size_t)B * P * QW;
+    c.k_lo = static_cast<__nv_bfloat16*>(c.k_hi) + (size_t)B * KVH * P * 128;
+    c.vt_hi = static_cast<__nv_bfloat16*>(c.k_lo) + (size_t)B * KVH * P * 128;
+    c.vt_lo = static_cast<__nv_bfloat16*>(c.vt_hi) + (size_t)B * KVH * 128 * Ppad;
+    return c;
+}
+
+vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, void* scratch, cudaStream_t s,
+                                     bool qk_ready) {
     if (a.D != 128 || a.H != 2 * a.KVH || a.p0 != 0 || a.C <= 0 || a.B <= 0)
         return fail(VB_ERR_UNSUPPORTED, "prompt attention (tensor cores): needs D 128, H 2*KVH, a prompt from 0");
     if (!a.out_hi || !a.out_lo) return fail(VB_ERR_ARG, "prompt attention (tensor cores): split output missing");
@@ -475,22 +527,26 @@ vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, v
     const int Ppad = (P + 63) / 64 * 64;
     if ((size_t)B * P > (size_t)1 << 30 || (size_t)B * KVH * 128 > (size_t)1 << 30)
         return fail(VB_ERR_UNSUPPORTED, "prompt attention (tensor cores): too many rows");
-    __nv_bfloat16* base = static_cast<__nv_bfloat16*>(scratch);
-    __nv_bfloat16* q_hi = base;
-    __nv_bfloat16* q_lo = q_hi + (size_t)B * P * QW;
-    __nv_bfloat16* k_hi = q_lo + (size_t)B * P * QW;
-    __nv_bfloat16* k_lo = k_hi + (size_t)B * KVH * P * 128;
-    __nv_bfloat16* vt_hi = k_lo + (size_t)B * KVH * P * 128;
-    __nv_bfloat16* vt_lo = vt_hi + (size_t)B * KVH * 128 * Ppad;
+    const PromptCopies cp = prompt_attention_copies(scratch, B, P, a.H, KVH);
+    __nv_bfloat16 *q_hi = static_cast<__nv_bfloat16*>(cp.q_hi), *q_lo = static_cast<__nv_bfloat16*>(cp.q_lo);
+    __nv_bfloat16 *k_hi = static_cast<__nv_bfloat16*>(cp.k_hi), *k_lo = static_cast<__nv_bfloat16*>(cp.k_lo);
+    __nv_bfloat16 *vt_hi = static_cast<__nv_bfloat16*>(cp.vt_hi), *vt_lo = static_cast<__nv_bfloat16*>(cp.vt_lo);
     vb_status st;
-    if (Ppad != P) {
-        // padding columns of V^T are read by the last key tile (with zero weights): keep them finite
-        VB_CUDA_TRY(cudaMemsetAsync(vt_hi, 0, (size_t)B * KVH * 128 * Ppad * 2 * 2, s));
+    if (qk_ready) {
+        // q and K copies were written by the q/k-norm kernel; V^T here (zero padding included)
+        prompt_vt_kernel<<<dim3(Ppad / 64, KVH, B), 256, 0, s>>>(a.v, a.stride_b, a.stride_h, P, Ppad, KVH, vt_hi,
+                                                                 vt_lo);
+        VB_LAUNCH_CHECK("prompt_vt_kernel");
+    } else {
+        if (Ppad != P) {
+            // padding columns of V^T are read by the last key tile (with zero weights): keep them finite
+            VB_CUDA_TRY(cudaMemsetAsync(vt_hi, 0, (size_t)B * KVH * 128 * Ppad * 2 * 2, s));
+        }
+        if ((st = launch_split_bf16(q, B * P, QW, QW, q_hi, q_lo, s, false))) return st;
+        prompt_kv_split_kernel<<<dim3((P + 31) / 32, KVH, B), 256, 0, s>>>(a.k, a.v, a.stride_b, a.stride_h, P, Ppad,
+                                                                          KVH, k_hi, k_lo, vt_hi, vt_lo);
+        VB_LAUNCH_CHECK("prompt_kv_split_kernel");
     }
-    if ((st = launch_split_bf16(q, B * P, QW, QW, q_hi, q_lo, s, false))) return st;
-    prompt_kv_split_kernel<<<dim3((P + 31) / 32, KVH, B), 256, 0, s>>>(a.k, a.v, a.stride_b, a.stride_h, P, Ppad, KVH,
-                                                                      k_hi, k_lo, vt_hi, vt_lo);
-    VB_LAUNCH_CHECK("prompt_kv_split_kernel");
     CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
     if ((st = tc_make_map(&mqh, q_hi, B * P, QW, 64)) || (st = tc_make_map(&mql, q_lo, B * P, QW, 64)) ||
         (st = tc_make_map(&mkh, k_hi, B * KVH * P, 128, 64)) || (st = tc_make_map(&mkl, k_lo, B * KVH * P, 128, 64)) ||
