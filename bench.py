@@ -676,6 +676,7 @@ def main():
                 "api": "vb_batch_step (host token ids in, host greedy ids out, per step)"},
         "gpu_launches": res["graph_nodes"] * K,
         "prefill_s": round(res["prefill_s"], 3),
+        "prefill_tok_s": round(N * B * args.prompt / res["prefill_s"], 1),
     }
     if grp.rank == 0 and N == 1 and not args.no_extras:
         names = {0: "fused step, grid barriers", 1: "per-op CUDA graph", 2: "clustered step, tagged exchange"}
