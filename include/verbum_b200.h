@@ -283,6 +283,27 @@ VB_API vb_status vb_engine_set_trace(vb_engine* e, int on);
 VB_API int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap);
 
 /* ------------------------------------------------------------------------ */
+/* Sampling: Sampler / SamplerConfig (generate.h:49-67, generate.cpp:197-252)  */
+/* on the device.  The host keeps the reference's generator                 */
+/* (std::mt19937_64(seed), one std::uniform_real_distribution<double> draw   */
+/* per non-greedy sample); the device sorts the logits, applies temperature, */
+/* top_k (0 disables) and top_p (1 disables) and picks.  temperature <= 0 or */
+/* top_k == 1 is the greedy argmax, as in the reference.                    */
+/* ------------------------------------------------------------------------ */
+typedef struct vb_sampler vb_sampler;
+VB_API vb_status vb_sampler_create(float temperature, int top_k, float top_p, uint64_t seed,
+                                   vb_sampler** out);
+VB_API vb_status vb_sampler_destroy(vb_sampler* s);
+/* One Sampler::sample of device logits [vocab]; synchronous on `stream`. */
+VB_API vb_status vb_sampler_sample(vb_sampler* s, const float* logits, int64_t vocab, void* stream,
+                                   int* token);
+/* n decode steps from first_token with each next token drawn by the sampler on
+ * the device (the generate loop of tools/generate.cpp:63-90 without a host
+ * round trip per token); the n picks go to tokens_host if not NULL. */
+VB_API vb_status vb_engine_decode_sampled(vb_engine* e, vb_sampler* s, int first_token, int n,
+                                          int* tokens_host);
+
+/* ------------------------------------------------------------------------ */
 /* Batched independent-sequence decode (no reference counterpart; the
  * reference is batch-1 only).  B sequences share the engine's weights; each
  * has its own KV cache and position.                                        */

@@ -66,6 +66,7 @@ def olib():
             "or_attention_decode": (None, [_P, _P, _P, _L, _I, _I, _I, _I, _P]),
             "or_silu_mul": (None, [_P, _P, _L]),
             "or_argmax": (_I, [_P, _L]),
+            "or_sample_seq": (_I, [_F, _I, _F, C.c_uint64, _P, _L, _I, _P]),
             "or_last_error": (C.c_char_p, []),
             "or_model_create": (_P, [C.POINTER(OrConfig), _P, _P, C.POINTER(OrLayer)]),
             "or_model_free": (None, [_P]),
@@ -115,6 +116,7 @@ def rlib():
             "ref_rope_table": (_I, [_I, _I, _F, _P, _P]),
             "ref_apply_rope": (_I, [_P, _L, _I, _I, _I, _F]),
             "ref_greedy": (_I, [_P, _L]),
+            "ref_sample_seq": (_I, [_F, _I, _F, C.c_uint64, _P, _L, _I, _P]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -204,6 +206,28 @@ def silu_mul(g, u):
 def argmax(logits):
     logits = f32(logits)
     return int(olib().or_argmax(_p(logits), logits.size))
+
+
+def sample_seq(logits, temperature, top_k, top_p, seed):
+    """generate.cpp:197-252: one Sampler over the rows of logits [n, vocab]."""
+    logits = f32(logits)
+    n, vocab = logits.shape
+    out = np.empty(n, np.int32)
+    if olib().or_sample_seq(float(temperature), int(top_k), float(top_p), int(seed), _p(logits), vocab, n,
+                            _p(out)) != 0:
+        raise MemoryError("or_sample_seq")
+    return out
+
+
+def ref_sample_seq(logits, temperature, top_k, top_p, seed):
+    """The reference Sampler itself (oracle/_ref), for pinning sample_seq."""
+    logits = f32(logits)
+    n, vocab = logits.shape
+    out = np.empty(n, np.int32)
+    if rlib().ref_sample_seq(float(temperature), int(top_k), float(top_p), int(seed), _p(logits), vocab, n,
+                             _p(out)) != 0:
+        raise RuntimeError(rlib().ref_last_error().decode())
+    return out
 
 
 # ---- whole model --------------------------------------------------------------

@@ -230,4 +230,18 @@ int ref_greedy(const float* logits, int64_t vocab) {
     return s.sample(logits, vocab);
 }
 
+// One Sampler, n calls: row i of logits [n][vocab] -> out[i].
+int ref_sample_seq(float temperature, int top_k, float top_p, uint64_t seed, const float* logits, int64_t vocab,
+                   int n, int* out) {
+    return guarded([&] {
+        verbum::SamplerConfig sc;
+        sc.temperature = temperature;
+        sc.top_k = top_k;
+        sc.top_p = top_p;
+        sc.seed = seed;
+        verbum::Sampler s(sc);
+        for (int i = 0; i < n; i++) out[i] = s.sample(logits + (size_t)i * vocab, vocab);
+    });
+}
+
 }  // extern "C"

@@ -205,6 +205,126 @@ int or_argmax(const float* logits, int64_t vocab) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* sampling (generate.cpp:197-252)                                          */
+/* ------------------------------------------------------------------------ */
+
+/* MT19937-64 (Matsumoto & Nishimura), the std::mt19937_64 parameters. */
+typedef struct {
+    uint64_t mt[312];
+    int idx;
+} or_mt64;
+
+static void or_mt64_seed(or_mt64* g, uint64_t seed) {
+    g->mt[0] = seed;
+    for (int i = 1; i < 312; i++)
+        g->mt[i] = 6364136223846793005ULL * (g->mt[i - 1] ^ (g->mt[i - 1] >> 62)) + (uint64_t)i;
+    g->idx = 312;
+}
+
+static uint64_t or_mt64_next(or_mt64* g) {
+    const uint64_t upper = 0xFFFFFFFF80000000ULL, lower = 0x7FFFFFFFULL;
+    if (g->idx >= 312) {
+        for (int i = 0; i < 312; i++) {
+            const uint64_t y = (g->mt[i] & upper) | (g->mt[(i + 1) % 312] & lower);
+            uint64_t v = g->mt[(i + 156) % 312] ^ (y >> 1);
+            if (y & 1ULL) v ^= 0xB5026F5AA96619E9ULL;
+            g->mt[i] = v;
+        }
+        g->idx = 0;
+    }
+    uint64_t x = g->mt[g->idx++];
+    x ^= (x >> 29) & 0x5555555555555555ULL;
+    x ^= (x << 17) & 0x71D67FFFEDA60000ULL;
+    x ^= (x << 37) & 0xFFF7EEE000000000ULL;
+    x ^= x >> 43;
+    return x;
+}
+
+static double or_uniform01(or_mt64* g) {
+    double r = (double)or_mt64_next(g) / 18446744073709551616.0;
+    if (r >= 1.0) r = nextafter(1.0, 0.0);
+    return r;
+}
+
+typedef struct {
+    float v;
+    int i;
+} or_cand;
+
+static int or_cand_cmp(const void* a, const void* b) {
+    const or_cand* x = (const or_cand*)a;
+    const or_cand* y = (const or_cand*)b;
+    if (x->v > y->v) return -1;
+    if (x->v < y->v) return 1;
+    return (x->i > y->i) - (x->i < y->i);
+}
+
+int or_sample_seq(float temperature, int top_k, float top_p, uint64_t seed, const float* logits, int64_t vocab,
+                  int n, int* out) {
+    or_mt64 g;
+    or_mt64_seed(&g, seed);
+    or_cand* c = (or_cand*)malloc(sizeof(or_cand) * (size_t)vocab);
+    float* p = (float*)malloc(sizeof(float) * (size_t)vocab);
+    if (!c || !p) {
+        free(c);
+        free(p);
+        return -1;
+    }
+    for (int s = 0; s < n; s++) {
+        const float* lg = logits + (size_t)s * vocab;
+        if (temperature <= 0.0f || top_k == 1) {
+            out[s] = or_argmax(lg, vocab);
+            continue;
+        }
+        for (int64_t i = 0; i < vocab; i++) {
+            c[i].v = lg[i];
+            c[i].i = (int)i;
+        }
+        qsort(c, (size_t)vocab, sizeof(or_cand), or_cand_cmp);
+        int64_t keep = vocab;
+        if (top_k > 0 && top_k < keep) keep = top_k;
+        const float m = c[0].v;
+        double sum = 0.0;
+        for (int64_t i = 0; i < keep; i++) {
+            const float d = c[i].v - m;
+            const float q = d / temperature;
+            p[i] = expf(q);
+            sum += p[i];
+        }
+        for (int64_t i = 0; i < keep; i++) p[i] = (float)(p[i] / sum);
+        if (top_p < 1.0f) {
+            double cum = 0.0;
+            int64_t cut = keep;
+            for (int64_t i = 0; i < keep; i++) {
+                cum += p[i];
+                if (cum >= top_p) {
+                    cut = i + 1;
+                    break;
+                }
+            }
+            keep = cut;
+            double renorm = 0.0;
+            for (int64_t i = 0; i < keep; i++) renorm += p[i];
+            for (int64_t i = 0; i < keep; i++) p[i] = (float)(p[i] / renorm);
+        }
+        const double r = or_uniform01(&g);
+        double cum = 0.0;
+        int pick = c[keep - 1].i;
+        for (int64_t i = 0; i < keep; i++) {
+            cum += p[i];
+            if (r <= cum) {
+                pick = c[i].i;
+                break;
+            }
+        }
+        out[s] = pick;
+    }
+    free(c);
+    free(p);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
 /* whole model                                                              */
 /* ------------------------------------------------------------------------ */
 

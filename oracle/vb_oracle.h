@@ -76,6 +76,16 @@ void or_silu_mul(float* gate, const float* up, int64_t n);
 /* generate.cpp:199-206  greedy pick: strict '>' scan from index 0. */
 int or_argmax(const float* logits, int64_t vocab);
 
+/* generate.cpp:197-252  Sampler(cfg).sample() called n times with one
+ * generator: row i of logits [n][vocab] gives out[i].  The generator is
+ * std::mt19937_64(seed) (the published MT19937-64 recurrence and seeding) and
+ * each non-greedy call draws one uniform double in [0, 1) the way
+ * std::uniform_real_distribution<double> does with libstdc++ (one 64-bit
+ * output scaled by 2^-64, clamped below 1).  Candidates are ordered by value,
+ * ties by index (the reference's partial_sort leaves tie order unspecified). */
+int or_sample_seq(float temperature, int top_k, float top_p, uint64_t seed,
+                  const float* logits, int64_t vocab, int n, int* out);
+
 /* ---- whole-model decode step (model.cpp:235-311, generate.cpp:24-108) ---- */
 
 typedef struct {

@@ -596,6 +596,36 @@ vb_status vb_engine_decode(vb_engine* e, int first_token, int n, int* tokens_hos
     return VB_OK;
 }
 
+vb_status vb_engine_decode_sampled(vb_engine* e, vb_sampler* sp, int first_token, int n, int* tokens_host) {
+    if (!e || !sp) return fail(VB_ERR_ARG, "null argument");
+    if (sampler_greedy(sp)) return vb_engine_decode(e, first_token, n, tokens_host, nullptr);
+    if (n <= 0) return VB_OK;
+    DeviceGuard dg(e->device);
+    vb_status st = pre_step(e, n);
+    if (st) return st;
+    if (first_token < 0 || first_token >= e->cfg.vocab)
+        return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    if ((st = sampler_draws(sp, n, e->stream))) return st;
+    e->h_pinned_i[0] = first_token;
+    e->h_pinned_i[1] = 0;
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_tok, e->h_pinned_i, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    VB_CUDA_TRY(cudaMemcpyAsync(e->d_step, e->h_pinned_i + 1, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    for (int i = 0; i < n; i++) {
+        // the step leaves the logits and its greedy pick; the sample replaces the pick
+        if ((st = launch_step(e))) return st;
+        if ((st = launch_sample(sp, e->logits, e->cfg.vocab, i, e->d_next, e->d_tok, e->d_next, e->d_hist, e->d_step,
+                                e->max_seq, e->stream)))
+            return st;
+    }
+    if (tokens_host)
+        VB_CUDA_TRY(cudaMemcpyAsync(tokens_host, e->d_hist, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost,
+                                    e->stream));
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if ((st = engine_check_err(e))) return st;
+    e->len += n;
+    return VB_OK;
+}
+
 vb_status vb_engine_prefill(vb_engine* e, const int* tokens_host, int n, float* logits_host) {
     if (!e || !tokens_host) return fail(VB_ERR_ARG, "null argument");
     if (n <= 0) return VB_OK;

@@ -119,4 +119,12 @@ int mega2_read_trace(vb_engine* e, unsigned long long* host, int cap);
 int mega_read_trace(vb_engine* e, unsigned long long* host, int cap);
 vb_status engine_check_err(vb_engine* e);
 void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s);
+// Device sampling (vb_sample.cu).
+bool sampler_greedy(const vb_sampler* sp);
+// n draws of the sampler's generator, uploaded for the next n samples.
+vb_status sampler_draws(vb_sampler* sp, int n, cudaStream_t s);
+// Sample logits [vocab] with draw `draw`; the pick goes to *out and, when tok
+// is set, into tok / next and hist[*step - 1].
+vb_status launch_sample(vb_sampler* sp, const float* logits, int64_t vocab, int draw, int* out, int* tok, int* next,
+                        int* hist, const int* step, int hist_cap, cudaStream_t s);
 }  // namespace vb

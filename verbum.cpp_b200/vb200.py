@@ -105,6 +105,10 @@ _SIGS = {
     "vb_batch_prefill": (_I, [_P, _P, _I, _P]),
     "vb_batch_graph_nodes": (_I, [_P]),
     "vb_batch_reset": (_I, [_P]),
+    "vb_sampler_create": (_I, [_F, _I, _F, C.c_uint64, _P]),
+    "vb_sampler_destroy": (_I, [_P]),
+    "vb_sampler_sample": (_I, [_P, _P, _L, _P, _P]),
+    "vb_engine_decode_sampled": (_I, [_P, _P, _I, _I, _P]),
     "vb_batch_truncate": (_I, [_P, _I]),
 }
 
@@ -219,6 +223,12 @@ class Engine:
             out = np.empty(self.vocab, dtype=np.float32)
         check(lib().vb_engine_step(self.h, int(token), _ptr(out)))
         return out
+
+    def decode_sampled(self, sampler: "Sampler", first_token: int, n: int) -> np.ndarray:
+        """n decode steps, each next token drawn by `sampler` on the device."""
+        toks = np.empty(int(n), dtype=np.int32)
+        check(lib().vb_engine_decode_sampled(self.h, sampler.h, int(first_token), int(n), _ptr(toks)))
+        return toks
 
     def decode(self, first_token: int, n: int, want_logits=False):
         toks = np.empty(int(n), dtype=np.int32)
@@ -414,6 +424,33 @@ def attn_prefill(q, k, v, out, B, C, p0, H, KVH, D, stride_b, stride_h, stream=N
     """Causal attention of a prompt chunk: q / out [B*C, H*D]; caches [B, KVH, n, D]."""
     check(lib().vb_attn_prefill(_tp(q), _tp(k), _tp(v), _tp(out), B, C, p0, H, KVH, D, stride_b,
                                 stride_h, _stream(stream)))
+
+
+class Sampler:
+    """Sampler / SamplerConfig (generate.h:49-67): temperature, top_k (0
+    disables), top_p (1 disables), seed of the host std::mt19937_64."""
+
+    def __init__(self, temperature=0.8, top_k=40, top_p=0.95, seed=0):
+        h = C.c_void_p()
+        check(lib().vb_sampler_create(float(temperature), int(top_k), float(top_p), int(seed), C.byref(h)))
+        self.h = h
+
+    def sample(self, logits, stream=None) -> int:
+        """One Sampler::sample of a device logits row."""
+        tok = C.c_int()
+        check(lib().vb_sampler_sample(self.h, _tp(logits), int(logits.numel()), _stream(stream), C.byref(tok)))
+        return tok.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vb_sampler_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def argmax_rows(logits, out_idx, stream=None):
