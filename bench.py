@@ -533,6 +533,18 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
     ev1.record(stream)
     ev1.synchronize()
     sec = ev0.elapsed_time(ev1) / 1e3
+    # the same decode with the reference's default sampler (T 0.8, top-k 40,
+    # top-p 0.95) on the device
+    e.reset_cache(max_seq)
+    e.prefill(prompt)
+    smp = vb200.Sampler(0.8, 40, 0.95, 1234)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    e.decode_sampled(smp, first, n_new)
+    ev1.record(stream)
+    ev1.synchronize()
+    sec_sampled = ev0.elapsed_time(ev1) / 1e3
+    smp.close()
     # end to end, reference semantics: step(token) -> logits in host memory
     e.reset_cache(max_seq)
     e.prefill(prompt)
@@ -565,6 +577,7 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
     return {"tok_s": n_new / sec, "ms_per_token": 1e3 * sec / n_new, "bytes_per_token": bytes_tok,
             "achieved_gbs": bytes_tok * n_new / sec / 1e9, "e2e_tok_s": n_new / e2e,
             "e2e_p50_ms": 1e3 * lat[len(lat) // 2], "e2e_p99_ms": 1e3 * lat[min(len(lat) - 1, int(0.99 * len(lat)))],
+            "sampled_tok_s": round(n_new / sec_sampled, 2),
             "graph_nodes": nodes, "weight_bytes": wb, "prompt": prompt_len, "decode_tokens": n_new,
             "path": "fused persistent step" if nodes == 1 else "per-op CUDA graph",
             "first_tokens": [int(t) for t in toks[:4]], **({"trace": tb} if tb else {})}
