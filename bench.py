@@ -535,9 +535,12 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
     sec = ev0.elapsed_time(ev1) / 1e3
     # the same decode with the reference's default sampler (T 0.8, top-k 40,
     # top-p 0.95) on the device
+    smp = vb200.Sampler(0.8, 40, 0.95, 1234)
     e.reset_cache(max_seq)
     e.prefill(prompt)
-    smp = vb200.Sampler(0.8, 40, 0.95, 1234)
+    e.decode_sampled(smp, first, warm)  # sizes the sampler's buffers
+    e.reset_cache(max_seq)
+    e.prefill(prompt)
     torch.cuda.synchronize()
     ev0.record(stream)
     e.decode_sampled(smp, first, n_new)

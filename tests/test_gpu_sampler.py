@@ -79,3 +79,19 @@ def eng_greedy(cfg, w, path, first, n):
     toks = e.decode(first, n)
     e.close()
     return toks
+
+
+def test_device_sampler_ties_at_the_threshold():
+    """More than 4096 logits tie with the k-th largest: the selection fallback
+    (ties ordered by index, like the oracle)."""
+    V = 20000
+    rng = np.random.default_rng(5)
+    lg = np.full((6, V), 1.0, np.float32)
+    for r in lg:
+        r[rng.choice(V, 10, replace=False)] = np.float32(2.0) + rng.permutation(10).astype(np.float32)
+    dev = torch.from_numpy(lg).cuda()
+    want = oracle.sample_seq(lg, 0.9, 40, 0.95, 3)
+    s = vb200.Sampler(0.9, 40, 0.95, 3)
+    got = [s.sample(dev[i]) for i in range(len(lg))]
+    s.close()
+    np.testing.assert_array_equal(np.array(got), want)
