@@ -238,6 +238,14 @@ VB_API vb_status vb_engine_set_layer(vb_engine* e, int layer, const vb_layer_hos
  * the f32 copies are freed.  Embedding, lm_head and norms stay f32. */
 VB_API vb_status vb_engine_quantize(vb_engine* e);
 VB_API int vb_engine_is_quantized(const vb_engine* e);
+/* Opt-in, no reference counterpart (the reference keeps the tied lm_head in
+ * f32, model.cpp:313-338): quantize_rows of the embedding rows becomes the
+ * lm_head (matmul_nt_q8); the embedding lookup keeps the f32 table.  Cuts the
+ * lm_head's 622 MB per token to 156 MB; logits then differ from the
+ * reference's by the quantisation of the lm_head (not a parity mode).  Applies
+ * to the engine's steps and to batches made from it. */
+VB_API vb_status vb_engine_quantize_lm_head(vb_engine* e);
+VB_API int vb_engine_lm_head_int8(const vb_engine* e);
 /* Model::weight_bytes (model.cpp:340-365). */
 VB_API size_t vb_engine_weight_bytes(const vb_engine* e);
 /* Model::reset_cache (model.cpp:277-282): (re)allocates the device KV cache

@@ -71,6 +71,7 @@ def olib():
             "or_model_create": (_P, [C.POINTER(OrConfig), _P, _P, C.POINTER(OrLayer)]),
             "or_model_free": (None, [_P]),
             "or_model_quantize": (_I, [_P]),
+            "or_model_quantize_lm_head": (_I, [_P]),
             "or_model_is_quantized": (_I, [_P]),
             "or_model_quant_tensor": (_I, [_P, _I, _I, C.POINTER(C.c_void_p),
                                            C.POINTER(C.c_void_p), C.POINTER(_L), C.POINTER(_L)]),
@@ -264,6 +265,10 @@ class OracleModel:
 
     def quantize(self):
         assert olib().or_model_quantize(self.h) == 0
+
+    def quantize_lm_head(self):
+        """Opt-in INT8 tied lm_head (no reference counterpart)."""
+        assert olib().or_model_quantize_lm_head(self.h) == 0
 
     def quant_tensor(self, layer, which):
         q, s = C.c_void_p(), C.c_void_p()

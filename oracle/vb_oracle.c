@@ -341,6 +341,8 @@ struct or_model {
     or_layer_weights* L;
     int quantized;
     qt* Q; /* [layers*7] */
+    int8_t* lm_q; /* opt-in INT8 tied lm_head (quantize_rows of embed), or NULL */
+    float* lm_s;
     float* rope_cos;
     float* rope_sin;
     /* caches */
@@ -409,6 +411,8 @@ void or_model_free(or_model* m) {
         }
         free(m->Q);
     }
+    free(m->lm_q);
+    free(m->lm_s);
     free(m->L);
     free(m->rope_cos);
     free(m->rope_sin);
@@ -559,7 +563,23 @@ int or_model_step(or_model* m, int token, float* logits) {
     }
     m->len++;
     or_rmsnorm(m->x, m->final_norm, c->eps, m->normed, 1, hd);
-    or_matmul_nt(m->normed, m->embed, logits, 1, c->vocab, hd);
+    if (m->lm_q)
+        or_matmul_nt_q8(m->normed, m->lm_q, m->lm_s, logits, 1, c->vocab, hd);
+    else
+        or_matmul_nt(m->normed, m->embed, logits, 1, c->vocab, hd);
+    return 0;
+}
+
+/* Opt-in (no reference counterpart: the reference keeps the tied lm_head in
+ * f32, model.cpp:313-338): the lm_head product with the embedding rows
+ * quantised by quantize_rows and multiplied as matmul_nt_q8. */
+int or_model_quantize_lm_head(or_model* m) {
+    if (m->lm_q) return 0;
+    const int64_t V = m->c.vocab, hd = m->c.hidden;
+    m->lm_q = (int8_t*)malloc((size_t)V * hd);
+    m->lm_s = (float*)malloc(sizeof(float) * (size_t)V);
+    if (!m->lm_q || !m->lm_s) return -1;
+    or_quantize_rows(m->embed, V, hd, m->lm_q, m->lm_s);
     return 0;
 }
 

@@ -130,6 +130,8 @@ or_model* or_model_create(const or_config* cfg, const float* embed,
 void or_model_free(or_model* m);
 /* model.cpp:313-338: quantize the 7 projections of every layer. */
 int or_model_quantize(or_model* m);
+/* Opt-in INT8 tied lm_head: quantize_rows of the embedding, matmul_nt_q8. */
+int or_model_quantize_lm_head(or_model* m);
 int or_model_is_quantized(const or_model* m);
 /* which: 0 q,1 k,2 v,3 o,4 gate,5 up,6 down. Pointers stay owned by m. */
 int or_model_quant_tensor(const or_model* m, int layer, int which,

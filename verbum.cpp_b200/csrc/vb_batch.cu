@@ -40,6 +40,7 @@ struct vb_batch {
     int* h_io = nullptr;  // pinned [2*B + 1]: tokens in, next tokens out, error word
     cudaGraphExec_t graph = nullptr;
     bool graph_q8 = false;
+    bool graph_lm8 = false;
     int graph_nodes = 0;
     void* arena = nullptr;    // prefill buffers, kept for the next prefill
     size_t arena_bytes = 0;
@@ -48,6 +49,7 @@ struct vb_batch {
     void* lm_hi = nullptr;
     void* lm_lo = nullptr;
     bool tc_q8 = false;       // which weights tcw holds
+    bool tc_lm8 = false;      // lm_hi holds the INT8 lm_head (exact in bf16), lm_lo unused
     bool tc_ready = false;
     void* a_hi = nullptr;     // [64][hidden] bf16 split of the normed input (QKV, gate/up, lm_head)
     void* a_lo = nullptr;
@@ -82,7 +84,7 @@ void free_tc_weights(vb_batch* b) {
 // quantised after the batch was made); the lm_head pair is built once.
 vb_status batch_tc_weights(vb_batch* b) {
     vb_engine* e = b->e;
-    if (b->tc_ready && b->tc_q8 == e->quantized) return VB_OK;
+    if (b->tc_ready && b->tc_q8 == e->quantized && b->tc_lm8 == e->lm_int8) return VB_OK;
     const vb_config& c = e->cfg;
     cudaStream_t s = e->stream;
     const bool q8 = e->quantized;
@@ -103,11 +105,16 @@ vb_status batch_tc_weights(vb_batch* b) {
             if ((st = launch_weights_bf16(src[j], q8, n, hl[0], hl[1], s))) return st;
         }
     }
-    if (!b->lm_hi) {
+    if (!b->lm_hi || b->tc_lm8 != e->lm_int8) {
         const size_t n = (size_t)c.vocab * c.hidden;
-        VB_CUDA_TRY(cudaMalloc(&b->lm_hi, n * 2));
-        VB_CUDA_TRY(cudaMalloc(&b->lm_lo, n * 2));
-        if ((st = launch_weights_bf16(e->embed, false, n, b->lm_hi, b->lm_lo, s))) return st;
+        if (!b->lm_hi) VB_CUDA_TRY(cudaMalloc(&b->lm_hi, n * 2));
+        if (!b->lm_lo) VB_CUDA_TRY(cudaMalloc(&b->lm_lo, n * 2));
+        if (e->lm_int8) {
+            if ((st = launch_weights_bf16(e->lm_q8, true, n, b->lm_hi, nullptr, s))) return st;
+        } else if ((st = launch_weights_bf16(e->embed, false, n, b->lm_hi, b->lm_lo, s))) {
+            return st;
+        }
+        b->tc_lm8 = e->lm_int8;
     }
     VB_CUDA_TRY(cudaStreamSynchronize(s));
     b->tc_q8 = q8;
@@ -220,8 +227,8 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     }
     {
         void* const lm[2] = {b->lm_hi, b->lm_lo};
-        if ((st = gemm(b->a_hi, b->a_lo, lm, nullptr, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore, false,
-                       nullptr, nullptr)))
+        if ((st = gemm(b->a_hi, b->a_lo, lm, e->lm_sc, b->logits, c.vocab, c.hidden, c.vocab, kEpiStore,
+                       e->lm_int8, nullptr, nullptr)))
             return st;
     }
     if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
@@ -438,8 +445,8 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
                                   sizeof(float) * H, B, cudaMemcpyDeviceToDevice, s));
     if ((st = launch_rmsnorm_rows(b->x, e->final_norm, b->xn, B, H, c.eps, s, b->a_hi, b->a_lo))) return st;
     void* const lm[2] = {b->lm_hi, b->lm_lo};
-    if ((st = gemm(B, b->a_hi, b->a_lo, lm, nullptr, b->logits, c.vocab, H, c.vocab, kEpiStore, false, nullptr,
-                   nullptr)))
+    if ((st = gemm(B, b->a_hi, b->a_lo, lm, e->lm_sc, b->logits, c.vocab, H, c.vocab, kEpiStore, e->lm_int8,
+                   nullptr, nullptr)))
         return st;
     if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
     // decode state after P steps: tokens = picks, positions += P
@@ -451,7 +458,7 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
 }
 
 vb_status batch_graph(vb_batch* b) {
-    if (b->graph && b->graph_q8 == b->e->quantized) return VB_OK;
+    if (b->graph && b->graph_q8 == b->e->quantized && b->graph_lm8 == b->e->lm_int8) return VB_OK;
     if (vb_status ws = batch_tc_weights(b)) return ws;
     if (b->graph) cudaGraphExecDestroy(b->graph);
     b->graph = nullptr;
@@ -475,6 +482,7 @@ vb_status batch_graph(vb_batch* b) {
         return cuda_fail(ce, "cudaGraphInstantiate");
     }
     b->graph_q8 = b->e->quantized;
+    b->graph_lm8 = b->e->lm_int8;
     // upload now so the first launch does not pay for it
     ce = cudaGraphUpload(b->graph, s);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphUpload");

@@ -210,14 +210,15 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
     lm.x = e->x;
     lm.norm_w = e->final_norm;
     lm.eps = c.eps;
-    lm.W = e->embed;
+    lm.W = e->lm_int8 ? static_cast<const void*>(e->lm_q8) : static_cast<const void*>(e->embed);
+    lm.scales = e->lm_int8 ? e->lm_sc : nullptr;
     lm.y = e->logits;
     lm.N = c.vocab;
     lm.K = c.hidden;
     lm.part_val = e->part_val;
     lm.part_idx = e->part_idx;
     int parts = 0;
-    if ((st = launch_gemv(lm, false, kProRms, kEpiArgmax, s, &parts))) return st;
+    if ((st = launch_gemv(lm, e->lm_int8, kProRms, kEpiArgmax, s, &parts))) return st;
     if ((st = launch_argmax_parts(e->part_val, e->part_idx, parts, e->d_next, s))) return st;
     engine_advance_kernel<<<1, 32, 0, s>>>(e->d_pos, e->d_tok, e->d_next, e->d_hist, e->d_step,
                                            e->max_seq);
@@ -354,7 +355,7 @@ vb_status vb_engine_create(const vb_config* cfg, int device, vb_engine** out) {
     if ((st = dalloc(&e->ctx, e->q_width, "ctx"))) return bail(st);
     if ((st = dalloc(&e->h, c.ffn, "h"))) return bail(st);
     if ((st = dalloc(&e->logits, c.vocab, "logits"))) return bail(st);
-    const int parts = gemv_grid(c.vocab, false, kEpiArgmax);
+    const int parts = std::max(gemv_grid(c.vocab, false, kEpiArgmax), gemv_grid(c.vocab, true, kEpiArgmax));
     if ((st = dalloc(&e->part_val, parts, "argmax parts"))) return bail(st);
     if ((st = dalloc(&e->part_idx, parts, "argmax parts"))) return bail(st);
     if ((st = dalloc(&e->d_tok, 1, "tok"))) return bail(st);
@@ -382,7 +383,7 @@ vb_status vb_engine_destroy(vb_engine* e) {
     mega2_release(e);
     free_cache(e);
     dfree(e->embed); dfree(e->final_norm); dfree(e->rope_cos); dfree(e->rope_sin);
-    dfree(e->norms); dfree(e->wf32); dfree(e->wi8); dfree(e->wscale);
+    dfree(e->norms); dfree(e->wf32); dfree(e->wi8); dfree(e->wscale); dfree(e->lm_q8); dfree(e->lm_sc);
     dfree(e->x); dfree(e->qkv); dfree(e->q); dfree(e->ctx); dfree(e->h); dfree(e->logits);
     dfree(e->part_val); dfree(e->part_idx); dfree(e->d_tok); dfree(e->d_pos); dfree(e->d_next);
     dfree(e->d_err); dfree(e->d_step);
@@ -476,6 +477,27 @@ vb_status vb_engine_quantize(vb_engine* e) {
 }
 
 int vb_engine_is_quantized(const vb_engine* e) { return e && e->quantized ? 1 : 0; }
+
+vb_status vb_engine_quantize_lm_head(vb_engine* e) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    if (e->lm_int8) return VB_OK;
+    if (!e->globals_set) return fail(VB_ERR_STATE, "engine weights not uploaded");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    vb_status st;
+    if ((st = dalloc(&e->lm_q8, (size_t)c.vocab * c.hidden, "int8 lm_head"))) return st;
+    if ((st = dalloc(&e->lm_sc, (size_t)c.vocab, "lm_head scales"))) return st;
+    if ((st = launch_quantize_rows(e->embed, c.vocab, c.hidden, e->lm_q8, e->lm_sc, e->stream))) return st;
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    e->lm_int8 = true;
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    e->graph = nullptr;
+    mega_release(e);
+    mega2_release(e);
+    return VB_OK;
+}
+
+int vb_engine_lm_head_int8(const vb_engine* e) { return e && e->lm_int8 ? 1 : 0; }
 
 size_t vb_engine_weight_bytes(const vb_engine* e) {
     if (!e) return 0;

@@ -58,6 +58,10 @@ struct vb_engine {
     float* wf32 = nullptr;     // all f32 projections
     int8_t* wi8 = nullptr;     // all int8 projections
     float* wscale = nullptr;   // all scales
+    // opt-in INT8 copy of the tied lm_head (the embedding lookup stays f32)
+    int8_t* lm_q8 = nullptr;
+    float* lm_sc = nullptr;
+    bool lm_int8 = false;
     std::vector<vb_layer_dev> L;
     std::vector<int> layer_set;
     bool globals_set = false;

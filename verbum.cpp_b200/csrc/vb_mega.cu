@@ -810,6 +810,7 @@ struct MegaState {
 
 vb_status mega_prepare(vb_engine* e) {
     const vb_config& c = e->cfg;
+    if (e->lm_int8) return fail(VB_ERR_UNSUPPORTED, "fused step: f32 lm_head only");
     if (c.heads != 2 * c.kv_heads || c.head_dim != 128)
         return fail(VB_ERR_UNSUPPORTED, "fused step: needs GQA group 2 and head_dim 128");
     const int ks[3] = {c.hidden, e->q_width, c.ffn};

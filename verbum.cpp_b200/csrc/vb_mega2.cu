@@ -85,6 +85,8 @@ struct M2Layer {
 struct M2Params {
     const M2Layer* layers;
     const float* embed;
+    const int8_t* lm_q8;   // opt-in INT8 lm_head rows (else the f32 embedding)
+    const float* lm_sc;
     const float* final_norm;
     const float* rope_cos;
     const float* rope_sin;
@@ -348,7 +350,7 @@ __device__ __forceinline__ Plan plan_dt(const M2Params& p, int l, bool q8, int b
 __device__ __forceinline__ Plan plan_lm(const M2Params& p, int b, int G) {
     int r0, r1;
     split(p.vocab, b, G, 1, r0, r1);
-    return make_plan(p.embed, p.hidden, false, r0, r1, 1);
+    return p.lm_q8 ? make_plan(p.lm_q8, p.hidden, true, r0, r1, 1) : make_plan(p.embed, p.hidden, false, r0, r1, 1);
 }
 
 // --------------------------------------------------------------- consumers
@@ -1293,12 +1295,22 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     if (!ok) goto consumer_exit;
     // ---- LM: final norm + lm_head + argmax
     if (!residual_norm(p, S, xs, p.xd + (size_t)((p.nlayers - 1) & 1) * p.nclusters * p.hidden, p.nclusters,
-                       xtag(ep1, p.nlayers - 1, kXGlobal), nullptr, nw, false, 0, -1))
+                       xtag(ep1, p.nlayers - 1, kXGlobal), nullptr, nw, p.lm_q8 != nullptr, 0, -1))
         goto consumer_exit;
     {
         const Plan pl = plan_lm(p, b, G);
         const Epi epi{kEpiLogits, 0u, 0u, nullptr, nullptr, 0, p.logits};
-        const bool r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, epi, nullptr, nullptr);
+        bool r;
+        if (p.lm_q8) {
+            // INT8 rows: this CTA's row scales into the exchange buffer, idle in this phase
+            // (every push into it for the last layer has been consumed)
+            float* sl = reinterpret_cast<float*>(&S.xu);
+            for (int i = threadIdx.x; i < pl.r1 - pl.r0; i += kCT) sl[i] = p.lm_sc[pl.r0 + i];
+            consumers_sync<kCT>();
+            r = gemv_rows<true, 8, kHid>(p, pl, g, ring, S, xs, sl, false, epi, nullptr, nullptr);
+        } else {
+            r = gemv_rows<false, 4, kHid>(p, pl, g, ring, S, xs, nullptr, false, epi, nullptr, nullptr);
+        }
         if (!consumers_sync_and<kCT>(r)) goto consumer_exit;
     }
     if (threadIdx.x == 0) {
@@ -1401,6 +1413,9 @@ vb_status mega2_prepare(vb_engine* e) {
         if ((c.ffn + nclusters * kCS - 1) / (nclusters * kCS) > 64)
             return fail(VB_ERR_UNSUPPORTED, "two-barrier step: ffn slice too wide");
     }
+    // the INT8 lm_head keeps a CTA's row scales in the exchange buffer
+    if (e->lm_int8 && (size_t)(c.vocab + nclusters * kCS - 1) / (nclusters * kCS) * sizeof(float) > sizeof(S2::xu))
+        return fail(VB_ERR_UNSUPPORTED, "clustered step: too few CTAs for the INT8 lm_head's scales");
     Mega2State* m = new Mega2State();
     cudaStream_t s = e->stream;
     const size_t es = q8 ? 1 : 4;
@@ -1499,6 +1514,8 @@ vb_status mega2_prepare(vb_engine* e) {
     M2Params& P = m->params;
     P.layers = m->d_layers;
     P.embed = e->embed;
+    P.lm_q8 = e->lm_int8 ? e->lm_q8 : nullptr;
+    P.lm_sc = e->lm_int8 ? e->lm_sc : nullptr;
     P.final_norm = e->final_norm;
     P.rope_cos = e->rope_cos;
     P.rope_sin = e->rope_sin;

@@ -106,6 +106,8 @@ _SIGS = {
     "vb_batch_graph_nodes": (_I, [_P]),
     "vb_batch_reset": (_I, [_P]),
     "vb_sampler_create": (_I, [_F, _I, _F, C.c_uint64, _P]),
+    "vb_engine_quantize_lm_head": (_I, [_P]),
+    "vb_engine_lm_head_int8": (_I, [_P]),
     "vb_sampler_destroy": (_I, [_P]),
     "vb_sampler_sample": (_I, [_P, _P, _L, _P, _P]),
     "vb_engine_decode_sampled": (_I, [_P, _P, _I, _I, _P]),
@@ -223,6 +225,11 @@ class Engine:
             out = np.empty(self.vocab, dtype=np.float32)
         check(lib().vb_engine_step(self.h, int(token), _ptr(out)))
         return out
+
+    def quantize_lm_head(self):
+        """Opt-in INT8 tied lm_head (not reference-identical; see the C header)."""
+        check(lib().vb_engine_quantize_lm_head(self.h))
+        return self
 
     def decode_sampled(self, sampler: "Sampler", first_token: int, n: int) -> np.ndarray:
         """n decode steps, each next token drawn by `sampler` on the device."""
