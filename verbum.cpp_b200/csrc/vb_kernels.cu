@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 
 #include "vb_kernels.cuh"
+#include "vb_tail.cuh"
 
 namespace vb {
 
@@ -22,14 +23,8 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kNumSMs = 148;
 
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
-    return v > bv || (v == bv && i < bi);
-}
-
-__device__ __forceinline__ float silu_f(float g) {
-    // model.cpp:15-18: x / (1 + exp(-x)), IEEE division, accurate expf.
-    return g / (1.0f + expf(-g));
-}
+// better() (argmax order, lowest index on ties) and silu_f() (model.cpp:15-18:
+// x / (1 + exp(-x)), IEEE division, accurate expf) come from vb_pipe.cuh.
 
 // Position of x[i] inside the per-CTA shared copy.  INT8 lanes load 16
 // consecutive weights; storing the matching activations lane-interleaved per
@@ -344,133 +339,22 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
 }
 
 // Split-K reduce of a residual projection fused with the following RMSNorm
-// (nn.cpp:8-42): x[b][i] += (sum_s parts[s][b][i]) * scale[i], then the normed
-// row and its bf16 split.  grid rows, block 256.
+// (residual_norm_row, vb_tail.cuh).  grid rows, block 256.
 __global__ void reduce_residual_norm_kernel(float* x, const float* parts, int splits, const float* scales,
                                             const float* w, float* out, int rows, int dim, float eps,
                                             __nv_bfloat16* hi, __nv_bfloat16* lo) {
     pdl_trigger();
     pdl_wait();
     __shared__ double red[8];
-    const int b = blockIdx.x;
-    float* xr = x + (size_t)b * dim;
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < dim; i += 256) {
-        float v = 0.f;
-        for (int q = 0; q < splits; q++) v += parts[((size_t)q * rows + b) * dim + i];
-        if (scales) v *= scales[i];
-        const float xv = xr[i] + v;
-        xr[i] = xv;
-        ss += (double)xv * (double)xv;
-    }
-    const float sc = rms_scale(block_sum_d<256>(ss, red), dim, eps);
-    for (int i = threadIdx.x; i < dim; i += 256) {
-        const float y = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
-        out[(size_t)b * dim + i] = y;
-        if (hi) {
-            const __nv_bfloat16 h = __float2bfloat16_rn(y);
-            hi[(size_t)b * dim + i] = h;
-            lo[(size_t)b * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
-        }
-    }
+    residual_norm_row<256>(x, parts, splits, scales, w, out, hi, lo, rows, dim, eps, blockIdx.x, red);
 }
 
-// generate.cpp:52-71 for B rows: per-head RMSNorm (q_norm / k_norm),
-// split-half RoPE from the host table, k and v rows written at pos[b] of the
-// row's sequence (b, or b / rows_per_seq for a prompt chunk).  One warp per
-// (row, head): lane l holds dims l, l + 32, l + 64, l + 96, so the RoPE pairs
-// (d, d + 64) sit in one lane.  grid (B, ceil((H + KVH) / 8)), 256 threads.
-// Optionally also writes bf16 hi/lo copies of q ([B][H*D]) and k
-// ([(seq*KVH + h) * kbf_rows + pos][D]) for the tensor-core prompt attention.
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkNormArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x, hd = blockIdx.y * 8 + (threadIdx.x >> 5);
+    const int hd = blockIdx.y * 8 + (threadIdx.x >> 5);
     if (hd >= a.H + a.KVH) return;
-    const int D = 128;
-    const int pos = a.pos[b];
-    if (pos < 0 || pos >= a.rope_positions) {
-        if (lane == 0 && a.err) atomicExch(a.err, kErrCacheFull);
-        return;
-    }
-    const int QW = a.H * D, KW = a.KVH * D, RW = QW + 2 * KW;
-    const bool isq = hd < a.H;
-    const int h = isq ? hd : hd - a.H;
-    const int col0 = isq ? h * D : QW + h * D;  // first column of this head's q or k
-    const int vcol0 = QW + KW + h * D;
-    float x[4], v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (a.parts) {
-#pragma unroll
-        for (int e = 0; e < 4; e++) x[e] = 0.f;
-        for (int q = 0; q < a.splits; q++) {
-            const float* pr = a.parts + ((size_t)q * a.B + b) * RW;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                x[e] += pr[col0 + lane + 32 * e];
-                if (!isq) v[e] += pr[vcol0 + lane + 32 * e];
-            }
-        }
-        if (a.scales) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                x[e] *= a.scales[col0 + lane + 32 * e];
-                if (!isq) v[e] *= a.scales[vcol0 + lane + 32 * e];
-            }
-        }
-    } else {
-        const float* row = a.qkv + (size_t)b * RW;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            x[e] = row[col0 + lane + 32 * e];
-            if (!isq) v[e] = row[vcol0 + lane + 32 * e];
-        }
-    }
-    double ss = 0.0;
-#pragma unroll
-    for (int e = 0; e < 4; e++) ss += (double)x[e] * (double)x[e];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float sc = rms_scale(ss, D, a.eps);
-    const float* nw = isq ? a.q_norm : a.k_norm;
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
-    const float* c = a.cos_tab + (size_t)pos * D;
-    const float* s = a.sin_tab + (size_t)pos * D;
-    float o[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const int d = lane + 32 * e;
-        o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
-                     : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
-    }
-    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(isq ? a.q_hi : a.k_hi);
-    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(isq ? a.q_lo : a.k_lo);
-    size_t bf = 0;
-    if (isq) {
-        const size_t qo = ((size_t)b * a.H + h) * D;
-        bf = qo;
-#pragma unroll
-        for (int e = 0; e < 4; e++) a.q_out[qo + lane + 32 * e] = o[e];
-    } else {
-        const int seq = a.rows_per_seq > 0 ? b / a.rows_per_seq : b;
-        const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos + (size_t)h * a.stride_h;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            a.kc[off + lane + 32 * e] = o[e];
-            a.vc[off + lane + 32 * e] = v[e];
-        }
-        bf = ((size_t)(seq * a.KVH + h) * a.kbf_rows + pos) * D;
-    }
-    if (hi) {
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const __nv_bfloat16 oh = __float2bfloat16_rn(o[e]);
-            hi[bf + lane + 32 * e] = oh;
-            lo[bf + lane + 32 * e] = __float2bfloat16_rn(o[e] - __bfloat162float(oh));
-        }
-    }
+    qk_norm_one(a, blockIdx.x, hd, threadIdx.x & 31);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,0 +1,148 @@
+// vb_tail.cuh -- consumers of split-K partials: the q/k norm + RoPE + cache
+// append of one (row, head) and the residual add + RMSNorm + bf16 split of one
+// row.  Partials are laid out [split][row][col] and summed in split order,
+// read with ld.global.cg (another kernel's output).
+#pragma once
+#include <cuda_bf16.h>
+
+#include "vb_kernels.cuh"
+#include "vb_pipe.cuh"
+
+namespace vb {
+
+// generate.cpp:52-71 for one (row b, head hd) by one warp: per-head RMSNorm
+// (q_norm / k_norm), split-half RoPE from the host table, k and v written at
+// pos[b] of the row's sequence.  Lane l holds dims l, l + 32, l + 64, l + 96,
+// so the RoPE pairs (d, d + 64) sit in one lane.
+static __device__ __noinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
+    const int D = 128;
+    const int pos = a.pos[b];
+    if (pos < 0 || pos >= a.rope_positions) {
+        if (lane == 0 && a.err) atomicExch(a.err, kErrCacheFull);
+        return;
+    }
+    const int QW = a.H * D, KW = a.KVH * D, RW = QW + 2 * KW;
+    const bool isq = hd < a.H;
+    const int h = isq ? hd : hd - a.H;
+    const int col0 = isq ? h * D : QW + h * D;  // first column of this head's q or k
+    const int vcol0 = QW + KW + h * D;
+    float x[4], v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (a.parts) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) x[e] = 0.f;
+#pragma unroll 4
+        for (int q = 0; q < a.splits; q++) {
+            const float* pr = a.parts + ((size_t)q * a.B + b) * RW;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                x[e] += __ldcg(pr + col0 + lane + 32 * e);
+                if (!isq) v[e] += __ldcg(pr + vcol0 + lane + 32 * e);
+            }
+        }
+        if (a.scales) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                x[e] *= a.scales[col0 + lane + 32 * e];
+                if (!isq) v[e] *= a.scales[vcol0 + lane + 32 * e];
+            }
+        }
+    } else {
+        const float* row = a.qkv + (size_t)b * RW;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            x[e] = row[col0 + lane + 32 * e];
+            if (!isq) v[e] = row[vcol0 + lane + 32 * e];
+        }
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) ss += (double)x[e] * (double)x[e];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float sc = rms_scale(ss, D, a.eps);
+    const float* nw = isq ? a.q_norm : a.k_norm;
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
+    const float* c = a.cos_tab + (size_t)pos * D;
+    const float* s = a.sin_tab + (size_t)pos * D;
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int d = lane + 32 * e;
+        o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
+                     : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
+    }
+    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(isq ? a.q_hi : a.k_hi);
+    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(isq ? a.q_lo : a.k_lo);
+    size_t bf = 0;
+    if (isq) {
+        const size_t qo = ((size_t)b * a.H + h) * D;
+        bf = qo;
+#pragma unroll
+        for (int e = 0; e < 4; e++) a.q_out[qo + lane + 32 * e] = o[e];
+    } else {
+        const int seq = a.rows_per_seq > 0 ? b / a.rows_per_seq : b;
+        const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos + (size_t)h * a.stride_h;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            a.kc[off + lane + 32 * e] = o[e];
+            a.vc[off + lane + 32 * e] = v[e];
+        }
+        bf = ((size_t)(seq * a.KVH + h) * a.kbf_rows + pos) * D;
+    }
+    if (hi) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const __nv_bfloat16 oh = __float2bfloat16_rn(o[e]);
+            hi[bf + lane + 32 * e] = oh;
+            lo[bf + lane + 32 * e] = __float2bfloat16_rn(o[e] - __bfloat162float(oh));
+        }
+    }
+}
+
+// Residual projection's partials into row b (nn.cpp:8-42 for the norm):
+// x[b][i] += (sum_s parts[s][b][i]) * scale[i]; out[b] = RMSNorm(x[b]) . w and
+// its bf16 split.  NT threads, dim % NT == 0, dim / NT <= 16; red holds NT/32
+// doubles.
+template <int NT>
+__device__ __forceinline__ void residual_norm_row(float* x, const float* parts, int splits, const float* scales,
+                                                  const float* w, float* out, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                                                  int rows, int dim, float eps, int b, double* red) {
+    float* xr = x + (size_t)b * dim;
+    float xv[16];
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int i = threadIdx.x + NT * j;
+        if (i >= dim) break;
+        // the splits' loads are independent: issue up to 16 before summing (in split order)
+        float t[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++) t[q] = q < splits ? __ldcg(parts + ((size_t)q * rows + b) * dim + i) : 0.f;
+        float v = 0.f;
+#pragma unroll
+        for (int q = 0; q < 16; q++)
+            if (q < splits) v += t[q];
+        for (int q = 16; q < splits; q++) v += __ldcg(parts + ((size_t)q * rows + b) * dim + i);
+        if (scales) v *= scales[i];
+        xv[j] = __ldcg(xr + i) + v;
+        xr[i] = xv[j];
+        ss += (double)xv[j] * (double)xv[j];
+    }
+    const float sc = rms_scale(block_sum_d<NT>(ss, red), dim, eps);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const int i = threadIdx.x + NT * j;
+        if (i >= dim) break;
+        const float y = __fmul_rn(__fmul_rn(xv[j], sc), w[i]);
+        out[(size_t)b * dim + i] = y;
+        if (hi) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(y);
+            hi[(size_t)b * dim + i] = h;
+            lo[(size_t)b * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
+        }
+    }
+}
+
+}  // namespace vb
