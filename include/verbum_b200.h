@@ -223,6 +223,12 @@ typedef struct {
     const float* wd;          /* [hidden, ffn]      */
 } vb_layer_host;
 
+/* The same tensors as bf16 bit patterns (the dtype of released checkpoints;
+ * the reference widens them on the host, safetensors.cpp:239-264). */
+typedef struct {
+    const uint16_t *input_norm, *post_norm, *wq, *wk, *wv, *wo, *q_norm, *k_norm, *wg, *wu, *wd;
+} vb_layer_host_bf16;
+
 typedef struct vb_engine vb_engine;
 
 /* Creates an engine on `device` (Model::to_cuda, model.cpp:367-443, minus the
@@ -233,6 +239,11 @@ VB_API vb_status vb_engine_destroy(vb_engine* e);
 VB_API vb_status vb_engine_set_globals(vb_engine* e, const float* embed, const float* final_norm);
 /* Uploads one layer's f32 weights (model.cpp:407-421). */
 VB_API vb_status vb_engine_set_layer(vb_engine* e, int layer, const vb_layer_host* w);
+/* bf16 uploads: half the host-to-device bytes, widened to f32 on the device
+ * (exactly: bf16 is the top half of an f32, as bf16_to_f32 in
+ * safetensors.cpp:59-66), giving the same device weights as the f32 calls. */
+VB_API vb_status vb_engine_set_globals_bf16(vb_engine* e, const uint16_t* embed, const uint16_t* final_norm);
+VB_API vb_status vb_engine_set_layer_bf16(vb_engine* e, int layer, const vb_layer_host_bf16* w);
 /* Model::quantize (model.cpp:313-338) on the device: the 7 projections of
  * every layer become INT8 + per-row scales bit-exactly as quantize_rows, and
  * the f32 copies are freed.  Embedding, lm_head and norms stay f32. */
@@ -333,6 +344,11 @@ VB_API vb_status vb_batch_prefill(vb_batch* b, const int* tokens_host, int P, in
 VB_API int vb_batch_graph_nodes(const vb_batch* b);
 VB_API int vb_batch_cache_len(const vb_batch* b);
 VB_API vb_status vb_batch_reset(vb_batch* b);
+/* Model::embed_text (model.cpp:191-233) on the device: the n ids' layers
+ * through the batched prefill path (a temporary one-sequence batch), the final
+ * RMSNorm of every position, the mean over positions and L2 normalisation into
+ * out_host [hidden].  f32 projections only, like the reference. */
+VB_API vb_status vb_engine_embed_text(vb_engine* e, const int* ids, int n, float* out_host);
 /* Roll every sequence back to len cached positions (0 <= len <= cache length):
  * the next step writes position len.  Cached entries past len are left in
  * place and overwritten before they are read again. */

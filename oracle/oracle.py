@@ -118,6 +118,7 @@ def rlib():
             "ref_apply_rope": (_I, [_P, _L, _I, _I, _I, _F]),
             "ref_greedy": (_I, [_P, _L]),
             "ref_sample_seq": (_I, [_F, _I, _F, C.c_uint64, _P, _L, _I, _P]),
+            "ref_model_embed_text": (_I, [_P, _P, _I, _P]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -354,6 +355,12 @@ class RefModel:
     def step(self, token):
         out = np.empty(self.vocab, np.float32)
         self._chk(rlib().ref_model_step(self.h, int(token), _p(out)))
+        return out
+
+    def embed_text(self, ids, hidden):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(hidden, np.float32)
+        self._chk(rlib().ref_model_embed_text(self.h, _p(ids), int(ids.size), _p(out)))
         return out
 
     def greedy_steps(self, first_token, n):

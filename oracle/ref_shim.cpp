@@ -108,6 +108,13 @@ int ref_model_greedy_steps(void* h, int first_token, int n_steps, int* tokens_ou
     });
 }
 
+int ref_model_embed_text(void* h, const int* ids, int n, float* out) {
+    return guarded([&] {
+        auto v = static_cast<verbum::Model*>(h)->embed_text(std::vector<int>(ids, ids + n));
+        std::memcpy(out, v.data(), sizeof(float) * v.size());
+    });
+}
+
 int ref_model_set_cache_len(void* h, int len) {
     auto* m = static_cast<verbum::Model*>(h);
     return guarded([&] {

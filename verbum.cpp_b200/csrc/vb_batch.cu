@@ -245,6 +245,37 @@ struct PrefillBufs {
     int *tok = nullptr, *pos = nullptr;
 };
 
+// embed_text's pooling (model.cpp:191-233): pool[b][d] += sum over the chunk's
+// positions of xn[b*C + c][d], in position order, one thread per (b, d).
+__global__ void pool_rows_kernel(const float* xn, int B, int C, int dim, float* pool) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * dim) return;
+    const int b = i / dim, d = i - b * dim;
+    float acc = pool[i];
+    for (int c = 0; c < C; c++) acc += xn[((size_t)b * C + c) * dim + d];
+    pool[i] = acc;
+}
+
+// Mean (x 1/n in float) and L2 normalisation (double norm, float 1/norm) of
+// each pooled row.  One block of 1024 threads per row.
+__global__ void __launch_bounds__(1024) pool_finish_kernel(float* pool, int dim, int n) {
+    __shared__ double red[32];
+    float* v = pool + (size_t)blockIdx.x * dim;
+    const float inv = 1.0f / (float)n;
+    double ss = 0.0;
+    for (int d = threadIdx.x; d < dim; d += 1024) {
+        const float x = v[d] * inv;
+        v[d] = x;
+        ss += (double)x * (double)x;
+    }
+    ss = block_sum_d<1024>(ss, red);
+    const double norm = sqrt(ss);
+    if (norm > 0) {
+        const float nf = (float)(1.0 / norm);
+        for (int d = threadIdx.x; d < dim; d += 1024) v[d] *= nf;
+    }
+}
+
 // Prefill of P positions for all B sequences (tokens_host [P][B]) as whole
 // chunks: the projections of all chunk rows run as tensor-core GEMMs (weights
 // read once per chunk instead of once per position), the q/k norm + RoPE +
@@ -253,7 +284,7 @@ struct PrefillBufs {
 // in a different summation order.  Afterwards the decode state is what P
 // decode steps leave: logits and greedy picks of the last position, tokens =
 // picks, positions advanced by P.
-vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
+vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P, float* pool = nullptr) {
     vb_engine* e = b->e;
     const vb_config& c = e->cfg;
     const bool q8 = e->quantized;
@@ -439,6 +470,17 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P) {
                            nullptr)))
                 return st;
         }
+        if (pool) {  // embed_text: final norm of every row, summed per sequence
+            if ((st = launch_rmsnorm_rows(pb.x, e->final_norm, pb.xn, Rn, H, c.eps, s))) return st;
+            pool_rows_kernel<<<(B * H + 255) / 256, 256, 0, s>>>(pb.xn, B, Cn, H, pool);
+            VB_LAUNCH_CHECK("pool_rows_kernel");
+        }
+    }
+    if (pool) {
+        pool_finish_kernel<<<B, 1024, 0, s>>>(pool, H, P);
+        VB_LAUNCH_CHECK("pool_finish_kernel");
+        VB_CUDA_TRY(cudaStreamSynchronize(s));
+        return VB_OK;
     }
     // the last position of every sequence: final norm, lm_head, greedy pick
     VB_CUDA_TRY(cudaMemcpy2DAsync(b->x, sizeof(float) * H, pb.x + (size_t)(Cn - 1) * H, sizeof(float) * H * Cn,
@@ -716,6 +758,41 @@ vb_status vb_batch_reset(vb_batch* b) {
     VB_CUDA_TRY(cudaStreamSynchronize(b->e->stream));
     b->len = 0;
     return VB_OK;
+}
+
+// Model::embed_text (model.cpp:191-233) on the device: the whole prompt's
+// layers through the prefill path (a temporary one-sequence batch whose cache
+// holds the n positions), the final norm of every position, mean pooling and
+// L2 normalisation.  Like the reference, f32 projections only.
+vb_status vb_engine_embed_text(vb_engine* e, const int* ids, int n, float* out_host) {
+    if (!e || !out_host) return fail(VB_ERR_ARG, "null argument");
+    if (e->quantized) return fail(VB_ERR_STATE, "embed_text needs the f32 path");
+    if (!ids || n <= 0) return fail(VB_ERR_ARG, "embed_text got no tokens");
+    if (!e->globals_set) return fail(VB_ERR_STATE, "engine weights not uploaded");
+    for (int l = 0; l < e->cfg.layers; l++)
+        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "layer not uploaded");
+    if (n > e->cfg.rope_positions) return fail(VB_ERR_ROPE, "position is outside the rope table");
+    for (int i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= e->cfg.vocab)
+            return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
+    Dev dg(e->device);
+    vb_batch* b = nullptr;
+    vb_status st = vb_batch_create(e, 1, n, &b);
+    if (st) return st;
+    float* pool = nullptr;
+    const size_t dim = e->cfg.hidden;
+    if ((st = balloc(&pool, dim, "embed_text pool")) == VB_OK &&
+        (st = cudaMemsetAsync(pool, 0, dim * 4, e->stream) ? fail(VB_ERR_CUDA, "memset") : VB_OK) == VB_OK &&
+        (st = batch_tc_weights(b)) == VB_OK && (st = batch_prefill_chunks(b, ids, n, pool)) == VB_OK) {
+        const cudaError_t ce = cudaMemcpy(out_host, pool, dim * 4, cudaMemcpyDeviceToHost);
+        if (ce != cudaSuccess) st = cuda_fail(ce, "embed_text copy");
+        int err = 0;
+        if (!st && cudaMemcpy(&err, b->d_err, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && err)
+            st = batch_err_status(b, err);
+    }
+    bfree(pool);
+    vb_batch_destroy(b);
+    return st;
 }
 
 vb_status vb_batch_truncate(vb_batch* b, int len) {

@@ -384,6 +384,7 @@ vb_status vb_engine_destroy(vb_engine* e) {
     free_cache(e);
     dfree(e->embed); dfree(e->final_norm); dfree(e->rope_cos); dfree(e->rope_sin);
     dfree(e->norms); dfree(e->wf32); dfree(e->wi8); dfree(e->wscale); dfree(e->lm_q8); dfree(e->lm_sc);
+    if (e->stage) cudaFree(e->stage);
     dfree(e->x); dfree(e->qkv); dfree(e->q); dfree(e->ctx); dfree(e->h); dfree(e->logits);
     dfree(e->part_val); dfree(e->part_idx); dfree(e->d_tok); dfree(e->d_pos); dfree(e->d_next);
     dfree(e->d_err); dfree(e->d_step);
@@ -400,6 +401,77 @@ vb_status vb_engine_set_globals(vb_engine* e, const float* embed, const float* f
     VB_CUDA_TRY(cudaMemcpy(e->embed, embed, (size_t)c.vocab * c.hidden * 4, cudaMemcpyHostToDevice));
     VB_CUDA_TRY(cudaMemcpy(e->final_norm, final_norm, (size_t)c.hidden * 4, cudaMemcpyHostToDevice));
     e->globals_set = true;
+    return VB_OK;
+}
+
+namespace vb {
+namespace {
+// dst[r * ld + k] = widen(src[r * cols + k]) for r < rows, k < cols.
+__global__ void widen_bf16_kernel(const uint16_t* src, int64_t rows, int64_t cols, float* dst, int64_t ld) {
+    const int64_t n = rows * cols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / cols, k = i - r * cols;
+        dst[r * ld + k] = __uint_as_float((unsigned)src[i] << 16);
+    }
+}
+}  // namespace
+
+// Uploads a bf16 [rows][cols] host tensor through a device staging buffer and
+// widens it into dst (row stride ld floats).
+vb_status upload_bf16(vb_engine* e, const uint16_t* host, int64_t rows, int64_t cols, float* dst, int64_t ld) {
+    const size_t bytes = (size_t)rows * cols * 2;
+    if (e->stage_bytes < bytes) {
+        if (e->stage) cudaFree(e->stage);
+        e->stage = nullptr;
+        e->stage_bytes = 0;
+        VB_CUDA_TRY(cudaMalloc(&e->stage, bytes));
+        e->stage_bytes = bytes;
+    }
+    VB_CUDA_TRY(cudaMemcpyAsync(e->stage, host, bytes, cudaMemcpyHostToDevice, e->stream));
+    widen_bf16_kernel<<<1184, 256, 0, e->stream>>>(static_cast<const uint16_t*>(e->stage), rows, cols, dst, ld);
+    VB_LAUNCH_CHECK("widen_bf16_kernel");
+    // the staging buffer is reused by the next call: keep the copies ordered
+    VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return VB_OK;
+}
+}  // namespace vb
+
+vb_status vb_engine_set_globals_bf16(vb_engine* e, const uint16_t* embed, const uint16_t* final_norm) {
+    if (!e || !embed || !final_norm) return fail(VB_ERR_ARG, "null argument");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    vb_status st;
+    if ((st = upload_bf16(e, embed, c.vocab, c.hidden, e->embed, c.hidden))) return st;
+    if ((st = upload_bf16(e, final_norm, 1, c.hidden, e->final_norm, c.hidden))) return st;
+    e->globals_set = true;
+    return VB_OK;
+}
+
+vb_status vb_engine_set_layer_bf16(vb_engine* e, int layer, const vb_layer_host_bf16* w) {
+    if (!e || !w) return fail(VB_ERR_ARG, "null argument");
+    if (layer < 0 || layer >= e->cfg.layers) return fail(VB_ERR_ARG, "layer index out of range");
+    if (e->quantized) return fail(VB_ERR_STATE, "engine already quantized; upload f32 layers first");
+    if (!w->input_norm || !w->post_norm || !w->wq || !w->wk || !w->wv || !w->wo || !w->q_norm ||
+        !w->k_norm || !w->wg || !w->wu || !w->wd)
+        return fail(VB_ERR_ARG, "null weight pointer");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const int64_t hd = c.hidden, D = c.head_dim;
+    vb_layer_dev& L = e->L[layer];
+    vb_status st;
+    if ((st = upload_bf16(e, w->input_norm, 1, hd, L.in_norm, hd)) ||
+        (st = upload_bf16(e, w->post_norm, 1, hd, L.post_norm, hd)) ||
+        (st = upload_bf16(e, w->q_norm, 1, D, L.q_norm, D)) || (st = upload_bf16(e, w->k_norm, 1, D, L.k_norm, D)) ||
+        (st = upload_bf16(e, w->wq, e->q_width, hd, L.wqkv, hd)) ||
+        (st = upload_bf16(e, w->wk, e->kv_width, hd, L.wqkv + (size_t)e->q_width * hd, hd)) ||
+        (st = upload_bf16(e, w->wv, e->kv_width, hd, L.wqkv + (size_t)(e->q_width + e->kv_width) * hd, hd)) ||
+        (st = upload_bf16(e, w->wo, hd, e->q_width, L.wo, e->q_width)) ||
+        // gate row j -> row 2j, up row j -> row 2j+1
+        (st = upload_bf16(e, w->wg, c.ffn, hd, L.wgu, 2 * hd)) ||
+        (st = upload_bf16(e, w->wu, c.ffn, hd, L.wgu + hd, 2 * hd)) ||
+        (st = upload_bf16(e, w->wd, hd, c.ffn, L.wd, c.ffn)))
+        return st;
+    e->layer_set[layer] = 1;
     return VB_OK;
 }
 

@@ -59,6 +59,8 @@ struct vb_engine {
     int8_t* wi8 = nullptr;     // all int8 projections
     float* wscale = nullptr;   // all scales
     // opt-in INT8 copy of the tied lm_head (the embedding lookup stays f32)
+    void* stage = nullptr;     // bf16 upload staging
+    size_t stage_bytes = 0;
     int8_t* lm_q8 = nullptr;
     float* lm_sc = nullptr;
     bool lm_int8 = false;

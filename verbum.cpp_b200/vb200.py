@@ -107,6 +107,9 @@ _SIGS = {
     "vb_batch_reset": (_I, [_P]),
     "vb_sampler_create": (_I, [_F, _I, _F, C.c_uint64, _P]),
     "vb_engine_quantize_lm_head": (_I, [_P]),
+    "vb_engine_set_globals_bf16": (_I, [_P, _P, _P]),
+    "vb_engine_embed_text": (_I, [_P, _P, _I, _P]),
+    "vb_engine_set_layer_bf16": (_I, [_P, _I, _P]),
     "vb_engine_lm_head_int8": (_I, [_P]),
     "vb_sampler_destroy": (_I, [_P]),
     "vb_sampler_sample": (_I, [_P, _P, _L, _P, _P]),
@@ -204,6 +207,18 @@ class Engine:
             check(lib().vb_engine_set_layer(self.h, i, C.byref(lh)))
         return self
 
+    def load_bf16(self, weights: dict):
+        """Uploads a {HF tensor name: uint16 bf16-bit-pattern array} dict, widened on the device."""
+        emb = np.ascontiguousarray(weights["model.embed_tokens.weight"], dtype=np.uint16)
+        fn = np.ascontiguousarray(weights["model.norm.weight"], dtype=np.uint16)
+        check(lib().vb_engine_set_globals_bf16(self.h, _ptr(emb), _ptr(fn)))
+        for i in range(self.vcfg.layers):
+            names = layer_names(i)
+            arrs = {k: np.ascontiguousarray(weights[v], dtype=np.uint16) for k, v in names.items()}
+            lh = VBLayerHost(**{k: a.ctypes.data for k, a in arrs.items()})  # same field order
+            check(lib().vb_engine_set_layer_bf16(self.h, i, C.byref(lh)))
+        return self
+
     def quantize(self):
         check(lib().vb_engine_quantize(self.h))
 
@@ -224,6 +239,13 @@ class Engine:
         if out is None:
             out = np.empty(self.vocab, dtype=np.float32)
         check(lib().vb_engine_step(self.h, int(token), _ptr(out)))
+        return out
+
+    def embed_text(self, ids) -> np.ndarray:
+        """Model::embed_text: mean-pooled, L2-normalised final hidden states."""
+        t = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(self.vcfg.hidden, dtype=np.float32)
+        check(lib().vb_engine_embed_text(self.h, _ptr(t), int(t.size), _ptr(out)))
         return out
 
     def quantize_lm_head(self):
