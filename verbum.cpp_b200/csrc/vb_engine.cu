@@ -156,9 +156,11 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         qa.rope_positions = std::min(c.rope_positions, e->max_seq);
         qa.eps = c.eps;
         qa.err = e->d_err;
-        if ((st = launch_qk_norm_rope_append(qa, s))) return st;
 
+        // the q/k norm, RoPE and cache append run inside the attention kernel
         AttnArgs aa{};
+        aa.fuse_qk = 1;
+        aa.qk = qa;
         aa.q = e->q;
         aa.k = qa.kc;
         aa.v = qa.vc;

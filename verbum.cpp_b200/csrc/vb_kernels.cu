@@ -382,10 +382,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     const float inv_sqrt_d = __fdiv_rn(1.0f, __fsqrt_rn((float)a.D));
 
     float4 q[G];
+    // fused q/k norm + RoPE (+ cache append): warps 0..G-1 the G query heads,
+    // warp G the KV head; the new k, v serve position `pos` from shared memory
+    __shared__ __align__(16) float qs[G][128];
+    __shared__ __align__(16) float kvs[2][128];
+    const int pos = n - 1;
+    const bool has_pos = a.fuse_qk && pos >= p0 && pos < p1;
+    if (a.fuse_qk) {
+        int ok = 1;
+        if (warp <= G) {
+            float o[4], v[4];
+            ok = qk_head(a.qk, b, warp < G ? kvh * G + warp : a.H + kvh, lane, o, v) ? 1 : 0;
 #pragma unroll
-    for (int g = 0; g < G; g++)
-        q[g] = *reinterpret_cast<const float4*>(a.q + ((size_t)b * a.H + kvh * G + g) * 128 +
-                                                4 * lane);
+            for (int e = 0; e < 4; e++) {
+                if (warp < G) {
+                    qs[warp][lane + 32 * e] = o[e];
+                } else {
+                    kvs[0][lane + 32 * e] = o[e];
+                    kvs[1][lane + 32 * e] = v[e];
+                }
+            }
+            if (warp == G && has_pos && ok) {
+                const size_t off = (size_t)b * a.stride_b + (size_t)pos * a.stride_pos + (size_t)kvh * a.stride_h;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    a.qk.kc[off + lane + 32 * e] = o[e];
+                    a.qk.vc[off + lane + 32 * e] = v[e];
+                }
+            }
+        }
+        if (!__syncthreads_and(ok)) return;  // the position is outside the rope table (error word set)
+#pragma unroll
+        for (int g = 0; g < G; g++) q[g] = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+            q[g] = *reinterpret_cast<const float4*>(a.q + ((size_t)b * a.H + kvh * G + g) * 128 + 4 * lane);
+    }
     float m[G], l[G];
     float4 acc[G];
 #pragma unroll
@@ -402,7 +435,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
 #pragma unroll
         for (int u = 0; u < kAttnPB; u++) {
             const int p = base + u;
-            if (p < p1) {
+            if (has_pos && p == pos) {  // this step's row: just computed, not read back
+                kk[u] = *reinterpret_cast<const float4*>(&kvs[0][4 * lane]);
+                vv[u] = *reinterpret_cast<const float4*>(&kvs[1][4 * lane]);
+            } else if (p < p1) {
                 kk[u] = ld_stream_f4(kb + (size_t)p * a.stride_pos);
                 vv[u] = ld_stream_f4(vb + (size_t)p * a.stride_pos);
             } else {
@@ -816,6 +852,8 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "attention: head_dim must be 128");
     if (a.H % a.KVH) return fail(VB_ERR_ARG, "attention: heads % kv_heads != 0");
     const int G = a.H / a.KVH;
+    if (a.fuse_qk && (G + 1 > kAttnWarps || a.lens || !a.pos))
+        return fail(VB_ERR_ARG, "attention: the fused q/k norm needs positions and G < warps");
     dim3 grid(a.splits, a.KVH, a.B);
     switch (G) {
         case 1: launch_pdl(attn_split_kernel<1>, grid, kAttnThreads, 0, s, a); break;

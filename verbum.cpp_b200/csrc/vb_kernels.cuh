@@ -93,6 +93,12 @@ struct AttnArgs {
     float* ws;             // partials
     void* out_hi;          // optional bf16 split of out (tensor-core GEMM operand)
     void* out_lo;
+    // fuse_qk: q is not read from `q` but normed and rotated by each CTA from
+    // qk's source (the q|k|v GEMV row or GEMM partials), and the CTA whose
+    // range holds position pos[b] also computes k, v, appends them to the cache
+    // and uses them for that position (generate.cpp:52-71 inside the attention)
+    int fuse_qk;
+    QkNormArgs qk;
 };
 int attn_splits_for(int B, int KVH, int n_max);
 size_t attn_ws_bytes(int B, int H, int splits);

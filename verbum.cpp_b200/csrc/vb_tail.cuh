@@ -10,23 +10,26 @@
 
 namespace vb {
 
-// generate.cpp:52-71 for one (row b, head hd) by one warp: per-head RMSNorm
-// (q_norm / k_norm), split-half RoPE from the host table, k and v written at
-// pos[b] of the row's sequence.  Lane l holds dims l, l + 32, l + 64, l + 96,
-// so the RoPE pairs (d, d + 64) sit in one lane.
-static __device__ __noinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
+// generate.cpp:52-64 for one (row b, head hd) by one warp: per-head RMSNorm
+// (q_norm / k_norm) and split-half RoPE from the host table; o[e] gets dim
+// lane + 32e of the normed, rotated q or k, v[e] (k heads) the v value.  Lane
+// l holds dims l, l + 32, l + 64, l + 96, so the RoPE pairs (d, d + 64) sit in
+// one lane.  False (and the error word set) for a position outside the table.
+static __device__ __forceinline__ bool qk_head(const QkNormArgs& a, int b, int hd, int lane, float* o, float* v) {
     const int D = 128;
     const int pos = a.pos[b];
     if (pos < 0 || pos >= a.rope_positions) {
         if (lane == 0 && a.err) atomicExch(a.err, kErrCacheFull);
-        return;
+        return false;
     }
     const int QW = a.H * D, KW = a.KVH * D, RW = QW + 2 * KW;
     const bool isq = hd < a.H;
     const int h = isq ? hd : hd - a.H;
     const int col0 = isq ? h * D : QW + h * D;  // first column of this head's q or k
     const int vcol0 = QW + KW + h * D;
-    float x[4], v[4] = {0.f, 0.f, 0.f, 0.f};
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[e] = 0.f;
     if (a.parts) {
 #pragma unroll
         for (int e = 0; e < 4; e++) x[e] = 0.f;
@@ -66,13 +69,24 @@ static __device__ __noinline__ void qk_norm_one(const QkNormArgs& a, int b, int 
     for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
     const float* c = a.cos_tab + (size_t)pos * D;
     const float* s = a.sin_tab + (size_t)pos * D;
-    float o[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) {
         const int d = lane + 32 * e;
         o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
                      : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
     }
+    return true;
+}
+
+// qk_head for (row b, head hd) plus its writes: q to q_out, k and v into the
+// cache at pos[b] of the row's sequence, and the optional bf16 copies.
+static __device__ __noinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
+    const int D = 128;
+    float o[4], v[4];
+    if (!qk_head(a, b, hd, lane, o, v)) return;
+    const int pos = a.pos[b];
+    const bool isq = hd < a.H;
+    const int h = isq ? hd : hd - a.H;
     __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(isq ? a.q_hi : a.k_hi);
     __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(isq ? a.q_lo : a.k_lo);
     size_t bf = 0;
