@@ -154,25 +154,4 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-// launch_pdl with thread-block clusters of `cluster` CTAs along x.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, int cluster, size_t smem,
-                               cudaStream_t s, Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    at[1].id = cudaLaunchAttributeClusterDimension;
-    at[1].val.clusterDim.x = cluster;
-    at[1].val.clusterDim.y = 1;
-    at[1].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
 }  // namespace vb

@@ -10,7 +10,6 @@
 #include <limits.h>
 #include <math.h>
 
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include "vb_kernels.cuh"
@@ -337,51 +336,6 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
             lo[(size_t)blockIdx.x * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
         }
     }
-}
-
-// The same with each row split over a cluster of 4 CTAs (256 columns each):
-// the partial sums of squares meet in distributed shared memory (summed in
-// rank order), so 4x the CTAs share the partials' loads.  grid 4 * rows,
-// cluster 4, block 256; dim == 1024.
-__global__ void __launch_bounds__(256) reduce_residual_norm_cluster_kernel(float* x, const float* parts, int splits,
-                                                                           const float* scales, const float* w,
-                                                                           float* out, int rows, int dim, float eps,
-                                                                           __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    pdl_trigger();
-    pdl_wait();
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    __shared__ double red[8];
-    __shared__ double part_ss;
-    const int rank = (int)cl.block_rank(), b = blockIdx.x / 4;
-    const int i = rank * 256 + threadIdx.x;
-    float t[16];
-#pragma unroll
-    for (int q = 0; q < 16; q++) t[q] = q < splits ? __ldcg(parts + ((size_t)q * rows + b) * dim + i) : 0.f;
-    float v = 0.f;
-#pragma unroll
-    for (int q = 0; q < 16; q++)
-        if (q < splits) v += t[q];
-    for (int q = 16; q < splits; q++) v += __ldcg(parts + ((size_t)q * rows + b) * dim + i);
-    if (scales) v *= scales[i];
-    float* xr = x + (size_t)b * dim;
-    const float xv = __ldcg(xr + i) + v;
-    xr[i] = xv;
-    const double ss = block_sum_d<256>((double)xv * (double)xv, red);
-    if (threadIdx.x == 0) part_ss = ss;
-    cl.sync();
-    double tot = 0.0;
-#pragma unroll
-    for (int r = 0; r < 4; r++) tot += *cl.map_shared_rank(&part_ss, r);
-    const float sc = rms_scale(tot, dim, eps);
-    const float y = __fmul_rn(__fmul_rn(xv, sc), w[i]);
-    out[(size_t)b * dim + i] = y;
-    if (hi) {
-        const __nv_bfloat16 h = __float2bfloat16_rn(y);
-        hi[(size_t)b * dim + i] = h;
-        lo[(size_t)b * dim + i] = __float2bfloat16_rn(y - __bfloat162float(h));
-    }
-    cl.sync();  // no CTA leaves while another still reads its part_ss
 }
 
 // Split-K reduce of a residual projection fused with the following RMSNorm
@@ -865,12 +819,8 @@ vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, 
                                       const float* w, float* out, void* hi, void* lo, int rows, int dim,
                                       float eps, cudaStream_t s) {
     if (rows <= 0 || dim <= 0 || splits <= 0) return fail(VB_ERR_ARG, "reduce_residual_norm: bad shape");
-    const cudaError_t ce =
-        (dim == 1024 && !getenv("VBX_RN_OLD")) ? launch_pdl_cluster(reduce_residual_norm_cluster_kernel, 4 * rows, 256, 4, 0, s, x, parts, splits,
-                                         scales, w, out, rows, dim, eps, static_cast<__nv_bfloat16*>(hi),
-                                         static_cast<__nv_bfloat16*>(lo))
-                    : launch_pdl(reduce_residual_norm_kernel, rows, 256, 0, s, x, parts, splits, scales, w, out, rows,
-                                 dim, eps, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+    const cudaError_t ce = launch_pdl(reduce_residual_norm_kernel, rows, 256, 0, s, x, parts, splits, scales, w, out,
+                                      rows, dim, eps, static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
     if (ce != cudaSuccess) return cuda_fail(ce, "reduce_residual_norm_kernel launch");
     return VB_OK;
 }
