@@ -169,12 +169,14 @@ __global__ void __launch_bounds__(kPThreads) prefill_attn_kernel(const PrefillAt
 // P_lo V_hi + P_hi V_lo, products exact in f32, dropped terms ~2^-16.
 //
 // CTA = 64 query positions x the 2 query heads of one KV head = 128 query rows
-// (MMA M, tensor-memory lanes; thread r owns row r).  Per 64-key tile: TMA
-// (double-buffered) -> S MMA into tensor memory (64 columns) -> each thread
-// reads its row of S, applies the causal mask and the online softmax, writes
-// P_hi / P_lo as its own 128-byte swizzled shared-memory row -> P.V MMA into
-// tensor memory (128 columns) -> each thread folds the tile into its 128
-// output registers.
+// (MMA M, tensor-memory lanes).  256 threads: threads r and 128 + r share row r,
+// the first taking keys 0-31 of a tile and output dims 0-63, the second keys
+// 32-63 and dims 64-127.  Per 64-key tile: TMA (double-buffered) -> S MMA into
+// tensor memory (64 columns) -> each thread reads its half row of S, the two
+// halves combine the row maximum and sum through shared memory (online
+// softmax, causal mask), each writes its half of P_hi / P_lo into the row's
+// 128-byte swizzled shared-memory line -> P.V MMA into tensor memory (128
+// columns) -> each thread folds its 64 dims into its output registers.
 constexpr int kAQ = 64;                         // query positions per CTA
 constexpr int kAK = 64;                         // keys per tile
 constexpr int kQT = 128 * 128;                  // [128 rows][64 bf16] swizzled tile, 16 KB
@@ -201,7 +203,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(256, 1)
     tc_prefill_attn_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
                            const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
                            const __grid_constant__ CUtensorMap mv_hi, const __grid_constant__ CUtensorMap mv_lo,
@@ -209,6 +211,7 @@ __global__ void __launch_bounds__(128, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) unsigned long long q_full, kv_full[2], s_done, pv_done;
     __shared__ unsigned tmem_slot;
+    __shared__ float xch[2][128];  // the row halves' maximum, then sum
     const unsigned sb = (smem_addr(smem_raw) + 1023u) & ~1023u;
     uint8_t* sg = smem_raw + (sb - smem_addr(smem_raw));
     const int t = threadIdx.x, warp = t >> 5;
@@ -260,14 +263,14 @@ __global__ void __launch_bounds__(128, 1)
         issue_kv(0, 0);
         if (nt > 1) issue_kv(1, 1);
     }
-    const int r = t;  // query row: position c0 + (r & 63) of head 2 kvh + (r >> 6)
+    const int r = t & 127, hf = t >> 7;  // query row: position c0 + (r & 63) of head 2 kvh + (r >> 6)
     const int qpos = c0 + (r & 63);
     const bool rvalid = (r & 63) < nq;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-    const unsigned lane_off = (unsigned)(32 * warp) << 16;
-    float o[128];
+    const unsigned lane_off = (unsigned)(32 * (warp & 3)) << 16;  // warp w reads lanes 32 (w % 4) ..
+    float o[64];
 #pragma unroll
-    for (int d = 0; d < 128; d++) o[d] = 0.f;
+    for (int d = 0; d < 64; d++) o[d] = 0.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int issued = nt > 1 ? 2 : 1;  // key tiles requested so far
@@ -297,32 +300,37 @@ __global__ void __launch_bounds__(128, 1)
         }
         ok = mbar_wait(smem_addr(&s_done), (unsigned)it & 1u, p.err, nullptr, kSiteFull, it) && ok;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        float sv[64];
-        tmem_ld64(tS + lane_off, sv);
-        const int k0 = it * kAK;
+        float sv[32];
+        tmem_ld32(tS + lane_off + 32u * (unsigned)hf, sv);
+        const int k0 = it * kAK + 32 * hf;
         float mx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 64; j++) {
+        for (int j = 0; j < 32; j++) {
             sv[j] = (rvalid && k0 + j <= qpos) ? sv[j] * scale : -INFINITY;
             mx = fmaxf(mx, sv[j]);
         }
+        xch[hf][r] = mx;
+        __syncthreads();
+        mx = fmaxf(xch[0][r], xch[1][r]);
+        __syncthreads();  // xch is reused for the sums
         const float mn = fmaxf(m, mx);
         const float alpha = (m == -INFINITY) ? 0.f : expf(m - mn);
         float sum = 0.f;
 #pragma unroll
-        for (int j = 0; j < 64; j++) {
+        for (int j = 0; j < 32; j++) {
             sv[j] = (sv[j] == -INFINITY) ? 0.f : expf(sv[j] - mn);
             sum += sv[j];
         }
-        l = l * alpha + sum;
+        xch[hf][r] = sum;
         m = mn;
-        // P_hi / P_lo: this thread's row, 8 chunks of 8 keys, 128-byte swizzle
+        // P_hi / P_lo: this thread's half row, chunks 4 hf .. 4 hf + 3 of 8 keys, 128-byte swizzle
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int cc = 0; cc < 4; cc++) {
+            const int c = 4 * hf + cc;
             uint32_t hv[4], lv[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-                const float a = sv[8 * c + 2 * q], bb = sv[8 * c + 2 * q + 1];
+                const float a = sv[8 * cc + 2 * q], bb = sv[8 * cc + 2 * q + 1];
                 const __nv_bfloat16 ah = __float2bfloat16_rn(a), bh = __float2bfloat16_rn(bb);
                 hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
                 lv[q] = pack_bf16(a - __bfloat162float(ah), bb - __bfloat162float(bh));
@@ -334,6 +342,7 @@ __global__ void __launch_bounds__(128, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncthreads();
+        l = l * alpha + (xch[0][r] + xch[1][r]);  // read before the iteration's closing barrier
         if (t == 32) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (ok) {
@@ -358,12 +367,11 @@ __global__ void __launch_bounds__(128, 1)
             issue_kv(it + 2, buf);
             issued = it + 3;
         }
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
+        {
             float pv[64];
-            tmem_ld64(tPV + lane_off + 64u * h, pv);
+            tmem_ld64(tPV + lane_off + 64u * (unsigned)hf, pv);
 #pragma unroll
-            for (int d = 0; d < 64; d++) o[64 * h + d] = fmaf(o[64 * h + d], alpha, pv[d]);
+            for (int d = 0; d < 64; d++) o[d] = fmaf(o[d], alpha, pv[d]);
         }
         if (!__syncthreads_and(ok)) {
             ok = false;
@@ -378,9 +386,9 @@ __global__ void __launch_bounds__(128, 1)
     }
     if (ok && rvalid) {
         const int hh = r >> 6;
-        const size_t base = (size_t)(b * p.P + qpos) * p.QW + (size_t)(2 * kvh + hh) * 128;
+        const size_t base = (size_t)(b * p.P + qpos) * p.QW + (size_t)(2 * kvh + hh) * 128 + 64 * hf;
 #pragma unroll
-        for (int d = 0; d < 128; d += 8) {
+        for (int d = 0; d < 64; d += 8) {
             float y[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) y[e] = o[d + e] / l;
@@ -568,7 +576,7 @@ vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, v
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.out = a.out;
     p.err = a.err;
-    tc_prefill_attn_kernel<<<dim3((P + kAQ - 1) / kAQ, KVH, B), 128, kTASmem, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
+    tc_prefill_attn_kernel<<<dim3((P + kAQ - 1) / kAQ, KVH, B), 256, kTASmem, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
     VB_LAUNCH_CHECK("tc_prefill_attn_kernel");
     return VB_OK;
 }
