@@ -283,19 +283,22 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
 }
 
 // ---------------------------------------------------------------------------
-// Wide tiles for many activation rows (a prompt chunk): one CTA computes 128
-// activation rows (the MMA's M, tensor-memory lanes) x 256 weight rows (the
-// MMA's N, 256 f32 columns) over all of K, so each SM takes in 64 KB (bf16
-// weights) or 96 KB (a weight pair) per 64-wide K step for 2 M MACs of
-// products -- half the bytes per MAC of the 128 x 64 decode tile.  Same
-// operands and accumulation as above; no split-K.
+// Wide tiles for many activation rows (a prompt chunk): one CTA computes
+// MB x 128 activation rows (the MMA's M, tensor-memory lanes; MB accumulators
+// of 256 columns) x 256 weight rows (the MMA's N) over all of K.  With MB = 2
+// (single bf16 weights) each SM takes in 96 KB per 64-wide K step for 4 M MACs
+// of products (weights shared by both row blocks); MB = 1 (and for a weight
+// pair) 64 / 96 KB for 2 M.  Same operands and accumulation as above; no
+// split-K.
 constexpr int kWM = 128;                 // activation rows per tile
 constexpr int kWN = 256;                 // weight rows per tile
 constexpr int kWA = kWM * kTK * 2;       // 16 KB per activation half
 constexpr int kWW = kWN * kTK * 2;       // 32 KB per weight half
-__host__ __device__ constexpr int wide_stage(int wp) { return 2 * kWA + wp * kWW; }
-__host__ __device__ constexpr int wide_stages(int wp) { return wp == 1 ? 3 : 2; }
-__host__ __device__ constexpr size_t wide_smem(int wp) { return (size_t)wide_stages(wp) * wide_stage(wp) + 1024; }
+__host__ __device__ constexpr int wide_stage(int wp, int mb) { return mb * 2 * kWA + wp * kWW; }
+__host__ __device__ constexpr int wide_stages(int wp, int mb) { return (wp == 1 && mb == 1) ? 3 : 2; }
+__host__ __device__ constexpr size_t wide_smem(int wp, int mb) {
+    return (size_t)wide_stages(wp, mb) * wide_stage(wp, mb) + 1024;
+}
 constexpr uint32_t kIdescWide = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kWN >> 3) << 17) |
                                 ((uint32_t)(kWM >> 4) << 24);
 
@@ -308,23 +311,26 @@ __device__ __forceinline__ void mma_wide(unsigned tmem, uint64_t adesc, uint64_t
 }
 
 
-// grid (ceil(N / 256), ceil(M / 128)); 128 threads: warp 0 lane 0 issues the
-// TMA copies, warp 1 lane 0 the MMAs, all four warps the epilogue (thread =
-// activation row m0 + 32 w + lane, 256 weight columns read out 64 at a time).
-template <int WP>
+// grid (ceil(N / 256), ceil(M / (128 MB))); 128 threads: warp 0 lane 0 issues
+// the TMA copies, warp 1 lane 0 the MMAs, all four warps the epilogue (thread =
+// activation row m0 + 128 mb + 32 w + lane, 256 weight columns read out 64 at
+// a time per row block).
+template <int WP, int MB>
 __global__ void __launch_bounds__(kTThreads, 1)
     tc_gemm_wide_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
                         const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                         const TcParams p) {
-    constexpr int NS = wide_stages(WP);
-    constexpr int kStage = wide_stage(WP);
+    constexpr int NS = wide_stages(WP, MB);
+    constexpr int kStage = wide_stage(WP, MB);
+    constexpr int kWOff = MB * 2 * kWA;  // weight tile offset within a stage
+    constexpr unsigned kCols = (unsigned)(kWN * MB);
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) unsigned long long full[NS], empty[NS], done;
     __shared__ unsigned tmem_slot;
     __shared__ int fail;
     const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kWN, m0 = blockIdx.y * kWM;
+    const int n0 = blockIdx.x * kWN, m0 = blockIdx.y * kWM * MB;
     const int nch = p.chunks;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
@@ -337,7 +343,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
-                     "r"(kWN)
+                     "r"(kCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -358,10 +364,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const unsigned fb = smem_addr(&full[s]);
             mbar_expect_tx(fb, (unsigned)kStage);
             const int x = i * kTK;
-            tma_load_2d(st, &ta_hi, x, m0, fb);
-            tma_load_2d(st + kWA, &ta_lo, x, m0, fb);
-            tma_load_2d(st + 2 * kWA, &tw_hi, x, n0, fb);
-            if (WP == 2) tma_load_2d(st + 2 * kWA + kWW, &tw_lo, x, n0, fb);
+#pragma unroll
+            for (int mb = 0; mb < MB; mb++) {
+                tma_load_2d(st + mb * 2 * kWA, &ta_hi, x, m0 + mb * kWM, fb);
+                tma_load_2d(st + mb * 2 * kWA + kWA, &ta_lo, x, m0 + mb * kWM, fb);
+            }
+            tma_load_2d(st + kWOff, &tw_hi, x, n0, fb);
+            if (WP == 2) tma_load_2d(st + kWOff + kWW, &tw_lo, x, n0, fb);
             issued = i + 1;
         }
         for (int i = issued > NS ? issued - NS : 0; i < issued; i++)
@@ -377,12 +386,16 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const unsigned st = sbase + (unsigned)s * kStage;
 #pragma unroll
             for (int kk = 0; kk < kTK / 16; kk++) {
-                const uint64_t ah = sw128_desc(st + 32u * kk);
-                const uint64_t al = sw128_desc(st + kWA + 32u * kk);
-                const uint64_t wh = sw128_desc(st + 2 * kWA + 32u * kk);
-                mma_wide(tmem, ah, wh, i > 0 || kk > 0);
-                mma_wide(tmem, al, wh, true);
-                if (WP == 2) mma_wide(tmem, ah, sw128_desc(st + 2 * kWA + kWW + 32u * kk), true);
+                const uint64_t wh = sw128_desc(st + kWOff + 32u * kk);
+#pragma unroll
+                for (int mb = 0; mb < MB; mb++) {
+                    const unsigned tm = tmem + (unsigned)(mb * kWN);
+                    const uint64_t ah = sw128_desc(st + mb * 2 * kWA + 32u * kk);
+                    const uint64_t al = sw128_desc(st + mb * 2 * kWA + kWA + 32u * kk);
+                    mma_wide(tm, ah, wh, i > 0 || kk > 0);
+                    mma_wide(tm, al, wh, true);
+                    if (WP == 2) mma_wide(tm, ah, sw128_desc(st + kWOff + kWW + 32u * kk), true);
+                }
             }
             mma_commit(smem_addr(&empty[s]));
         }
@@ -398,11 +411,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
         // columns 2j, 2j + 1, so every store instruction covers 256
         // consecutive bytes of one output row.
         float* T = reinterpret_cast<float*>(smem_raw + (sbase - smem_addr(smem_raw))) + warp * 32 * 68;
-        for (int cb = 0; cb < kWN; cb += 64) {
+        for (int blk = 0; blk < MB * (kWN / 64); blk++) {
+            const int mb = blk / (kWN / 64), cb = (blk % (kWN / 64)) * 64;
             const int nb = n0 + cb;
-            if (nb >= p.N) break;  // uniform across the CTA
+            if (nb >= p.N) continue;  // uniform across the CTA
+            const int mrow0 = m0 + mb * kWM;
             float v[64];
-            tmem_ld64(tmem + ((unsigned)(32 * warp) << 16) + (unsigned)cb, v);
+            tmem_ld64(tmem + ((unsigned)(32 * warp) << 16) + (unsigned)(mb * kWN + cb), v);
 #pragma unroll
             for (int j = 0; j < 64; j += 4)
                 *reinterpret_cast<float4*>(T + lane * 68 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -411,9 +426,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
             const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
             const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
             const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
-            const int rows = min(32, p.M - (m0 + 32 * warp));
+            const int rows = min(32, p.M - (mrow0 + 32 * warp));
             for (int r = 0; r < rows; r++) {
-                const size_t m = (size_t)(m0 + 32 * warp + r);
+                const size_t m = (size_t)(mrow0 + 32 * warp + r);
                 const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
                 const float g = t2.x * s0, u = t2.y * s1;
                 if (p.epi == kEpiSwiGLU) {
@@ -451,7 +466,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
 // A [M][lda] f32 -> A_hi, A_lo [rows][K] bf16 with A = A_hi + A_lo (rows >= M
@@ -595,15 +610,20 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
         if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
         if (a.M / kWM + 1 > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
-        static bool wide_attr[2] = {false, false};
-        if (!wide_attr[wp - 1]) {
+        // two 128-row activation blocks share each weight tile (single bf16 weights, >= 256 rows)
+        const int mb = (wp == 1 && a.M >= 2 * kWM) ? 2 : 1;
+        static bool wide_attr[3] = {false, false, false};
+        const int ai = wp == 2 ? 2 : mb - 1;
+        if (!wide_attr[ai]) {
             const cudaError_t ce =
-                wp == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)wide_smem(2))
-                        : cudaFuncSetAttribute(tc_gemm_wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)wide_smem(1));
+                wp == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)wide_smem(2, 1))
+                : mb == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<1, 2>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(1, 2))
+                          : cudaFuncSetAttribute(tc_gemm_wide_kernel<1, 1>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(1, 1));
             if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
-            wide_attr[wp - 1] = true;
+            wide_attr[ai] = true;
         }
         if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
         if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kWN))) return st;
@@ -622,11 +642,13 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
         p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
         p.err = a.err;
-        const dim3 grid((a.N + kWN - 1) / kWN, (a.M + kWM - 1) / kWM);
+        const dim3 grid((a.N + kWN - 1) / kWN, (a.M + kWM * mb - 1) / (kWM * mb));
         if (wp == 2)
-            tc_gemm_wide_kernel<2><<<grid, kTThreads, wide_smem(2), s>>>(mwh, mwl, mah, mal, p);
+            tc_gemm_wide_kernel<2, 1><<<grid, kTThreads, wide_smem(2, 1), s>>>(mwh, mwl, mah, mal, p);
+        else if (mb == 2)
+            tc_gemm_wide_kernel<1, 2><<<grid, kTThreads, wide_smem(1, 2), s>>>(mwh, mwl, mah, mal, p);
         else
-            tc_gemm_wide_kernel<1><<<grid, kTThreads, wide_smem(1), s>>>(mwh, mwl, mah, mal, p);
+            tc_gemm_wide_kernel<1, 1><<<grid, kTThreads, wide_smem(1, 1), s>>>(mwh, mwl, mah, mal, p);
         VB_LAUNCH_CHECK("tc_gemm_wide_kernel");
         return VB_OK;
     }
