@@ -469,6 +469,197 @@ __global__ void __launch_bounds__(kTThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Persistent form of the wide tiles (single bf16 weights): one CTA per SM loops
+// over 128 x 256 tiles (weight tile fastest, so neighbouring CTAs share the
+// activation tile in L2) with two accumulators in tensor memory, so the
+// epilogue of one tile overlaps the MMAs of the next.  Warps 0-3: epilogue
+// (tensor-memory lane quarters, staging in their own shared memory), warp 4
+// lane 0: TMA producer (a 2-stage ring), warp 5 lane 0: MMA issuer.
+constexpr int kPersistStages = 2;
+constexpr int kPersistStage = 2 * kWA + kWW;        // A_hi, A_lo, W: 64 KB
+constexpr int kPersistStaging = 4 * 32 * 68 * 4;    // epilogue rows, 34 KB
+constexpr size_t kPersistSmem = (size_t)kPersistStages * kPersistStage + kPersistStaging + 1024;
+
+// AND of a predicate over the 128 epilogue threads (named barrier 1)
+__device__ __forceinline__ bool epilogue_all(bool v) {
+    unsigned r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 1, 128, p; "
+        "selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"((unsigned)v)
+        : "memory");
+    return r != 0;
+}
+
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap ta_hi,
+                           const __grid_constant__ CUtensorMap ta_lo, const TcParams p, int ntn, int ntiles) {
+    constexpr int NS = kPersistStages;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) unsigned long long full[NS], empty[NS], acc_full[2], acc_empty[2];
+    __shared__ unsigned tmem_slot;
+    __shared__ int fail;
+    const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.chunks;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(smem_addr(&acc_full[b]), 1);
+            mbar_init(smem_addr(&acc_empty[b]), 1);
+        }
+        fail = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(2 * kWN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = tmem_slot;
+    const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    if (warp == 4) {
+        if (lane == 0) {
+            int g = 0;  // stage counter across tiles
+            for (int j = 0; j < my_tiles && !fail; j++) {
+                const int tile = (int)blockIdx.x + j * (int)gridDim.x;
+                const int n0 = (tile % ntn) * kWN, m0 = (tile / ntn) * kWM;
+                for (int i = 0; i < nch; i++, g++) {
+                    const int s = g % NS;
+                    if (g >= NS &&
+                        !mbar_wait(smem_addr(&empty[s]), ((unsigned)(g / NS) & 1u) ^ 1u, p.err, nullptr, kSiteEmpty, g)) {
+                        fail = 1;
+                        break;
+                    }
+                    const unsigned st = sbase + (unsigned)s * kPersistStage;
+                    const unsigned fb = smem_addr(&full[s]);
+                    mbar_expect_tx(fb, (unsigned)kPersistStage);
+                    const int x = i * kTK;
+                    tma_load_2d(st, &ta_hi, x, m0, fb);
+                    tma_load_2d(st + kWA, &ta_lo, x, m0, fb);
+                    tma_load_2d(st + 2 * kWA, &tw_hi, x, n0, fb);
+                }
+            }
+            // never leave with copies in flight
+            for (int q = g > NS ? g - NS : 0; q < g; q++)
+                mbar_wait(smem_addr(&full[q % NS]), (unsigned)(q / NS) & 1u, p.err, nullptr, kSiteFull, q);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            int g = 0;
+            for (int j = 0; j < my_tiles && !fail; j++) {
+                const int ab = j & 1;
+                // the epilogue has read this accumulator's previous tile
+                if (j >= 2 && !mbar_wait(smem_addr(&acc_empty[ab]), (unsigned)((j >> 1) - 1) & 1u, p.err, nullptr,
+                                         kSiteEmpty, -j)) {
+                    fail = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const unsigned tm = tmem + (unsigned)(ab * kWN);
+                for (int i = 0; i < nch; i++, g++) {
+                    const int s = g % NS;
+                    if (!mbar_wait(smem_addr(&full[s]), (unsigned)(g / NS) & 1u, p.err, nullptr, kSiteFull, g)) {
+                        fail = 1;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const unsigned st = sbase + (unsigned)s * kPersistStage;
+#pragma unroll
+                    for (int kk = 0; kk < kTK / 16; kk++) {
+                        const uint64_t ah = sw128_desc(st + 32u * kk);
+                        const uint64_t al = sw128_desc(st + kWA + 32u * kk);
+                        const uint64_t wh = sw128_desc(st + 2 * kWA + 32u * kk);
+                        mma_wide(tm, ah, wh, i > 0 || kk > 0);
+                        mma_wide(tm, al, wh, true);
+                    }
+                    mma_commit(smem_addr(&empty[s]));
+                }
+                mma_commit(smem_addr(&acc_full[ab]));  // (also after a failed wait: releases the epilogue)
+            }
+        }
+    } else {
+        // epilogue warps 0-3
+        float* T = reinterpret_cast<float*>(smem_raw + (sbase - smem_addr(smem_raw)) + NS * kPersistStage) +
+                   warp * 32 * 68;
+        for (int j = 0; j < my_tiles; j++) {
+            const int ab = j & 1;
+            const bool ok = mbar_wait(smem_addr(&acc_full[ab]), (unsigned)(j >> 1) & 1u, p.err, nullptr, kSiteFull, j);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            // one verdict for the four epilogue warps (they meet at barrier 1 below)
+            if (!epilogue_all(ok && !fail)) break;
+            const int tile = (int)blockIdx.x + j * (int)gridDim.x;
+            const int n0 = (tile % ntn) * kWN, m0 = (tile / ntn) * kWM;
+            for (int cb = 0; cb < kWN; cb += 64) {
+                const int nb = n0 + cb;
+                if (nb >= p.N) break;  // uniform across the epilogue warps
+                float v[64];
+                tmem_ld64(tmem + ((unsigned)(32 * warp) << 16) + (unsigned)(ab * kWN + cb), v);
+#pragma unroll
+                for (int q = 0; q < 64; q += 4)
+                    *reinterpret_cast<float4*>(T + lane * 68 + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                __syncwarp();
+                const int n = nb + 2 * lane;
+                const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
+                const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
+                const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
+                const int rows = min(32, p.M - (m0 + 32 * warp));
+                for (int r = 0; r < rows; r++) {
+                    const size_t m = (size_t)(m0 + 32 * warp + r);
+                    const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
+                    const float gv = t2.x * s0, u = t2.y * s1;
+                    if (p.epi == kEpiSwiGLU) {
+                        if (c1ok) {
+                            const size_t o = m * p.ldc + (n >> 1);
+                            const float h = silu_f(gv) * u;
+                            p.C[o] = h;
+                            if (p.out_hi) {
+                                const __nv_bfloat16 hb = __float2bfloat16_rn(h);
+                                p.out_hi[o] = hb;
+                                p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
+                            }
+                        }
+                    } else {
+                        float* c = p.C + m * p.ldc + n;
+                        if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                            float2 o2 = make_float2(gv, u);
+                            if (p.epi == kEpiResidual) {
+                                const float2 old = *reinterpret_cast<const float2*>(c);
+                                o2.x += old.x;
+                                o2.y += old.y;
+                            }
+                            *reinterpret_cast<float2*>(c) = o2;
+                        } else {
+                            if (c0ok) c[0] = p.epi == kEpiResidual ? c[0] + gv : gv;
+                            if (c1ok) c[1] = p.epi == kEpiResidual ? c[1] + u : u;
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            // this accumulator may take the tile after next
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (threadIdx.x == 0) mbar_arrive(smem_addr(&acc_empty[ab]), 1u);
+        }
+    }
+    __syncwarp();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (fail && threadIdx.x == 0) atomicCAS(p.err, 0, kErrPipeTimeout);
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kWN) : "memory");
+}
+
 // A [M][lda] f32 -> A_hi, A_lo [rows][K] bf16 with A = A_hi + A_lo (rows >= M
 // zero).
 __global__ void split_bf16_kernel(const float* A, int M, int K, int lda, int rows, __nv_bfloat16* hi,
@@ -610,6 +801,39 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
         if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
         if (a.M / kWM + 1 > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
+        if (wp == 1) {
+            // single bf16 weights: the persistent form
+            static bool pattr = false;
+            if (!pattr) {
+                const cudaError_t ce = cudaFuncSetAttribute(tc_gemm_persist_kernel,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            (int)kPersistSmem);
+                if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
+                pattr = true;
+            }
+            if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
+            if ((st = make_map(&mah, a.a_hi, a.M, a.K, kWM))) return st;
+            if ((st = make_map(&mal, a.a_lo, a.M, a.K, kWM))) return st;
+            TcParams p{};
+            p.M = a.M;
+            p.N = a.N;
+            p.chunks = a.K / kTK;
+            p.per_split = p.chunks;
+            p.splits = 1;
+            p.scales = a.scales;
+            p.C = a.C;
+            p.ldc = a.ldc;
+            p.epi = a.epi;
+            p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
+            p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
+            p.err = a.err;
+            const int ntn = (a.N + kWN - 1) / kWN, ntm = (a.M + kWM - 1) / kWM;
+            const int ntiles = ntn * ntm;
+            const int grid = ntiles < kTSMs ? ntiles : kTSMs;
+            tc_gemm_persist_kernel<<<grid, 192, kPersistSmem, s>>>(mwh, mah, mal, p, ntn, ntiles);
+            VB_LAUNCH_CHECK("tc_gemm_persist_kernel");
+            return VB_OK;
+        }
         // two 128-row activation blocks share each weight tile (single bf16 weights, >= 256 rows)
         const int mb = (wp == 1 && a.M >= 2 * kWM) ? 2 : 1;
         static bool wide_attr[3] = {false, false, false};
