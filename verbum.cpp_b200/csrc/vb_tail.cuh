@@ -80,7 +80,7 @@ static __device__ __forceinline__ bool qk_head(const QkNormArgs& a, int b, int h
 
 // qk_head for (row b, head hd) plus its writes: q to q_out, k and v into the
 // cache at pos[b] of the row's sequence, and the optional bf16 copies.
-static __device__ __noinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
+static __device__ __forceinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
     const int D = 128;
     float o[4], v[4];
     if (!qk_head(a, b, hd, lane, o, v)) return;
