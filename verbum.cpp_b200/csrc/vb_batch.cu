@@ -314,7 +314,7 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P, float
         (size_t)R * H * 4,              // x
         (size_t)R * H * 4,              // xn
         (size_t)R * e->qkv_rows * 4,    // qkv
-        (size_t)R * e->q_width * 4,     // q
+        tc_att ? 0 : (size_t)R * e->q_width * 4,  // q (f32, CUDA-core attention only)
         tc_att ? 0 : (size_t)R * e->q_width * 4,  // ctx (f32 attention output, CUDA-core form only)
         (size_t)R * c.ffn * 4,          // h
         pb.ws_floats * 4,               // ws

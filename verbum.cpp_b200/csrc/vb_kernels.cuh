@@ -62,7 +62,7 @@ struct QkNormArgs {
     const float* cos_tab;   // [rope_positions, D]
     const float* sin_tab;
     const int* pos;         // [B] device positions (write row)
-    float* q_out;           // [B, H, D]
+    float* q_out;           // [B, H, D] (null: only the bf16 copies)
     float* kc;              // cache base
     float* vc;
     int64_t stride_b, stride_pos, stride_h;  // cache strides (floats)

@@ -203,6 +203,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// bf16 hi / lo split of a pair: hi = rn(a) | rn(b), lo = rn(a - hi) | rn(b - hi)
+// (the widened hi values are the packed word's halves shifted into place)
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    hi = pack_bf16(a, b);
+    lo = pack_bf16(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+}
+
+// 2^x by the PTX ex2.approx instruction (relative error ~2^-22, -inf -> +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __global__ void __launch_bounds__(256, 1)
     tc_prefill_attn_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
                            const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
@@ -211,7 +225,7 @@ __global__ void __launch_bounds__(256, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) unsigned long long q_full, kv_full[2], s_done, pv_done;
     __shared__ unsigned tmem_slot;
-    __shared__ float xch[2][128];  // the row halves' maximum, then sum
+    __shared__ float xch[2][128];  // the row halves' maximum per key tile, their sums at the end
     const unsigned sb = (smem_addr(smem_raw) + 1023u) & ~1023u;
     uint8_t* sg = smem_raw + (sb - smem_addr(smem_raw));
     const int t = threadIdx.x, warp = t >> 5;
@@ -266,7 +280,8 @@ __global__ void __launch_bounds__(256, 1)
     const int r = t & 127, hf = t >> 7;  // query row: position c0 + (r & 63) of head 2 kvh + (r >> 6)
     const int qpos = c0 + (r & 63);
     const bool rvalid = (r & 63) < nq;
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+    // logits in base 2: exp(s / sqrt(D) - m) = 2^(s log2(e) / sqrt(D) - m')
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(128.0f)) * 1.44269504088896341f;
     const unsigned lane_off = (unsigned)(32 * (warp & 3)) << 16;  // warp w reads lanes 32 (w % 4) ..
     float o[64];
 #pragma unroll
@@ -309,19 +324,21 @@ __global__ void __launch_bounds__(256, 1)
             sv[j] = (rvalid && k0 + j <= qpos) ? sv[j] * scale : -INFINITY;
             mx = fmaxf(mx, sv[j]);
         }
+        // the two halves of a row sit in warps w and w + 4: a barrier of that pair only
         xch[hf][r] = mx;
-        __syncthreads();
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
         mx = fmaxf(xch[0][r], xch[1][r]);
-        __syncthreads();  // xch is reused for the sums
         const float mn = fmaxf(m, mx);
-        const float alpha = (m == -INFINITY) ? 0.f : expf(m - mn);
+        const float mb = mn == -INFINITY ? 0.f : mn;  // a row with no key yet: every weight 0
+        const float alpha = ex2_approx(m - mb);
         float sum = 0.f;
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-            sv[j] = (sv[j] == -INFINITY) ? 0.f : expf(sv[j] - mn);
+            sv[j] = ex2_approx(sv[j] - mb);
             sum += sv[j];
         }
-        xch[hf][r] = sum;
+        // this half's share of the row sum (alpha is the same for both halves)
+        l = l * alpha + sum;
         m = mn;
         // P_hi / P_lo: this thread's half row, chunks 4 hf .. 4 hf + 3 of 8 keys, 128-byte swizzle
 #pragma unroll
@@ -329,12 +346,7 @@ __global__ void __launch_bounds__(256, 1)
             const int c = 4 * hf + cc;
             uint32_t hv[4], lv[4];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const float a = sv[8 * cc + 2 * q], bb = sv[8 * cc + 2 * q + 1];
-                const __nv_bfloat16 ah = __float2bfloat16_rn(a), bh = __float2bfloat16_rn(bb);
-                hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
-                lv[q] = pack_bf16(a - __bfloat162float(ah), bb - __bfloat162float(bh));
-            }
+            for (int q = 0; q < 4; q++) split_pair(sv[8 * cc + 2 * q], sv[8 * cc + 2 * q + 1], hv[q], lv[q]);
             const int off = r * 128 + ((c ^ (r & 7)) << 4);
             *reinterpret_cast<uint4*>(sg + kOffP + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
             *reinterpret_cast<uint4*>(sg + kOffP + kQT + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
@@ -342,7 +354,6 @@ __global__ void __launch_bounds__(256, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncthreads();
-        l = l * alpha + (xch[0][r] + xch[1][r]);  // read before the iteration's closing barrier
         if (t == 32) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (ok) {
@@ -378,6 +389,10 @@ __global__ void __launch_bounds__(256, 1)
             break;
         }
     }
+    // the row sum from its two halves (every thread has left the loop's last barrier)
+    xch[hf][r] = l;
+    __syncthreads();
+    l = xch[0][r] + xch[1][r];
     if (t == 0) {
         // never leave with copies in flight (the last two requested tiles)
         for (int i = issued > 2 ? issued - 2 : 0; i < issued; i++)
@@ -394,11 +409,7 @@ __global__ void __launch_bounds__(256, 1)
             for (int e = 0; e < 8; e++) y[e] = o[d + e] / l;
             uint32_t hv[4], lv[4];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const __nv_bfloat16 ah = __float2bfloat16_rn(y[2 * q]), bh = __float2bfloat16_rn(y[2 * q + 1]);
-                hv[q] = pack_bf16(__bfloat162float(ah), __bfloat162float(bh));
-                lv[q] = pack_bf16(y[2 * q] - __bfloat162float(ah), y[2 * q + 1] - __bfloat162float(bh));
-            }
+            for (int q = 0; q < 4; q++) split_pair(y[2 * q], y[2 * q + 1], hv[q], lv[q]);
             *reinterpret_cast<uint4*>(p.out_hi + base + d) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
             *reinterpret_cast<uint4*>(p.out_lo + base + d) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
             if (p.out) {

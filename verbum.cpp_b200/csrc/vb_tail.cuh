@@ -78,7 +78,7 @@ static __device__ __forceinline__ bool qk_head(const QkNormArgs& a, int b, int h
     return true;
 }
 
-// qk_head for (row b, head hd) plus its writes: q to q_out, k and v into the
+// qk_head for (row b, head hd) plus its writes: q to q_out (when set), k and v into the
 // cache at pos[b] of the row's sequence, and the optional bf16 copies.
 static __device__ __forceinline__ void qk_norm_one(const QkNormArgs& a, int b, int hd, int lane) {
     const int D = 128;
@@ -94,7 +94,8 @@ static __device__ __forceinline__ void qk_norm_one(const QkNormArgs& a, int b, i
         const size_t qo = ((size_t)b * a.H + h) * D;
         bf = qo;
 #pragma unroll
-        for (int e = 0; e < 4; e++) a.q_out[qo + lane + 32 * e] = o[e];
+        for (int e = 0; e < 4; e++)
+            if (a.q_out) a.q_out[qo + lane + 32 * e] = o[e];
     } else {
         const int seq = a.rows_per_seq > 0 ? b / a.rows_per_seq : b;
         const size_t off = (size_t)seq * a.stride_b + (size_t)pos * a.stride_pos + (size_t)h * a.stride_h;
