@@ -289,31 +289,38 @@ __global__ void __launch_bounds__(256, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     int issued = nt > 1 ? 2 : 1;  // key tiles requested so far
+    int s_issued = -1, s_seen = -1;  // last S product issued (thread 32) / waited for (all)
+    // thread 32: S = Q K^T of key tile `tile` into tS (false: its copies never came)
+    auto issue_s = [&](int tile) -> bool {
+        const int bf = tile & 1;
+        const bool w = (tile > 0 || mbar_wait(smem_addr(&q_full), 0u, p.err, nullptr, kSiteFull, -1)) &&
+                       mbar_wait(smem_addr(&kv_full[bf]), (unsigned)(tile >> 1) & 1u, p.err, nullptr, kSiteFull, tile);
+        if (w) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const unsigned kb = sb + kOffKV + (unsigned)bf * kKVBuf;
+#pragma unroll
+            for (int dh = 0; dh < 2; dh++)
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t qh = sw128_desc(sb + kOffQ + dh * kQT + 32u * kk);
+                    const uint64_t ql = sw128_desc(sb + kOffQ + (2 + dh) * kQT + 32u * kk);
+                    const uint64_t kh = sw128_desc(kb + dh * kKT + 32u * kk);
+                    const uint64_t kl = sw128_desc(kb + (2 + dh) * kKT + 32u * kk);
+                    mma_f16(tS, qh, kh, kIdS, dh > 0 || kk > 0);
+                    mma_f16(tS, qh, kl, kIdS, true);
+                    mma_f16(tS, ql, kh, kIdS, true);
+                }
+        }
+        // commit even after a failed wait so the waiters are released
+        mma_commit(smem_addr(&s_done));
+        s_issued = tile;
+        return w;
+    };
     for (int it = 0; it < nt; it++) {
         const int buf = it & 1;
-        if (t == 32) {
-            bool w = (it > 0 || mbar_wait(smem_addr(&q_full), 0u, p.err, nullptr, kSiteFull, -1)) &&
-                     mbar_wait(smem_addr(&kv_full[buf]), (unsigned)(it >> 1) & 1u, p.err, nullptr, kSiteFull, it);
-            if (w) {
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const unsigned kb = sb + kOffKV + (unsigned)buf * kKVBuf;
-#pragma unroll
-                for (int dh = 0; dh < 2; dh++)
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++) {
-                        const uint64_t qh = sw128_desc(sb + kOffQ + dh * kQT + 32u * kk);
-                        const uint64_t ql = sw128_desc(sb + kOffQ + (2 + dh) * kQT + 32u * kk);
-                        const uint64_t kh = sw128_desc(kb + dh * kKT + 32u * kk);
-                        const uint64_t kl = sw128_desc(kb + (2 + dh) * kKT + 32u * kk);
-                        mma_f16(tS, qh, kh, kIdS, dh > 0 || kk > 0);
-                        mma_f16(tS, qh, kl, kIdS, true);
-                        mma_f16(tS, ql, kh, kIdS, true);
-                    }
-            }
-            // commit even after a failed wait so the waiters below are released
-            mma_commit(smem_addr(&s_done));
-        }
+        if (t == 32 && it == 0 && !issue_s(0)) ok = false;
         ok = mbar_wait(smem_addr(&s_done), (unsigned)it & 1u, p.err, nullptr, kSiteFull, it) && ok;
+        s_seen = it;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         float sv[32];
         tmem_ld32(tS + lane_off + 32u * (unsigned)hf, sv);
@@ -370,6 +377,9 @@ __global__ void __launch_bounds__(256, 1)
                 }
             }
             mma_commit(smem_addr(&pv_done));
+            // the next key tile's S runs while the threads fold this P.V in (every thread
+            // read this tile's S before the barrier above)
+            if (it + 1 < nt && !issue_s(it + 1)) ok = false;
         }
         ok = mbar_wait(smem_addr(&pv_done), (unsigned)it & 1u, p.err, nullptr, kSiteFull, it) && ok;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -393,6 +403,8 @@ __global__ void __launch_bounds__(256, 1)
     xch[hf][r] = l;
     __syncthreads();
     l = xch[0][r] + xch[1][r];
+    if (t == 32 && s_issued > s_seen)  // a failed pass left the next S product in flight
+        mbar_wait(smem_addr(&s_done), (unsigned)s_issued & 1u, p.err, nullptr, kSiteFull, s_issued);
     if (t == 0) {
         // never leave with copies in flight (the last two requested tiles)
         for (int i = issued > 2 ? issued - 2 : 0; i < issued; i++)
