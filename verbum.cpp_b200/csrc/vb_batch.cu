@@ -312,7 +312,7 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P, float
     }
     const size_t sz[] = {
         (size_t)R * H * 4,              // x
-        (size_t)R * H * 4,              // xn
+        pool ? (size_t)R * H * 4 : 0,   // xn (f32 final norm rows for embed_text)
         (size_t)R * e->qkv_rows * 4,    // qkv
         tc_att ? 0 : (size_t)R * e->q_width * 4,  // q (f32, CUDA-core attention only)
         tc_att ? 0 : (size_t)R * e->q_width * 4,  // ctx (f32 attention output, CUDA-core form only)
@@ -406,7 +406,8 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P, float
         for (int l = 0; l < c.layers; l++) {
             const vb_layer_dev& L = e->L[l];
             void* const* tw = &b->tcw[(size_t)l * 8];
-            if ((st = launch_rmsnorm_rows(pb.x, L.in_norm, pb.xn, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
+            // (the GEMMs read the bf16 split only)
+            if ((st = launch_rmsnorm_rows(pb.x, L.in_norm, nullptr, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
             if ((st = gemm(Rn, pb.a_hi, pb.a_lo, tw + 0, L.sqkv, pb.qkv, e->qkv_rows, H, e->qkv_rows, kEpiStore, q8,
                            nullptr, nullptr)))
                 return st;
@@ -465,8 +466,11 @@ vb_status batch_prefill_chunks(vb_batch* b, const int* tokens_host, int P, float
             if ((st = gemm(Rn, pb.y_hi, pb.y_lo, tw + 2, L.so, pb.x, H, e->q_width, H, kEpiResidual, q8, nullptr,
                            nullptr)))
                 return st;
-            if ((st = launch_rmsnorm_rows(pb.x, L.post_norm, pb.xn, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
-            if ((st = gemm(Rn, pb.a_hi, pb.a_lo, tw + 4, L.sgu, pb.h, 2 * c.ffn, H, c.ffn, kEpiSwiGLU, q8, pb.y_hi,
+            if ((st = launch_rmsnorm_rows(pb.x, L.post_norm, nullptr, Rn, H, c.eps, s, pb.a_hi, pb.a_lo))) return st;
+            // the down projection reads the bf16 split of h: its f32 copy only where the
+            // small-M (split-K) form needs an output
+            float* hf = (Rn >= 128 && 2 * c.ffn >= 256) ? nullptr : pb.h;
+            if ((st = gemm(Rn, pb.a_hi, pb.a_lo, tw + 4, L.sgu, hf, 2 * c.ffn, H, c.ffn, kEpiSwiGLU, q8, pb.y_hi,
                            pb.y_lo)))
                 return st;
             if ((st = gemm(Rn, pb.y_hi, pb.y_lo, tw + 6, L.sd, pb.x, H, c.ffn, H, kEpiResidual, q8, nullptr,

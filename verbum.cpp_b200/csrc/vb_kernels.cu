@@ -320,7 +320,6 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
     pdl_wait();
     __shared__ double red[8];
     const float* xr = x + (size_t)blockIdx.x * dim;
-    float* orow = out + (size_t)blockIdx.x * dim;
     double ss = 0.0;
     for (int i = threadIdx.x; i < dim; i += 256) {
         const float v = xr[i];
@@ -329,7 +328,7 @@ __global__ void rmsnorm_rows_kernel(const float* x, const float* w, float* out, 
     const float sc = rms_scale(block_sum_d<256>(ss, red), dim, eps);
     for (int i = threadIdx.x; i < dim; i += 256) {
         const float y = __fmul_rn(__fmul_rn(xr[i], sc), w[i]);
-        orow[i] = y;
+        if (out) out[(size_t)blockIdx.x * dim + i] = y;  // (null: the bf16 split only)
         if (hi) {
             const __nv_bfloat16 h = __float2bfloat16_rn(y);
             hi[(size_t)blockIdx.x * dim + i] = h;
@@ -809,6 +808,7 @@ vb_status launch_quantize_rows(const float* W, int64_t rows, int64_t cols, int8_
 vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int rows, int dim,
                               float eps, cudaStream_t s, void* hi, void* lo) {
     if (rows <= 0 || dim <= 0) return fail(VB_ERR_ARG, "rmsnorm: empty shape");
+    if (!out && !hi) return fail(VB_ERR_ARG, "rmsnorm: no output");
     launch_pdl(rmsnorm_rows_kernel, rows, 256, 0, s, x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
                static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("rmsnorm_rows_kernel");

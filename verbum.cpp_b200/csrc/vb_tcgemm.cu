@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     if (c1ok) {  // gate row n, up row n + 1 -> output n / 2
                         const size_t o = m * p.ldc + (n >> 1);
                         const float h = silu_f(g) * u;
-                        p.C[o] = h;
+                        if (p.C) p.C[o] = h;
                         if (p.out_hi) {
                             const __nv_bfloat16 hb = __float2bfloat16_rn(h);
                             p.out_hi[o] = hb;
@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(192, 1)
                         if (c1ok) {
                             const size_t o = m * p.ldc + (n >> 1);
                             const float h = silu_f(gv) * u;
-                            p.C[o] = h;
+                            if (p.C) p.C[o] = h;
                             if (p.out_hi) {
                                 const __nv_bfloat16 hb = __float2bfloat16_rn(h);
                                 p.out_hi[o] = hb;
@@ -797,8 +797,10 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     CUtensorMap mwh, mwl, mah, mal;
     vb_status st;
     if (a.M >= kWM && a.N >= kWN && !a.partials_only) {
-        // many activation rows: wide tiles (boxes within the tensors), no split-K
-        if (!a.C) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
+        // many activation rows: wide tiles (boxes within the tensors), no split-K; SwiGLU
+        // may write its bf16 split alone
+        if (!a.C && !(a.epi == kEpiSwiGLU && a.out_hi && a.out_lo))
+            return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
         if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
         if (a.M / kWM + 1 > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
         if (wp == 1) {
