@@ -310,6 +310,77 @@ __device__ __forceinline__ void mma_wide(unsigned tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
+// One warp's staged rows (T: up to 32 rows x 64 columns, row stride 68 floats)
+// to the output rows mrow .. mrow + rows - 1, columns nb .. nb + 63: lane j takes
+// columns nb + 2j and nb + 2j + 1, so each store instruction covers 256
+// contiguous bytes of a row.  The residual form loads 16 rows' old values before
+// it stores any of them (the stores could alias later loads, so the compiler
+// would otherwise wait out one load latency per row).
+__device__ __forceinline__ void wide_store_rows(const TcParams& p, const float* T, int mrow, int rows, int nb,
+                                                int lane) {
+    const int n = nb + 2 * lane;
+    const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
+    const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
+    const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
+    if (p.epi == kEpiResidual) {
+        constexpr int kB = 16;
+        for (int r0 = 0; r0 < rows; r0 += kB) {
+            float2 old[kB];
+#pragma unroll
+            for (int q = 0; q < kB; q++) {
+                old[q] = make_float2(0.f, 0.f);
+                if (r0 + q < rows) {
+                    const float* c = p.C + (size_t)(mrow + r0 + q) * p.ldc + n;
+                    if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                        old[q] = *reinterpret_cast<const float2*>(c);
+                    } else {
+                        if (c0ok) old[q].x = c[0];
+                        if (c1ok) old[q].y = c[1];
+                    }
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < kB; q++) {
+                if (r0 + q >= rows) break;
+                const float2 t2 = *reinterpret_cast<const float2*>(T + (r0 + q) * 68 + 2 * lane);
+                const float2 o2 = make_float2(old[q].x + t2.x * s0, old[q].y + t2.y * s1);
+                float* c = p.C + (size_t)(mrow + r0 + q) * p.ldc + n;
+                if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                    *reinterpret_cast<float2*>(c) = o2;
+                } else {
+                    if (c0ok) c[0] = o2.x;
+                    if (c1ok) c[1] = o2.y;
+                }
+            }
+        }
+        return;
+    }
+    for (int r = 0; r < rows; r++) {
+        const size_t m = (size_t)(mrow + r);
+        const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
+        const float g = t2.x * s0, u = t2.y * s1;
+        if (p.epi == kEpiSwiGLU) {
+            if (c1ok) {  // gate row n, up row n + 1 -> output n / 2
+                const size_t o = m * p.ldc + (n >> 1);
+                const float h = silu_f(g) * u;
+                if (p.C) p.C[o] = h;
+                if (p.out_hi) {
+                    const __nv_bfloat16 hb = __float2bfloat16_rn(h);
+                    p.out_hi[o] = hb;
+                    p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
+                }
+            }
+        } else {
+            float* c = p.C + m * p.ldc + n;
+            if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                *reinterpret_cast<float2*>(c) = make_float2(g, u);
+            } else {
+                if (c0ok) c[0] = g;
+                if (c1ok) c[1] = u;
+            }
+        }
+    }
+}
 
 // grid (ceil(N / 256), ceil(M / (128 MB))); 128 threads: warp 0 lane 0 issues
 // the TMA copies, warp 1 lane 0 the MMAs, all four warps the epilogue (thread =
@@ -422,42 +493,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             for (int j = 0; j < 64; j += 4)
                 *reinterpret_cast<float4*>(T + lane * 68 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             __syncwarp();
-            const int n = nb + 2 * lane;
-            const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
-            const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
-            const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
-            const int rows = min(32, p.M - (mrow0 + 32 * warp));
-            for (int r = 0; r < rows; r++) {
-                const size_t m = (size_t)(mrow0 + 32 * warp + r);
-                const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
-                const float g = t2.x * s0, u = t2.y * s1;
-                if (p.epi == kEpiSwiGLU) {
-                    if (c1ok) {  // gate row n, up row n + 1 -> output n / 2
-                        const size_t o = m * p.ldc + (n >> 1);
-                        const float h = silu_f(g) * u;
-                        if (p.C) p.C[o] = h;
-                        if (p.out_hi) {
-                            const __nv_bfloat16 hb = __float2bfloat16_rn(h);
-                            p.out_hi[o] = hb;
-                            p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
-                        }
-                    }
-                } else {
-                    float* c = p.C + m * p.ldc + n;
-                    if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
-                        float2 o2 = make_float2(g, u);
-                        if (p.epi == kEpiResidual) {
-                            const float2 old = *reinterpret_cast<const float2*>(c);
-                            o2.x += old.x;
-                            o2.y += old.y;
-                        }
-                        *reinterpret_cast<float2*>(c) = o2;
-                    } else {
-                        if (c0ok) c[0] = p.epi == kEpiResidual ? c[0] + g : g;
-                        if (c1ok) c[1] = p.epi == kEpiResidual ? c[1] + u : u;
-                    }
-                }
-            }
+            wide_store_rows(p, T, mrow0 + 32 * warp, min(32, p.M - (mrow0 + 32 * warp)), nb, lane);
             __syncwarp();
         }
     } else if (threadIdx.x == 0) {
@@ -608,42 +644,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int q = 0; q < 64; q += 4)
                     *reinterpret_cast<float4*>(T + lane * 68 + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
                 __syncwarp();
-                const int n = nb + 2 * lane;
-                const bool c0ok = n < p.N, c1ok = n + 1 < p.N;
-                const float s0 = (p.scales && c0ok) ? p.scales[n] : 1.f;
-                const float s1 = (p.scales && c1ok) ? p.scales[n + 1] : 1.f;
-                const int rows = min(32, p.M - (m0 + 32 * warp));
-                for (int r = 0; r < rows; r++) {
-                    const size_t m = (size_t)(m0 + 32 * warp + r);
-                    const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
-                    const float gv = t2.x * s0, u = t2.y * s1;
-                    if (p.epi == kEpiSwiGLU) {
-                        if (c1ok) {
-                            const size_t o = m * p.ldc + (n >> 1);
-                            const float h = silu_f(gv) * u;
-                            if (p.C) p.C[o] = h;
-                            if (p.out_hi) {
-                                const __nv_bfloat16 hb = __float2bfloat16_rn(h);
-                                p.out_hi[o] = hb;
-                                p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
-                            }
-                        }
-                    } else {
-                        float* c = p.C + m * p.ldc + n;
-                        if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
-                            float2 o2 = make_float2(gv, u);
-                            if (p.epi == kEpiResidual) {
-                                const float2 old = *reinterpret_cast<const float2*>(c);
-                                o2.x += old.x;
-                                o2.y += old.y;
-                            }
-                            *reinterpret_cast<float2*>(c) = o2;
-                        } else {
-                            if (c0ok) c[0] = p.epi == kEpiResidual ? c[0] + gv : gv;
-                            if (c1ok) c[1] = p.epi == kEpiResidual ? c[1] + u : u;
-                        }
-                    }
-                }
+                wide_store_rows(p, T, m0 + 32 * warp, min(32, p.M - (m0 + 32 * warp)), nb, lane);
                 __syncwarp();
             }
             // this accumulator may take the tile after next
