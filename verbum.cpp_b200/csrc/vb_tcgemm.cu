@@ -355,28 +355,44 @@ __device__ __forceinline__ void wide_store_rows(const TcParams& p, const float* 
         }
         return;
     }
-    for (int r = 0; r < rows; r++) {
-        const size_t m = (size_t)(mrow + r);
-        const float2 t2 = *reinterpret_cast<const float2*>(T + r * 68 + 2 * lane);
-        const float g = t2.x * s0, u = t2.y * s1;
+    // 8 rows at a time: their staged values are read before any store (the
+    // compiler cannot move shared-memory reads past global stores), so the rows'
+    // arithmetic overlaps
+    constexpr int kB = 8;
+    for (int r0 = 0; r0 < rows; r0 += kB) {
+        float2 t2[kB];
+#pragma unroll
+        for (int q = 0; q < kB; q++)
+            t2[q] = r0 + q < rows ? *reinterpret_cast<const float2*>(T + (r0 + q) * 68 + 2 * lane)
+                                  : make_float2(0.f, 0.f);
         if (p.epi == kEpiSwiGLU) {
-            if (c1ok) {  // gate row n, up row n + 1 -> output n / 2
-                const size_t o = m * p.ldc + (n >> 1);
-                const float h = silu_f(g) * u;
-                if (p.C) p.C[o] = h;
+            if (!c1ok) continue;  // gate row n, up row n + 1 -> output n / 2
+            float h[kB];
+#pragma unroll
+            for (int q = 0; q < kB; q++) h[q] = silu_f(t2[q].x * s0) * (t2[q].y * s1);
+#pragma unroll
+            for (int q = 0; q < kB; q++) {
+                if (r0 + q >= rows) break;
+                const size_t o = (size_t)(mrow + r0 + q) * p.ldc + (n >> 1);
+                if (p.C) p.C[o] = h[q];
                 if (p.out_hi) {
-                    const __nv_bfloat16 hb = __float2bfloat16_rn(h);
+                    const __nv_bfloat16 hb = __float2bfloat16_rn(h[q]);
                     p.out_hi[o] = hb;
-                    p.out_lo[o] = __float2bfloat16_rn(h - __bfloat162float(hb));
+                    p.out_lo[o] = __float2bfloat16_rn(h[q] - __bfloat162float(hb));
                 }
             }
         } else {
-            float* c = p.C + m * p.ldc + n;
-            if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
-                *reinterpret_cast<float2*>(c) = make_float2(g, u);
-            } else {
-                if (c0ok) c[0] = g;
-                if (c1ok) c[1] = u;
+#pragma unroll
+            for (int q = 0; q < kB; q++) {
+                if (r0 + q >= rows) break;
+                const float g = t2[q].x * s0, u = t2[q].y * s1;
+                float* c = p.C + (size_t)(mrow + r0 + q) * p.ldc + n;
+                if (c1ok && ((reinterpret_cast<uintptr_t>(c) & 7) == 0)) {
+                    *reinterpret_cast<float2*>(c) = make_float2(g, u);
+                } else {
+                    if (c0ok) c[0] = g;
+                    if (c1ok) c[1] = u;
+                }
             }
         }
     }
