@@ -98,6 +98,18 @@ def test_rmsnorm_rows():
     assert np.mean(got == ref) > 0.99  # double sum of squares as the reference: ~all bits equal
 
 
+def test_rmsnorm_many_rows():
+    # 1024 rows and more take the warp-per-row form (8 rows per CTA)
+    x = xvec(1027, 1024, 14) * 3
+    w = (1 + 0.1 * xvec(1, 1024, 15)[0]).astype(np.float32)
+    out = torch.empty(1027, 1024, device="cuda")
+    vb200.rmsnorm(dev(x), dev(w), out, 1e-6)
+    ref = oracle.rmsnorm(x, w, 1e-6)
+    got = host(out)
+    assert np.max(np.abs(got - ref)) < 1e-6
+    assert np.mean(got == ref) > 0.99
+
+
 def test_rope_bitexact():
     c, s = oracle.rope_table(128, 4096, 1e6)
     for pos in (0, 7, 4095):

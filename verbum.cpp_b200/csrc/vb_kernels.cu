@@ -348,6 +348,63 @@ __global__ void reduce_residual_norm_kernel(float* x, const float* parts, int sp
     residual_norm_row<256>(x, parts, splits, scales, w, out, hi, lo, rows, dim, eps, blockIdx.x, red);
 }
 
+// Many rows (a prompt chunk): a warp per row, 8 rows per CTA; dim % 128 == 0,
+// dim <= 2048.  Lane l holds elements 4l + 128j as float4s.
+__global__ void __launch_bounds__(256) rmsnorm_rows_warp_kernel(const float* x, const float* w, float* out, int rows,
+                                                                int dim, float eps, __nv_bfloat16* hi,
+                                                                __nv_bfloat16* lo) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nj = dim >> 7;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * dim);
+    float4 v[16];
+    double ss = 0.0;
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+        if (j < nj) v[j] = xr[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+        if (j < nj)
+            ss += (double)v[j].x * v[j].x + (double)v[j].y * v[j].y + (double)v[j].z * v[j].z +
+                  (double)v[j].w * v[j].w;
+    const float sc = rms_scale(warp_sum_d(ss), dim, eps);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        if (j >= nj) break;
+        const int i = 4 * lane + 128 * j;
+        const float4 wv = *reinterpret_cast<const float4*>(w + i);
+        const float y0 = __fmul_rn(__fmul_rn(v[j].x, sc), wv.x), y1 = __fmul_rn(__fmul_rn(v[j].y, sc), wv.y);
+        const float y2 = __fmul_rn(__fmul_rn(v[j].z, sc), wv.z), y3 = __fmul_rn(__fmul_rn(v[j].w, sc), wv.w);
+        const size_t o = (size_t)row * dim + i;
+        if (out) *reinterpret_cast<float4*>(out + o) = make_float4(y0, y1, y2, y3);
+        if (hi) {
+            const __nv_bfloat162 h01 = __floats2bfloat162_rn(y0, y1), h23 = __floats2bfloat162_rn(y2, y3);
+            const __nv_bfloat162 l01 = __floats2bfloat162_rn(y0 - __low2float(h01), y1 - __high2float(h01));
+            const __nv_bfloat162 l23 = __floats2bfloat162_rn(y2 - __low2float(h23), y3 - __high2float(h23));
+            uint2 hv, lv;
+            hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+            lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+            lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+            *reinterpret_cast<uint2*>(hi + o) = hv;
+            *reinterpret_cast<uint2*>(lo + o) = lv;
+        }
+    }
+}
+
+// Many rows (a prompt chunk): 8 rows per CTA, its 8 warps taking the rows'
+// (row, head) pairs in turn (fewer, longer CTAs than one CTA per 8 heads).
+__global__ void __launch_bounds__(256) qk_norm_rope_rows_kernel(QkNormArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int nh = a.H + a.KVH;
+    const int r0 = blockIdx.x * 8;
+    const int tasks = min(8, a.B - r0) * nh;
+    for (int t = threadIdx.x >> 5; t < tasks; t += 8) qk_norm_one(a, r0 + t / nh, t % nh, threadIdx.x & 31);
+}
+
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkNormArgs a) {
     pdl_trigger();
     pdl_wait();
@@ -809,6 +866,15 @@ vb_status launch_rmsnorm_rows(const float* x, const float* w, float* out, int ro
                               float eps, cudaStream_t s, void* hi, void* lo) {
     if (rows <= 0 || dim <= 0) return fail(VB_ERR_ARG, "rmsnorm: empty shape");
     if (!out && !hi) return fail(VB_ERR_ARG, "rmsnorm: no output");
+    const uintptr_t al16 = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                           reinterpret_cast<uintptr_t>(out);
+    const uintptr_t al8 = reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo);
+    if (rows >= 1024 && dim % 128 == 0 && dim <= 2048 && (al16 & 15) == 0 && (al8 & 7) == 0) {
+        launch_pdl(rmsnorm_rows_warp_kernel, (rows + 7) / 8, 256, 0, s, x, w, out, rows, dim, eps,
+                   static_cast<__nv_bfloat16*>(hi), static_cast<__nv_bfloat16*>(lo));
+        VB_LAUNCH_CHECK("rmsnorm_rows_warp_kernel");
+        return VB_OK;
+    }
     launch_pdl(rmsnorm_rows_kernel, rows, 256, 0, s, x, w, out, dim, eps, static_cast<__nv_bfloat16*>(hi),
                static_cast<__nv_bfloat16*>(lo));
     VB_LAUNCH_CHECK("rmsnorm_rows_kernel");
@@ -827,6 +893,11 @@ vb_status launch_reduce_residual_norm(float* x, const float* parts, int splits, 
 
 vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (a.B >= 4096) {
+        launch_pdl(qk_norm_rope_rows_kernel, (a.B + 7) / 8, 256, 0, s, a);
+        VB_LAUNCH_CHECK("qk_norm_rope_rows_kernel");
+        return VB_OK;
+    }
     dim3 grid(a.B, (a.H + a.KVH + 7) / 8);  // rows on x: a prompt chunk has up to 2^31 - 1
     launch_pdl(qk_norm_rope_kernel, grid, 256, 0, s, a);
     VB_LAUNCH_CHECK("qk_norm_rope_kernel");
