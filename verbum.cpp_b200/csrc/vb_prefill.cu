@@ -326,10 +326,18 @@ __global__ void __launch_bounds__(256, 1)
         tmem_ld32(tS + lane_off + 32u * (unsigned)hf, sv);
         const int k0 = it * kAK + 32 * hf;
         float mx = -INFINITY;
+        if (rvalid && k0 + 31 <= qpos) {  // every key of this half tile is visible
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            sv[j] = (rvalid && k0 + j <= qpos) ? sv[j] * scale : -INFINITY;
-            mx = fmaxf(mx, sv[j]);
+            for (int j = 0; j < 32; j++) {
+                sv[j] *= scale;
+                mx = fmaxf(mx, sv[j]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                sv[j] = (rvalid && k0 + j <= qpos) ? sv[j] * scale : -INFINITY;
+                mx = fmaxf(mx, sv[j]);
+            }
         }
         // the two halves of a row sit in warps w and w + 4: a barrier of that pair only
         xch[hf][r] = mx;
