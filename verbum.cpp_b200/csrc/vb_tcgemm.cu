@@ -525,27 +525,31 @@ __global__ void __launch_bounds__(kTThreads, 1)
 // Persistent form of the wide tiles (single bf16 weights): one CTA per SM loops
 // over 128 x 256 tiles (weight tile fastest, so neighbouring CTAs share the
 // activation tile in L2) with two accumulators in tensor memory, so the
-// epilogue of one tile overlaps the MMAs of the next.  Warps 0-3: epilogue
-// (tensor-memory lane quarters, staging in their own shared memory), warp 4
-// lane 0: TMA producer (a 2-stage ring), warp 5 lane 0: MMA issuer.
+// epilogue of one tile overlaps the MMAs of the next.  Warps 0-7: epilogue
+// (warp w reads tensor-memory lane quarter w % 4 and the column blocks
+// 64 (w / 4) + 128 i, staging in its own shared memory), warp 8 lane 0: TMA
+// producer (a 2-stage ring), warp 9 lane 0: MMA issuer.
+constexpr int kPersistEpiWarps = 8;
+constexpr int kPersistThreads = 32 * (kPersistEpiWarps + 2);
 constexpr int kPersistStages = 2;
-constexpr int kPersistStage = 2 * kWA + kWW;        // A_hi, A_lo, W: 64 KB
-constexpr int kPersistStaging = 4 * 32 * 68 * 4;    // epilogue rows, 34 KB
+constexpr int kPersistStage = 2 * kWA + kWW;                       // A_hi, A_lo, W: 64 KB
+constexpr int kPersistStaging = kPersistEpiWarps * 32 * 68 * 4;    // epilogue rows, 68 KB
 constexpr size_t kPersistSmem = (size_t)kPersistStages * kPersistStage + kPersistStaging + 1024;
+static_assert(kPersistSmem + 256 <= 232448, "persistent gemm: shared memory");
 
-// AND of a predicate over the 128 epilogue threads (named barrier 1)
+// AND of a predicate over the epilogue threads (named barrier 1)
 __device__ __forceinline__ bool epilogue_all(bool v) {
     unsigned r;
     asm volatile(
-        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 1, 128, p; "
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, 1, %2, p; "
         "selp.u32 %0, 1, 0, q; }"
         : "=r"(r)
-        : "r"((unsigned)v)
+        : "r"((unsigned)v), "r"(32 * kPersistEpiWarps)
         : "memory");
     return r != 0;
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kPersistThreads, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap ta_hi,
                            const __grid_constant__ CUtensorMap ta_lo, const TcParams p, int ntn, int ntiles) {
     constexpr int NS = kPersistStages;
@@ -579,7 +583,7 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const unsigned tmem = tmem_slot;
     const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
-    if (warp == 4) {
+    if (warp == kPersistEpiWarps) {
         if (lane == 0) {
             int g = 0;  // stage counter across tiles
             for (int j = 0; j < my_tiles && !fail; j++) {
@@ -605,7 +609,7 @@ __global__ void __launch_bounds__(192, 1)
             for (int q = g > NS ? g - NS : 0; q < g; q++)
                 mbar_wait(smem_addr(&full[q % NS]), (unsigned)(q / NS) & 1u, p.err, nullptr, kSiteFull, q);
         }
-    } else if (warp == 5) {
+    } else if (warp == kPersistEpiWarps + 1) {
         if (lane == 0) {
             int g = 0;
             for (int j = 0; j < my_tiles && !fail; j++) {
@@ -640,32 +644,33 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
-        // epilogue warps 0-3
+        // epilogue warps
+        const int quarter = warp & 3;  // tensor-memory lanes 32 quarter .. + 31
         float* T = reinterpret_cast<float*>(smem_raw + (sbase - smem_addr(smem_raw)) + NS * kPersistStage) +
                    warp * 32 * 68;
         for (int j = 0; j < my_tiles; j++) {
             const int ab = j & 1;
             const bool ok = mbar_wait(smem_addr(&acc_full[ab]), (unsigned)(j >> 1) & 1u, p.err, nullptr, kSiteFull, j);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            // one verdict for the four epilogue warps (they meet at barrier 1 below)
+            // one verdict for the epilogue warps (they meet at barrier 1 below)
             if (!epilogue_all(ok && !fail)) break;
             const int tile = (int)blockIdx.x + j * (int)gridDim.x;
             const int n0 = (tile % ntn) * kWN, m0 = (tile / ntn) * kWM;
-            for (int cb = 0; cb < kWN; cb += 64) {
+            for (int cb = 64 * (warp >> 2); cb < kWN; cb += 64 * (kPersistEpiWarps / 4)) {
                 const int nb = n0 + cb;
-                if (nb >= p.N) break;  // uniform across the epilogue warps
+                if (nb >= p.N) break;  // uniform across the warp
                 float v[64];
-                tmem_ld64(tmem + ((unsigned)(32 * warp) << 16) + (unsigned)(ab * kWN + cb), v);
+                tmem_ld64(tmem + ((unsigned)(32 * quarter) << 16) + (unsigned)(ab * kWN + cb), v);
 #pragma unroll
                 for (int q = 0; q < 64; q += 4)
                     *reinterpret_cast<float4*>(T + lane * 68 + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
                 __syncwarp();
-                wide_store_rows(p, T, m0 + 32 * warp, min(32, p.M - (m0 + 32 * warp)), nb, lane);
+                wide_store_rows(p, T, m0 + 32 * quarter, min(32, p.M - (m0 + 32 * quarter)), nb, lane);
                 __syncwarp();
             }
             // this accumulator may take the tile after next
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * kPersistEpiWarps) : "memory");
             if (threadIdx.x == 0) mbar_arrive(smem_addr(&acc_empty[ab]), 1u);
         }
     }
@@ -849,7 +854,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
             const int ntn = (a.N + kWN - 1) / kWN, ntm = (a.M + kWM - 1) / kWM;
             const int ntiles = ntn * ntm;
             const int grid = ntiles < kTSMs ? ntiles : kTSMs;
-            tc_gemm_persist_kernel<<<grid, 192, kPersistSmem, s>>>(mwh, mah, mal, p, ntn, ntiles);
+            tc_gemm_persist_kernel<<<grid, kPersistThreads, kPersistSmem, s>>>(mwh, mah, mal, p, ntn, ntiles);
             VB_LAUNCH_CHECK("tc_gemm_persist_kernel");
             return VB_OK;
         }
