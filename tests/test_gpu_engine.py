@@ -7,7 +7,7 @@
   32-token-prompt + 128-greedy-token f32 run and a 512 + 64 INT8 run.
 - decode() (device-side greedy feedback, graph replay) == step() loop.
 - KV cache contents, weight_bytes, and the reference's error behaviour.
-Bars (north star): f32 logits max-abs <= 1e-3, INT8 logits <= 1e-2, greedy
+Bars: f32 logits max-abs <= 1e-3, INT8 logits <= 1e-2, greedy
 tokens identical.
 """
 import json
