@@ -368,7 +368,13 @@ __global__ void __launch_bounds__(256, 1)
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
+        // One barrier per key tile: it orders this tile's P writes before its P.V, every
+        // read of S before the next S product, the previous fold before this P.V, and the
+        // row-maximum exchange before the next one; and it carries the failure verdict.
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+        }
         if (t == 32) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (ok) {
@@ -402,14 +408,10 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int d = 0; d < 64; d++) o[d] = fmaf(o[d], alpha, pv[d]);
         }
-        if (!__syncthreads_and(ok)) {
-            ok = false;
-            break;
-        }
     }
-    // the row sum from its two halves (every thread has left the loop's last barrier)
+    // the row sum from its two halves (every thread has passed the last tile's barrier)
     xch[hf][r] = l;
-    __syncthreads();
+    ok = __syncthreads_and(ok);
     l = xch[0][r] + xch[1][r];
     if (t == 32 && s_issued > s_seen)  // a failed pass left the next S product in flight
         mbar_wait(smem_addr(&s_done), (unsigned)s_issued & 1u, p.err, nullptr, kSiteFull, s_issued);
