@@ -285,11 +285,11 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
 // ---------------------------------------------------------------------------
 // Wide tiles for many activation rows (a prompt chunk): one CTA computes
 // MB x 128 activation rows (the MMA's M, tensor-memory lanes; MB accumulators
-// of 256 columns) x 256 weight rows (the MMA's N) over all of K.  With MB = 2
-// (single bf16 weights) each SM takes in 96 KB per 64-wide K step for 4 M MACs
-// of products (weights shared by both row blocks); MB = 1 (and for a weight
-// pair) 64 / 96 KB for 2 M.  Same operands and accumulation as above; no
-// split-K.
+// of 256 columns) x 256 weight rows (the MMA's N) over all of K: 96 KB in per
+// 64-wide K step for a weight pair (MB = 1, 3 MMAs per product), 64 KB for
+// single bf16 weights.  Same operands and accumulation as above; no split-K.
+// The launcher runs it for weight pairs; single bf16 weights (the INT8 model)
+// take the persistent form further below.
 constexpr int kWM = 128;                 // activation rows per tile
 constexpr int kWN = 256;                 // weight rows per tile
 constexpr int kWA = kWM * kTK * 2;       // 16 KB per activation half
@@ -858,23 +858,16 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
             VB_LAUNCH_CHECK("tc_gemm_persist_kernel");
             return VB_OK;
         }
-        // two 128-row activation blocks share each weight tile (single bf16 weights, >= 256 rows)
-        const int mb = (wp == 1 && a.M >= 2 * kWM) ? 2 : 1;
-        static bool wide_attr[3] = {false, false, false};
-        const int ai = wp == 2 ? 2 : mb - 1;
-        if (!wide_attr[ai]) {
-            const cudaError_t ce =
-                wp == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)wide_smem(2, 1))
-                : mb == 2 ? cudaFuncSetAttribute(tc_gemm_wide_kernel<1, 2>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(1, 2))
-                          : cudaFuncSetAttribute(tc_gemm_wide_kernel<1, 1>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(1, 1));
+        // a weight pair (f32 weights as bf16 hi + lo): one CTA per tile
+        static bool wide_attr = false;
+        if (!wide_attr) {
+            const cudaError_t ce = cudaFuncSetAttribute(
+                tc_gemm_wide_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(2, 1));
             if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
-            wide_attr[ai] = true;
+            wide_attr = true;
         }
         if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
-        if ((st = make_map(&mwl, wp == 2 ? a.w_lo : a.w_hi, a.N, a.K, kWN))) return st;
+        if ((st = make_map(&mwl, a.w_lo, a.N, a.K, kWN))) return st;
         if ((st = make_map(&mah, a.a_hi, a.M, a.K, kWM))) return st;
         if ((st = make_map(&mal, a.a_lo, a.M, a.K, kWM))) return st;
         TcParams p{};
@@ -890,13 +883,8 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
         p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
         p.err = a.err;
-        const dim3 grid((a.N + kWN - 1) / kWN, (a.M + kWM * mb - 1) / (kWM * mb));
-        if (wp == 2)
-            tc_gemm_wide_kernel<2, 1><<<grid, kTThreads, wide_smem(2, 1), s>>>(mwh, mwl, mah, mal, p);
-        else if (mb == 2)
-            tc_gemm_wide_kernel<1, 2><<<grid, kTThreads, wide_smem(1, 2), s>>>(mwh, mwl, mah, mal, p);
-        else
-            tc_gemm_wide_kernel<1, 1><<<grid, kTThreads, wide_smem(1, 1), s>>>(mwh, mwl, mah, mal, p);
+        const dim3 grid((a.N + kWN - 1) / kWN, (a.M + kWM - 1) / kWM);
+        tc_gemm_wide_kernel<2, 1><<<grid, kTThreads, wide_smem(2, 1), s>>>(mwh, mwl, mah, mal, p);
         VB_LAUNCH_CHECK("tc_gemm_wide_kernel");
         return VB_OK;
     }
