@@ -528,12 +528,10 @@ vb_status launch_prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
     if (a.D != 128) return fail(VB_ERR_UNSUPPORTED, "prefill attention: head_dim must be 128");
     if (a.KVH <= 0 || a.H != 2 * a.KVH) return fail(VB_ERR_UNSUPPORTED, "prefill attention: needs H == 2 * KVH");
     if (a.B <= 0 || a.C <= 0 || a.p0 < 0 || a.B > 65535) return fail(VB_ERR_ARG, "prefill attention: bad shape");
-    static bool attr_done = false;
-    if (!attr_done) {
-        const cudaError_t ce =
-            cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
+    {
+        static std::atomic<unsigned long long> done{0};
+        const cudaError_t ce = smem_attr_once(prefill_attn_kernel, (int)kPSmem, done);
         if (ce != cudaSuccess) return cuda_fail(ce, "prefill attention: shared memory attribute");
-        attr_done = true;
     }
     const dim3 grid((a.C + kPQ - 1) / kPQ, a.KVH, a.B);
     prefill_attn_kernel<<<grid, kPThreads, kPSmem, s>>>(a);
@@ -594,12 +592,10 @@ vb_status launch_prompt_attention_tc(const PrefillAttnArgs& a, const float* q, v
         (st = tc_make_map(&mvh, vt_hi, B * KVH * 128, Ppad, 128)) ||
         (st = tc_make_map(&mvl, vt_lo, B * KVH * 128, Ppad, 128)))
         return st;
-    static bool attr_done = false;
-    if (!attr_done) {
-        const cudaError_t ce =
-            cudaFuncSetAttribute(tc_prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTASmem);
+    {
+        static std::atomic<unsigned long long> done{0};
+        const cudaError_t ce = smem_attr_once(tc_prefill_attn_kernel, (int)kTASmem, done);
         if (ce != cudaSuccess) return cuda_fail(ce, "prompt attention: shared memory attribute");
-        attr_done = true;
     }
     TcAttnParams p{};
     p.P = P;

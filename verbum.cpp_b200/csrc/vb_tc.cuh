@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "vb_pipe.cuh"
 
 namespace vb {
@@ -90,5 +92,20 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, float* v) {
 // 2-D bf16 tensor map over [rows][cols], boxes of 64 columns x box_rows rows,
 // 128-byte swizzle (vb_tcgemm.cu).
 vb_status tc_make_map(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) holds for the current
+// device only: set it once per device (bit d of `done`) before the kernel's
+// first launch there.
+template <typename Kernel>
+cudaError_t smem_attr_once(Kernel* kern, int bytes, std::atomic<unsigned long long>& done) {
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return ce;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (ce == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return ce;
+}
 
 }  // namespace vb

@@ -805,16 +805,12 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     const int splits = mtiles > 1 ? 1 : tc_gemm_splits(a.N, a.K, wp == 2);
     if ((splits > 1 || a.partials_only) && (size_t)splits * a.M * a.N > a.ws_floats)
         return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
-    static bool attr_done[2] = {false, false};
-    if (!attr_done[wp - 1]) {
-        cudaError_t ce = wp == 2 ? cudaFuncSetAttribute(tc_gemm_kernel<2, kPStages>,
-                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)tc_smem(2, kPStages))
-                                 : cudaFuncSetAttribute(tc_gemm_kernel<1, kQStages>,
-                                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        (int)tc_smem(1, kQStages));
+    {
+        static std::atomic<unsigned long long> done_pair{0}, done_single{0};
+        const cudaError_t ce = wp == 2 ? smem_attr_once(tc_gemm_kernel<2, kPStages>, (int)tc_smem(2, kPStages), done_pair)
+                                       : smem_attr_once(tc_gemm_kernel<1, kQStages>, (int)tc_smem(1, kQStages),
+                                                        done_single);
         if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
-        attr_done[wp - 1] = true;
     }
     CUtensorMap mwh, mwl, mah, mal;
     vb_status st;
@@ -827,14 +823,9 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         if (a.M / kWM + 1 > 65535) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M too large");
         if (wp == 1) {
             // single bf16 weights: the persistent form
-            static bool pattr = false;
-            if (!pattr) {
-                const cudaError_t ce = cudaFuncSetAttribute(tc_gemm_persist_kernel,
-                                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                            (int)kPersistSmem);
-                if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
-                pattr = true;
-            }
+            static std::atomic<unsigned long long> done_persist{0};
+            const cudaError_t ce = smem_attr_once(tc_gemm_persist_kernel, (int)kPersistSmem, done_persist);
+            if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
             if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
             if ((st = make_map(&mah, a.a_hi, a.M, a.K, kWM))) return st;
             if ((st = make_map(&mal, a.a_lo, a.M, a.K, kWM))) return st;
@@ -859,13 +850,9 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
             return VB_OK;
         }
         // a weight pair (f32 weights as bf16 hi + lo): one CTA per tile
-        static bool wide_attr = false;
-        if (!wide_attr) {
-            const cudaError_t ce = cudaFuncSetAttribute(
-                tc_gemm_wide_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem(2, 1));
-            if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
-            wide_attr = true;
-        }
+        static std::atomic<unsigned long long> done_wide{0};
+        const cudaError_t ce = smem_attr_once(tc_gemm_wide_kernel<2, 1>, (int)wide_smem(2, 1), done_wide);
+        if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
         if ((st = make_map(&mwh, a.w_hi, a.N, a.K, kWN))) return st;
         if ((st = make_map(&mwl, a.w_lo, a.N, a.K, kWN))) return st;
         if ((st = make_map(&mah, a.a_hi, a.M, a.K, kWM))) return st;
