@@ -252,38 +252,46 @@ def run_batched(args, grp, weights, cfg):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(list(range(grp.world)) if grp.world > 1 else [dev]).start() \
         if grp.rank == 0 else None
-    grp.barrier()
-    torch.cuda.synchronize()
     nx0, len0 = nx.copy(), bt.cache_len()
-    ev0.record(stream)
-    nx = bt.decode(nx, K)
-    ev1.record(stream)
-    ev1.synchronize()
-    torch.cuda.synchronize()
-    grp.barrier()
-    ms = ev0.elapsed_time(ev1)
+    # R repeats of the same K timed steps (the caches are rolled back to where
+    # the first repeat started, so every repeat decodes the same positions);
+    # the line reports the median repeat, max over ranks within each repeat
+    ms_reps = []
+    for _ in range(args.repeats):
+        bt.truncate(len0)
+        grp.barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        nx = bt.decode(nx0, K)
+        ev1.record(stream)
+        ev1.synchronize()
+        torch.cuda.synchronize()
+        grp.barrier()
+        ms_reps.append(grp.reduce_max(ev0.elapsed_time(ev1)))
     nx_dev = nx.copy()
     # end to end through the C ABI with host buffers (tokens in, next tokens
-    # out, one call per step) over the same K steps: the caches are rolled
-    # back to where the device-timed run started
-    bt.truncate(len0)
-    nx = nx0
-    grp.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(K):
-        _, nx = bt.step(nx, want_logits=False, want_next=True)
-    e2e_s = time.perf_counter() - t0
-    if not np.array_equal(nx, nx_dev):
-        raise SystemExit("batched decode: per-step API and device loop disagree")
+    # out, one call per step) over the same K steps at the same positions
+    e2e_reps = []
+    for _ in range(args.repeats):
+        bt.truncate(len0)
+        nx = nx0
+        grp.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            _, nx = bt.step(nx, want_logits=False, want_next=True)
+        e2e_reps.append(grp.reduce_max(time.perf_counter() - t0))
+        if not np.array_equal(nx, nx_dev):
+            raise SystemExit("batched decode: per-step API and device loop disagree")
     grp.barrier()
     clocks = clk.stop() if clk else None
-    ms_max = grp.reduce_max(ms)
-    e2e_max = grp.reduce_max(e2e_s)
+    ms = statistics.median(ms_reps)
+    e2e_s = statistics.median(e2e_reps)
     checksum = grp.gather_ints([int(x) for x in nx[:4]])
     n_mid = P + W + K // 2
     res = {
-        "ms": ms_max, "e2e_s": e2e_max, "prefill_s": grp.reduce_max(prefill_s),
+        "ms": ms, "e2e_s": e2e_s, "prefill_s": grp.reduce_max(prefill_s),
+        "ms_repeats": [round(x, 3) for x in ms_reps], "e2e_s_repeats": [round(x, 4) for x in e2e_reps],
         "graph_nodes": bt.graph_nodes(), "n_mid": n_mid, "clocks": clocks,
         "checksum": checksum, "weight_bytes": eng.weight_bytes(),
     }
@@ -422,44 +430,6 @@ def attn_microbench(dev=0, ns=(512, 2048, 8192, 32768), Bs=(1, 32), H=16, KVH=8,
     return out
 
 
-PHASES = ("qkv", "att", "o", "gu", "d")
-
-
-def trace_breakdown(tr, layers=28, stride=1024, words=6):
-    """Timeline of one fused step from per-CTA %globaltimer words (6 per phase
-    b: activation loaded, first stage observed, arrival at / release from grid
-    barrier b, first / last stage issued by the producer).  Per phase type,
-    medians over layers and CTAs, in us, relative to the previous release:
-      loaded, first, arrive, release   (consumer)
-      issue0, issueN                   (producer: first / last stage issued)
-    plus spread = last - first arrival."""
-    import numpy as np
-    G = len(tr) // stride
-    if G == 0:
-        return None
-    t = np.asarray(tr, dtype=np.int64).reshape(G, stride).astype(np.float64)
-    nb = 5 * layers
-    w = t[:, 1:1 + words * nb].reshape(G, nb, words)
-    if t[0, 0] == 0 or (w[:, :, 3] == 0).any():
-        return None
-    rel = w[..., 3]
-    prev = np.concatenate([np.full((G, 1), t[:, 0].max()), rel[:, :-1]], axis=1)
-    prev = np.median(prev, axis=0, keepdims=True)
-    out = {}
-    med = lambda x: round(float(np.median(x)) / 1e3, 2)
-    for k, ph in enumerate(PHASES):
-        i = np.arange(k, nb, 5)
-        d = {}
-        for j, name in enumerate(("loaded", "first", "arrive", "release", "issue0", "issueN")):
-            x = w[:, i, j]
-            d[name] = med(np.where(x > 0, x - prev[:, i], np.nan)[~np.isnan(np.where(x > 0, x, np.nan))]) \
-                if (x > 0).any() else None
-        d["spread"] = med(w[:, i, 2].max(0) - w[:, i, 2].min(0))
-        out[ph] = d
-    out["total_us"] = round(float(rel[:, -1].max() - t[:, 0].min()) / 1e3, 1)
-    return out
-
-
 STEPS2 = ("A.poll", "A.norm", "A.qkv", "A.gather", "A.attn", "A.merge", "A.oproj",
           "B.poll", "B.norm", "B.gateup", "B.down", "B.reduce")
 
@@ -505,7 +475,7 @@ def trace_breakdown2(tr, layers=28, stride=2048):
     return out
 
 
-def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=False, lm8=False):
+def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=-1, trace=False, lm8=False):
     import numpy as np
     import torch
 
@@ -567,8 +537,9 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
         V, H = cfg["vocab_size"], cfg["hidden_size"]
         wb = wb - 4 * V * H + V * H + 4 * V
     nodes = e.graph_nodes()
+    engine_path = e.path()
     tb = None
-    if trace and path in (0, 2):
+    if trace and e.path() == 2:
         e.set_trace(True)
         e.reset_cache(max_seq)
         e.prefill(prompt)
@@ -577,7 +548,7 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
         if os.environ.get("VB_TRACE_DUMP"):
             import numpy as np
             np.save(os.environ["VB_TRACE_DUMP"] + f"_{mode}.npy", raw)
-        tb = (trace_breakdown if path == 0 else trace_breakdown2)(raw, cfg["num_hidden_layers"])
+        tb = trace_breakdown2(raw, cfg["num_hidden_layers"])
     e.close()
     mean_ctx = prompt_len + (n_new - 1) / 2.0
     bytes_tok = wb + step_kv_bytes(mean_ctx)
@@ -587,7 +558,8 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
             "e2e_p50_ms": 1e3 * lat[len(lat) // 2], "e2e_p99_ms": 1e3 * lat[min(len(lat) - 1, int(0.99 * len(lat)))],
             "sampled_tok_s": round(n_new / sec_sampled, 2),
             "graph_nodes": nodes, "weight_bytes": wb, "prompt": prompt_len, "decode_tokens": n_new,
-            "path": "fused persistent step" if nodes == 1 else "per-op CUDA graph",
+            "engine_path": engine_path,
+            "path": "clustered persistent step" if nodes == 1 else "per-op CUDA graph",
             "first_tokens": [int(t) for t in toks[:4]], **({"trace": tb} if tb else {})}
 
 
@@ -595,10 +567,26 @@ def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=0, trace=
 # main
 # ---------------------------------------------------------------------------
 
+def workload_config(args, n_gpus):
+    """The `config` object of the JSON line (identical for both arms)."""
+    B, K = args.batch, args.steps
+    return {
+        "workload": f"batched-int8: {B} independent sequences per GPU, {args.prompt}-token "
+                    f"prompts, greedy decode steps {args.warmup}+{K} (warm-up+timed)",
+        "model": "Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8 heads, D 128, "
+                 "ffn 3072, vocab 151936, tied)",
+        "global_batch": B * n_gpus, "seq_len": args.prompt + args.warmup + K,
+        "parallelism": f"replicas x{n_gpus}: sequences sharded, weights replicated, no collective",
+        "l2": "inputs larger than L2 (>=1.06 GB of weights and ~32 GB of KV per step)",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=252)
+    ap.add_argument("--steps", type=int, default=120)
+    ap.add_argument("--repeats", type=int, default=3,
+                    help="timed repeats of the K steps (median reported)")
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["batched-int8"], default="batched-int8")
@@ -608,8 +596,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--only", choices=["gemv", "attn", "bs1", "prefill"], help="one workload (for profiling)")
     ap.add_argument("--mode", choices=["f32", "int8"], default="int8", help="--only bs1: weights")
-    ap.add_argument("--path", type=int, default=0, help="--only bs1: 0 fused step, 1 per-op graph")
-    ap.add_argument("--trace", action="store_true", help="--only bs1: per-phase trace of the fused step")
+    ap.add_argument("--path", type=int, default=-1,
+                    help="--only bs1: 1 per-op graph, 2 clustered step, -1 the engine's automatic choice")
+    ap.add_argument("--trace", action="store_true",
+                    help="--only bs1: per-phase trace of the clustered step (needs a VB_STEP_TRACE=1 build)")
     ap.add_argument("--ctx", type=int, default=2048, help="--only attn: context length")
     ap.add_argument("--shape", default=None, help="--only gemv: one of q,k,v,o,gate,up,down,lm_head")
     args = ap.parse_args()
@@ -672,17 +662,9 @@ def main():
         "dtype": "f32",
         "weights": "int8 (per-row absmax) projections, f32 embedding/lm_head",
         "data": "synthetic: seeded N(0,0.02) random-init weights, uniform random prompt ids",
-        "config": {
-            "workload": f"batched-int8: {B} independent sequences per GPU, {args.prompt}-token "
-                        f"prompts, greedy decode steps {args.warmup}+{K} (warm-up+timed)",
-            "model": "Qwen3-0.6B architecture (28 layers, hidden 1024, 16/8 heads, D 128, "
-                     "ffn 3072, vocab 151936, tied)",
-            "global_batch": B * N, "seq_len": args.prompt + args.warmup + K,
-            "parallelism": f"replicas x{N}: sequences sharded, weights replicated, no collective",
-            "l2": "inputs larger than L2 (>=1.06 GB of weights and ~32 GB of KV per step)",
-            "step_roofline_frac": round(step_bytes / (sec / K) / 1e9 / peak, 4),
-            "step_bytes": step_bytes,
-        },
+        "config": workload_config(args, N),
+        "step_roofline_frac": round(step_bytes / (sec / K) / 1e9 / peak, 4),
+        "step_bytes": step_bytes,
         "roofline": {
             "bound": "hbm", "kernel": attn["kernel"],
             "achieved": round(a_gbs, 1), "peak": peak, "unit": "GB/s",
@@ -696,17 +678,23 @@ def main():
                 "h2d_bytes_per_step": 4 * B * N, "d2h_bytes_per_step": 4 * B * N,
                 "api": "vb_batch_step (host token ids in, host greedy ids out, per step)"},
         "gpu_launches": res["graph_nodes"] * K,
+        "repeats": {"n": args.repeats, "reported": "median",
+                    "ms_per_step": [round(x / K, 4) for x in res["ms_repeats"]],
+                    "e2e_tok_s": [round(N * B * K / x, 1) for x in res["e2e_s_repeats"]]},
         "prefill_s": round(res["prefill_s"], 3),
         "prefill_tok_s": round(N * B * args.prompt / res["prefill_s"], 1),
     }
     if grp.rank == 0 and N == 1 and not args.no_extras:
-        names = {0: "fused step, grid barriers", 1: "per-op CUDA graph", 2: "clustered step, tagged exchange"}
+        names = {1: "per-op CUDA graph", 2: "clustered step, tagged exchange"}
         for mode, P, G in (("f32", 32, 128), ("int8", 512, 512)):
-            # every step path on the same inputs; the line reports the fastest
-            runs = {pth: run_bs1(mode, P, G, weights, cfg, dev=local_rank, path=pth) for pth in (0, 1, 2)}
-            best = max(runs, key=lambda k: runs[k]["tok_s"])
-            r = dict(runs[best])
-            r["path"] = names[best]
+            # the engine's automatic path (what a Model::step caller gets) is the
+            # reported line; the other path is timed on the same inputs beside it
+            r_auto = run_bs1(mode, P, G, weights, cfg, dev=local_rank, path=-1)
+            auto = r_auto["engine_path"]
+            other = 1 if auto == 2 else 2
+            runs = {auto: r_auto, other: run_bs1(mode, P, G, weights, cfg, dev=local_rank, path=other)}
+            r = dict(runs[auto])
+            r["path"] = names[auto] + " (automatic)"
             r["roofline_frac"] = round(r["achieved_gbs"] / peak, 4)
             r["paths_tok_s"] = {names[k]: round(v["tok_s"], 2) for k, v in runs.items()}
             line[f"bs1_{mode}"] = r
@@ -751,8 +739,20 @@ def cpu_baseline(cfg, weights, args):
     return out
 
 
+def reference_weights(cfg):
+    """The benchmark's weights drawn by the oracle's copy of the generator: the
+    reference arm never loads the engine library."""
+    import oracle
+    import vbsynth
+    return vbsynth.make_weights(cfg, seed=WEIGHT_SEED, normal=oracle.synth_normal)
+
+
 def main_reference(args, rank, world):
-    """Reference arm: the reference's own CPU decode (oracle/_ref), same workload."""
+    """Reference arm: the reference's own CPU decode (oracle/_ref, Model::step
+    compiled from its sources) on this host's cores, same metric and workload
+    config as the engine's line.  One step = one decode token of each of P
+    single-threaded reference processes (the engine has no batching), each at
+    the workload's context length; K timed steps after W warm-up steps."""
     if rank != 0:
         return 0
     import oracle
@@ -761,27 +761,23 @@ def main_reference(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libverbum_ref.so not built"}))
         return 0
     cfg = vbsynth.qwen3_config()
-    weights = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+    weights = reference_weights(cfg)
     procs = ref_procs()
-    # each "step" is one decode token for each of `procs` sequences; bounded so
-    # the whole run stays within a few minutes (~1.3 s per step at context 2048)
-    steps = max(1, min(args.steps, 6))
-    warm = 1 if args.warmup > 0 else 0
+    K, W = args.steps, args.warmup
     with tempfile.TemporaryDirectory() as td:
         mdir = write_model(td, cfg, weights)
         del weights
-        rate, secs = ref_time(mdir, "int8", args.prompt, warm, steps, procs)
-    sample = (f"reference Model::step (oracle/_ref, compiled from the reference sources), INT8, "
-              f"context {args.prompt}, {procs} single-threaded processes x {steps} timed steps "
-              f"(+{warm} warm-up); one sequence per process")
+        rate, secs = ref_time(mdir, "int8", args.prompt, W, K, procs)
+    sample = (f"reference Model::step (oracle/_ref, compiled from the reference sources), INT8 "
+              f"projections + f32 lm_head, context {args.prompt}: {procs} single-threaded "
+              f"processes, one sequence each; a step is one decode token of every process")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(rate, 4), "unit": "tok/s",
-        "n_gpus": world, "steps": steps, "warmup": warm,
+        "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(1e3 * statistics.mean(secs), 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded N(0,0.02) random-init weights",
-        "config": {"workload": f"batched-int8 decode at context {args.prompt} (CPU sample)",
-                   "model": "Qwen3-0.6B architecture", "parallelism": f"{procs} CPU processes"},
+        "data": "synthetic: seeded N(0,0.02) random-init weights, uniform random prompt ids",
+        "config": workload_config(args, world),
         "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": procs,
                          "kind": "reference", "sample": sample, "cpu": cpu_model()},
         "e2e": {"value": round(rate, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,

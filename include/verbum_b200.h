@@ -141,11 +141,14 @@ VB_API vb_status vb_attn_decode(const float* q, const float* kcache, const float
  * budgeted pool, a plugin whose enqueue path may not allocate, a serving loop
  * that cannot afford cudaMalloc's implicit synchronisation).  No counterpart
  * in the reference.  The split partials live in a 1 MiB array compiled into
- * the library (held by every GPU that loads it until the process exits);
- * shapes needing more (H * splits * 130 floats + 256 B; Qwen3-0.6B's 16/8
- * heads need at most 616 KB) return VB_ERR_UNSUPPORTED.  The first call on a
- * device looks up the array's device address, so make that call before any
- * stream capture.  All calls share the array: calls that overlap on the GPU
+ * the library (held by every GPU that loads it until the process exits).  The
+ * split count is capped at what that array holds (H * splits * 130 floats,
+ * plus 512 B: 125 splits for 16 heads), so every context length runs, with
+ * longer splits past about 32k positions; only a head count too large for one
+ * split (H > 2015) returns VB_ERR_UNSUPPORTED.  The first call on a device (and
+ * the first after the device's context was replaced, e.g. by cudaDeviceReset)
+ * looks up the array's device address, so make that call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU
  * (different streams, or devices sharing nothing but this array's name) race
  * and must be serialised by the caller.  Nothing in it needs clearing between
  * calls.  Calls no cudaMalloc, cudaFree or allocating routine. */
@@ -283,21 +286,24 @@ VB_API int vb_engine_graph_nodes(const vb_engine* e);
 /* Copies layer `layer`'s K (which=0) or V cache rows [0, len) into host
  * memory as [len, KVH*D] (the reference KVCache layout). */
 VB_API vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host);
-/* Selects the bs1 step implementation: 0 = persistent fused kernel with five
- * grid barriers per layer, 1 = one kernel per op in a CUDA graph, 2 =
- * persistent kernel on KV-head thread-block clusters exchanging tagged data
- * words (no barriers), -1 = automatic (default: 2 for INT8 weights, 0 for
- * f32, the faster of each on B200).  A fused path whose shape requirements
- * are not met falls back to 1. */
+/* Selects the bs1 step implementation: 1 = one kernel per op in a CUDA graph,
+ * 2 = persistent kernel on KV-head thread-block clusters exchanging tagged
+ * data words (no barriers), -1 = automatic (the default: the faster of the two
+ * for the weight format as measured on B200 -- 2 for INT8 weights, 1 for f32).
+ * Path 2 needs hidden 1024, GQA group 2 and head_dim 128; where those are not
+ * met the step falls back to 1. */
 VB_API vb_status vb_engine_set_path(vb_engine* e, int path);
+/* The path the next step runs (1 or 2; the automatic choice if not fixed). */
+VB_API int vb_engine_path(const vb_engine* e);
 /* The stream the engine runs on (a cudaStream_t). */
 VB_API void* vb_engine_stream(vb_engine* e);
-/* Phase tracing of the fused step (no reference counterpart; the reference
- * times whole steps with steady_clock, tools/bench.cpp:63-69): when on, each
- * CTA c of the next fused steps records %globaltimer nanoseconds in words
- * [c*512, c*512+512): word 0 = start, 2b-1 / 2b = arrival at / release from
- * grid barrier b (b = 1..5*layers).  read_trace copies up to cap words of the
- * last step and returns how many it copied (grid * 512 at most). */
+/* Phase tracing of the clustered step (path 2; no reference counterpart, the
+ * reference times whole steps with steady_clock, tools/bench.cpp:63-69): when
+ * on, each CTA c of the next steps records %globaltimer nanoseconds in words
+ * [c*2048, c*2048+2048): word 0 = start, then 12 stamps per layer (phase ends)
+ * and from word 400 a 40-word clock64 profile per layer.  Only libraries built
+ * with VB_STEP_TRACE=1 record anything; others return 0 words.  read_trace
+ * copies up to cap words of the last step and returns how many it copied. */
 VB_API vb_status vb_engine_set_trace(vb_engine* e, int on);
 VB_API int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap);
 

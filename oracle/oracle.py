@@ -66,6 +66,7 @@ def olib():
             "or_attention_decode": (None, [_P, _P, _P, _L, _I, _I, _I, _I, _P]),
             "or_silu_mul": (None, [_P, _P, _L]),
             "or_argmax": (_I, [_P, _L]),
+            "or_synth_normal": (None, [_P, C.c_uint64, C.c_uint64, _F]),
             "or_sample_seq": (_I, [_F, _I, _F, C.c_uint64, _P, _L, _I, _P]),
             "or_last_error": (C.c_char_p, []),
             "or_model_create": (_P, [C.POINTER(OrConfig), _P, _P, C.POINTER(OrLayer)]),
@@ -77,6 +78,7 @@ def olib():
                                            C.POINTER(C.c_void_p), C.POINTER(_L), C.POINTER(_L)]),
             "or_model_reset_cache": (_I, [_P, _I]),
             "or_model_step": (_I, [_P, _I, _P]),
+            "or_model_prefill": (_I, [_P, _P, _I, _P]),
             "or_model_cache_len": (_I, [_P]),
             "or_model_weight_bytes": (_Z, [_P]),
             "or_model_kv": (_P, [_P, _I, _I]),
@@ -210,6 +212,14 @@ def argmax(logits):
     return int(olib().or_argmax(_p(logits), logits.size))
 
 
+def synth_normal(n: int, seed: int, std: float = 0.02) -> np.ndarray:
+    """The seeded N(0, std) weight generator (same values as the engine
+    library's vb_synth_normal), so CPU-only callers need not load it."""
+    out = np.empty(int(n), dtype=np.float32)
+    olib().or_synth_normal(_p(out), int(n), int(seed) & (2**64 - 1), float(std))
+    return out
+
+
 def sample_seq(logits, temperature, top_k, top_p, seed):
     """generate.cpp:197-252: one Sampler over the rows of logits [n, vocab]."""
     logits = f32(logits)
@@ -287,6 +297,17 @@ class OracleModel:
     def step(self, token):
         out = np.empty(self.c.vocab, np.float32)
         rc = olib().or_model_step(self.h, int(token), _p(out))
+        if rc:
+            raise RuntimeError(olib().or_last_error().decode())
+        return out
+
+    def prefill(self, tokens):
+        """Feeds the tokens from the current position (layer by layer over
+        all of them; bit-identical to one step() per token) and returns the
+        last position's logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(self.c.vocab, np.float32)
+        rc = olib().or_model_prefill(self.h, _p(t), int(t.size), _p(out))
         if rc:
             raise RuntimeError(olib().or_last_error().decode())
         return out

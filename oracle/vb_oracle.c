@@ -570,6 +570,247 @@ int or_model_step(or_model* m, int token, float* logits) {
     return 0;
 }
 
+/* ---- prefill: many positions, layer by layer -----------------------------
+ * The reference feeds a prompt one position at a time through Model::step
+ * (tools/generate.cpp:75-77).  Position p's layer-l values depend only on its
+ * own layer-l input and on the K/V rows of positions <= p, so running every
+ * position through layer l before layer l+1 computes the very same numbers --
+ * each dot product, norm and softmax below is the per-position operation of
+ * or_model_step in the same order -- while every weight row is read once per
+ * block of positions instead of once per position.  or_model_prefill is
+ * therefore bit-identical to n calls of or_model_step (tested), only faster. */
+
+/* Y[p][j] = sum_k X[p][k] * W[j][k] (sequential in k, as ops.cpp:42-70) for a
+ * block of positions at a time: the block's accumulators are independent, so
+ * they vectorise without reordering any one sum. */
+#define OR_PB 32   /* positions per block (independent accumulators) */
+/* 4 independent float lanes; each lane's product and sum round exactly as the
+ * scalar statement acc += x * w (no contraction: -ffp-contract=off) */
+typedef float or_v4 __attribute__((vector_size(16)));
+#define OR_RB 128  /* weight rows per block */
+
+/* Tasks are (row block, position block) pairs; a thread takes consecutive
+ * position blocks of one row block, so the row block stays in its cache
+ * while the transposed activations stream past. */
+#define OR_ROWS_BODY(WTYPE, CONV, FINISH)                                                        \
+    const int64_t nrb = (N + OR_RB - 1) / OR_RB, npb = (P + OR_PB - 1) / OR_PB;                 \
+    /* XT[pb][k][u] = X[pb * OR_PB + u][k]: one position block is contiguous */                 \
+    _Pragma("omp parallel for schedule(static)")                                                 \
+    for (int64_t pb = 0; pb < npb; pb++)                                                        \
+        for (int64_t k = 0; k < K; k++)                                                         \
+            for (int u = 0; u < OR_PB; u++) {                                                   \
+                const int64_t p = pb * OR_PB + u;                                               \
+                XT[(pb * K + k) * OR_PB + u] = p < P ? X[p * K + k] : 0.0f;                     \
+            }                                                                                   \
+    _Pragma("omp parallel for collapse(2) schedule(static)")                                     \
+    for (int64_t rb = 0; rb < nrb; rb++)                                                        \
+        for (int64_t pb = 0; pb < npb; pb++) {                                                  \
+            const int64_t p0 = pb * OR_PB, nb = (P - p0 < OR_PB) ? P - p0 : OR_PB;              \
+            const int64_t j1 = (rb + 1) * OR_RB < N ? (rb + 1) * OR_RB : N;                     \
+            for (int64_t j = rb * OR_RB; j < j1; j++) {                                         \
+                const WTYPE* w = W + j * K;                                                     \
+                float acc[OR_PB] = {0};                                                         \
+                if (nb == OR_PB) {                                                              \
+                    or_v4 a[8];                                                                 \
+                    for (int i = 0; i < 8; i++) a[i] = (or_v4){0.0f, 0.0f, 0.0f, 0.0f};         \
+                    const float* xt = XT + pb * K * OR_PB;                                      \
+                    for (int64_t k = 0; k < K; k++, xt += OR_PB) {                              \
+                        const float wk = CONV(w[k]);                                            \
+                        const or_v4 wv = {wk, wk, wk, wk};                                      \
+                        for (int i = 0; i < 8; i++) {                                           \
+                            or_v4 xv;                                                           \
+                            memcpy(&xv, xt + 4 * i, 16);                                        \
+                            a[i] += xv * wv;                                                    \
+                        }                                                                       \
+                    }                                                                           \
+                    memcpy(acc, a, sizeof a);                                                   \
+                } else {                                                                        \
+                    for (int64_t k = 0; k < K; k++) {                                           \
+                        const float wk = CONV(w[k]);                                            \
+                        const float* xt = XT + (pb * K + k) * OR_PB;                            \
+                        for (int64_t u = 0; u < nb; u++) acc[u] += xt[u] * wk;                  \
+                    }                                                                           \
+                }                                                                               \
+                for (int64_t u = 0; u < nb; u++) Y[(p0 + u) * N + j] = FINISH(acc[u]);          \
+            }                                                                                   \
+        }
+
+#define OR_ID(v) (v)
+#define OR_I2F(v) ((float)(v))
+
+/* Y[p][j] = sum_k X[p][k] * W[j][k], sequential in k as ops.cpp:42-70; the
+ * OR_PB accumulators of a block are independent, so they vectorise without
+ * reordering any one sum. */
+static void rows_matmul_nt(const float* X, int64_t P, const float* W, int64_t N, int64_t K, float* Y,
+                           float* XT) {
+    OR_ROWS_BODY(float, OR_ID, OR_ID)
+}
+
+/* The INT8 twin (quant.cpp:43-70): acc += x[k] * float(q[j][k]), then
+ * acc * scale[j]. */
+static void rows_matmul_nt_q8(const float* X, int64_t P, const int8_t* W, const float* scales, int64_t N,
+                              int64_t K, float* Y, float* XT) {
+#define OR_SCALE(a) ((a) * scales[j])
+    OR_ROWS_BODY(int8_t, OR_I2F, OR_SCALE)
+#undef OR_SCALE
+}
+
+static void rows_proj(const or_model* m, int l, int which, const float* X, int64_t P, float* Y, float* XT) {
+    int64_t rows, cols;
+    proj_shape(&m->c, which, &rows, &cols);
+    if (m->quantized) {
+        const qt* t = &m->Q[l * 7 + which];
+        rows_matmul_nt_q8(X, P, t->q, t->s, rows, cols, Y, XT);
+    } else {
+        rows_matmul_nt(X, P, proj_ptr(&m->L[l], which), rows, cols, Y, XT);
+    }
+}
+
+/* One head of or_attention_decode (generate.cpp:73-105) for one query, with
+ * the keys of its KV head transposed (KT[d][j], row length ldk) so four
+ * positions' dot products run in four vector lanes, each lane summing over d
+ * in order; the P.V sum runs four dims per lane, each over j in order. */
+static void attention_head(const float* qh, const float* KT, int64_t ldk, const float* vcache,
+                           int64_t row_stride, int kvh, int D, int n, float* scores, float* c) {
+    const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+    float m = -INFINITY;
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+        or_v4 dot = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int d = 0; d < D; d++) {
+            or_v4 kv;
+            memcpy(&kv, KT + (size_t)d * ldk + j, 16);
+            const or_v4 qv = {qh[d], qh[d], qh[d], qh[d]};
+            dot += qv * kv;
+        }
+        for (int u = 0; u < 4; u++) {
+            scores[j + u] = dot[u] * inv_sqrt_d;
+            m = (m < scores[j + u]) ? scores[j + u] : m;
+        }
+    }
+    for (; j < n; j++) {
+        float dot = 0.0f;
+        for (int d = 0; d < D; d++) dot += qh[d] * KT[(size_t)d * ldk + j];
+        scores[j] = dot * inv_sqrt_d;
+        m = (m < scores[j]) ? scores[j] : m;
+    }
+    double sum = 0.0;
+    for (j = 0; j < n; j++) {
+        scores[j] = expf(scores[j] - m);
+        sum += scores[j];
+    }
+    const float inv = (float)(1.0 / sum);
+    or_v4 acc[32];
+    for (int i = 0; i < D / 4; i++) acc[i] = (or_v4){0.0f, 0.0f, 0.0f, 0.0f};
+    for (j = 0; j < n; j++) {
+        const float pj = scores[j] * inv;
+        const or_v4 pv = {pj, pj, pj, pj};
+        const float* vj = vcache + (size_t)j * row_stride + (size_t)kvh * D;
+        for (int i = 0; i < D / 4; i++) {
+            or_v4 vv;
+            memcpy(&vv, vj + 4 * i, 16);
+            acc[i] += pv * vv;
+        }
+    }
+    memcpy(c, acc, sizeof(float) * (size_t)D);
+}
+
+int or_model_prefill(or_model* m, const int* tokens, int n, float* logits) {
+    const or_config* c = &m->c;
+    if (!m->kc) { set_err("call reset_cache() first"); return OR_ERR_NO_CACHE; }
+    if (n <= 0) return 0;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= c->vocab) {
+            set_err("token id out of range for the embedding table");
+            return OR_ERR_TOKEN;
+        }
+    if (m->len + n > m->max_seq) { set_err("kv cache is full"); return OR_ERR_CACHE_FULL; }
+    if (m->len + n > c->rope_positions) {
+        set_err("position is outside the rope table");
+        return OR_ERR_ROPE;
+    }
+    const int64_t P = n, hd = c->hidden, H = c->heads, KVH = c->kv_heads, D = c->head_dim;
+    const int64_t qd = H * D, kd = KVH * D, fd = c->ffn;
+    const int64_t widest = (fd > qd ? fd : qd) > hd ? (fd > qd ? fd : qd) : hd;
+    float* X = (float*)malloc(sizeof(float) * P * hd);
+    float* X2 = (float*)malloc(sizeof(float) * P * hd);
+    float* NR = (float*)malloc(sizeof(float) * P * hd);
+    float* T = (float*)malloc(sizeof(float) * P * hd);
+    float* Qb = (float*)malloc(sizeof(float) * P * qd);
+    float* Kb = (float*)malloc(sizeof(float) * P * kd);
+    float* Vb = (float*)malloc(sizeof(float) * P * kd);
+    float* CX = (float*)malloc(sizeof(float) * P * qd);
+    float* G = (float*)malloc(sizeof(float) * P * fd);
+    float* U = (float*)malloc(sizeof(float) * P * fd);
+    float* XT = (float*)malloc(sizeof(float) * (P + OR_PB) * widest);
+    float* KTa = (float*)malloc(sizeof(float) * (size_t)(m->len + P) * kd);
+    int rc = 0;
+    if (!X || !X2 || !NR || !T || !Qb || !Kb || !Vb || !CX || !G || !U || !XT || !KTa) {
+        set_err("out of memory");
+        rc = OR_ERR_OOM;
+        goto done;
+    }
+    const int p0 = m->len;
+    for (int64_t p = 0; p < P; p++) memcpy(X + p * hd, m->embed + (size_t)tokens[p] * hd, (size_t)hd * 4);
+    for (int l = 0; l < c->layers; l++) {
+        const or_layer_weights* L = &m->L[l];
+        or_rmsnorm(X, L->input_norm, c->eps, NR, P, hd);
+        rows_proj(m, l, 0, NR, P, Qb, XT);
+        rows_proj(m, l, 1, NR, P, Kb, XT);
+        rows_proj(m, l, 2, NR, P, Vb, XT);
+        for (int64_t p = 0; p < P; p++) {
+            float* q = Qb + p * qd;
+            float* k = Kb + p * kd;
+            or_rmsnorm(q, L->q_norm, c->eps, q, H, D);
+            or_apply_rope(q, H, (int)D, p0 + (int)p, c->rope_positions, m->rope_cos, m->rope_sin);
+            or_rmsnorm(k, L->k_norm, c->eps, k, KVH, D);
+            or_apply_rope(k, KVH, (int)D, p0 + (int)p, c->rope_positions, m->rope_cos, m->rope_sin);
+            memcpy(m->kc[l] + (size_t)(p0 + p) * kd, k, (size_t)kd * 4);
+            memcpy(m->vc[l] + (size_t)(p0 + p) * kd, Vb + p * kd, (size_t)kd * 4);
+        }
+        const int group = (int)(H / KVH);
+        const int64_t nk = p0 + P;
+        /* keys transposed per KV head: KTa[kvh][d][j] */
+#pragma omp parallel for schedule(static)
+        for (int64_t hk = 0; hk < KVH; hk++)
+            for (int64_t j = 0; j < nk; j++)
+                for (int64_t d = 0; d < D; d++)
+                    KTa[(hk * D + d) * nk + j] = m->kc[l][(size_t)j * kd + hk * D + d];
+#pragma omp parallel
+        {
+            float* scores = (float*)malloc(sizeof(float) * (size_t)nk);
+#pragma omp for schedule(dynamic, 1)
+            for (int64_t t = P * H - 1; t >= 0; t--) { /* longest rows first */
+                const int64_t p = t / H, h = t % H, hk = h / group;
+                attention_head(Qb + p * qd + h * D, KTa + hk * D * nk, nk, m->vc[l], kd, (int)hk, (int)D,
+                               p0 + (int)p + 1, scores, CX + p * qd + h * D);
+            }
+            free(scores);
+        }
+        rows_proj(m, l, 3, CX, P, T, XT);
+        for (int64_t i = 0; i < P * hd; i++) X2[i] = X[i] + T[i];
+        or_rmsnorm(X2, L->post_norm, c->eps, NR, P, hd);
+        rows_proj(m, l, 4, NR, P, G, XT);
+        rows_proj(m, l, 5, NR, P, U, XT);
+        for (int64_t p = 0; p < P; p++) or_silu_mul(G + p * fd, U + p * fd, fd);
+        rows_proj(m, l, 6, G, P, T, XT);
+        for (int64_t i = 0; i < P * hd; i++) X[i] = X2[i] + T[i];
+    }
+    m->len += n;
+    memcpy(m->x, X + (P - 1) * hd, (size_t)hd * 4);
+    if (logits) {
+        or_rmsnorm(m->x, m->final_norm, c->eps, m->normed, 1, hd);
+        if (m->lm_q)
+            or_matmul_nt_q8(m->normed, m->lm_q, m->lm_s, logits, 1, c->vocab, hd);
+        else
+            or_matmul_nt(m->normed, m->embed, logits, 1, c->vocab, hd);
+    }
+done:
+    free(X); free(X2); free(NR); free(T); free(Qb); free(Kb); free(Vb); free(CX); free(G); free(U); free(XT);
+    free(KTa);
+    return rc;
+}
+
 /* Opt-in (no reference counterpart: the reference keeps the tied lm_head in
  * f32, model.cpp:313-338): the lm_head product with the embedding rows
  * quantised by quantize_rows and multiplied as matmul_nt_q8. */
@@ -596,4 +837,34 @@ size_t or_model_weight_bytes(const or_model* m) {
         }
     }
     return total;
+}
+
+/* ---- synthetic weights ---------------------------------------------------
+ * The seeded N(0, std) generator every benchmark and test model is drawn from,
+ * restated here so the reference arm of the benchmark can produce the same
+ * weights without loading the engine library: element pair p takes the
+ * SplitMix64 finaliser (Steele, Lea & Flood, OOPSLA 2014) of
+ * seed + (p + 1) * golden-gamma as two 24-bit uniforms in (0, 1), turned into
+ * two normals by the Box-Muller transform in double.  Pairs are independent,
+ * so the result does not depend on the thread count. */
+static uint64_t or_mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void or_synth_normal(float* out, uint64_t n, uint64_t seed, float stdv) {
+    const double two_pi = 6.283185307179586476925286766559;
+    const int64_t pairs = (int64_t)((n + 1) / 2);
+#pragma omp parallel for schedule(static) if (pairs > (1 << 16))
+    for (int64_t p = 0; p < pairs; p++) {
+        const uint64_t z = or_mix64(seed + ((uint64_t)p + 1) * 0x9E3779B97F4A7C15ull);
+        const double u1 = ((double)(z >> 40) + 0.5) * (1.0 / 16777216.0);
+        const double u2 = ((double)(z & 0xFFFFFFull) + 0.5) * (1.0 / 16777216.0);
+        const double r = sqrt(-2.0 * log(u1));
+        const double a = two_pi * u2;
+        const uint64_t i = 2 * (uint64_t)p;
+        out[i] = (float)(r * cos(a) * stdv);
+        if (i + 1 < n) out[i + 1] = (float)(r * sin(a) * stdv);
+    }
 }

@@ -76,6 +76,10 @@ void or_silu_mul(float* gate, const float* up, int64_t n);
 /* generate.cpp:199-206  greedy pick: strict '>' scan from index 0. */
 int or_argmax(const float* logits, int64_t vocab);
 
+/* Seeded N(0, std) fill (the synthetic-weight generator; identical output for
+ * a given (seed, n) whatever the thread count). */
+void or_synth_normal(float* out, uint64_t n, uint64_t seed, float stdv);
+
 /* generate.cpp:197-252  Sampler(cfg).sample() called n times with one
  * generator: row i of logits [n][vocab] gives out[i].  The generator is
  * std::mt19937_64(seed) (the published MT19937-64 recurrence and seeding) and
@@ -141,6 +145,10 @@ int or_model_quant_tensor(const or_model* m, int layer, int which,
 int or_model_reset_cache(or_model* m, int max_seq);
 /* model.cpp:284-311: logits [vocab] f32. */
 int or_model_step(or_model* m, int token, float* logits);
+/* Feeds tokens[0..n) from the current position, layer by layer over all n
+ * positions: bit-identical to n or_model_step calls; logits (if not NULL)
+ * receives the last position's [vocab]. */
+int or_model_prefill(or_model* m, const int* tokens, int n, float* logits);
 int or_model_cache_len(const or_model* m);
 /* model.cpp:340-365 */
 size_t or_model_weight_bytes(const or_model* m);

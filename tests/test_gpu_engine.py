@@ -156,8 +156,5 @@ def test_qwen3_full_f32_prompt32_decode128():
     assert tg == to
     assert worst <= TOL["f32"], worst
 
-
-def test_qwen3_full_int8_prompt512_decode64():
-    worst, to, tg = _full_run("int8", 512, 64, seed=4321)
-    assert tg == to
-    assert worst <= TOL["int8"], worst
+# The INT8 configuration (512-token prompt) runs over its whole benchmarked
+# length, 512 + 512, in test_gpu_parity_full.py.

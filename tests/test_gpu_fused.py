@@ -1,8 +1,9 @@
-"""The persistent fused decode step (one cooperative launch per token) against
-the oracle: f32 and INT8, a small model whose widths are multiples of 512 and
-a cache length that is not a multiple of the 32-position attention chunk, then
-the full Qwen3-0.6B shape.  Same bars as the per-op path: f32 logits
-max-abs <= 1e-3, INT8 <= 1e-2, greedy tokens identical."""
+"""The persistent clustered decode step (path 2, one launch per token) against
+the oracle: f32 and INT8 at full widths with 2 layers and a cache length that
+is not a multiple of the 32-position attention chunk, then the full
+Qwen3-0.6B shape; and the engine's automatic choice of step path.  Same bars
+as the per-op path: f32 logits max-abs <= 1e-3, INT8 <= 1e-2, greedy tokens
+identical."""
 import numpy as np
 import pytest
 
@@ -15,18 +16,13 @@ pytestmark = pytest.mark.gpu
 TOL = {"f32": 1e-3, "int8": 1e-2}
 
 
-def cfg512():
-    return vbsynth.qwen3_config(hidden_size=512, num_hidden_layers=2, num_attention_heads=4,
-                                num_key_value_heads=2, intermediate_size=1024, vocab_size=2000)
-
-
 def cfg_wide():
     """Full Qwen3-0.6B widths (hidden 1024, 16/8 heads, ffn 3072), 2 layers,
     small vocab: the shapes the two-barrier clustered step is laid out for."""
     return vbsynth.qwen3_config(num_hidden_layers=2, vocab_size=4096)
 
 
-def run_pair(cfg, w, mode, prompt, n_new, max_seq, path=0):
+def run_pair(cfg, w, mode, prompt, n_new, max_seq, path=2):
     orc = oracle.OracleModel(cfg, w)
     e = vb200.Engine(cfg).load(w)
     if mode == "int8":
@@ -39,7 +35,8 @@ def run_pair(cfg, w, mode, prompt, n_new, max_seq, path=0):
     for t in prompt:
         lo, lg = orc.step(int(t)), e.step(int(t))
         worst = max(worst, float(np.max(np.abs(lo - lg))))
-    assert e.graph_nodes() == 1, "fused path did not run"
+    if path == 2:
+        assert e.graph_nodes() == 1, "clustered step did not run"
     to, tg = [], []
     for _ in range(n_new):
         a, b = oracle.argmax(lo), int(np.argmax(lg))
@@ -48,27 +45,6 @@ def run_pair(cfg, w, mode, prompt, n_new, max_seq, path=0):
         lo, lg = orc.step(a), e.step(b)
         worst = max(worst, float(np.max(np.abs(lo - lg))))
     return e, orc, worst, to, tg
-
-
-@pytest.mark.parametrize("mode", ["f32", "int8"])
-def test_fused_small_model(mode):
-    cfg = cfg512()
-    w = vbsynth.make_weights(cfg, seed=61)
-    prompt = vbsynth.prompt_ids(7, 9, cfg["vocab_size"])
-    e, orc, worst, to, tg = run_pair(cfg, w, mode, prompt, 30, 45)
-    assert tg == to and worst <= TOL[mode], worst
-    for layer in range(cfg["num_hidden_layers"]):
-        for which in (0, 1):
-            assert np.max(np.abs(e.read_kv(layer, which) - orc.kv(layer, which))) < 1e-4
-    # device-side greedy decode through the fused step == step() loop
-    e.reset_cache(45)
-    lg = e.prefill(prompt, want_logits=True)
-    toks = e.decode(int(np.argmax(lg)), 30)
-    assert [int(np.argmax(lg))] + list(toks[:-1]) == to
-    # errors keep the reference's wording on this path too
-    with pytest.raises(vb200.VBError, match="kv cache is full"):
-        e.decode(0, 10)
-    e.close()
 
 
 @pytest.mark.parametrize("mode", ["f32", "int8"])
@@ -87,24 +63,50 @@ def test_two_barrier_step_wide_model(mode):
     lg = e.prefill(prompt, want_logits=True)
     toks = e.decode(int(np.argmax(lg)), 24)
     assert [int(np.argmax(lg))] + list(toks[:-1]) == to
+    # errors keep the reference's wording on this path too
+    with pytest.raises(vb200.VBError, match="kv cache is full"):
+        e.decode(0, 10)
     e.close()
 
 
-@pytest.mark.parametrize("path", [0, 2])
-def test_fused_full_f32_prompt32_decode128(path):
+def test_clustered_full_f32_prompt32_decode128():
     cfg = vbsynth.qwen3_config()
     w = vbsynth.make_weights(cfg, seed=1234)
     prompt = vbsynth.prompt_ids(32, 1235, cfg["vocab_size"])
-    e, orc, worst, to, tg = run_pair(cfg, w, "f32", prompt, 128, 168, path=path)
+    e, orc, worst, to, tg = run_pair(cfg, w, "f32", prompt, 128, 168, path=2)
     assert tg == to and worst <= TOL["f32"], worst
     e.close()
 
 
-@pytest.mark.parametrize("path", [0, 2])
-def test_fused_full_int8_prompt512_decode64(path):
+def test_per_op_full_int8_prompt512_decode64():
     cfg = vbsynth.qwen3_config()
     w = vbsynth.make_weights(cfg, seed=4321)
     prompt = vbsynth.prompt_ids(512, 4322, cfg["vocab_size"])
-    e, orc, worst, to, tg = run_pair(cfg, w, "int8", prompt, 64, 584, path=path)
+    e, orc, worst, to, tg = run_pair(cfg, w, "int8", prompt, 64, 584, path=1)
     assert tg == to and worst <= TOL["int8"], worst
+    assert e.graph_nodes() > 1
+    e.close()
+
+
+def test_automatic_path_is_the_measured_fastest():
+    """set_path(-1) (the default) takes the per-op graph for f32 weights and
+    the clustered step for INT8 -- the faster of each on B200 -- and path 0
+    (a removed implementation) is refused."""
+    cfg = cfg_wide()
+    w = vbsynth.make_weights(cfg, seed=3)
+    e = vb200.Engine(cfg).load(w)
+    e.reset_cache(16)
+    assert e.path() == 1
+    e.step(1)
+    assert e.graph_nodes() > 1
+    with pytest.raises(vb200.VBError):
+        e.set_path(0)
+    e.set_path(2)
+    assert e.path() == 2
+    e.set_path(-1)
+    e.quantize()
+    e.reset_cache(16)
+    assert e.path() == 2
+    e.step(1)
+    assert e.graph_nodes() == 1
     e.close()

@@ -6,8 +6,9 @@ instead of vb_attn_decode (which cudaMalloc's its scratch on first use).  Its
 scratch is a fixed array compiled into the library.  This test drives it
 through the C ABI and checks it against vb_attn_decode within the attention
 tolerance of the other GPU tests, on two calls in a row (the second with a
-shorter cache, so leftovers of the first call would show), and checks that a
-shape needing more than the static buffer is refused.  It sits in its own file
+shorter cache, so leftovers of the first call would show), at long contexts
+where the split count is capped to fit the static buffer, and checks that a
+head count needing more than the static buffer for one split is refused.  It sits in its own file
 named to be collected last, and works alone in a fresh process too: its first
 call also performs the one-time address lookup for the device.
 """
@@ -30,20 +31,38 @@ def _inputs(n, seed):
     return q, kc, vc
 
 
+def _compare(n, seed):
+    q, kc, vc = _inputs(n, seed)
+    got = torch.empty(H, D, device="cuda")
+    vb200.attn_decode_noalloc(q, kc, vc, got, H, KVH, D, n)
+    ref = torch.empty(H, D, device="cuda")
+    vb200.attn_decode(q, kc, vc, ref, H, KVH, D, n)
+    torch.cuda.synchronize()
+    return float((got - ref).abs().max())
+
+
 def test_noalloc_matches_allocating_entry_point_twice():
     for call, n in enumerate((4096, 777)):
-        q, kc, vc = _inputs(n, 900 + call)
-        got = torch.empty(H, D, device="cuda")
-        vb200.attn_decode_noalloc(q, kc, vc, got, H, KVH, D, n)
-        ref = torch.empty(H, D, device="cuda")
-        vb200.attn_decode(q, kc, vc, ref, H, KVH, D, n)
-        torch.cuda.synchronize()
-        diff = float((got - ref).abs().max())
+        diff = _compare(n, 900 + call)
         assert np.isfinite(diff) and diff <= 2e-5, (call, n, diff)
 
 
-def test_noalloc_refuses_shapes_beyond_the_static_buffer():
-    h, kvh, n = 64, 1, 40000  # 592 splits x 64 heads x 130 floats: ~19.7 MB
+def test_noalloc_long_contexts_run_with_capped_splits():
+    # 16/8 heads: past ~32k positions the allocating entry point would use more
+    # splits than the 1 MiB array holds; the no-alloc one caps the split count
+    # (longer splits) and must still agree.  40960 is the model's
+    # max_position_embeddings; 32000 is just below the cap, 32256 just above.
+    for n in (32000, 32256, 40960):
+        diff = _compare(n, n)
+        assert np.isfinite(diff) and diff <= 2e-5, (n, diff)
+        torch.cuda.empty_cache()
+
+
+def test_noalloc_refuses_heads_beyond_the_static_buffer():
+    # one split of 2048 heads needs 2048 x 130 floats + 512 B > 1 MiB, so the
+    # size check refuses it before anything is launched (GQA group 2 is a
+    # shape the attention kernels take, so only the size check can refuse it)
+    h, kvh, n = 2048, 1024, 4
     q = torch.zeros(h, D, device="cuda")
     kc = torch.zeros(n, kvh * D, device="cuda")
     vc = torch.zeros(n, kvh * D, device="cuda")

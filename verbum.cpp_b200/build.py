@@ -4,7 +4,10 @@ Usage:  python verbum.cpp_b200/build.py [--force] [--verbose]
 
 Every .cu / .cpp under csrc/ (and host/) is compiled to an object in
 verbum.cpp_b200/_build/ and linked into one shared library with the shared
-CUDA runtime.  Objects are rebuilt only when a source or header is newer.
+CUDA runtime.  Objects are rebuilt only when a source or header is newer, or
+when the preprocessor definitions differ from the last build's
+(--define VB_STEP_TRACE=1 gives the profiling build whose clustered step
+records its phase trace).
 """
 import argparse
 import concurrent.futures as cf
@@ -48,6 +51,9 @@ def headers():
     return hs
 
 
+DEFINES = []
+
+
 def compile_one(src, verbose=False, ptxas_v=False):
     obj = BUILD / (src.name + ".o")
     newest_hdr = max((h.stat().st_mtime for h in headers()), default=0)
@@ -58,7 +64,7 @@ def compile_one(src, verbose=False, ptxas_v=False):
         inc += ["-I", str(HOST / "include")]
     cmd = [nvcc_path(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
            "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", *inc,
-           "-c", str(src), "-o", str(obj)]
+           *[f"-D{d}" for d in DEFINES], "-c", str(src), "-o", str(obj)]
     if ptxas_v and src.suffix == ".cu":
         cmd.insert(1, "-Xptxas=-v")
     if verbose:
@@ -69,9 +75,14 @@ def compile_one(src, verbose=False, ptxas_v=False):
     return obj, r.stderr
 
 
-def build(force=False, verbose=False, ptxas_v=False):
+def build(force=False, verbose=False, ptxas_v=False, defines=()):
     BUILD.mkdir(exist_ok=True)
     LIB.mkdir(exist_ok=True)
+    DEFINES[:] = sorted(defines)
+    stamp = BUILD / "defines.txt"
+    if not stamp.exists() or stamp.read_text() != " ".join(DEFINES):
+        force = True
+        stamp.write_text(" ".join(DEFINES))
     if force:
         for o in BUILD.glob("*.o"):
             o.unlink()
@@ -102,8 +113,9 @@ def main():
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage")
+    ap.add_argument("--define", action="append", default=[], help="NAME=VALUE passed to nvcc as -D")
     a = ap.parse_args()
-    out = build(a.force, a.verbose, a.ptxas_v)
+    out = build(a.force, a.verbose, a.ptxas_v, a.define)
     print(out)
 
 

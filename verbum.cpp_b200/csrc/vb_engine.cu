@@ -100,11 +100,10 @@ vb_status engine_check_err(vb_engine* e) {
     int err = 0;
     VB_CUDA_TRY(cudaMemcpy(&err, e->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err == kErrNone) return VB_OK;
-    const std::string where = mega_debug(e);
+    const std::string where = mega2_debug(e);
     cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream);
     cudaStreamSynchronize(e->stream);
-    mega_reset_counters(e);  // a step that stopped early leaves its tickets set
-    mega2_reset_counters(e);
+    mega2_reset_counters(e);  // a step that stopped early leaves its tickets set
     switch (err) {
         case kErrBadToken:
             return fail(VB_ERR_TOKEN, "token id out of range for the embedding table");
@@ -240,18 +239,15 @@ static vb_status launch_step(vb_engine* e) {
         VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
         return VB_OK;
     }
-    return (e->path == 0 && e->mega)    ? mega_enqueue_step(e, e->stream)
-           : (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream)
-                                        : enqueue_step_ops(e, e->stream);
+    return (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream) : enqueue_step_ops(e, e->stream);
 }
 
 static vb_status ensure_graph(vb_engine* e) {
     if (e->graph) return VB_OK;
     cudaGraph_t g = nullptr;
     VB_CUDA_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    vb_status st = (e->path == 0 && e->mega)    ? mega_enqueue_step(e, e->stream)
-                   : (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream)
-                                                : enqueue_step_ops(e, e->stream);
+    vb_status st = (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream)
+                                              : enqueue_step_ops(e, e->stream);
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (st) {
         if (g) cudaGraphDestroy(g);
@@ -381,7 +377,6 @@ vb_status vb_engine_destroy(vb_engine* e) {
     if (!e) return VB_OK;
     DeviceGuard dg(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
-    mega_release(e);
     mega2_release(e);
     free_cache(e);
     dfree(e->embed); dfree(e->final_norm); dfree(e->rope_cos); dfree(e->rope_sin);
@@ -545,7 +540,6 @@ vb_status vb_engine_quantize(vb_engine* e) {
     e->quantized = true;
     if (e->graph) cudaGraphExecDestroy(e->graph);
     e->graph = nullptr;
-    mega_release(e);
     mega2_release(e);
     return VB_OK;
 }
@@ -566,7 +560,6 @@ vb_status vb_engine_quantize_lm_head(vb_engine* e) {
     e->lm_int8 = true;
     if (e->graph) cudaGraphExecDestroy(e->graph);
     e->graph = nullptr;
-    mega_release(e);
     mega2_release(e);
     return VB_OK;
 }
@@ -598,8 +591,7 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
         VB_CUDA_TRY(cudaMemsetAsync(e->vc, 0, n * 4, e->stream));
     } else {
         free_cache(e);
-        mega_release(e);
-    mega2_release(e);
+        mega2_release(e);
         const size_t n = (size_t)c.layers * c.kv_heads * max_seq * c.head_dim;
         vb_status st;
         if ((st = dalloc(&e->kc, n, "kv cache"))) return st;
@@ -621,22 +613,19 @@ vb_status vb_engine_reset_cache(vb_engine* e, int max_seq) {
 
 int vb_engine_cache_len(const vb_engine* e) { return e ? e->len : 0; }
 
+// The automatic step path: the one measured fastest on B200 for the weight
+// format (f32: the per-op graph, 985 against 867 tok/s for the clustered
+// step; INT8: the clustered step, 1175 against 943).  A clustered step whose
+// shape requirements are not met falls back to the per-op graph.
+static int auto_path(const vb_engine* e) { return e->quantized ? 2 : 1; }
+
 static vb_status pre_step(vb_engine* e, int n_tokens) {
     vb_status st = check_ready(e);
     if (st) return st;
     if (e->len + n_tokens > e->max_seq) return fail(VB_ERR_CACHE_FULL, "kv cache is full");
     if (e->len + n_tokens > e->cfg.rope_positions)
         return fail(VB_ERR_ROPE, "position is outside the rope table");
-    if (e->path_auto && !e->graph) {
-        // measured fastest on B200: INT8 on the clustered step, f32 on the
-        // grid-barrier step (each falls back to the per-op graph if unsupported)
-        e->path = e->quantized ? 2 : 0;
-    }
-    if (e->path == 0 && !e->mega) {
-        st = mega_prepare(e);
-        if (st == VB_ERR_UNSUPPORTED) e->path = 1;
-        else if (st) return st;
-    }
+    if (e->path_auto && !e->graph) e->path = auto_path(e);
     if (e->path == 2 && !e->mega2) {
         st = mega2_prepare(e);
         if (st == VB_ERR_UNSUPPORTED) e->path = 1;
@@ -751,6 +740,8 @@ vb_status vb_engine_prefill(vb_engine* e, const int* tokens_host, int n, float* 
 
 int vb_engine_graph_nodes(const vb_engine* e) { return e ? e->graph_nodes : 0; }
 
+int vb_engine_path(const vb_engine* e) { return !e ? 0 : (e->path_auto && !e->graph) ? auto_path(e) : e->path; }
+
 vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* host) {
     if (!e || !host) return fail(VB_ERR_ARG, "null argument");
     if (!e->kc) return fail(VB_ERR_NO_CACHE, "call reset_cache() first");
@@ -771,7 +762,7 @@ vb_status vb_engine_read_kv(const vb_engine* e, int layer, int which, float* hos
 }
 
 vb_status vb_engine_set_path(vb_engine* e, int path) {
-    if (!e || path < -1 || path > 2) return fail(VB_ERR_ARG, "path must be -1 (automatic), 0, 1 or 2");
+    if (!e || path < -1 || path == 0 || path > 2) return fail(VB_ERR_ARG, "path must be -1 (automatic), 1 or 2");
     DeviceGuard dg(e->device);
     cudaStreamSynchronize(e->stream);
     e->path_auto = path < 0;
@@ -791,8 +782,7 @@ vb_status vb_engine_set_trace(vb_engine* e, int on) {
     if (e->trace_on != (on != 0)) {
         cudaStreamSynchronize(e->stream);
         e->trace_on = on != 0;
-        mega_release(e);
-    mega2_release(e);
+        mega2_release(e);
         if (e->graph) cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;
     }
@@ -802,8 +792,7 @@ vb_status vb_engine_set_trace(vb_engine* e, int on) {
 int vb_engine_read_trace(vb_engine* e, uint64_t* out, int cap) {
     if (!e || !out || cap <= 0) return 0;
     DeviceGuard dg(e->device);
-    if (e->mega2) return mega2_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
-    return mega_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
+    return mega2_read_trace(e, reinterpret_cast<unsigned long long*>(out), cap);
 }
 
 }  // extern "C"

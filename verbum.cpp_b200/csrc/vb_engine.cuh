@@ -38,7 +38,7 @@ struct vb_engine {
     int device = 0;
     cudaStream_t stream = nullptr;
     bool quantized = false;
-    int path = 1;          // effective step path (0, 1, 2)
+    int path = 1;          // effective step path (1, 2)
     bool path_auto = true; // pick the path per weight format at graph build
 
     // sizes
@@ -98,9 +98,7 @@ struct vb_engine {
     int graph_nodes = 0;
     int* d_prompt = nullptr;   // prefill tokens [max_seq]
 
-    // persistent fused step (vb_mega.cu)
-    void* mega = nullptr;
-    // two-barrier clustered step (vb_mega2.cu)
+    // clustered persistent step (vb_mega2.cu)
     void* mega2 = nullptr;
     bool trace_on = false;
 };
@@ -110,19 +108,14 @@ namespace vb {
 // per-op kernels.  Leaves logits in e->logits and the greedy pick in d_next,
 // then advances d_pos / d_tok and appends the pick to the history.
 vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s);
-// Fused persistent step (vb_mega.cu). Returns VB_ERR_UNSUPPORTED when the
-// shapes are outside what it handles.
-vb_status mega_prepare(vb_engine* e);
-vb_status mega_enqueue_step(vb_engine* e, cudaStream_t s);
-void mega_release(vb_engine* e);
-void mega_reset_counters(vb_engine* e);
-std::string mega_debug(vb_engine* e);
+// Clustered persistent step (vb_mega2.cu). Returns VB_ERR_UNSUPPORTED when
+// the shapes are outside what it handles.
 vb_status mega2_prepare(vb_engine* e);
 vb_status mega2_enqueue_step(vb_engine* e, cudaStream_t s);
 void mega2_release(vb_engine* e);
 void mega2_reset_counters(vb_engine* e);
 int mega2_read_trace(vb_engine* e, unsigned long long* host, int cap);
-int mega_read_trace(vb_engine* e, unsigned long long* host, int cap);
+std::string mega2_debug(vb_engine* e);
 vb_status engine_check_err(vb_engine* e);
 void build_rope_table_host(int head_dim, int max_pos, float theta, float* c, float* s);
 // Device sampling (vb_sample.cu).

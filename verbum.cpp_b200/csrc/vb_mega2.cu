@@ -117,8 +117,20 @@ struct M2Params {
 // B down + push, B reduce.
 constexpr int kTraceStride2 = 2048;
 constexpr int kTraceMarks = 12;
+// The phase trace and cycle profile are compiled in only with VB_STEP_TRACE=1
+// (a profiling build): the product kernel carries none of their code.
+#ifndef VB_STEP_TRACE
+#define VB_STEP_TRACE 0
+#endif
+__device__ __forceinline__ long long tclk() {
+#if VB_STEP_TRACE
+    return clock64();
+#else
+    return 0;
+#endif
+}
 __device__ __forceinline__ void tmark(const M2Params& p, int l, int i) {
-    if (p.trace && threadIdx.x == 0 && 1 + kTraceMarks * (l + 1) < kTraceStride2)
+    if (VB_STEP_TRACE && p.trace && threadIdx.x == 0 && 1 + kTraceMarks * (l + 1) < kTraceStride2)
         p.trace[(size_t)blockIdx.x * kTraceStride2 + 1 + kTraceMarks * l + i] = now_ns();
 }
 
@@ -132,7 +144,7 @@ __device__ __forceinline__ void tmark(const M2Params& p, int l, int i) {
 constexpr int kProfBase = 400;
 constexpr int kProfWords = 40;
 __device__ __forceinline__ long long* prof_ptr(const M2Params& p, int l) {
-    if (!p.trace || threadIdx.x != 0 || kProfBase + kProfWords * (l + 1) > kTraceStride2) return nullptr;
+    if (!VB_STEP_TRACE || !p.trace || threadIdx.x != 0 || kProfBase + kProfWords * (l + 1) > kTraceStride2) return nullptr;
     return reinterpret_cast<long long*>(p.trace + (size_t)blockIdx.x * kTraceStride2 + kProfBase + kProfWords * l);
 }
 
@@ -599,25 +611,25 @@ __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbas
     float best_v = -INFINITY;
     int best_i = INT_MAX;
     long long t_wait = 0, t_dot = 0, t_epi = 0, t_first = -1;
-    const long long t_start = clock64();
+    const long long t_start = tclk();
     const int items = g.nstages * parts;
     for (int it = warp; it < items; it += kCW) {
         const int j = it / parts, part = it - j * parts;
         const int gs = gbase + j;
-        const long long tw = clock64();
+        const long long tw = tclk();
         if (!stage_wait(p, S, gs, false)) return false;
-        t_wait += clock64() - tw;
+        t_wait += tclk() - tw;
         const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
         const int rA = g.r0 + j * g.rps;
         const int nr = min(g.rps, g.r1 - rA);
         const int lo = part * NR;
         const int cnt = max(0, min(NR, nr - lo));
         float acc[NR];
-        const long long td = clock64();
+        const long long td = tclk();
         if constexpr (Q8) dot_rows_i8<NR, K>(st + (size_t)lo * g.row_bytes, g.row_bytes, cnt, xs, lane, acc);
         else dot_rows_f32<NR, K>(st + (size_t)lo * g.row_bytes, g.row_bytes, cnt, xs, lane, acc);
         if (prof2) asm volatile("" : "+f"(acc[0]));
-        const long long te = clock64();
+        const long long te = tclk();
         t_dot += te - td;
         stage_release(S, gs, share);
         const int row0 = rA + lo;
@@ -631,7 +643,7 @@ __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbas
             }
             epi_apply(epi, row, a, bval, best_v, best_i);
         }
-        const long long tf = clock64();
+        const long long tf = tclk();
         t_epi += tf - te;
         if (t_first < 0) t_first = tf - td;
     }
@@ -652,7 +664,7 @@ __device__ __noinline__ bool gemv_rows(const M2Params& p, const Plan g, int gbas
     }
     if (prof) {
         prof[0] += t_wait;
-        prof[1] += clock64() - t_start;
+        prof[1] += tclk() - t_start;
     }
     if (prof2) {
         prof2[0] += t_first;
@@ -742,12 +754,12 @@ __device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, 
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const M2Layer& L = p.layers[l];
     {
-        const long long c0 = clock64();
+        const long long c0 = tclk();
         const unsigned tag = xtag(ep1, l, kXQkv);
         bool ok = true;
         for (int i = t; i < 512 && ok; i += kCT) ok = wait_own(p, &S.qkv64[i], tag, 7, S.qkv[i]);
         if (!consumers_sync_and<kCT>(ok)) return false;
-        if (prof) prof[8] += clock64() - c0;
+        if (prof) prof[8] += tclk() - c0;
     }
     tmark(p, l, 3);
     const int hs = t >> 7, d = t & 127;
@@ -799,11 +811,11 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
     for (int j = warp; j < njl && ok; j += kCW) {
         const int c = rank + kCS * j;
         const int gk = g + 2 * j, gv = gk + 1;
-        const long long tw = clock64();
+        const long long tw = tclk();
         ok = stage_wait(p, S, gk, false) && stage_wait(p, S, gv, false);
         if (!ok) break;
         if (prof) {
-            prof[11] += clock64() - tw;
+            prof[11] += tclk() - tw;
             prof[12] += 1;
         }
         const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(gk % kStages) * kStageBytes);
@@ -906,7 +918,7 @@ __device__ __noinline__ bool merge_ctx(const M2Params& p, S2& S, float* xs, int 
     VB_SHARED(&S);
     VB_SHARED(xs);
     const int t = threadIdx.x;
-    const long long c0 = clock64();
+    const long long c0 = tclk();
     const unsigned tag = xtag(ep1, l, kXAtt);
     const int hs = t >> 7, d = t & 127;
     const unsigned base = smem_addr(&S.xu.att64[rank][0]);
@@ -942,7 +954,7 @@ __device__ __noinline__ bool merge_ctx(const M2Params& p, S2& S, float* xs, int 
         A = fmaf(ar, f, A);
     }
     if (!consumers_sync_and<kCT>(ok)) return false;
-    if (prof) prof[9] += clock64() - c0;
+    if (prof) prof[9] += tclk() - c0;
     const float cval = (Lsum > 0.f) ? A / Lsum : 0.f;
     const int i = hs * 128 + d;
     xs[perm ? perm_index(i) : i] = cval;
@@ -960,13 +972,13 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
     VB_SHARED(ring);
     const int t = threadIdx.x;
     f2 alo = 0ull, ahi = 0ull;  // outputs 4t, 4t+1 | 4t+2, 4t+3
-    const long long d0 = clock64();
+    const long long d0 = tclk();
     long long dw = 0;
     for (int j = 0; j < pl.nstages; j++) {
         const int gs = g + j;
-        const long long tw = clock64();
+        const long long tw = tclk();
         if (!stage_wait(p, S, gs, true)) return false;
-        dw += clock64() - tw;
+        dw += tclk() - tw;
         const char* st = ring + (size_t)(gs % kStages) * kStageBytes;
         const int rA = pl.r0 + j * pl.rps;
         const int nr = min(pl.rps, pl.r1 - rA);
@@ -989,7 +1001,7 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
     }
     if (prof) {
         prof[6] += dw;
-        prof[7] += clock64() - d0;
+        prof[7] += tclk() - d0;
     }
     const unsigned tag = xtag(ep1, l, kXRed);
     const int per = p.hidden / kCS;
@@ -1010,7 +1022,7 @@ __device__ __noinline__ bool down_push(const M2Params& p, S2& S, const char* rin
 __device__ __noinline__ bool reduce_store(const M2Params& p, S2& S, int l, int cid, int rank, unsigned ep1,
                                           bool q8, long long* prof) {
     VB_SHARED(&S);
-    const long long c0 = clock64();
+    const long long c0 = tclk();
     const unsigned tag = xtag(ep1, l, kXRed);
     const int t = threadIdx.x;
     const int per = p.hidden / kCS;
@@ -1029,7 +1041,7 @@ __device__ __noinline__ bool reduce_store(const M2Params& p, S2& S, int l, int c
                    xpack(v, xtag(ep1, l, kXGlobal)));
     }
     if (!consumers_sync_and<kCT>(ok)) return false;
-    if (prof) prof[10] += clock64() - c0;
+    if (prof) prof[10] += tclk() - c0;
     return true;
 }
 
@@ -1133,7 +1145,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cid = (int)cluster_id(), rank = (int)cluster_rank();
 
-    if (p.trace)
+    if (VB_STEP_TRACE && p.trace)
         for (int i = threadIdx.x; i < kTraceStride2; i += kThreads)
             p.trace[(size_t)blockIdx.x * kTraceStride2 + i] = 0ull;
     // exchange words start with tag 0, which no launch uses; the cluster
@@ -1141,7 +1153,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
     for (int i = threadIdx.x; i < 512; i += kThreads) S.qkv64[i] = 0ull;
     for (int i = threadIdx.x; i < kCS * kAttWords; i += kThreads) (&S.xu.att64[0][0])[i] = 0ull;
     if (threadIdx.x == 0) {
-        if (p.trace) p.trace[(size_t)blockIdx.x * kTraceStride2] = now_ns();
+        if (VB_STEP_TRACE && p.trace) p.trace[(size_t)blockIdx.x * kTraceStride2] = now_ns();
         for (int s = 0; s < kStages; s++) {
             mbar_init(smem_addr(&S.full[s]), 1);
             mbar_init(smem_addr(&S.empty[s]), kCW);
@@ -1197,7 +1209,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
         const M2Layer& L = p.layers[l];
         long long* prof = prof_ptr(p, l);
         if (prof) {
-            prof[14] = clock64();
+            prof[14] = tclk();
             prof[15] = (long long)now_ns();
         }
         const unsigned long long* xd_prev = p.xd + (size_t)((l + 1) & 1) * p.nclusters * p.hidden;
@@ -1227,12 +1239,12 @@ __global__ void __launch_bounds__(kThreads, 1) mega2_kernel(const __grid_constan
             }
             if (!qkv_finish(p, S, l, cid, rank, pos, ep1, prof)) { ok = false; break; }
             {
-                const long long t_att = clock64();
+                const long long t_att = tclk();
                 const bool r = attention(p, S, ring, l, rank, pos, nchunks, g, prof);
                 g += 2 * (rank < nchunks ? (nchunks - rank + kCS - 1) / kCS : 0);
                 if (!r) { ok = false; break; }
                 tmark(p, l, 4);
-                if (prof) prof[13] += clock64() - t_att;
+                if (prof) prof[13] += tclk() - t_att;
             }
             if (!merge_ctx(p, S, xs, l, rank, ep1, Q8, prof)) { ok = false; break; }
             tmark(p, l, 5);
@@ -1545,7 +1557,7 @@ vb_status mega2_prepare(vb_engine* e) {
     P.nclusters = nclusters;
     P.eps = c.eps;
     P.trace = nullptr;
-    if (e->trace_on) {
+    if (VB_STEP_TRACE && e->trace_on) {
         const size_t tb = (size_t)G * kTraceStride2 * sizeof(unsigned long long);
         if (cudaMalloc(&m->trace, tb) == cudaSuccess) {
             m->bufs.push_back(m->trace);
@@ -1600,6 +1612,29 @@ int mega2_read_trace(vb_engine* e, unsigned long long* host, int cap) {
     if (cudaMemcpy(host, m->trace, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost) != cudaSuccess)
         return 0;
     return n;
+}
+
+// Where the last failed step gave up, from the debug words the first failing
+// wait recorded: " [code c, cta b, <site>, index i, extra x]" or "".
+std::string mega2_debug(vb_engine* e) {
+    Mega2State* m = static_cast<Mega2State*>(e->mega2);
+    if (!m) return "";
+    int d[5] = {0, 0, 0, 0, 0};
+    if (cudaMemcpy(d, m->params.dbg, sizeof d, cudaMemcpyDeviceToHost) != cudaSuccess) return "";
+    if (!d[0]) return "";
+    static const char* sites[] = {"?",
+                                  "producer empty-slot wait",
+                                  "consumer stage wait",
+                                  "attention stage wait",
+                                  "global partials exchange",
+                                  "slot order wait",
+                                  "?",
+                                  "cluster q/k/v gather",
+                                  "cluster attention merge",
+                                  "cluster down-proj reduce"};
+    const int si = (d[2] >= 1 && d[2] <= 9) ? d[2] : 0;
+    return std::string(" [code ") + std::to_string(d[0]) + ", cta " + std::to_string(d[1]) + ", " + sites[si] +
+           ", index " + std::to_string(d[3]) + ", extra " + std::to_string(d[4]) + "]";
 }
 
 void mega2_reset_counters(vb_engine* e) {

@@ -94,6 +94,7 @@ _SIGS = {
     "vb_engine_prefill": (_I, [_P, _P, _I, _P]),
     "vb_engine_graph_nodes": (_I, [_P]),
     "vb_engine_set_path": (_I, [_P, _I]),
+    "vb_engine_path": (_I, [_P]),
     "vb_engine_stream": (_P, [_P]),
     "vb_engine_set_trace": (_I, [_P, _I]),
     "vb_engine_read_trace": (_I, [_P, _P, _I]),
@@ -283,7 +284,13 @@ class Engine:
         return out
 
     def set_path(self, path: int):
+        """1 = per-op CUDA graph, 2 = clustered persistent step, -1 = automatic."""
         check(lib().vb_engine_set_path(self.h, int(path)))
+        return self
+
+    def path(self) -> int:
+        """The step path the next step runs (the automatic choice if not fixed)."""
+        return lib().vb_engine_path(self.h)
 
     def set_trace(self, on: bool):
         check(lib().vb_engine_set_trace(self.h, int(bool(on))))

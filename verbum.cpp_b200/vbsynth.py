@@ -64,12 +64,17 @@ def tensor_specs(cfg: dict):
     return specs
 
 
-def make_weights(cfg: dict, seed: int = 1234, std: float = 0.02, norm_value: float = 1.0) -> dict:
+def make_weights(cfg: dict, seed: int = 1234, std: float = 0.02, norm_value: float = 1.0,
+                 normal=None) -> dict:
+    """normal(n, seed, std) -> f32 array: the generator (default the engine
+    library's vb_synth_normal; the oracle's or_synth_normal gives the same
+    values for callers that must not load the engine library)."""
+    normal = normal or vb200.synth_normal
     out = {}
     for idx, (name, shape, kind) in enumerate(tensor_specs(cfg)):
         n = int(np.prod(shape))
         if kind == "linear":
-            a = vb200.synth_normal(n, seed * 1000003 + idx, std)
+            a = normal(n, seed * 1000003 + idx, std)
         else:
             a = np.full(n, norm_value, dtype=np.float32)
         out[name] = a.reshape(shape)
