@@ -48,6 +48,17 @@ enum {
 VB_API const char* vb_last_error(void);
 /* "sm_100a" build tag + version string. */
 VB_API const char* vb_version(void);
+/* Test hook for the failure paths (no reference counterpart; the reference's
+ * CUDA_CHECK aborts, kernels/cuda_ops.cu:9-16): arms one launch of a kernel to
+ * wait for something nothing will produce, so that one of its bounded waits
+ * (2 s of %globaltimer) runs out.  site 1: the next clustered decode step
+ * (vb_engine_step / decode on path 2) -- one CTA waits for an exchange word no
+ * CTA writes; site 2: the next tensor-core GEMM launched outside a stream
+ * capture (vb_matmul_nt_tc with M <= 64) -- its first CTA never fills its first
+ * stage.  The kernel records the timeout, lets its own copies and MMAs land,
+ * releases its tensor memory and returns; the call returns VB_ERR_TIMEOUT and
+ * the engine stays usable.  0 disarms.  Nothing faults, traps or hangs. */
+VB_API vb_status vb_debug_arm_fault(int site);
 
 /* ------------------------------------------------------------------------ */
 /* Device and memory: replaces cuda_backend.h:12-21                          */
@@ -247,6 +258,20 @@ VB_API vb_status vb_engine_set_layer(vb_engine* e, int layer, const vb_layer_hos
  * safetensors.cpp:59-66), giving the same device weights as the f32 calls. */
 VB_API vb_status vb_engine_set_globals_bf16(vb_engine* e, const uint16_t* embed, const uint16_t* final_norm);
 VB_API vb_status vb_engine_set_layer_bf16(vb_engine* e, int layer, const vb_layer_host_bf16* w);
+/* One layer already quantized on the host (the reference's QuantLayer,
+ * quant.h:29-36, as Model::quantize leaves it, model.cpp:313-338): int8 rows
+ * [rows][cols] and one f32 scale per row for each projection, plus the f32
+ * norms.  The first call switches the engine to INT8 weights (the f32
+ * projection memory is released); every layer must then come through this
+ * call.  The device holds exactly these bytes, so the weights are the
+ * reference's own quantized values.  Replaces the refusal of quantized
+ * weights at model.cpp:374-377. */
+typedef struct {
+    const float *input_norm, *post_norm, *q_norm, *k_norm;
+    const int8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const float *sq, *sk, *sv, *so, *sg, *su, *sd;
+} vb_layer_host_q8;
+VB_API vb_status vb_engine_set_layer_q8(vb_engine* e, int layer, const vb_layer_host_q8* w);
 /* Model::quantize (model.cpp:313-338) on the device: the 7 projections of
  * every layer become INT8 + per-row scales bit-exactly as quantize_rows, and
  * the f32 copies are freed.  Embedding, lm_head and norms stay f32. */

@@ -1,6 +1,7 @@
 // vb_capi.cu -- extern "C" kernel entry points, memory helpers and error
 // state of the C ABI declared in include/verbum_b200.h.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -64,7 +65,14 @@ vb_status scratch_for(size_t need, void** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+std::atomic<int> g_fault_site{kFaultNone};
+
 }  // namespace
+
+bool fault_take(int site) {
+    int want = site;
+    return site != kFaultNone && g_fault_site.compare_exchange_strong(want, kFaultNone);
+}
 }  // namespace vb
 
 using namespace vb;
@@ -74,6 +82,12 @@ extern "C" {
 const char* vb_last_error(void) { return g_last_error.c_str(); }
 
 const char* vb_version(void) { return "verbum-b200 0.1 (sm_100a)"; }
+
+vb_status vb_debug_arm_fault(int site) {
+    if (site < kFaultNone || site > kFaultGemmStage) return fail(VB_ERR_ARG, "fault site must be 0, 1 or 2");
+    g_fault_site.store(site);
+    return VB_OK;
+}
 
 int vb_device_count(void) {
     int n = 0;

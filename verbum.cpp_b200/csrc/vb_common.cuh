@@ -33,6 +33,12 @@ vb_status cuda_fail(cudaError_t e, const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Failure-path test hook (vb_debug_arm_fault): the site armed for the next
+// launch.  fault_take(site) returns true once -- for the first launch of that
+// site after arming -- and disarms it.
+enum FaultSite : int { kFaultNone = 0, kFaultStepExchange = 1, kFaultGemmStage = 2 };
+bool fault_take(int site);
+
 constexpr int kWarp = 32;
 
 // ---------------------------------------------------------------------------

@@ -235,11 +235,26 @@ static vb_status launch_step(vb_engine* e) {
         const char* v = getenv("VB_STEP_DIRECT");
         return v && v[0] == '1';
     }();
-    if (!direct) {
-        VB_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
-        return VB_OK;
+    // failure-path test: the armed step's CTA 0 waits for an exchange word
+    // nothing writes (the hook word is written and complete before the launch)
+    const bool inject = e->path == 2 && e->mega2 && fault_take(kFaultStepExchange);
+    if (inject) {
+        vb_status st = mega2_set_fault(1, e->stream);
+        if (st) return st;
+        VB_CUDA_TRY(cudaStreamSynchronize(e->stream));
     }
-    return (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream) : enqueue_step_ops(e, e->stream);
+    vb_status st = VB_OK;
+    if (!direct) {
+        const cudaError_t ce = cudaGraphLaunch(e->graph, e->stream);
+        if (ce != cudaSuccess) st = cuda_fail(ce, "cudaGraphLaunch");
+    } else {
+        st = (e->path == 2 && e->mega2) ? mega2_enqueue_step(e, e->stream) : enqueue_step_ops(e, e->stream);
+    }
+    if (inject) {
+        const vb_status s2 = mega2_set_fault(0, e->stream);
+        if (!st) st = s2;
+    }
+    return st;
 }
 
 static vb_status ensure_graph(vb_engine* e) {
@@ -505,12 +520,11 @@ vb_status vb_engine_set_layer(vb_engine* e, int layer, const vb_layer_host* w) {
     return VB_OK;
 }
 
-vb_status vb_engine_quantize(vb_engine* e) {
-    if (!e) return fail(VB_ERR_ARG, "null engine");
-    if (e->quantized) return VB_OK;  // model.cpp:314
-    for (int l = 0; l < e->cfg.layers; l++)
-        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "quantize before all layers are uploaded");
-    DeviceGuard dg(e->device);
+namespace vb {
+namespace {
+// INT8 storage of every layer (same layout the device quantizer writes) with
+// the per-layer pointers set; releases the f32 projections.
+vb_status alloc_int8_layers(vb_engine* e) {
     const vb_config& c = e->cfg;
     const size_t hd = c.hidden;
     vb_status st;
@@ -528,6 +542,75 @@ vb_status vb_engine_quantize(vb_engine* e) {
         L.so = L.sqkv + e->qkv_rows;
         L.sgu = L.so + hd;
         L.sd = L.sgu + 2 * c.ffn;
+    }
+    return VB_OK;
+}
+
+void drop_step_state(vb_engine* e) {
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    e->graph = nullptr;
+    mega2_release(e);
+}
+}  // namespace
+}  // namespace vb
+
+vb_status vb_engine_set_layer_q8(vb_engine* e, int layer, const vb_layer_host_q8* w) {
+    if (!e || !w) return fail(VB_ERR_ARG, "null argument");
+    if (layer < 0 || layer >= e->cfg.layers) return fail(VB_ERR_ARG, "layer index out of range");
+    if (!w->input_norm || !w->post_norm || !w->q_norm || !w->k_norm || !w->wq || !w->wk || !w->wv || !w->wo ||
+        !w->wg || !w->wu || !w->wd || !w->sq || !w->sk || !w->sv || !w->so || !w->sg || !w->su || !w->sd)
+        return fail(VB_ERR_ARG, "null weight pointer");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const size_t hd = c.hidden, D = c.head_dim, qw = e->q_width, kw = e->kv_width, F = c.ffn;
+    vb_status st;
+    if (!e->quantized) {
+        // switching to INT8 uploads: every layer comes through this call now
+        for (int l = 0; l < c.layers; l++) e->layer_set[l] = 0;
+        if ((st = alloc_int8_layers(e))) return st;
+        dfree(e->wf32);
+        for (auto& L : e->L) L.wqkv = L.wo = L.wgu = L.wd = nullptr;
+        e->quantized = true;
+        drop_step_state(e);
+    }
+    vb_layer_dev& L = e->L[layer];
+    auto up = [](void* d, const void* h, size_t bytes) { return cudaMemcpy(d, h, bytes, cudaMemcpyHostToDevice); };
+    VB_CUDA_TRY(up(L.in_norm, w->input_norm, hd * 4));
+    VB_CUDA_TRY(up(L.post_norm, w->post_norm, hd * 4));
+    VB_CUDA_TRY(up(L.q_norm, w->q_norm, D * 4));
+    VB_CUDA_TRY(up(L.k_norm, w->k_norm, D * 4));
+    // q | k | v rows stacked, with their scales
+    VB_CUDA_TRY(up(L.qqkv, w->wq, qw * hd));
+    VB_CUDA_TRY(up(L.qqkv + qw * hd, w->wk, kw * hd));
+    VB_CUDA_TRY(up(L.qqkv + (qw + kw) * hd, w->wv, kw * hd));
+    VB_CUDA_TRY(up(L.sqkv, w->sq, qw * 4));
+    VB_CUDA_TRY(up(L.sqkv + qw, w->sk, kw * 4));
+    VB_CUDA_TRY(up(L.sqkv + qw + kw, w->sv, kw * 4));
+    VB_CUDA_TRY(up(L.qo, w->wo, hd * qw));
+    VB_CUDA_TRY(up(L.so, w->so, hd * 4));
+    // gate row j -> row 2j, up row j -> row 2j+1 (scales alike)
+    VB_CUDA_TRY(cudaMemcpy2D(L.qgu, 2 * hd, w->wg, hd, hd, F, cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(cudaMemcpy2D(L.qgu + hd, 2 * hd, w->wu, hd, hd, F, cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(cudaMemcpy2D(L.sgu, 8, w->sg, 4, 4, F, cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(cudaMemcpy2D(L.sgu + 1, 8, w->su, 4, 4, F, cudaMemcpyHostToDevice));
+    VB_CUDA_TRY(up(L.qd, w->wd, hd * F));
+    VB_CUDA_TRY(up(L.sd, w->sd, hd * 4));
+    e->layer_set[layer] = 1;
+    return VB_OK;
+}
+
+vb_status vb_engine_quantize(vb_engine* e) {
+    if (!e) return fail(VB_ERR_ARG, "null engine");
+    if (e->quantized) return VB_OK;  // model.cpp:314
+    for (int l = 0; l < e->cfg.layers; l++)
+        if (!e->layer_set[l]) return fail(VB_ERR_STATE, "quantize before all layers are uploaded");
+    DeviceGuard dg(e->device);
+    const vb_config& c = e->cfg;
+    const size_t hd = c.hidden;
+    vb_status st;
+    if ((st = alloc_int8_layers(e))) return st;
+    for (int l = 0; l < c.layers; l++) {
+        vb_layer_dev& L = e->L[l];
         if ((st = launch_quantize_rows(L.wqkv, e->qkv_rows, hd, L.qqkv, L.sqkv, e->stream))) return st;
         if ((st = launch_quantize_rows(L.wo, hd, e->q_width, L.qo, L.so, e->stream))) return st;
         if ((st = launch_quantize_rows(L.wgu, 2 * c.ffn, hd, L.qgu, L.sgu, e->stream))) return st;

@@ -114,6 +114,8 @@ vb_status mega2_prepare(vb_engine* e);
 vb_status mega2_enqueue_step(vb_engine* e, cudaStream_t s);
 void mega2_release(vb_engine* e);
 void mega2_reset_counters(vb_engine* e);
+// Sets the clustered step's failure-test hook word (ordered on s).
+vb_status mega2_set_fault(int v, cudaStream_t s);
 int mega2_read_trace(vb_engine* e, unsigned long long* host, int cap);
 std::string mega2_debug(vb_engine* e);
 vb_status engine_check_err(vb_engine* e);

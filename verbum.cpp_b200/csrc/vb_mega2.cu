@@ -755,7 +755,8 @@ __device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, 
     const M2Layer& L = p.layers[l];
     {
         const long long c0 = tclk();
-        const unsigned tag = xtag(ep1, l, kXQkv);
+        // (armed failure test: CTA 0 waits at layer 0 for a tag no CTA writes)
+        const unsigned tag = (l == 0 && blockIdx.x == 0 && fault_armed()) ? 0xFFFFFFFFu : xtag(ep1, l, kXQkv);
         bool ok = true;
         for (int i = t; i < 512 && ok; i += kCT) ok = wait_own(p, &S.qkv64[i], tag, 7, S.qkv[i]);
         if (!consumers_sync_and<kCT>(ok)) return false;
@@ -1567,6 +1568,11 @@ vb_status mega2_prepare(vb_engine* e) {
         }
     }
     e->mega2 = m;
+    return VB_OK;
+}
+
+vb_status mega2_set_fault(int v, cudaStream_t s) {
+    VB_CUDA_TRY(set_fault_word(v, s));
     return VB_OK;
 }
 

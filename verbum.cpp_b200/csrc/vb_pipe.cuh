@@ -10,6 +10,19 @@ namespace {
 
 constexpr unsigned long long kWaitNs = 2000000000ull;  // every wait gives up after 2 s
 
+// Test hook for the failure paths, armed from the host for exactly one launch
+// (vb_debug_arm_fault): non-zero makes the armed kernel wait for something
+// nothing will produce -- an exchange word no CTA writes, a stage no copy
+// fills -- so one of its bounded waits runs out, it records the timeout and
+// returns, and the host reports VB_ERR_TIMEOUT.  Each kernel file has its own
+// copy (this header is compiled into each); zero in normal operation.
+__device__ int g_fault_arm = 0;
+__device__ __forceinline__ bool fault_armed() { return *reinterpret_cast<volatile int*>(&g_fault_arm) != 0; }
+// Host side: sets this file's hook word on `s` (ordered with the launch).
+inline cudaError_t set_fault_word(int v, cudaStream_t s) {
+    return cudaMemcpyToSymbolAsync(g_fault_arm, &v, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+}
+
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ unsigned smem_addr(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
@@ -75,6 +88,18 @@ __device__ __noinline__ bool mbar_wait_slow(unsigned a, unsigned parity, int* er
 }
 __device__ __forceinline__ bool mbar_wait(unsigned a, unsigned parity, int* err, int* dbg, int site, int index) {
     return mbar_try(a, parity) || mbar_wait_slow(a, parity, err, dbg, site, index);
+}
+// Bounded wait that does NOT give up when the error word is set: a CTA that
+// is leaving (after its own or another CTA's failure) uses it to let the bulk
+// copies and tensor-core operations it issued land first, since its shared
+// and tensor memory go to the next CTA once it exits.  Only the time bound
+// ends it early.
+__device__ __noinline__ bool mbar_drain(unsigned a, unsigned parity) {
+    const unsigned long long t0 = now_ns();
+    for (unsigned it = 1;; it++) {
+        if (mbar_try(a, parity)) return true;
+        if ((it & 255u) == 0 && now_ns() - t0 > kWaitNs) return false;
+    }
 }
 // Bounded wait until the previous round of `slot` (stage s - kStages) has been
 // observed by a consumer (or this round already has, by another warp sharing

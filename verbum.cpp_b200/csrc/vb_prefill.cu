@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     int issued = nt > 1 ? 2 : 1;  // key tiles requested so far
     int s_issued = -1, s_seen = -1;  // last S product issued (thread 32) / waited for (all)
+    int pv_committed = -1;           // last P.V commit (thread 32)
     // thread 32: S = Q K^T of key tile `tile` into tS (false: its copies never came)
     auto issue_s = [&](int tile) -> bool {
         const int bf = tile & 1;
@@ -391,6 +392,7 @@ __global__ void __launch_bounds__(256, 1)
                 }
             }
             mma_commit(smem_addr(&pv_done));
+            pv_committed = it;
             // the next key tile's S runs while the threads fold this P.V in (every thread
             // read this tile's S before the barrier above)
             if (it + 1 < nt && !issue_s(it + 1)) ok = false;
@@ -413,13 +415,18 @@ __global__ void __launch_bounds__(256, 1)
     xch[hf][r] = l;
     ok = __syncthreads_and(ok);
     l = xch[0][r] + xch[1][r];
-    if (t == 32 && s_issued > s_seen)  // a failed pass left the next S product in flight
-        mbar_wait(smem_addr(&s_done), (unsigned)s_issued & 1u, p.err, nullptr, kSiteFull, s_issued);
+    if (t == 32) {
+        // never release tensor memory with an MMA in flight: a failed pass can
+        // leave the next S product and the last P.V unobserved (these waits
+        // end only when the products land, or at the time bound)
+        if (s_issued > s_seen) mbar_drain(smem_addr(&s_done), (unsigned)s_issued & 1u);
+        if (pv_committed >= 0) mbar_drain(smem_addr(&pv_done), (unsigned)pv_committed & 1u);
+    }
     if (t == 0) {
         // never leave with copies in flight (the last two requested tiles)
         for (int i = issued > 2 ? issued - 2 : 0; i < issued; i++)
-            mbar_wait(smem_addr(&kv_full[i & 1]), (unsigned)(i >> 1) & 1u, p.err, nullptr, kSiteFull, i);
-        mbar_wait(smem_addr(&q_full), 0u, p.err, nullptr, kSiteFull, -1);
+            mbar_drain(smem_addr(&kv_full[i & 1]), (unsigned)(i >> 1) & 1u);
+        mbar_drain(smem_addr(&q_full), 0u);
     }
     if (ok && rvalid) {
         const int hh = r >> 6;

@@ -139,7 +139,10 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
         // weight tiles are requested before waiting for it, the activation
         // tiles after.
         const int pre = min(nch, kTStages);
+        // (armed failure test: the first CTA never fills its first stage)
+        const int withheld = (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && fault_armed()) ? 0 : -1;
         for (int i = 0; i < pre; i++) {
+            if (i == withheld) continue;
             const unsigned st = sbase + (unsigned)i * kTStage;
             const unsigned fb = smem_addr(&full[i]);
             mbar_expect_tx(fb, (unsigned)(WP * kWTile + 2 * kATile));
@@ -164,15 +167,17 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
                 tma_load_2d(st, &tw_hi, x, n0, fb);
                 if (WP == 2) tma_load_2d(st + kWTile, &tw_lo, x, n0, fb);
             }
-            tma_load_2d(st + kAOff, &ta_hi, x, m0, fb);
-            tma_load_2d(st + kAOff + kATile, &ta_lo, x, m0, fb);
+            if (i != withheld) {
+                tma_load_2d(st + kAOff, &ta_hi, x, m0, fb);
+                tma_load_2d(st + kAOff + kATile, &ta_lo, x, m0, fb);
+            }
             issued = i + 1;
         }
         // a stage whose weights went out before a failure still has its copies in flight
         if (issued < pre) issued = pre;
         // never leave with copies in flight
         for (int i = issued > kTStages ? issued - kTStages : 0; i < issued; i++)
-            mbar_wait(smem_addr(&full[i % kTStages]), (unsigned)(i / kTStages) & 1u, p.err, nullptr, kSiteFull, i);
+            if (i != withheld) mbar_drain(smem_addr(&full[i % kTStages]), (unsigned)(i / kTStages) & 1u);
     } else if (warp == 1 && lane == 0 && nch > 0) {
         // ------------------------------------------------------- MMA issuer
         int committed = 0;
@@ -204,7 +209,9 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
     pdl_wait();  // partials and outputs are read / written by neighbouring kernels
     bool ok = nch > 0;
     if (ok) {
-        ok = mbar_wait(smem_addr(&done), 0u, p.err, nullptr, kSiteFull, -1);
+        // the MMA thread commits `done` after its last MMA, also after a
+        // failed wait: once it completes no MMA is in flight
+        ok = mbar_drain(smem_addr(&done), 0u);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     }
     ok = __syncthreads_and(ok && !fail);
@@ -460,8 +467,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
             if (WP == 2) tma_load_2d(st + kWOff + kWW, &tw_lo, x, n0, fb);
             issued = i + 1;
         }
+        // never leave with copies in flight
         for (int i = issued > NS ? issued - NS : 0; i < issued; i++)
-            mbar_wait(smem_addr(&full[i % NS]), (unsigned)(i / NS) & 1u, p.err, nullptr, kSiteFull, i);
+            mbar_drain(smem_addr(&full[i % NS]), (unsigned)(i / NS) & 1u);
     } else if (warp == 1 && lane == 0) {
         for (int i = 0; i < nch && !fail; i++) {
             const int s = i % NS;
@@ -489,7 +497,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
         mma_commit(smem_addr(&done));
     }
     __syncwarp();
-    bool ok = mbar_wait(smem_addr(&done), 0u, p.err, nullptr, kSiteFull, -1);
+    // committed after the last MMA, also after a failed wait
+    bool ok = mbar_drain(smem_addr(&done), 0u);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     ok = __syncthreads_and(ok && !fail);
     if (ok) {
@@ -554,7 +563,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                            const __grid_constant__ CUtensorMap ta_lo, const TcParams p, int ntn, int ntiles) {
     constexpr int NS = kPersistStages;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) unsigned long long full[NS], empty[NS], acc_full[2], acc_empty[2];
+    __shared__ __align__(8) unsigned long long full[NS], empty[NS], acc_full[2], acc_empty[2], done;
     __shared__ unsigned tmem_slot;
     __shared__ int fail;
     const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
@@ -569,6 +578,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             mbar_init(smem_addr(&acc_full[b]), 1);
             mbar_init(smem_addr(&acc_empty[b]), 1);
         }
+        mbar_init(smem_addr(&done), 1);
         fail = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -606,8 +616,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                 }
             }
             // never leave with copies in flight
-            for (int q = g > NS ? g - NS : 0; q < g; q++)
-                mbar_wait(smem_addr(&full[q % NS]), (unsigned)(q / NS) & 1u, p.err, nullptr, kSiteFull, q);
+            for (int q = g > NS ? g - NS : 0; q < g; q++) mbar_drain(smem_addr(&full[q % NS]), (unsigned)(q / NS) & 1u);
         }
     } else if (warp == kPersistEpiWarps + 1) {
         if (lane == 0) {
@@ -642,6 +651,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                 }
                 mma_commit(smem_addr(&acc_full[ab]));  // (also after a failed wait: releases the epilogue)
             }
+            mma_commit(smem_addr(&done));  // completes once no MMA of this CTA is in flight
         }
     } else {
         // epilogue warps
@@ -678,8 +688,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (fail && threadIdx.x == 0) atomicCAS(p.err, 0, kErrPipeTimeout);
-    if (warp == 0)
+    if (warp == 0) {
+        // no MMA may still write the accumulators being released
+        if (lane == 0) mbar_drain(smem_addr(&done), 0u);
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kWN) : "memory");
+    }
 }
 
 // A [M][lda] f32 -> A_hi, A_lo [rows][K] bf16 with A = A_hi + A_lo (rows >= M
@@ -899,11 +914,21 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
     const dim3 grid((a.N + kTM - 1) / kTM, splits, mtiles);
+    // failure-path test: an armed launch (never one being captured) withholds
+    // a stage; the hook word is written and complete before the launch
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    VB_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+    const bool inject = cs == cudaStreamCaptureStatusNone && fault_take(kFaultGemmStage);
+    if (inject) {
+        VB_CUDA_TRY(set_fault_word(1, s));
+        VB_CUDA_TRY(cudaStreamSynchronize(s));
+    }
     const cudaError_t ce =
         wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages>, grid, kTThreads, tc_smem(2, kPStages), s, mwh, mwl, mah,
                              mal, p)
                 : launch_pdl(tc_gemm_kernel<1, kQStages>, grid, kTThreads, tc_smem(1, kQStages), s, mwh, mwl, mah,
                              mal, p);
+    if (inject) VB_CUDA_TRY(set_fault_word(0, s));
     if (ce != cudaSuccess) return cuda_fail(ce, "tc_gemm_kernel launch");
     if (splits == 1 || a.partials_only) return VB_OK;
     GemmArgs g{};

@@ -47,6 +47,12 @@ class VBLayerHost(C.Structure):
         "input_norm", "post_norm", "wq", "wk", "wv", "wo", "q_norm", "k_norm", "wg", "wu", "wd")]
 
 
+class VBLayerHostQ8(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "input_norm", "post_norm", "q_norm", "k_norm", "wq", "wk", "wv", "wo", "wg", "wu", "wd",
+        "sq", "sk", "sv", "so", "sg", "su", "sd")]
+
+
 _LIB = None
 
 # name -> (restype, argtypes)
@@ -54,6 +60,7 @@ _P, _I, _Z, _F, _L = C.c_void_p, C.c_int, C.c_size_t, C.c_float, C.c_int64
 _SIGS = {
     "vb_last_error": (C.c_char_p, []),
     "vb_version": (C.c_char_p, []),
+    "vb_debug_arm_fault": (_I, [_I]),
     "vb_device_count": (_I, []),
     "vb_device_name": (_I, [_I, C.c_char_p, _Z]),
     "vb_free_memory": (_I, [_I, C.POINTER(C.c_size_t)]),
@@ -83,6 +90,7 @@ _SIGS = {
     "vb_engine_destroy": (_I, [_P]),
     "vb_engine_set_globals": (_I, [_P, _P, _P]),
     "vb_engine_set_layer": (_I, [_P, _I, C.POINTER(VBLayerHost)]),
+    "vb_engine_set_layer_q8": (_I, [_P, _I, C.POINTER(VBLayerHostQ8)]),
     "vb_engine_quantize": (_I, [_P]),
     "vb_engine_is_quantized": (_I, [_P]),
     "vb_engine_weight_bytes": (_Z, [_P]),
@@ -155,6 +163,12 @@ def synth_normal(n: int, seed: int, std: float = 0.02) -> np.ndarray:
     return out
 
 
+def debug_arm_fault(site: int):
+    """Arms the failure-path test hook for one launch (1 = clustered step,
+    2 = tensor-core GEMM; 0 disarms)."""
+    check(lib().vb_debug_arm_fault(int(site)))
+
+
 def device_count() -> int:
     return lib().vb_device_count()
 
@@ -206,6 +220,31 @@ class Engine:
             arrs = {k: np.ascontiguousarray(weights[v], dtype=np.float32) for k, v in names.items()}
             lh = VBLayerHost(**{k: a.ctypes.data for k, a in arrs.items()})
             check(lib().vb_engine_set_layer(self.h, i, C.byref(lh)))
+        return self
+
+    def load_quantized(self, weights: dict, qlayers):
+        """Uploads the f32 globals and norms from `weights` and, per layer,
+        already-quantized projections: qlayers[i] = {name: (int8 [rows][cols],
+        f32 scales [rows])} for name in wq wk wv wo wg wu wd (the reference's
+        QuantLayer).  The engine then holds exactly these INT8 weights."""
+        emb = np.ascontiguousarray(weights["model.embed_tokens.weight"], dtype=np.float32)
+        fn = np.ascontiguousarray(weights["model.norm.weight"], dtype=np.float32)
+        check(lib().vb_engine_set_globals(self.h, _ptr(emb), _ptr(fn)))
+        keep = []
+        for i in range(self.vcfg.layers):
+            names = layer_names(i)
+            f = {k: np.ascontiguousarray(weights[names[k]], dtype=np.float32)
+                 for k in ("input_norm", "post_norm", "q_norm", "k_norm")}
+            args = {k: a.ctypes.data for k, a in f.items()}
+            for k, sk in (("wq", "sq"), ("wk", "sk"), ("wv", "sv"), ("wo", "so"), ("wg", "sg"),
+                          ("wu", "su"), ("wd", "sd")):
+                q, sc = qlayers[i][k]
+                q = np.ascontiguousarray(q, dtype=np.int8)
+                sc = np.ascontiguousarray(sc, dtype=np.float32)
+                keep += [q, sc]
+                args[k], args[sk] = q.ctypes.data, sc.ctypes.data
+            keep += list(f.values())
+            check(lib().vb_engine_set_layer_q8(self.h, i, C.byref(VBLayerHostQ8(**args))))
         return self
 
     def load_bf16(self, weights: dict):
