@@ -475,6 +475,33 @@ def trace_breakdown2(tr, layers=28, stride=2048):
     return out
 
 
+def profile_bs1(mode, prompt_len, n_tokens, weights, cfg, dev=0, path=-1):
+    """For ncu --profile-from-start off: n_tokens greedy decode steps bracketed
+    by cudaProfilerStart/Stop after the prompt and a warm-up, so a launch list
+    holds exactly those steps' kernels."""
+    import numpy as np
+    import torch
+
+    import vb200
+    import vbsynth
+    e = vb200.Engine(cfg, device=dev).load(weights)
+    if mode == "int8":
+        e.quantize()
+    e.set_path(path)
+    prompt = vbsynth.prompt_ids(prompt_len, 77 + prompt_len, cfg["vocab_size"])
+    e.reset_cache(prompt_len + n_tokens + 16)
+    lg = e.prefill(prompt, want_logits=True)
+    tok = int(e.decode(int(np.argmax(lg)), 8)[-1])
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    e.decode(tok, n_tokens)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    out = {"mode": mode, "path": e.path(), "graph_nodes": e.graph_nodes(), "tokens": n_tokens}
+    e.close()
+    return out
+
+
 def run_bs1(mode, prompt_len, n_new, weights, cfg, dev=0, warm=8, path=-1, trace=False, lm8=False):
     import numpy as np
     import torch
@@ -600,6 +627,9 @@ def main():
                     help="--only bs1: 1 per-op graph, 2 clustered step, -1 the engine's automatic choice")
     ap.add_argument("--trace", action="store_true",
                     help="--only bs1: per-phase trace of the clustered step (needs a VB_STEP_TRACE=1 build)")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="--only bs1: decode this many tokens inside cudaProfilerStart/Stop (for ncu "
+                         "--profile-from-start off) instead of the timed run")
     ap.add_argument("--ctx", type=int, default=2048, help="--only attn: context length")
     ap.add_argument("--shape", default=None, help="--only gemv: one of q,k,v,o,gate,up,down,lm_head")
     args = ap.parse_args()
@@ -619,6 +649,10 @@ def main():
         cfg = vbsynth.qwen3_config()
         w = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
         P, G = (32, 128) if args.mode == "f32" else (512, 512)
+        if args.profile:
+            print(json.dumps({"bs1_profile": profile_bs1(args.mode, P + G // 2, args.profile, w, cfg,
+                                                         dev=local_rank, path=args.path)}), flush=True)
+            return 0
         r = run_bs1(args.mode, P, min(G, args.steps), w, cfg, dev=local_rank, path=args.path,
                     trace=args.trace)
         print(json.dumps({"bs1": r}), flush=True)

@@ -153,10 +153,10 @@ VB_API vb_status vb_attn_decode(const float* q, const float* kcache, const float
  * that cannot afford cudaMalloc's implicit synchronisation).  No counterpart
  * in the reference.  The split partials live in a 1 MiB array compiled into
  * the library (held by every GPU that loads it until the process exits).  The
- * split count is capped at what that array holds (H * splits * 130 floats,
- * plus 512 B: 125 splits for 16 heads), so every context length runs, with
- * longer splits past about 32k positions; only a head count too large for one
- * split (H > 2015) returns VB_ERR_UNSUPPORTED.  The first call on a device (and
+ * split count is capped at what that array holds (H * splits * 132 floats,
+ * plus 512 B: 124 splits for 16 heads), so every context length runs, with
+ * longer splits past about 8k positions; only a head count too large for one
+ * split (H > 1984) returns VB_ERR_UNSUPPORTED.  The first call on a device (and
  * the first after the device's context was replaced, e.g. by cudaDeviceReset)
  * looks up the array's device address, so make that call before any stream
  * capture.  All calls share the array: calls that overlap on the GPU
@@ -171,7 +171,8 @@ VB_API vb_status vb_attn_decode_noalloc(const float* q, const float* kcache,
  * q [B, H, D]; element (b, pos, kvh, d) of K/V is at
  *   base + b*stride_b + pos*stride_pos + kvh*stride_h + d   (floats);
  * lens[b] (device int array) is each sequence's cache length (>=1, <= n_max).
- * workspace: vb_attn_workspace_bytes(B, H, n_max) bytes of device memory.
+ * workspace: vb_attn_workspace_bytes(B, H, n_max) bytes of device memory,
+ * 16-byte aligned.
  * out [B, H, D].  No reference counterpart beyond generate.cpp:73-105 applied
  * per sequence. */
 VB_API size_t vb_attn_workspace_bytes(int B, int H, int n_max);

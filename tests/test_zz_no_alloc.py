@@ -48,18 +48,19 @@ def test_noalloc_matches_allocating_entry_point_twice():
 
 
 def test_noalloc_long_contexts_run_with_capped_splits():
-    # 16/8 heads: past ~32k positions the allocating entry point would use more
-    # splits than the 1 MiB array holds; the no-alloc one caps the split count
-    # (longer splits) and must still agree.  40960 is the model's
-    # max_position_embeddings; 32000 is just below the cap, 32256 just above.
-    for n in (32000, 32256, 40960):
+    # 16/8 heads: past ~8k positions the allocating entry point uses more
+    # splits (up to 296, of >= 64 positions) than the 1 MiB array holds (124);
+    # the no-alloc one caps the split count (longer splits) and must still
+    # agree.  40960 is the model's max_position_embeddings; 7936 is the last
+    # length whose split count fits, 8000 the first that is capped.
+    for n in (7936, 8000, 32768, 40960):
         diff = _compare(n, n)
         assert np.isfinite(diff) and diff <= 2e-5, (n, diff)
         torch.cuda.empty_cache()
 
 
 def test_noalloc_refuses_heads_beyond_the_static_buffer():
-    # one split of 2048 heads needs 2048 x 130 floats + 512 B > 1 MiB, so the
+    # one split of 2048 heads needs 2048 x 132 floats + 512 B > 1 MiB, so the
     # size check refuses it before anything is launched (GQA group 2 is a
     # shape the attention kernels take, so only the size check can refuse it)
     h, kvh, n = 2048, 1024, 4

@@ -75,8 +75,11 @@ def compile_one(src, verbose=False, ptxas_v=False):
     return obj, r.stderr
 
 
-def build(force=False, verbose=False, ptxas_v=False, defines=()):
-    BUILD.mkdir(exist_ok=True)
+def build(force=False, verbose=False, ptxas_v=False, defines=(), build_dir=None, out=None):
+    global BUILD
+    if build_dir:
+        BUILD = Path(build_dir)
+    BUILD.mkdir(parents=True, exist_ok=True)
     LIB.mkdir(exist_ok=True)
     DEFINES[:] = sorted(defines)
     stamp = BUILD / "defines.txt"
@@ -94,7 +97,8 @@ def build(force=False, verbose=False, ptxas_v=False, defines=()):
         for s, (_, log) in zip(srcs, results):
             if log:
                 print(f"== {s.name}\n{log}")
-    out = LIB / LIBNAME
+    out = Path(out) if out else LIB / LIBNAME
+    out.parent.mkdir(parents=True, exist_ok=True)
     if out.exists() and not force and all(o.stat().st_mtime <= out.stat().st_mtime for o in objs):
         return out
     cudalib = cuda_home() / "lib64"
@@ -114,8 +118,10 @@ def main():
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage")
     ap.add_argument("--define", action="append", default=[], help="NAME=VALUE passed to nvcc as -D")
+    ap.add_argument("--build-dir", default=None, help="object directory (default verbum.cpp_b200/_build)")
+    ap.add_argument("--out", default=None, help="library path (default verbum.cpp_b200/lib/libverbum_b200.so)")
     a = ap.parse_args()
-    out = build(a.force, a.verbose, a.ptxas_v, a.define)
+    out = build(a.force, a.verbose, a.ptxas_v, a.define, a.build_dir, a.out)
     print(out)
 
 

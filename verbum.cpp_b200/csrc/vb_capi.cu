@@ -165,6 +165,9 @@ vb_status vb_matmul_nt_f32(const float* A, const float* W, float* C, int M, int 
         g.y = C;
         g.N = N;
         g.K = K;
+        // weights that fit one prefetched slice per SM: the prefetching GEMV
+        // (its weights stream in while the previous kernel on the stream runs)
+        if (K <= 4096 && gemv_pf_parts(N, K, false, kEpiStore) == 1) return launch_gemv_pf(g, false, kProNone, kEpiStore, s);
         return launch_gemv(g, false, kProNone, kEpiStore, s);
     }
     if (M <= 64 && K % 32 == 0) {
@@ -205,6 +208,7 @@ vb_status vb_matmul_nt_q8(const float* A, const int8_t* Wq, const float* scales,
         g.y = C;
         g.N = N;
         g.K = K;
+        if (K <= 4096 && gemv_pf_parts(N, K, true, kEpiStore) == 1) return launch_gemv_pf(g, true, kProNone, kEpiStore, s);
         return launch_gemv(g, true, kProNone, kEpiStore, s);
     }
     if (M <= 64 && K % 32 == 0) {
@@ -324,7 +328,8 @@ vb_status vb_attn_decode_batched(const float* q, const float* k, const float* v,
     if (!q || !k || !v || !out || !lens || !workspace) return fail(VB_ERR_ARG, "null pointer");
     if (B <= 0 || H <= 0 || KVH <= 0 || n_max <= 0) return fail(VB_ERR_ARG, "attention: non-positive shape");
     if (D != 128) return fail(VB_ERR_UNSUPPORTED, "attention: head_dim must be 128");
-    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (stride_b | stride_pos | stride_h) & 3)
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(workspace) ||
+        (stride_b | stride_pos | stride_h) & 3)
         return fail(VB_ERR_UNSUPPORTED, "attention: 16-byte alignment required");
     AttnArgs a{};
     a.q = q; a.k = k; a.v = v; a.out = out; a.lens = lens;

@@ -86,6 +86,18 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
 // subtraction of 2^23 + 128 then leaves b exactly.  This is the standard
 // "magic number" integer-to-float construction (IEEE-754 binary32 has a
 // 23-bit mantissa, so every integer below 2^24 is representable).
+// Position of x[i] inside a GEMV's shared copy of its input.  INT8 lanes
+// load 16 consecutive weights; storing the matching activations
+// lane-interleaved per 512-element chunk makes every lane's float4 reads
+// bank-conflict free.
+template <bool Q8>
+__device__ __forceinline__ int xs_index(int i) {
+    if (!Q8) return i;
+    const int c = i >> 9, r = i & 511;
+    const int l = r >> 4, j = (r >> 2) & 3, e = r & 3;
+    return (c << 9) + (j << 7) + (l << 2) + e;
+}
+
 struct f4 {
     float v[4];
 };

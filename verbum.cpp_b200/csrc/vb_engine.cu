@@ -116,6 +116,44 @@ vb_status engine_check_err(vb_engine* e) {
     }
 }
 
+// A layer projection of the per-op step: the prefetching GEMV (weights in
+// shared memory before it waits for the previous kernel) when its slices fit,
+// the streaming GEMV otherwise.
+// Weights of GEMV number j of the step (4 per layer: q|k|v, o, gate|up,
+// down; then the lm_head): base pointer and bytes, for the L2 look-ahead.
+static void step_weights(const vb_engine* e, int j, const void** w, size_t* bytes) {
+    const vb_config& c = e->cfg;
+    const bool q8 = e->quantized;
+    const size_t es = q8 ? 1 : 4, hd = c.hidden;
+    *w = nullptr;
+    *bytes = 0;
+    const int l = j / 4, k = j % 4;
+    if (l >= c.layers) {  // the lm_head: its first part (it streams the rest at full rate)
+        const size_t lm = (size_t)c.vocab * hd * (e->lm_int8 ? 1 : 4);
+        const size_t part = (size_t)48 << 20;
+        const size_t off = (size_t)(j - 4 * c.layers) * part;
+        if (off < lm) {
+            *w = static_cast<const char*>(e->lm_int8 ? (const void*)e->lm_q8 : (const void*)e->embed) + off;
+            *bytes = lm - off < part ? lm - off : part;
+        }
+        return;
+    }
+    const vb_layer_dev& L = e->L[l];
+    switch (k) {
+        case 0: *w = q8 ? (const void*)L.qqkv : (const void*)L.wqkv; *bytes = (size_t)e->qkv_rows * hd * es; break;
+        case 1: *w = q8 ? (const void*)L.qo : (const void*)L.wo; *bytes = hd * e->q_width * es; break;
+        case 2: *w = q8 ? (const void*)L.qgu : (const void*)L.wgu; *bytes = 2 * (size_t)c.ffn * hd * es; break;
+        default: *w = q8 ? (const void*)L.qd : (const void*)L.wd; *bytes = hd * (size_t)c.ffn * es; break;
+    }
+}
+
+static vb_status step_gemv(vb_engine* e, int j, GemvArgs g, bool q8, int pro, int epi, cudaStream_t s) {
+    g.err = e->d_err;
+    step_weights(e, j + 2, &g.l2_ahead, &g.l2_ahead_bytes);  // two GEMVs ahead
+    if (g.K <= 4096 && gemv_pf_parts(g.N, g.K, q8, epi) > 0) return launch_gemv_pf(g, q8, pro, epi, s);
+    return launch_gemv(g, q8, pro, epi, s);
+}
+
 vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
     const vb_config& c = e->cfg;
     const bool q8 = e->quantized;
@@ -133,7 +171,13 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         g.y = e->qkv;
         g.N = e->qkv_rows;
         g.K = c.hidden;
-        if ((st = launch_gemv(g, q8, kProRms, kEpiStore, s))) return st;
+        // this layer's cached K / V rows into L2 for the attention below
+        g.kv_k = e->kc + l * layer_kv;
+        g.kv_v = e->vc + l * layer_kv;
+        g.kv_pos = e->d_pos;
+        g.kv_heads = c.kv_heads;
+        g.kv_stride_h = (int64_t)e->max_seq * c.head_dim;
+        if ((st = step_gemv(e, 4 * l + 0, g, q8, kProRms, kEpiStore, s))) return st;
 
         QkNormArgs qa{};
         qa.qkv = e->qkv;
@@ -185,7 +229,7 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         o.y = e->x;
         o.N = c.hidden;
         o.K = e->q_width;
-        if ((st = launch_gemv(o, q8, kProNone, kEpiResidual, s))) return st;
+        if ((st = step_gemv(e, 4 * l + 1, o, q8, kProNone, kEpiResidual, s))) return st;
 
         GemvArgs gu{};
         gu.x = e->x;
@@ -196,7 +240,7 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         gu.y = e->h;
         gu.N = 2 * c.ffn;
         gu.K = c.hidden;
-        if ((st = launch_gemv(gu, q8, kProRms, kEpiSwiGLU, s))) return st;
+        if ((st = step_gemv(e, 4 * l + 2, gu, q8, kProRms, kEpiSwiGLU, s))) return st;
 
         GemvArgs dn{};
         dn.x = e->h;
@@ -205,7 +249,7 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         dn.y = e->x;
         dn.N = c.hidden;
         dn.K = c.ffn;
-        if ((st = launch_gemv(dn, q8, kProNone, kEpiResidual, s))) return st;
+        if ((st = step_gemv(e, 4 * l + 3, dn, q8, kProNone, kEpiResidual, s))) return st;
     }
     GemvArgs lm{};
     lm.x = e->x;

@@ -1,0 +1,308 @@
+// vb_gemv_pf.cu -- batch-1 GEMV whose weights are in shared memory before it
+// waits for the kernel in front of it.
+//
+// y = W . x for one activation row (ops.cpp:42-70 matmul_nt, quant.cpp:43-70
+// matmul_nt_q8), the projections of one decode step.  One CTA per SM owns a
+// contiguous slice of W's rows (at most kPfSliceBytes).  Its first act is to
+// request the whole slice with bulk copies; only then does it release its own
+// successor (griddepcontrol.launch_dependents) and wait for its predecessor
+// (griddepcontrol.wait).  Launched back to back with programmatic dependent
+// launch, kernel i+1's weights therefore stream in while kernel i computes:
+// what is left on the step's dependency chain is reading x, the dot products
+// out of shared memory and the stores.  The slice budget keeps two such CTAs
+// on one SM (the running kernel's and the next one's).
+//
+// Arithmetic per row as the streaming GEMV: lanes stride K (16-byte groups),
+// f32 FMAs, one warp reduction; INT8 bytes dequantised exactly (byte into the
+// mantissa of 2^23, one subtraction) and the row scale applied after the sum.
+#include <cuda_bf16.h>
+
+#include <atomic>
+
+#include "vb_kernels.cuh"
+#include "vb_pipe.cuh"
+
+namespace vb {
+namespace {
+
+constexpr int kPfThreads = 256;
+constexpr int kPfWarps = kPfThreads / 32;
+constexpr int kPfChunk = 32768;  // bytes per bulk copy
+constexpr int kPfMaxK = 4096;
+
+// Bounded wait (thread 0) for the slice; no error word on this path's
+// arguments is required: a timeout is reported through a.err when present.
+__device__ __noinline__ bool pf_wait_slice(unsigned a) {
+    const unsigned long long t0 = now_ns();
+    for (unsigned it = 1;; it++) {
+        if (mbar_try(a, 0u)) return true;
+        if ((it & 255u) == 0 && now_ns() - t0 > kWaitNs) return false;
+    }
+}
+
+template <bool Q8, int PRO, int EPI>
+__global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) unsigned char pf_smem[];
+    __shared__ __align__(8) unsigned long long full;
+    __shared__ double red[kPfWarps];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K, G = gridDim.x, c = blockIdx.x;
+    constexpr int unit = (EPI == kEpiSwiGLU) ? 2 : 1;  // gate/up rows stay together
+    const int units = a.N / unit;
+    const int u0 = (int)((long long)c * units / G), u1 = (int)((long long)(c + 1) * units / G);
+    const int r0 = u0 * unit, rows = (u1 - u0) * unit;
+    const size_t row_bytes = (size_t)K * (Q8 ? 1 : 4);
+    const size_t bytes = (size_t)rows * row_bytes;
+    unsigned char* wsm = pf_smem;
+    float* xs = reinterpret_cast<float*>(pf_smem + kPfSliceBytes);
+
+    // 1. the slice: requested before anything else (it depends on no kernel)
+    if (tid == 0) {
+        mbar_init(smem_addr(&full), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (bytes) {
+            unsigned long long pol;
+            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+            mbar_expect_tx(smem_addr(&full), (unsigned)bytes);
+            const char* src = static_cast<const char*>(a.W) + (size_t)r0 * row_bytes;
+            for (size_t off = 0; off < bytes; off += kPfChunk) {
+                const unsigned n = (unsigned)(bytes - off < (size_t)kPfChunk ? bytes - off : (size_t)kPfChunk);
+                bulk_g2s(smem_addr(wsm + off), src + off, n, smem_addr(&full), pol);
+            }
+        }
+    }
+    // 1b. a later kernel's weights into L2 (this CTA's share, 16-byte pieces),
+    //     so the HBM stream runs ahead of the kernels that consume it
+    if (tid == 32 && a.l2_ahead && a.l2_ahead_bytes) {
+        const size_t share = (a.l2_ahead_bytes / G + 15) & ~size_t(15);
+        const size_t b0 = share * c;
+        const size_t b1 = b0 + share < a.l2_ahead_bytes ? b0 + share : a.l2_ahead_bytes;
+        const char* base = static_cast<const char*>(a.l2_ahead);
+        for (size_t off = b0; off + 16 <= b1; off += kPfChunk) {
+            const size_t n = (b1 - off < (size_t)kPfChunk ? b1 - off : (size_t)kPfChunk) & ~size_t(15);
+            if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"((unsigned)n) : "memory");
+        }
+    }
+    // 1c. the attention's cached K / V rows into L2: span s = (head, K or V)
+    //     of pos * 512 bytes, split into G / (2 heads) pieces
+    if (tid == 64 && a.kv_k && a.kv_heads > 0) {
+        const int spans = 2 * a.kv_heads;
+        const int pieces = G / spans > 0 ? G / spans : 1;
+        const int sp = c % spans, pc = c / spans;
+        const int pos = *a.kv_pos;  // written before this step (positions already cached)
+        if (pc < pieces && pos > 0) {
+            const size_t span = (size_t)pos * 512;
+            const size_t share = (span / pieces + 15) & ~size_t(15);
+            const size_t b0 = share * pc, b1 = b0 + share < span ? b0 + share : span;
+            const float* h = ((sp & 1) ? a.kv_v : a.kv_k) + (size_t)(sp >> 1) * a.kv_stride_h;
+            const char* base = reinterpret_cast<const char*>(h);
+            for (size_t off = b0; off + 16 <= b1; off += kPfChunk) {
+                const size_t n = (b1 - off < (size_t)kPfChunk ? b1 - off : (size_t)kPfChunk) & ~size_t(15);
+                if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"((unsigned)n) : "memory");
+            }
+        }
+    }
+    // 2. let the next kernel start prefetching its own slice, then wait for
+    //    the kernels this one reads from
+    pdl_trigger();
+    pdl_wait();
+
+    // 3. x (normalised when PRO is kProRms), laid out for conflict-free reads
+    const float* x = a.x;
+    if (a.x_tok) x += (size_t)(*a.x_tok) * (size_t)K;
+    float sc = 1.0f;
+    if (PRO == kProRms) {
+        double ss = 0.0;
+        for (int i = tid; i < K; i += kPfThreads) {
+            const float v = x[i];
+            ss += (double)v * (double)v;
+        }
+        sc = rms_scale(block_sum_d<kPfThreads>(ss, red), K, a.eps);
+    }
+    for (int i = tid; i < K; i += kPfThreads) {
+        float v = x[i];
+        if (PRO == kProRms) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[i]);
+        xs[xs_index<Q8>(i)] = v;
+    }
+
+    // 4. the slice has landed (thread 0 waits; every thread then observes the
+    //    completed phase itself, which orders its reads after the copies)
+    int ok = 1;
+    if (tid == 0 && bytes) ok = pf_wait_slice(smem_addr(&full)) ? 1 : 0;
+    if (!__syncthreads_and(ok)) {
+        // a copy that never completed: record it, give the copies in flight
+        // their bound to land (the shared memory goes to the next CTA), leave
+        if (tid == 0) {
+            if (a.err) atomicCAS(a.err, 0, kErrPipeTimeout);
+            mbar_drain(smem_addr(&full), 0u);
+        }
+        return;
+    }
+    if (bytes) (void)mbar_try(smem_addr(&full), 0u);
+
+    // 5. dot products: row pairs (or single rows) round-robin over the warps
+    constexpr int R = 2;
+    for (int rg = warp * R; rg < rows; rg += kPfWarps * R) {
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = 0.0f;
+        const int nr = rows - rg < R ? rows - rg : R;
+        if (!Q8) {
+            const int K4 = K >> 2;
+            for (int k4 = lane; k4 < K4; k4 += 32) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + 4 * k4);
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (r < nr) {
+                        const float4 w = *reinterpret_cast<const float4*>(wsm + (size_t)(rg + r) * row_bytes + 16 * k4);
+                        acc[r] = fmaf(w.x, xv.x, acc[r]);
+                        acc[r] = fmaf(w.y, xv.y, acc[r]);
+                        acc[r] = fmaf(w.z, xv.z, acc[r]);
+                        acc[r] = fmaf(w.w, xv.w, acc[r]);
+                    }
+                }
+            }
+        } else {
+            const int G16 = K >> 4;
+            for (int gi = lane; gi < G16; gi += 32) {
+                const float* xc = xs + ((gi >> 5) << 9) + 4 * lane;
+                const float4 x0 = *reinterpret_cast<const float4*>(xc);
+                const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
+                const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
+                const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (r < nr) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(wsm + (size_t)(rg + r) * row_bytes + 16 * gi);
+                        const f4 a0 = i8x4_to_f32(w.x), a1 = i8x4_to_f32(w.y);
+                        const f4 a2 = i8x4_to_f32(w.z), a3 = i8x4_to_f32(w.w);
+                        float s = acc[r];
+                        s = fmaf(a0.v[0], x0.x, s); s = fmaf(a0.v[1], x0.y, s);
+                        s = fmaf(a0.v[2], x0.z, s); s = fmaf(a0.v[3], x0.w, s);
+                        s = fmaf(a1.v[0], x1.x, s); s = fmaf(a1.v[1], x1.y, s);
+                        s = fmaf(a1.v[2], x1.z, s); s = fmaf(a1.v[3], x1.w, s);
+                        s = fmaf(a2.v[0], x2.x, s); s = fmaf(a2.v[1], x2.y, s);
+                        s = fmaf(a2.v[2], x2.z, s); s = fmaf(a2.v[3], x2.w, s);
+                        s = fmaf(a3.v[0], x3.x, s); s = fmaf(a3.v[1], x3.y, s);
+                        s = fmaf(a3.v[2], x3.z, s); s = fmaf(a3.v[3], x3.w, s);
+                        acc[r] = s;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            acc[r] = warp_sum(acc[r]);
+            if (Q8 && r < nr) acc[r] *= a.scales[r0 + rg + r];
+        }
+        if (lane == 0) {
+            const int row = r0 + rg;
+            if (EPI == kEpiSwiGLU) {
+                a.y[row >> 1] = silu_f(acc[0]) * acc[1];  // gate row 2j, up row 2j + 1
+            } else {
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    if (r < nr) {
+                        if (EPI == kEpiResidual) a.y[row + r] = a.y[row + r] + acc[r];
+                        else a.y[row + r] = acc[r];
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <bool Q8, int PRO>
+cudaError_t pf_dispatch(const GemvArgs& a, int epi, int grid, size_t smem, cudaStream_t s) {
+    switch (epi) {
+        case kEpiStore: return launch_pdl(gemv_pf_kernel<Q8, PRO, kEpiStore>, grid, kPfThreads, smem, s, a);
+        case kEpiResidual: return launch_pdl(gemv_pf_kernel<Q8, PRO, kEpiResidual>, grid, kPfThreads, smem, s, a);
+        default: return launch_pdl(gemv_pf_kernel<Q8, PRO, kEpiSwiGLU>, grid, kPfThreads, smem, s, a);
+    }
+}
+
+template <bool Q8, int PRO, int EPI>
+cudaError_t pf_attr() {
+    return cudaFuncSetAttribute(gemv_pf_kernel<Q8, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(kPfSliceBytes + sizeof(float) * kPfMaxK));
+}
+
+}  // namespace
+
+int gemv_pf_parts(int N, int K, bool q8, int epi) {
+    const int unit = epi == kEpiSwiGLU ? 2 : 1;
+    const size_t row_bytes = (size_t)K * (q8 ? 1 : 4);
+    const size_t units = (size_t)N / unit;
+    // the smallest part count whose largest per-CTA slice fits the budget
+    for (int parts = 1; parts <= 8; parts++) {
+        const size_t units_part = (units + parts - 1) / parts;
+        const size_t per_cta = (units_part + kPfCtas - 1) / kPfCtas * unit * row_bytes;
+        if (per_cta <= kPfSliceBytes) return parts;
+    }
+    return 0;
+}
+
+vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s) {
+    if (a.N <= 0 || a.K <= 0) return fail(VB_ERR_ARG, "gemv: empty shape");
+    if (q8 ? (a.K % 16) : (a.K % 4)) return fail(VB_ERR_UNSUPPORTED, "gemv: K alignment");
+    if (a.K > kPfMaxK) return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: K > 4096");
+    if (epi != kEpiStore && epi != kEpiResidual && epi != kEpiSwiGLU)
+        return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: epilogue");
+    if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemv: swiglu needs even N");
+    if ((reinterpret_cast<uintptr_t>(a.W) & 15u) != 0) return fail(VB_ERR_UNSUPPORTED, "gemv: W must be 16-byte aligned");
+    const int parts = gemv_pf_parts(a.N, a.K, q8, epi);
+    if (parts == 0) return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: weights too large for the slices");
+    {
+        static std::atomic<unsigned long long> done{0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const unsigned long long bit = 1ull << (dev & 63);
+        if (!(done.load() & bit)) {
+            cudaError_t ce = cudaSuccess;
+            if (ce == cudaSuccess) ce = pf_attr<false, kProNone, kEpiStore>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProNone, kEpiResidual>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProNone, kEpiSwiGLU>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProRms, kEpiStore>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProRms, kEpiResidual>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProRms, kEpiSwiGLU>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProNone, kEpiStore>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProNone, kEpiResidual>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProNone, kEpiSwiGLU>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiStore>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiResidual>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiSwiGLU>();
+            if (ce != cudaSuccess) return cuda_fail(ce, "prefetching gemv: shared memory attribute");
+            done.fetch_or(bit);
+        }
+    }
+    const int unit = epi == kEpiSwiGLU ? 2 : 1;
+    const int units = a.N / unit;
+    const size_t es = q8 ? 1 : 4;
+    const size_t smem = kPfSliceBytes + sizeof(float) * (size_t)(q8 ? ((a.K + 511) / 512) * 512 : a.K);
+    for (int p = 0; p < parts; p++) {
+        const int uu0 = (int)((long long)p * units / parts), uu1 = (int)((long long)(p + 1) * units / parts);
+        GemvArgs g = a;
+        const int n0 = uu0 * unit;
+        g.N = (uu1 - uu0) * unit;
+        if (g.N == 0) continue;
+        g.W = static_cast<const char*>(a.W) + (size_t)n0 * a.K * es;
+        if (q8) g.scales = a.scales + n0;
+        g.y = a.y + (epi == kEpiSwiGLU ? n0 / 2 : n0);
+        if (p > 0) g.kv_k = nullptr;           // the cache rows once, by the first part
+        if (a.l2_ahead && a.l2_ahead_bytes) {  // each part pulls its share of the look-ahead
+            const size_t share = (a.l2_ahead_bytes / parts + 15) & ~size_t(15);
+            const size_t b0 = share * p;
+            g.l2_ahead = static_cast<const char*>(a.l2_ahead) + b0;
+            g.l2_ahead_bytes = b0 < a.l2_ahead_bytes ? (a.l2_ahead_bytes - b0 < share ? a.l2_ahead_bytes - b0 : share) : 0;
+        }
+        const int grid = g.N / unit < kPfCtas ? g.N / unit : kPfCtas;
+        const cudaError_t ce = q8 ? (pro == kProRms ? pf_dispatch<true, kProRms>(g, epi, grid, smem, s)
+                                                    : pf_dispatch<true, kProNone>(g, epi, grid, smem, s))
+                                  : (pro == kProRms ? pf_dispatch<false, kProRms>(g, epi, grid, smem, s)
+                                                    : pf_dispatch<false, kProNone>(g, epi, grid, smem, s));
+        if (ce != cudaSuccess) return cuda_fail(ce, "gemv_pf_kernel launch");
+    }
+    return VB_OK;
+}
+
+}  // namespace vb

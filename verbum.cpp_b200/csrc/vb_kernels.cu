@@ -26,16 +26,6 @@ constexpr int kNumSMs = 148;
 // better() (argmax order, lowest index on ties) and silu_f() (model.cpp:15-18:
 // x / (1 + exp(-x)), IEEE division, accurate expf) come from vb_pipe.cuh.
 
-// Position of x[i] inside the per-CTA shared copy.  INT8 lanes load 16
-// consecutive weights; storing the matching activations lane-interleaved per
-// 512-element chunk makes every lane's float4 reads bank-conflict free.
-template <bool Q8>
-__device__ __forceinline__ int xs_index(int i) {
-    if (!Q8) return i;
-    const int c = i >> 9, r = i & 511;
-    const int l = r >> 4, j = (r >> 2) & 3, e = r & 3;
-    return (c << 9) + (j << 7) + (l << 2) + e;
-}
 
 // ---------------------------------------------------------------------------
 // GEMV: y = W . x with W [N, K] row-major (f32 or int8 + per-row scale).
@@ -559,36 +549,90 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
             }
         }
         const int h = kvh * G + g;
-        float* part = a.ws + (((size_t)b * a.H + h) * S + split) * (128 + 2);
-        part[2 + di] = A;
+        float* part = a.ws + (((size_t)b * a.H + h) * S + split) * kAttnPart;
+        part[4 + di] = A;
         if (di == 0) { part[0] = M; part[1] = L; }
     }
 }
 
-// grid (H, B), block 128: merges the splits of one (b, h).
-__global__ void attn_merge_kernel(AttnArgs a) {
+// grid (H, B), 256 threads: merges the S split partials of one (b, h):
+// M = max_s m_s, L = sum_s l_s e^(m_s - M), A = sum_s acc_s e^(m_s - M),
+// out = A / L.  Every thread takes a share of the maxima; then warp w sums
+// splits w, w + 8, ... (each lane 4 of the 128 dims, four splits' loads in
+// flight at once) and the 8 warp sums are added in warp order.
+constexpr int kMergeThreads = 256;
+__global__ void __launch_bounds__(kMergeThreads) attn_merge_kernel(AttnArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NW = kMergeThreads / 32;
     const int S = a.splits;
-    const float* base = a.ws + ((size_t)b * a.H + h) * S * (128 + 2);
+    const float* base = a.ws + ((size_t)b * a.H + h) * S * kAttnPart;
+    __shared__ float s_m[NW], s_l[NW];
+    __shared__ float4 s_a[NW][32];
     float M = -INFINITY;
-    for (int s = 0; s < S; s++) M = fmaxf(M, base[s * 130]);
-    float L = 0.0f, A = 0.0f;
-    for (int s = 0; s < S; s++) {
-        const float ms = base[s * 130];
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - M);
-        L = fmaf(base[s * 130 + 1], f, L);
-        A = fmaf(base[s * 130 + 2 + d], f, A);
+    for (int sp = threadIdx.x; sp < S; sp += kMergeThreads) M = fmaxf(M, base[(size_t)sp * kAttnPart]);
+    M = warp_max(M);
+    if (lane == 0) s_m[warp] = M;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < NW; w++) M = fmaxf(M, s_m[w]);
+    float L = 0.0f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+        constexpr int U = 4;
+        for (int s0 = warp; s0 < S; s0 += NW * U) {
+            float ms[U], ls[U];
+            float4 av[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int sp = s0 + NW * u;
+                if (sp < S) {
+                    const float* pp = base + (size_t)sp * kAttnPart;
+                    ms[u] = pp[0];
+                    ls[u] = pp[1];
+                    av[u] = *reinterpret_cast<const float4*>(pp + 4 + 4 * lane);
+                } else {
+                    ms[u] = -INFINITY;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (ms[u] == -INFINITY) continue;
+                const float f = expf(ms[u] - M);
+                L = fmaf(ls[u], f, L);
+                A.x = fmaf(av[u].x, f, A.x);
+                A.y = fmaf(av[u].y, f, A.y);
+                A.z = fmaf(av[u].z, f, A.z);
+                A.w = fmaf(av[u].w, f, A.w);
+            }
+        }
     }
-    const float c = (L > 0.0f) ? A / L : 0.0f;
-    const size_t o = ((size_t)b * a.H + h) * 128 + d;
-    a.out[o] = c;
-    if (a.out_hi) {
-        const __nv_bfloat16 hv = __float2bfloat16_rn(c);
-        static_cast<__nv_bfloat16*>(a.out_hi)[o] = hv;
-        static_cast<__nv_bfloat16*>(a.out_lo)[o] = __float2bfloat16_rn(c - __bfloat162float(hv));
+    if (lane == 0) s_l[warp] = L;
+    s_a[warp][lane] = A;
+    __syncthreads();
+    if (warp == 0) {
+        float Lt = 0.0f;
+        float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            Lt += s_l[w];
+            const float4 v = s_a[w][lane];
+            At.x += v.x; At.y += v.y; At.z += v.z; At.w += v.w;
+        }
+        const float c[4] = {At.x, At.y, At.z, At.w};
+        const size_t o = ((size_t)b * a.H + h) * 128 + 4 * lane;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float y = (Lt > 0.0f) ? c[e] / Lt : 0.0f;
+            a.out[o + e] = y;
+            if (a.out_hi) {
+                const __nv_bfloat16 hv = __float2bfloat16_rn(y);
+                static_cast<__nv_bfloat16*>(a.out_hi)[o + e] = hv;
+                static_cast<__nv_bfloat16*>(a.out_lo)[o + e] = __float2bfloat16_rn(y - __bfloat162float(hv));
+            }
+        }
     }
 }
 
@@ -905,18 +949,20 @@ vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
 }
 
 int attn_splits_for(int B, int KVH, int n_max) {
-    // ~16 (sequence, KV head, split) CTAs per SM, >= 256 positions per split:
-    // at 64 sequences x 8 KV heads x 2178 positions this is 5 splits, measured
-    // at 93% of HBM peak (2 splits: 86%, 16 splits: 83%)
+    // ~16 (sequence, KV head, split) CTAs per SM, >= 64 positions per split
+    // (two passes of the 8 warps' 4-position blocks): at 64 sequences x 8 KV
+    // heads x 2178 positions this is 5 splits, measured at 93% of HBM peak
+    // (2 splits: 86%, 16 splits: 83%); a single sequence gets up to 296
+    // splits, so a short cache still spreads over the SMs
     const int target = kNumSMs * 16;
-    int by_len = (n_max + 255) / 256;
+    int by_len = (n_max + kAttnMinSplit - 1) / kAttnMinSplit;
     int by_grid = (target + B * KVH - 1) / (B * KVH);
     int s = by_len < by_grid ? by_len : by_grid;
     return s < 1 ? 1 : s;
 }
 
 size_t attn_ws_bytes(int B, int H, int splits) {
-    return sizeof(float) * (size_t)B * H * splits * (128 + 2);
+    return sizeof(float) * (size_t)B * H * splits * kAttnPart;
 }
 
 vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
@@ -933,7 +979,7 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
         default: return fail(VB_ERR_UNSUPPORTED, "attention: GQA group must be 1, 2 or 4");
     }
     VB_LAUNCH_CHECK("attn_split_kernel");
-    launch_pdl(attn_merge_kernel, dim3(a.H, a.B), 128, 0, s, a);
+    launch_pdl(attn_merge_kernel, dim3(a.H, a.B), kMergeThreads, 0, s, a);
     VB_LAUNCH_CHECK("attn_merge_kernel");
     return VB_OK;
 }

@@ -5,6 +5,13 @@
 
 namespace vb {
 
+// Split-K decode attention: one partial per (sequence, head, split) is
+// kAttnPart floats -- m, l, two pad words, then the 128 accumulators (16-byte
+// aligned for vector loads) -- and a split covers at least kAttnMinSplit
+// positions.
+constexpr int kAttnPart = 132;
+constexpr int kAttnMinSplit = 64;
+
 // GEMV prologue: the input vector is used as is, or RMS-normalised with a
 // weight vector first (the rmsnorm that precedes every projection).
 enum GemvPro : int { kProNone = 0, kProRms = 1 };
@@ -27,7 +34,27 @@ struct GemvArgs {
     int N, K;
     float* part_val;       // [gridDim] (kEpiArgmax)
     int* part_idx;         // [gridDim]
+    int* err;              // optional: device error word (bounded waits)
+    const void* l2_ahead;  // optional (prefetching GEMV): bytes a later kernel reads,
+    size_t l2_ahead_bytes; //   pulled into L2 by this kernel's CTAs (a 1/grid share each)
+    // optional (prefetching GEMV): the cached K and V rows [0, *kv_pos) of
+    // kv_heads heads (head h at kv_k / kv_v + h * kv_stride_h floats, D = 128),
+    // pulled into L2 for the attention that follows
+    const float* kv_k;
+    const float* kv_v;
+    const int* kv_pos;
+    int kv_heads;
+    int64_t kv_stride_h;
 };
+
+// Batch-1 GEMV with its weights prefetched into shared memory before it waits
+// for the previous kernel (vb_gemv_pf.cu): one CTA per SM, each a contiguous
+// slice of at most kPfSliceBytes of W; larger matrices run as several launches
+// (gemv_pf_parts).  Store, residual and SwiGLU epilogues; RMSNorm prologue.
+constexpr size_t kPfSliceBytes = 96 * 1024;
+constexpr int kPfCtas = 148;
+int gemv_pf_parts(int N, int K, bool q8, int epi);  // 0: does not fit
+vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s);
 
 // Launch config chosen so every SM streams weights even for 1024-row outputs.
 vb_status launch_gemv(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s,

@@ -19,7 +19,7 @@
 namespace vb {
 namespace {
 
-// 1 MiB: the split partials (H * splits * 130 floats) plus one length word.
+// 1 MiB: the split partials (H * splits * 132 floats) plus one length word.
 // Every GPU that loads the library holds this array until the process exits.
 constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

@@ -13,12 +13,15 @@ CPU fallback anywhere in this module.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 import numpy as np
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "lib" / "libverbum_b200.so"
+# VB200_LIB selects another build of the library (e.g. a VB_STEP_TRACE=1
+# profiling build); the default is the in-tree one
+LIB_PATH = Path(os.environ["VB200_LIB"]) if os.environ.get("VB200_LIB") else PKG / "lib" / "libverbum_b200.so"
 
 VB_OK = 0
 ERR_NAMES = {
