@@ -155,7 +155,7 @@ VB_API vb_status vb_attn_decode(const float* q, const float* kcache, const float
  * the library (held by every GPU that loads it until the process exits).  The
  * split count is capped at what that array holds (H * splits * 132 floats,
  * plus 512 B: 124 splits for 16 heads), so every context length runs, with
- * longer splits past about 8k positions; only a head count too large for one
+ * longer splits past about 16k positions; only a head count too large for one
  * split (H > 1984) returns VB_ERR_UNSUPPORTED.  The first call on a device (and
  * the first after the device's context was replaced, e.g. by cudaDeviceReset)
  * looks up the array's device address, so make that call before any stream

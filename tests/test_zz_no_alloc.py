@@ -48,12 +48,12 @@ def test_noalloc_matches_allocating_entry_point_twice():
 
 
 def test_noalloc_long_contexts_run_with_capped_splits():
-    # 16/8 heads: past ~8k positions the allocating entry point uses more
-    # splits (up to 296, of >= 64 positions) than the 1 MiB array holds (124);
+    # 16/8 heads: past ~16k positions the allocating entry point uses more
+    # splits (up to 148, of >= 128 positions) than the 1 MiB array holds (124);
     # the no-alloc one caps the split count (longer splits) and must still
-    # agree.  40960 is the model's max_position_embeddings; 7936 is the last
-    # length whose split count fits, 8000 the first that is capped.
-    for n in (7936, 8000, 32768, 40960):
+    # agree.  40960 is the model's max_position_embeddings; 15872 is the last
+    # length whose split count fits, 16000 the first that is capped.
+    for n in (15872, 16000, 32768, 40960):
         diff = _compare(n, n)
         assert np.isfinite(diff) and diff <= 2e-5, (n, diff)
         torch.cuda.empty_cache()

@@ -27,13 +27,28 @@ constexpr int kNumSMs = 148;
 // x / (1 + exp(-x)), IEEE division, accurate expf) come from vb_pipe.cuh.
 
 
+// The 16-byte groups lane and lane + 32 of INT8 rows r0 .. r0 + R - 1 (zero
+// past the matrix or the row), streamed past L1.
+template <int R>
+__device__ __forceinline__ void q8_load_group(const int8_t* W, int r0, int N, int K, int lane, uint4 (&w)[R][2]) {
+    const int G16 = K >> 4;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int gi = 32 * u + lane;
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            w[r][u] = (gi < G16 && r0 + r < N) ? ld_stream_u4(W + (size_t)(r0 + r) * K + 16 * (size_t)gi)
+                                                : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // GEMV: y = W . x with W [N, K] row-major (f32 or int8 + per-row scale).
 // One warp owns R consecutive rows at a time; lanes stride K with 16-byte
 // streaming loads, all of a row group's loads issued before the FMAs.
 // ---------------------------------------------------------------------------
 template <bool Q8, int R, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
     pdl_trigger();
     {
         // The weights do not depend on the previous kernel: while it drains,
@@ -78,13 +93,65 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
     float best_v = -INFINITY;
     int best_i = INT_MAX;
 
-    for (int g = blockIdx.x * kGemvWarps + warp; g < ngroups; g += gridDim.x * kGemvWarps) {
+    // INT8 rows of at most 1024 bytes: each lane holds two 16-byte groups of
+    // every row of a group; the next group's loads are issued before this
+    // group's dot products, and dequantisation and FMAs run on f32 pairs
+    const bool q8_short = Q8 && K <= 1024;
+    uint4 wn[R][2];
+    const int gstride = gridDim.x * kGemvWarps;
+    if (q8_short) {
+        const int g = blockIdx.x * kGemvWarps + warp;
+        if (g < ngroups) q8_load_group<R>(static_cast<const int8_t*>(a.W), g * R, N, K, lane, wn);
+    }
+    for (int g = blockIdx.x * kGemvWarps + warp; g < ngroups; g += gstride) {
         const int r0 = g * R;
         float acc[R];
 #pragma unroll
         for (int r = 0; r < R; r++) acc[r] = 0.0f;
 
-        if (!Q8) {
+        if (q8_short) {
+            uint4 w[R][2];
+#pragma unroll
+            for (int r = 0; r < R; r++) { w[r][0] = wn[r][0]; w[r][1] = wn[r][1]; }
+            if (g + gstride < ngroups)
+                q8_load_group<R>(static_cast<const int8_t*>(a.W), (g + gstride) * R, N, K, lane, wn);
+            f2 A[R], B[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) { A[r] = 0ull; B[r] = 0ull; }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int gi = 32 * u + lane;
+                if (gi < (K >> 4)) {
+                    const float* xc = xs + ((gi >> 5) << 9) + 4 * lane;
+                    const float4 x0 = *reinterpret_cast<const float4*>(xc);
+                    const float4 x1 = *reinterpret_cast<const float4*>(xc + 128);
+                    const float4 x2 = *reinterpret_cast<const float4*>(xc + 256);
+                    const float4 x3 = *reinterpret_cast<const float4*>(xc + 384);
+                    const f2 x0l = f2pack(x0.x, x0.y), x0h = f2pack(x0.z, x0.w);
+                    const f2 x1l = f2pack(x1.x, x1.y), x1h = f2pack(x1.z, x1.w);
+                    const f2 x2l = f2pack(x2.x, x2.y), x2h = f2pack(x2.z, x2.w);
+                    const f2 x3l = f2pack(x3.x, x3.y), x3h = f2pack(x3.z, x3.w);
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        f2 lo, hi;
+                        i8x4_to_f2(w[r][u].x, lo, hi);
+                        A[r] = f2fma(lo, x0l, A[r]);
+                        B[r] = f2fma(hi, x0h, B[r]);
+                        i8x4_to_f2(w[r][u].y, lo, hi);
+                        A[r] = f2fma(lo, x1l, A[r]);
+                        B[r] = f2fma(hi, x1h, B[r]);
+                        i8x4_to_f2(w[r][u].z, lo, hi);
+                        A[r] = f2fma(lo, x2l, A[r]);
+                        B[r] = f2fma(hi, x2h, B[r]);
+                        i8x4_to_f2(w[r][u].w, lo, hi);
+                        A[r] = f2fma(lo, x3l, A[r]);
+                        B[r] = f2fma(hi, x3h, B[r]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) acc[r] = f2sum(A[r]) + f2sum(B[r]);
+        } else if (!Q8) {
             const float* W = static_cast<const float*>(a.W);
             const int K4 = K >> 2;
             constexpr int U = 8;
@@ -117,6 +184,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
                 }
             }
         } else {
+            // INT8 rows longer than 1024 bytes
             const int8_t* W = static_cast<const int8_t*>(a.W);
             const int G16 = K >> 4;  // 16-byte groups per row
             constexpr int U = 4;
@@ -412,7 +480,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkNormArgs a) {
 // ---------------------------------------------------------------------------
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = 8;
-constexpr int kAttnPB = 4;  // positions per warp iteration
+constexpr int kAttnPB = 4;  // positions per warp iteration (8 measured slower)
 
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
@@ -949,14 +1017,20 @@ vb_status launch_qk_norm_rope_append(const QkNormArgs& a, cudaStream_t s) {
 }
 
 int attn_splits_for(int B, int KVH, int n_max) {
-    // ~16 (sequence, KV head, split) CTAs per SM, >= 64 positions per split
-    // (two passes of the 8 warps' 4-position blocks): at 64 sequences x 8 KV
-    // heads x 2178 positions this is 5 splits, measured at 93% of HBM peak
-    // (2 splits: 86%, 16 splits: 83%); a single sequence gets up to 296
-    // splits, so a short cache still spreads over the SMs
-    const int target = kNumSMs * 16;
-    int by_len = (n_max + kAttnMinSplit - 1) / kAttnMinSplit;
-    int by_grid = (target + B * KVH - 1) / (B * KVH);
+    // Measured on B200 (decode attention alone, GB/s of K/V reads):
+    //  - many (sequence, KV head) pairs (>= 512): ~16 CTAs per SM -- at 64
+    //    sequences x 8 KV heads x 2063 positions 5 splits give 93% of the HBM
+    //    copy peak, 3 splits 90%, 2 splits 86%, 16 splits 83%;
+    //  - fewer pairs: ~8 CTAs per SM -- 32 x 8 at 2048 positions: 5 splits
+    //    5.77 TB/s against 10 splits 5.38; 1 x 8 at 32768: 148 splits 4.87
+    //    against 296 splits 4.16;
+    //  - splits of >= 64 positions (>= 128 from 4096 positions on: 1 x 8 at
+    //    8192, 64 splits 3.84 TB/s against 128 splits 3.51).
+    const int pairs = B * KVH;
+    const int min_split = n_max >= 4096 ? 128 : kAttnMinSplit;
+    const int target = kNumSMs * (pairs >= 512 ? 16 : 8);
+    int by_len = (n_max + min_split - 1) / min_split;
+    int by_grid = (target + pairs - 1) / pairs;
     int s = by_len < by_grid ? by_len : by_grid;
     return s < 1 ? 1 : s;
 }

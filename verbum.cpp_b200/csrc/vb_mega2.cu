@@ -371,48 +371,6 @@ __device__ __forceinline__ int perm_index(int i) {
     return (c << 9) + (((r >> 2) & 3) << 7) + ((r >> 4) << 2) + (r & 3);
 }
 
-// Packed f32x2 arithmetic (sm_100): two lanes of f32 math per instruction,
-// each lane rounded exactly like the scalar operation.
-typedef unsigned long long f2;
-__device__ __forceinline__ f2 f2pack(float lo, float hi) {
-    f2 r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ float f2sum(f2 v) {
-    float lo, hi;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-    return lo + hi;
-}
-__device__ __forceinline__ void f2unpack(f2 v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ f2 f2fma(f2 a, f2 b, f2 c) {
-    f2 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ f2 f2sub(f2 a, f2 b) {
-    f2 d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ f2 f2mul(f2 a, f2 b) {
-    f2 d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// 4 int8 -> two exact f32 pairs (q0, q1), (q2, q3): each byte is placed in
-// the mantissa of 2^23 (after a bias of 128) and the offset subtracted.
-__device__ __forceinline__ void i8x4_to_f2(uint32_t w, f2& lo, f2& hi) {
-    const uint32_t u = w ^ 0x80808080u;
-    const f2 bias = f2pack(8388736.0f, 8388736.0f);  // 2^23 + 128
-    lo = f2sub(f2pack(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
-                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), bias);
-    hi = f2sub(f2pack(__int_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
-                      __int_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), bias);
-}
-
 // Stage wait shared by all consumer modes.  in_order: every warp takes every
 // stage (no slot-order gate needed); otherwise warps take stages out of order
 // and wait for the slot's previous round first.
