@@ -75,10 +75,12 @@ def compile_one(src, verbose=False, ptxas_v=False):
     return obj, r.stderr
 
 
-def build(force=False, verbose=False, ptxas_v=False, defines=(), build_dir=None, out=None):
-    global BUILD
+def build(force=False, verbose=False, ptxas_v=False, defines=(), build_dir=None, out=None, src_dir=None):
+    global BUILD, CSRC
     if build_dir:
         BUILD = Path(build_dir)
+    if src_dir:
+        CSRC = Path(src_dir).resolve()
     BUILD.mkdir(parents=True, exist_ok=True)
     LIB.mkdir(exist_ok=True)
     DEFINES[:] = sorted(defines)
@@ -120,8 +122,9 @@ def main():
     ap.add_argument("--define", action="append", default=[], help="NAME=VALUE passed to nvcc as -D")
     ap.add_argument("--build-dir", default=None, help="object directory (default verbum.cpp_b200/_build)")
     ap.add_argument("--out", default=None, help="library path (default verbum.cpp_b200/lib/libverbum_b200.so)")
+    ap.add_argument("--src-dir", default=None, help="kernel sources (default verbum.cpp_b200/csrc)")
     a = ap.parse_args()
-    out = build(a.force, a.verbose, a.ptxas_v, a.define, a.build_dir, a.out)
+    out = build(a.force, a.verbose, a.ptxas_v, a.define, a.build_dir, a.out, a.src_dir)
     print(out)
 
 

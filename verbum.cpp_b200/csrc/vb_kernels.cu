@@ -544,12 +544,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
     const float* kb = a.k + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
     const float* vb = a.v + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
 
-    for (int base = p0 + warp * kAttnPB; base < p1; base += kAttnWarps * kAttnPB) {
-        float4 kk[kAttnPB], vv[kAttnPB];
+    // K / V rows of the block of kAttnPB positions at `base` (this step's row
+    // from shared memory: just computed, not read back)
+    auto load_block = [&](int base, float4 (&kk)[kAttnPB], float4 (&vv)[kAttnPB]) {
 #pragma unroll
         for (int u = 0; u < kAttnPB; u++) {
             const int p = base + u;
-            if (has_pos && p == pos) {  // this step's row: just computed, not read back
+            if (has_pos && p == pos) {
                 kk[u] = *reinterpret_cast<const float4*>(&kvs[0][4 * lane]);
                 vv[u] = *reinterpret_cast<const float4*>(&kvs[1][4 * lane]);
             } else if (p < p1) {
@@ -560,6 +561,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
                 vv[u] = kk[u];
             }
         }
+    };
+    for (int base = p0 + warp * kAttnPB; base < p1; base += kAttnWarps * kAttnPB) {
+        // (issuing the next block's loads first measured slower: 118 registers,
+        // two CTAs per SM instead of three)
+        float4 kk[kAttnPB], vv[kAttnPB];
+        load_block(base, kk, vv);
 #pragma unroll
         for (int g = 0; g < G; g++) {
             float s[kAttnPB];
