@@ -47,6 +47,8 @@ __device__ __forceinline__ void q8_load_group(const int8_t* W, int r0, int N, in
 // One warp owns R consecutive rows at a time; lanes stride K with 16-byte
 // streaming loads, all of a row group's loads issued before the FMAs.
 // ---------------------------------------------------------------------------
+// Two CTAs per SM (INT8 lm_head shape: 4.9 TB/s; three CTAs spill, 3.4 TB/s;
+// two rows per warp, 4.4 TB/s).
 template <bool Q8, int R, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(GemvArgs a) {
     pdl_trigger();
@@ -482,8 +484,12 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = 8;
 constexpr int kAttnPB = 4;  // positions per warp iteration (8 measured slower)
 
+// Three CTAs per SM (at most 85 registers): measured 5.97 TB/s at 64 sequences
+// x 2063 positions against 4.84 with 96 registers (two CTAs) and 5.70 with four
+// CTAs (64 registers, spills).  (GQA group 4 keeps two CTAs: its larger
+// state would spill at three.)
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, G >= 4 ? 2 : 3) attn_split_kernel(AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
