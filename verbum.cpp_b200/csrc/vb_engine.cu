@@ -149,7 +149,8 @@ static void step_weights(const vb_engine* e, int j, const void** w, size_t* byte
 
 static vb_status step_gemv(vb_engine* e, int j, GemvArgs g, bool q8, int pro, int epi, cudaStream_t s) {
     g.err = e->d_err;
-    step_weights(e, j + 2, &g.l2_ahead, &g.l2_ahead_bytes);  // two GEMVs ahead
+    // two GEMVs ahead (measured: without it INT8 per-op 1005 against 1033 tok/s)
+    step_weights(e, j + 2, &g.l2_ahead, &g.l2_ahead_bytes);
     if (g.K <= 4096 && gemv_pf_parts(g.N, g.K, q8, epi) > 0) return launch_gemv_pf(g, q8, pro, epi, s);
     return launch_gemv(g, q8, pro, epi, s);
 }
@@ -220,6 +221,12 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         aa.stride_h = qa.stride_h;
         aa.splits = e->attn_splits;
         aa.ws = e->attn_ws;
+        // the positions come from the previous step: the first cached rows and
+        // the rope row are requested before the kernel waits for q|k|v
+        // (INT8 per-op step 1059 -> 1085 tok/s).  Merging the splits in the
+        // last split CTA instead of the merge kernel measured slower (1031):
+        // its fence and ticket round trip cost more than the launch.
+        aa.pos_stable = 1;
         if ((st = launch_attention(aa, s))) return st;
 
         GemvArgs o{};

@@ -488,12 +488,50 @@ constexpr int kAttnPB = 4;  // positions per warp iteration (8 measured slower)
 // x 2063 positions against 4.84 with 96 registers (two CTAs) and 5.70 with four
 // CTAs (64 registers, spills).  (GQA group 4 keeps two CTAs: its larger
 // state would spill at three.)
-template <int G>
-__global__ void __launch_bounds__(kAttnThreads, G >= 4 ? 2 : 3) attn_split_kernel(AttnArgs a) {
+template <int G, bool PRE>
+__global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_split_kernel(AttnArgs a) {
     pdl_trigger();
-    pdl_wait();
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* kb = a.k + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
+    const float* vb = a.v + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
+    // Stable positions: read them, pull the rope row and norm weights into L1
+    // and load this warp's first block of cached rows (those before this
+    // step's position) while the predecessor is still running.
+    float4 kpre[kAttnPB], vpre[kAttnPB];
+    bool pre = false;
+    if constexpr (PRE) {
+        int n0 = a.lens ? a.lens[b] : a.pos[b] + 1;
+        n0 = n0 < 0 ? 0 : (n0 > a.n_max ? a.n_max : n0);
+        const int c0 = (n0 + a.splits - 1) / a.splits;
+        const int q0 = split * c0, q1 = min(n0, q0 + c0);
+        const int base = q0 + warp * kAttnPB;
+        if (base < q1) {
+            pre = true;
+#pragma unroll
+            for (int u = 0; u < kAttnPB; u++) {
+                const int p = base + u;
+                if (p < q1 && p < n0 - 1) {
+                    kpre[u] = ld_stream_f4(kb + (size_t)p * a.stride_pos);
+                    vpre[u] = ld_stream_f4(vb + (size_t)p * a.stride_pos);
+                } else {
+                    kpre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vpre[u] = kpre[u];
+                }
+            }
+        }
+        if (a.fuse_qk && warp <= G && n0 >= 1 && n0 - 1 < a.qk.rope_positions) {
+            const size_t r = (size_t)(n0 - 1) * 128 + lane;
+            const float* nw = warp < G ? a.qk.q_norm : a.qk.k_norm;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(a.qk.cos_tab + r + 32 * e));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(a.qk.sin_tab + r + 32 * e));
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(nw + lane + 32 * e));
+            }
+        }
+    }
+    pdl_wait();
     int n = a.lens ? a.lens[b] : a.pos[b] + 1;
     n = n < 0 ? 0 : (n > a.n_max ? a.n_max : n);
     const int chunk = (n + a.splits - 1) / a.splits;
@@ -547,9 +585,6 @@ __global__ void __launch_bounds__(kAttnThreads, G >= 4 ? 2 : 3) attn_split_kerne
         l[g] = 0.0f;
         acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const float* kb = a.k + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
-    const float* vb = a.v + (size_t)b * a.stride_b + (size_t)kvh * a.stride_h + 4 * lane;
-
     // K / V rows of the block of kAttnPB positions at `base` (this step's row
     // from shared memory: just computed, not read back)
     auto load_block = [&](int base, float4 (&kk)[kAttnPB], float4 (&vv)[kAttnPB]) {
@@ -572,7 +607,17 @@ __global__ void __launch_bounds__(kAttnThreads, G >= 4 ? 2 : 3) attn_split_kerne
         // (issuing the next block's loads first measured slower: 118 registers,
         // two CTAs per SM instead of three)
         float4 kk[kAttnPB], vv[kAttnPB];
-        load_block(base, kk, vv);
+        if (PRE && pre) {  // the first block, loaded before the wait (this step's row from shared memory)
+            pre = false;
+#pragma unroll
+            for (int u = 0; u < kAttnPB; u++) {
+                const bool mine = has_pos && base + u == pos;
+                kk[u] = mine ? *reinterpret_cast<const float4*>(&kvs[0][4 * lane]) : kpre[u];
+                vv[u] = mine ? *reinterpret_cast<const float4*>(&kvs[1][4 * lane]) : vpre[u];
+            }
+        } else {
+            load_block(base, kk, vv);
+        }
 #pragma unroll
         for (int g = 0; g < G; g++) {
             float s[kAttnPB];
@@ -1033,7 +1078,7 @@ int attn_splits_for(int B, int KVH, int n_max) {
     // Measured on B200 (decode attention alone, GB/s of K/V reads):
     //  - many (sequence, KV head) pairs (>= 512): ~16 CTAs per SM -- at 64
     //    sequences x 8 KV heads x 2063 positions 5 splits give 93% of the HBM
-    //    copy peak, 3 splits 90%, 2 splits 86%, 16 splits 83%;
+    //    copy peak (4 and 6 the same within 1%), 3 and 8 splits 88%;
     //  - fewer pairs: ~8 CTAs per SM -- 32 x 8 at 2048 positions: 5 splits
     //    5.77 TB/s against 10 splits 5.38; 1 x 8 at 32768: 148 splits 4.87
     //    against 296 splits 4.16;
@@ -1059,10 +1104,16 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.fuse_qk && (G + 1 > kAttnWarps || a.lens || !a.pos))
         return fail(VB_ERR_ARG, "attention: the fused q/k norm needs positions and G < warps");
     dim3 grid(a.splits, a.KVH, a.B);
+    // the pre-wait form (positions stable: a decode step's graph) keeps its
+    // first block in registers and runs two CTAs per SM; the other form three
+    const bool pre = a.pos_stable != 0;
     switch (G) {
-        case 1: launch_pdl(attn_split_kernel<1>, grid, kAttnThreads, 0, s, a); break;
-        case 2: launch_pdl(attn_split_kernel<2>, grid, kAttnThreads, 0, s, a); break;
-        case 4: launch_pdl(attn_split_kernel<4>, grid, kAttnThreads, 0, s, a); break;
+        case 1: pre ? launch_pdl(attn_split_kernel<1, true>, grid, kAttnThreads, 0, s, a)
+                    : launch_pdl(attn_split_kernel<1, false>, grid, kAttnThreads, 0, s, a); break;
+        case 2: pre ? launch_pdl(attn_split_kernel<2, true>, grid, kAttnThreads, 0, s, a)
+                    : launch_pdl(attn_split_kernel<2, false>, grid, kAttnThreads, 0, s, a); break;
+        case 4: pre ? launch_pdl(attn_split_kernel<4, true>, grid, kAttnThreads, 0, s, a)
+                    : launch_pdl(attn_split_kernel<4, false>, grid, kAttnThreads, 0, s, a); break;
         default: return fail(VB_ERR_UNSUPPORTED, "attention: GQA group must be 1, 2 or 4");
     }
     VB_LAUNCH_CHECK("attn_split_kernel");

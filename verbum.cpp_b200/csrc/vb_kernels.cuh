@@ -126,6 +126,10 @@ struct AttnArgs {
     // and uses them for that position (generate.cpp:52-71 inside the attention)
     int fuse_qk;
     QkNormArgs qk;
+    // positions (pos / lens) and the cached rows before them were written
+    // before this launch's predecessor started (a decode step's graph): the
+    // kernel may read them, and request the rows, before griddepcontrol.wait
+    int pos_stable;
 };
 int attn_splits_for(int B, int KVH, int n_max);
 size_t attn_ws_bytes(int B, int H, int splits);
