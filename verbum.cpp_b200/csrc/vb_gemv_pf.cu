@@ -9,8 +9,10 @@
 // (griddepcontrol.wait).  Launched back to back with programmatic dependent
 // launch, kernel i+1's weights therefore stream in while kernel i computes:
 // what is left on the step's dependency chain is reading x, the dot products
-// out of shared memory and the stores.  The slice budget keeps two such CTAs
-// on one SM (the running kernel's and the next one's).
+// out of shared memory and the stores.  The slice budget takes most of an
+// SM's shared memory (one such CTA per SM); the weights of the GEMV two
+// launches ahead are pulled into L2 meanwhile, so the next slice copies come
+// out of L2.
 //
 // Arithmetic per row as the streaming GEMV: lanes stride K (16-byte groups),
 // f32 FMAs, one warp reduction; INT8 bytes dequantised exactly (byte into the

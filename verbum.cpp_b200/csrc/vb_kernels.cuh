@@ -51,7 +51,10 @@ struct GemvArgs {
 // for the previous kernel (vb_gemv_pf.cu): one CTA per SM, each a contiguous
 // slice of at most kPfSliceBytes of W; larger matrices run as several launches
 // (gemv_pf_parts).  Store, residual and SwiGLU epilogues; RMSNorm prologue.
-constexpr size_t kPfSliceBytes = 96 * 1024;
+// The budget fills an SM's shared memory, so one such CTA runs per SM: with
+// 96 KB slices (two per SM, the next kernel's prefetching while this one
+// computes) the per-op step measured slower (f32 1001 against 1101 tok/s).
+constexpr size_t kPfSliceBytes = 200 * 1024;
 constexpr int kPfCtas = 148;
 int gemv_pf_parts(int N, int K, bool q8, int epi);  // 0: does not fit
 vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStream_t s);
