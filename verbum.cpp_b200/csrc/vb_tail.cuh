@@ -127,23 +127,45 @@ __device__ __forceinline__ void residual_norm_row(float* x, const float* parts, 
     float* xr = x + (size_t)b * dim;
     float xv[16];
     double ss = 0.0;
+    // Four elements per thread at a time, with every split's load of all four
+    // (and their residuals) in flight before any is summed (in split order) or
+    // stored: a store to x between elements would hold the next element's loads
+    // back behind it (it may alias them).
+    constexpr int JB = 4;
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-        const int i = threadIdx.x + NT * j;
-        if (i >= dim) break;
-        // the splits' loads are independent: issue up to 16 before summing (in split order)
-        float t[16];
+    for (int j0 = 0; j0 < 16; j0 += JB) {
+        if (threadIdx.x + NT * j0 >= dim) break;
+        float v[JB], xo[JB];
 #pragma unroll
-        for (int q = 0; q < 16; q++) t[q] = q < splits ? __ldcg(parts + ((size_t)q * rows + b) * dim + i) : 0.f;
-        float v = 0.f;
+        for (int jj = 0; jj < JB; jj++) {
+            const int i = threadIdx.x + NT * (j0 + jj);
+            v[jj] = 0.f;
+            xo[jj] = i < dim ? __ldcg(xr + i) : 0.f;
+        }
+        for (int q0 = 0; q0 < splits; q0 += 16) {
+            float t[JB][16];
 #pragma unroll
-        for (int q = 0; q < 16; q++)
-            if (q < splits) v += t[q];
-        for (int q = 16; q < splits; q++) v += __ldcg(parts + ((size_t)q * rows + b) * dim + i);
-        if (scales) v *= scales[i];
-        xv[j] = __ldcg(xr + i) + v;
-        xr[i] = xv[j];
-        ss += (double)xv[j] * (double)xv[j];
+            for (int jj = 0; jj < JB; jj++) {
+                const int i = threadIdx.x + NT * (j0 + jj);
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                    t[jj][u] = (i < dim && q0 + u < splits) ? __ldcg(parts + ((size_t)(q0 + u) * rows + b) * dim + i) : 0.f;
+            }
+#pragma unroll
+            for (int jj = 0; jj < JB; jj++)
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                    if (q0 + u < splits) v[jj] += t[jj][u];
+        }
+#pragma unroll
+        for (int jj = 0; jj < JB; jj++) {
+            const int i = threadIdx.x + NT * (j0 + jj);
+            if (i >= dim) break;
+            if (scales) v[jj] *= scales[i];
+            xv[j0 + jj] = xo[jj] + v[jj];
+            xr[i] = xv[j0 + jj];
+            ss += (double)xv[j0 + jj] * (double)xv[j0 + jj];
+        }
     }
     const float sc = rms_scale(block_sum_d<NT>(ss, red), dim, eps);
 #pragma unroll
