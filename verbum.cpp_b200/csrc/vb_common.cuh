@@ -62,6 +62,38 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// 2^x by the PTX ex2.approx instruction (relative error ~2^-22, -inf -> +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Warp sums of NV values at once (NV a power of two <= 32): a transposed
+// butterfly -- at each of the first log2(NV) xor steps a lane sends half of its
+// values and keeps the other half -- then plain xor steps.  Returns, in every
+// lane, the warp-wide sum of value lane >> (5 - log2(NV)): NV - 1 + 5 - log2(NV)
+// shuffles in all instead of 5 * NV.
+template <int NV>
+__device__ __forceinline__ float warp_sum_scatter(float (&v)[NV], int lane) {
+    static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "NV: a power of two <= 32");
+    int mask = 16;
+#pragma unroll
+    for (int n = NV; n > 1; n >>= 1, mask >>= 1) {
+        const bool upper = lane & mask;
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) {
+            const float send = upper ? v[i] : v[i + n / 2];
+            const float keep = upper ? v[i + n / 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (; mask > 0; mask >>= 1) r += __shfl_xor_sync(0xffffffffu, r, mask);
+    return r;
+}
+
 // Streaming 16-byte global load that does not allocate in L1 (weights and KV
 // rows are touched exactly once per step).
 __device__ __forceinline__ float4 ld_stream_f4(const void* p) {

@@ -577,13 +577,25 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
         for (int g = 0; g < G; g++)
             q[g] = *reinterpret_cast<const float4*>(a.q + ((size_t)b * a.H + kvh * G + g) * 128 + 4 * lane);
     }
+    // scores in base 2: q is pre-scaled by log2(e) / sqrt(D) and the
+    // exponentials are ex2; the running max m is in the same units and is
+    // converted back to natural units for the split partial
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float qscale = inv_sqrt_d * kLog2e;
+    f2 qa[G], qb[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        qa[g] = f2pack(q[g].x * qscale, q[g].y * qscale);
+        qb[g] = f2pack(q[g].z * qscale, q[g].w * qscale);
+    }
     float m[G], l[G];
-    float4 acc[G];
+    f2 acca[G], accb[G];
 #pragma unroll
     for (int g = 0; g < G; g++) {
         m[g] = -INFINITY;
         l[g] = 0.0f;
-        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        acca[g] = f2pack(0.f, 0.f);
+        accb[g] = acca[g];
     }
     // K / V rows of the block of kAttnPB positions at `base` (this step's row
     // from shared memory: just computed, not read back)
@@ -603,6 +615,8 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
             }
         }
     };
+    constexpr int NV = G * kAttnPB;                           // dot products per block
+    constexpr int kShift = NV >= 16 ? 1 : (NV >= 8 ? 2 : 3);  // 5 - log2(NV)
     for (int base = p0 + warp * kAttnPB; base < p1; base += kAttnWarps * kAttnPB) {
         // (issuing the next block's loads first measured slower: 118 registers,
         // two CTAs per SM instead of three)
@@ -618,32 +632,44 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
         } else {
             load_block(base, kk, vv);
         }
+        // this lane's share of the G x kAttnPB dot products, summed over the
+        // warp together; value g * kAttnPB + u is then read from lane
+        // (g * kAttnPB + u) << kShift
+        float d[NV];
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int u = 0; u < kAttnPB; u++)
+                d[g * kAttnPB + u] = f2sum(f2fma(qb[g], f2pack(kk[u].z, kk[u].w),
+                                                 f2mul(qa[g], f2pack(kk[u].x, kk[u].y))));
+        const float r = warp_sum_scatter<NV>(d, lane);
 #pragma unroll
         for (int g = 0; g < G; g++) {
             float s[kAttnPB];
             float mx = m[g];
 #pragma unroll
             for (int u = 0; u < kAttnPB; u++) {
-                float d = q[g].x * kk[u].x;
-                d = fmaf(q[g].y, kk[u].y, d);
-                d = fmaf(q[g].z, kk[u].z, d);
-                d = fmaf(q[g].w, kk[u].w, d);
-                d = warp_sum(d) * inv_sqrt_d;
-                s[u] = (base + u < p1) ? d : -INFINITY;
+                const float x = __shfl_sync(0xffffffffu, r, (g * kAttnPB + u) << kShift);
+                s[u] = (u == 0 || base + u < p1) ? x : -INFINITY;
                 mx = fmaxf(mx, s[u]);
             }
-            const float corr = (m[g] == -INFINITY) ? 0.0f : expf(m[g] - mx);
-            l[g] *= corr;
-            acc[g].x *= corr; acc[g].y *= corr; acc[g].z *= corr; acc[g].w *= corr;
+            // (the block's first position is always valid, so mx is finite;
+            // ex2(-inf) = 0 covers the first block and the masked positions)
+            const float corr = ex2_approx(m[g] - mx);
+            const f2 c2 = f2pack(corr, corr);
+            float lg = l[g] * corr;
+            f2 aa = f2mul(acca[g], c2), ab = f2mul(accb[g], c2);
 #pragma unroll
             for (int u = 0; u < kAttnPB; u++) {
-                const float e = (s[u] == -INFINITY) ? 0.0f : expf(s[u] - mx);
-                l[g] += e;
-                acc[g].x = fmaf(e, vv[u].x, acc[g].x);
-                acc[g].y = fmaf(e, vv[u].y, acc[g].y);
-                acc[g].z = fmaf(e, vv[u].z, acc[g].z);
-                acc[g].w = fmaf(e, vv[u].w, acc[g].w);
+                const float e = ex2_approx(s[u] - mx);
+                const f2 e2 = f2pack(e, e);
+                lg += e;
+                aa = f2fma(e2, f2pack(vv[u].x, vv[u].y), aa);
+                ab = f2fma(e2, f2pack(vv[u].z, vv[u].w), ab);
             }
+            l[g] = lg;
+            acca[g] = aa;
+            accb[g] = ab;
             m[g] = mx;
         }
     }
@@ -653,7 +679,10 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
 #pragma unroll
     for (int g = 0; g < G; g++) {
         if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
-        sm_acc[warp][g][lane] = acc[g];
+        float4 o;
+        f2unpack(acca[g], o.x, o.y);
+        f2unpack(accb[g], o.z, o.w);
+        sm_acc[warp][g][lane] = o;
     }
     __syncthreads();
     // thread -> (g, float index); G*128 values per CTA
@@ -668,7 +697,7 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
 #pragma unroll
             for (int w = 0; w < kAttnWarps; w++) {
                 if (sm_m[w][g] == -INFINITY) continue;
-                const float f = expf(sm_m[w][g] - M);
+                const float f = ex2_approx(sm_m[w][g] - M);
                 L = fmaf(sm_l[w][g], f, L);
                 const float* av = reinterpret_cast<const float*>(&sm_acc[w][g][0]);
                 A = fmaf(av[di], f, A);
@@ -677,7 +706,7 @@ __global__ void __launch_bounds__(kAttnThreads, (G >= 4 || PRE) ? 2 : 3) attn_sp
         const int h = kvh * G + g;
         float* part = a.ws + (((size_t)b * a.H + h) * S + split) * kAttnPart;
         part[4 + di] = A;
-        if (di == 0) { part[0] = M; part[1] = L; }
+        if (di == 0) { part[0] = M * (1.0f / kLog2e); part[1] = L; }  // M back to natural units
     }
 }
 

@@ -210,13 +210,6 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
     lo = pack_bf16(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
 }
 
-// 2^x by the PTX ex2.approx instruction (relative error ~2^-22, -inf -> +0)
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
 __global__ void __launch_bounds__(256, 1)
     tc_prefill_attn_kernel(const __grid_constant__ CUtensorMap mq_hi, const __grid_constant__ CUtensorMap mq_lo,
                            const __grid_constant__ CUtensorMap mk_hi, const __grid_constant__ CUtensorMap mk_lo,
