@@ -90,3 +90,36 @@ def test_batch64_full_model_two_sequences():
         o.close()
     bt.close()
     eng.close()
+
+
+@pytest.mark.parametrize("mode", ["f32", "int8"])
+def test_batch33_matches_oracle(mode):
+    """33 sequences (one more than a 32-row tile half): sequences at the ends
+    and in the middle give the oracle's logits and greedy tokens."""
+    cfg = mini_config()
+    w = vbsynth.make_weights(cfg, seed=43)
+    B, P, G = 33, 6, 5
+    prompts = np.stack([vbsynth.prompt_ids(P, 300 + b, cfg["vocab_size"]) for b in range(B)])
+    eng = vb200.Engine(cfg).load(w)
+    if mode == "int8":
+        eng.quantize()
+    bt = vb200.Batch(eng, B, P + G + 4)
+    for t in range(P):
+        lg, nx = bt.step(prompts[:, t])
+    nxt = bt.decode(nx, G)
+    for b in (0, 15, 16, 32):
+        o = oracle.OracleModel(cfg, w)
+        if mode == "int8":
+            o.quantize()
+        o.reset_cache(P + G + 4)
+        for t in range(P):
+            lo = o.step(int(prompts[b, t]))
+        assert np.max(np.abs(lo - lg[b])) <= TOL[mode], b
+        tok = oracle.argmax(lo)
+        assert tok == int(nx[b]), b
+        for _ in range(G):
+            tok = oracle.argmax(o.step(tok))
+        assert tok == int(nxt[b]), b
+        o.close()
+    bt.close()
+    eng.close()
