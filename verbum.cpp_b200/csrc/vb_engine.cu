@@ -147,12 +147,17 @@ static void step_weights(const vb_engine* e, int j, const void** w, size_t* byte
     }
 }
 
+// step_gemv takes the prefetching GEMV for this shape
+static bool step_gemv_pf_fits(const vb_engine*, int N, int K, bool q8, int epi) {
+    return K <= 4096 && gemv_pf_parts(N, K, q8, epi) > 0;
+}
+
 static vb_status step_gemv(vb_engine* e, int j, GemvArgs g, bool q8, int pro, int epi, cudaStream_t s) {
     g.err = e->d_err;
     // two GEMVs ahead (measured: without it INT8 per-op 1005 against 1033 tok/s)
     // (one or three ahead measured the same within 2 %)
     step_weights(e, j + 2, &g.l2_ahead, &g.l2_ahead_bytes);
-    if (g.K <= 4096 && gemv_pf_parts(g.N, g.K, q8, epi) > 0) return launch_gemv_pf(g, q8, pro, epi, s);
+    if (step_gemv_pf_fits(e, g.N, g.K, q8, epi)) return launch_gemv_pf(g, q8, pro, epi, s);
     return launch_gemv(g, q8, pro, epi, s);
 }
 
@@ -228,16 +233,25 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         // last split CTA instead of the merge kernel measured slower (1031):
         // its fence and ticket round trip cost more than the launch.
         aa.pos_stable = 1;
+        // With few splits the o projection merges the split partials in its
+        // prologue: one launch fewer on the step's dependency chain (f32 at
+        // 3 splits, context <= 168: 1136 -> 1162 tok/s).  Every CTA merges all
+        // heads, a serial pass over the splits: at 13 splits (INT8, context
+        // ~770) that measured slower than the merge launch (1185 -> 1052).
+        const bool merge_in_o = e->attn_splits <= 4 && step_gemv_pf_fits(e, c.hidden, e->q_width, q8, kEpiResidual);
+        aa.no_merge = merge_in_o ? 1 : 0;
         if ((st = launch_attention(aa, s))) return st;
 
         GemvArgs o{};
         o.x = e->ctx;
+        o.attn_parts = e->attn_ws;
+        o.attn_splits = e->attn_splits;
         o.W = q8 ? (const void*)L.qo : (const void*)L.wo;
         o.scales = L.so;
         o.y = e->x;
         o.N = c.hidden;
         o.K = e->q_width;
-        if ((st = step_gemv(e, 4 * l + 1, o, q8, kProNone, kEpiResidual, s))) return st;
+        if ((st = step_gemv(e, 4 * l + 1, o, q8, merge_in_o ? kProMerge : kProNone, kEpiResidual, s))) return st;
 
         GemvArgs gu{};
         gu.x = e->x;

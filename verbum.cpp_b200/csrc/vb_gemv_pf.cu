@@ -109,10 +109,55 @@ __global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
     pdl_trigger();
     pdl_wait();
 
-    // 3. x (normalised when PRO is kProRms), laid out for conflict-free reads
+    // 3. x (normalised when PRO is kProRms, merged from the attention's split
+    //    partials when kProMerge), laid out for conflict-free reads
     const float* x = a.x;
     if (a.x_tok) x += (size_t)(*a.x_tok) * (size_t)K;
     float sc = 1.0f;
+    if (PRO == kProMerge) {
+        // half-warp per head, lane l of it dims 8l .. 8l + 7: M = max_s m_s,
+        // L = sum_s l_s e^(m_s - M), A = sum_s acc_s e^(m_s - M) in split order
+        // (an empty split has m = -inf, l = 0, acc = 0), x = A / L
+        const int S = a.attn_splits, H = K >> 7;
+        const int hl = lane & 15;
+        for (int h0 = 2 * warp; h0 < H; h0 += 2 * kPfWarps) {
+            const int h = h0 + (lane >> 4);
+            const bool act = h < H;
+            const float* base = a.attn_parts + (size_t)(act ? h : 0) * S * kAttnPart;
+            float M = -INFINITY;
+            if (act)
+                for (int sp = hl; sp < S; sp += 16) M = fmaxf(M, base[(size_t)sp * kAttnPart]);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float L = 0.0f;
+            f2 A[4] = {0ull, 0ull, 0ull, 0ull};
+            if (act && M != -INFINITY) {
+#pragma unroll 4
+                for (int sp = 0; sp < S; sp++) {
+                    const float* pp = base + (size_t)sp * kAttnPart;
+                    const float f = expf(pp[0] - M);
+                    const f2 f2v = f2pack(f, f);
+                    L = fmaf(pp[1], f, L);
+                    const float4 v0 = *reinterpret_cast<const float4*>(pp + 4 + 8 * hl);
+                    const float4 v1 = *reinterpret_cast<const float4*>(pp + 8 + 8 * hl);
+                    A[0] = f2fma(f2pack(v0.x, v0.y), f2v, A[0]);
+                    A[1] = f2fma(f2pack(v0.z, v0.w), f2v, A[1]);
+                    A[2] = f2fma(f2pack(v1.x, v1.y), f2v, A[2]);
+                    A[3] = f2fma(f2pack(v1.z, v1.w), f2v, A[3]);
+                }
+            }
+            if (act) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float lo, hi;
+                    f2unpack(A[e], lo, hi);
+                    const int i = h * 128 + 8 * hl + 2 * e;
+                    xs[xs_index<Q8>(i)] = L > 0.0f ? lo / L : 0.0f;
+                    xs[xs_index<Q8>(i + 1)] = L > 0.0f ? hi / L : 0.0f;
+                }
+            }
+        }
+    }
     if (PRO == kProRms) {
         double ss = 0.0;
         for (int i = tid; i < K; i += kPfThreads) {
@@ -121,10 +166,12 @@ __global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
         }
         sc = rms_scale(block_sum_d<kPfThreads>(ss, red), K, a.eps);
     }
-    for (int i = tid; i < K; i += kPfThreads) {
-        float v = x[i];
-        if (PRO == kProRms) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[i]);
-        xs[xs_index<Q8>(i)] = v;
+    if (PRO != kProMerge) {
+        for (int i = tid; i < K; i += kPfThreads) {
+            float v = x[i];
+            if (PRO == kProRms) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[i]);
+            xs[xs_index<Q8>(i)] = v;
+        }
     }
 
     // 4. the slice has landed (thread 0 waits; every thread then observes the
@@ -252,6 +299,10 @@ vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStrea
         return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: epilogue");
     if (epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "gemv: swiglu needs even N");
     if ((reinterpret_cast<uintptr_t>(a.W) & 15u) != 0) return fail(VB_ERR_UNSUPPORTED, "gemv: W must be 16-byte aligned");
+    if (pro == kProMerge &&
+        (epi != kEpiResidual || a.K % 128 || !a.attn_parts || a.attn_splits < 1 || a.x_tok ||
+         (reinterpret_cast<uintptr_t>(a.attn_parts) & 15u) != 0))
+        return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: merge prologue needs K = heads * 128, partials, residual");
     const int parts = gemv_pf_parts(a.N, a.K, q8, epi);
     if (parts == 0) return fail(VB_ERR_UNSUPPORTED, "prefetching gemv: weights too large for the slices");
     {
@@ -273,6 +324,8 @@ vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStrea
             if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiStore>();
             if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiResidual>();
             if (ce == cudaSuccess) ce = pf_attr<true, kProRms, kEpiSwiGLU>();
+            if (ce == cudaSuccess) ce = pf_attr<false, kProMerge, kEpiResidual>();
+            if (ce == cudaSuccess) ce = pf_attr<true, kProMerge, kEpiResidual>();
             if (ce != cudaSuccess) return cuda_fail(ce, "prefetching gemv: shared memory attribute");
             done.fetch_or(bit);
         }
@@ -298,10 +351,16 @@ vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStrea
             g.l2_ahead_bytes = b0 < a.l2_ahead_bytes ? (a.l2_ahead_bytes - b0 < share ? a.l2_ahead_bytes - b0 : share) : 0;
         }
         const int grid = g.N / unit < kPfCtas ? g.N / unit : kPfCtas;
-        const cudaError_t ce = q8 ? (pro == kProRms ? pf_dispatch<true, kProRms>(g, epi, grid, smem, s)
-                                                    : pf_dispatch<true, kProNone>(g, epi, grid, smem, s))
-                                  : (pro == kProRms ? pf_dispatch<false, kProRms>(g, epi, grid, smem, s)
-                                                    : pf_dispatch<false, kProNone>(g, epi, grid, smem, s));
+        cudaError_t ce;
+        if (pro == kProMerge)
+            ce = q8 ? launch_pdl(gemv_pf_kernel<true, kProMerge, kEpiResidual>, grid, kPfThreads, smem, s, g)
+                    : launch_pdl(gemv_pf_kernel<false, kProMerge, kEpiResidual>, grid, kPfThreads, smem, s, g);
+        else if (q8)
+            ce = pro == kProRms ? pf_dispatch<true, kProRms>(g, epi, grid, smem, s)
+                                : pf_dispatch<true, kProNone>(g, epi, grid, smem, s);
+        else
+            ce = pro == kProRms ? pf_dispatch<false, kProRms>(g, epi, grid, smem, s)
+                                : pf_dispatch<false, kProNone>(g, epi, grid, smem, s);
         if (ce != cudaSuccess) return cuda_fail(ce, "gemv_pf_kernel launch");
     }
     return VB_OK;

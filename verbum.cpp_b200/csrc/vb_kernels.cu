@@ -1146,6 +1146,7 @@ vb_status launch_attention(const AttnArgs& a, cudaStream_t s) {
         default: return fail(VB_ERR_UNSUPPORTED, "attention: GQA group must be 1, 2 or 4");
     }
     VB_LAUNCH_CHECK("attn_split_kernel");
+    if (a.no_merge) return VB_OK;
     launch_pdl(attn_merge_kernel, dim3(a.H, a.B), kMergeThreads, 0, s, a);
     VB_LAUNCH_CHECK("attn_merge_kernel");
     return VB_OK;

@@ -14,7 +14,7 @@ constexpr int kAttnMinSplit = 64;
 
 // GEMV prologue: the input vector is used as is, or RMS-normalised with a
 // weight vector first (the rmsnorm that precedes every projection).
-enum GemvPro : int { kProNone = 0, kProRms = 1 };
+enum GemvPro : int { kProNone = 0, kProRms = 1, kProMerge = 2 };
 // GEMV epilogue.
 enum GemvEpi : int {
     kEpiStore = 0,     // y[j] = dot_j
@@ -45,6 +45,11 @@ struct GemvArgs {
     const int* kv_pos;
     int kv_heads;
     int64_t kv_stride_h;
+    // kProMerge (prefetching GEMV): x is the batch-1 attention output merged
+    // from the split attention's partials ([head][split] records of
+    // kAttnPart floats: M, L, -, -, 128 weighted sums), K = heads * 128
+    const float* attn_parts;
+    int attn_splits;
 };
 
 // Batch-1 GEMV with its weights prefetched into shared memory before it waits
@@ -133,6 +138,9 @@ struct AttnArgs {
     // before this launch's predecessor started (a decode step's graph): the
     // kernel may read them, and request the rows, before griddepcontrol.wait
     int pos_stable;
+    // the split partials are left in ws for the consumer to merge (the
+    // batch-1 o projection's prologue); no merge launch, out is not written
+    int no_merge;
 };
 int attn_splits_for(int B, int KVH, int n_max);
 size_t attn_ws_bytes(int B, int H, int splits);
