@@ -123,3 +123,32 @@ def test_batch33_matches_oracle(mode):
         o.close()
     bt.close()
     eng.close()
+
+
+def test_batch_full_model_f32_matches_oracle():
+    """Full Qwen3-0.6B with f32 weights (bf16 pair operands, one GEMM CTA per
+    SM, the q|k|v splits summed in 4-CTA clusters with the q/k norm), 8
+    sequences: sequences 0 and 7 against the oracle's logits and picks."""
+    cfg = vbsynth.qwen3_config()
+    w = vbsynth.make_weights(cfg, seed=57)
+    B, P, G = 8, 5, 3
+    prompts = np.stack([vbsynth.prompt_ids(P, 700 + b, cfg["vocab_size"]) for b in range(B)])
+    eng = vb200.Engine(cfg).load(w)
+    bt = vb200.Batch(eng, B, P + G + 4)
+    for t in range(P):
+        lg, nx = bt.step(prompts[:, t])
+    nxt = bt.decode(nx, G)
+    for b in (0, B - 1):
+        o = oracle.OracleModel(cfg, w)
+        o.reset_cache(P + G + 4)
+        for t in range(P):
+            lo = o.step(int(prompts[b, t]))
+        assert np.max(np.abs(lo - lg[b])) <= TOL["f32"], b
+        tok = oracle.argmax(lo)
+        assert tok == int(nx[b]), b
+        for _ in range(G):
+            tok = oracle.argmax(o.step(tok))
+        assert tok == int(nxt[b]), b
+        o.close()
+    bt.close()
+    eng.close()

@@ -133,7 +133,8 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
     const size_t layer_kv = per_seq * B;
     // C (epilogue) A . W^T on the tensor cores from A's bf16 split (ahi, alo)
     auto gemm = [&](const void* ahi, const void* alo, void* const* w, const float* sc, float* C, int N, int K,
-                    int ldc, int epi, bool wq8, void* ohi, void* olo, bool partials = false) {
+                    int ldc, int epi, bool wq8, void* ohi, void* olo, bool partials = false,
+                    const QkNormArgs* qk = nullptr) {
         TcGemmArgs t{};
         t.w_hi = w[0];
         t.w_lo = wq8 ? nullptr : w[1];
@@ -152,20 +153,20 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         t.out_lo = olo;
         t.partials_only = partials;
         t.err = b->d_err;
+        t.qk = qk;
         return launch_tc_gemm(t, s);
     };
-    // Split-K partials of the q|k|v, o and down projections are left in the
-    // GEMM workspace and summed by their consumer: q/k-norm + RoPE + append,
-    // and residual add + the next RMSNorm (nn.cpp:8-42) + bf16 split.
+    // The q|k|v GEMM sums its splits inside thread-block clusters and applies
+    // the q/k norm + RoPE + append itself (or, past 8 splits, leaves them to the
+    // q/k-norm kernel); the o and down partials are left in the GEMM workspace
+    // and summed by the residual add + the next RMSNorm (nn.cpp:8-42) + bf16 split.
+    const bool qk_fused = tc_gemm_cluster_reduce(B, e->qkv_rows, c.hidden, !q8);
     const float* parts = b->gemm_ws;
     if ((st = launch_rmsnorm_rows(b->x, e->L[0].in_norm, b->xn, B, c.hidden, c.eps, s, b->a_hi, b->a_lo)))
         return st;
     for (int l = 0; l < c.layers; l++) {
         const vb_layer_dev& L = e->L[l];
         void* const* tw = &b->tcw[(size_t)l * 8];
-        if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, nullptr, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore, q8,
-                       nullptr, nullptr, true)))
-            return st;
         QkNormArgs qa{};
         qa.parts = parts;
         qa.splits = tc_gemm_splits(e->qkv_rows, c.hidden, !q8);
@@ -188,10 +189,19 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
         qa.rope_positions = c.rope_positions < b->max_seq ? c.rope_positions : b->max_seq;
         qa.eps = c.eps;
         qa.err = b->d_err;
-        // A separate kernel: inside the attention (fuse_qk) each of the 2560
-        // CTAs would redo the q norm from the partials before streaming its
-        // cache slice, measured 1% slower at 64 sequences.
-        if ((st = launch_qk_norm_rope_append(qa, s))) return st;
+        // (Inside the attention (fuse_qk) each of the 2560 CTAs would redo the
+        // q norm from the partials before streaming its cache slice: measured
+        // 1% slower at 64 sequences than a separate kernel.)
+        if (qk_fused) {
+            if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, nullptr, e->qkv_rows, c.hidden, e->qkv_rows, kEpiQkNorm,
+                           q8, nullptr, nullptr, false, &qa)))
+                return st;
+        } else {
+            if ((st = gemm(b->a_hi, b->a_lo, tw + 0, L.sqkv, nullptr, e->qkv_rows, c.hidden, e->qkv_rows, kEpiStore,
+                           q8, nullptr, nullptr, true)))
+                return st;
+            if ((st = launch_qk_norm_rope_append(qa, s))) return st;
+        }
         AttnArgs aa{};
         aa.q = b->q;
         aa.k = qa.kc;

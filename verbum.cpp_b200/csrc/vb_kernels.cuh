@@ -21,6 +21,8 @@ enum GemvEpi : int {
     kEpiResidual = 1,  // y[j] += dot_j                        (o_proj / down_proj + residual)
     kEpiSwiGLU = 2,    // rows interleaved gate/up: y[j] = silu(dot_2j) * dot_2j+1
     kEpiArgmax = 3,    // y[j] = dot_j and per-CTA (max, argmax) partials
+    kEpiQkNorm = 4,    // tensor-core GEMM of the q|k|v rows (one head per 128-row tile): the
+                       // per-head q/k norm + RoPE, q out, k and v appended to the cache
 };
 
 struct GemvArgs {
@@ -234,9 +236,14 @@ struct TcGemmArgs {
     void* out_lo;
     bool partials_only;    // leave the split partials in ws for a fused consumer
     int* err;
+    const QkNormArgs* qk;  // kEpiQkNorm: norms, rope table, positions, q out, cache (parts / qkv unused)
 };
 // split-K factor of a tensor-core GEMM (pair: f32 weights as a bf16 pair)
 int tc_gemm_splits(int N, int K, bool pair);
+// True when a GEMM of M <= 64 rows can take the kEpiQkNorm epilogue: its
+// split-K partials summed inside a thread-block cluster (at most 8 splits), no
+// workspace round trip and no q/k-norm launch.
+bool tc_gemm_cluster_reduce(int M, int N, int K, bool pair);
 size_t tc_gemm_ws_floats(int M, int N, int K);
 int tc_gemm_tiles(int N);
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s);

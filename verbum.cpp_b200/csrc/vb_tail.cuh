@@ -10,6 +10,32 @@
 
 namespace vb {
 
+// The per-head RMSNorm (q_norm / k_norm, double sum of squares) and split-half
+// RoPE from the host table (generate.cpp:52-64) of one head held by one warp:
+// x[e] is dim lane + 32e, o[e] gets the normed, rotated value.
+static __device__ __forceinline__ void qk_finish(const QkNormArgs& a, bool isq, int pos, const float* x, int lane,
+                                                 float* o) {
+    constexpr int D = 128;
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) ss += (double)x[e] * (double)x[e];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float sc = rms_scale(ss, D, a.eps);
+    const float* nw = isq ? a.q_norm : a.k_norm;
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
+    const float* c = a.cos_tab + (size_t)pos * D;
+    const float* s = a.sin_tab + (size_t)pos * D;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const int d = lane + 32 * e;
+        o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
+                     : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
+    }
+}
+
 // generate.cpp:52-64 for one (row b, head hd) by one warp: per-head RMSNorm
 // (q_norm / k_norm) and split-half RoPE from the host table; o[e] gets dim
 // lane + 32e of the normed, rotated q or k, v[e] (k heads) the v value.  Lane
@@ -57,24 +83,7 @@ static __device__ __forceinline__ bool qk_head(const QkNormArgs& a, int b, int h
             if (!isq) v[e] = row[vcol0 + lane + 32 * e];
         }
     }
-    double ss = 0.0;
-#pragma unroll
-    for (int e = 0; e < 4; e++) ss += (double)x[e] * (double)x[e];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float sc = rms_scale(ss, D, a.eps);
-    const float* nw = isq ? a.q_norm : a.k_norm;
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) y[e] = __fmul_rn(__fmul_rn(x[e], sc), nw[lane + 32 * e]);
-    const float* c = a.cos_tab + (size_t)pos * D;
-    const float* s = a.sin_tab + (size_t)pos * D;
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const int d = lane + 32 * e;
-        o[e] = e < 2 ? __fsub_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e + 2], s[d]))
-                     : __fadd_rn(__fmul_rn(y[e], c[d]), __fmul_rn(y[e - 2], s[d]));
-    }
+    qk_finish(a, isq, pos, x, lane, o);
     return true;
 }
 

@@ -39,6 +39,7 @@
 
 #include "vb_engine.cuh"
 #include "vb_pipe.cuh"
+#include "vb_tail.cuh"
 #include "vb_tc.cuh"
 
 namespace vb {
@@ -74,9 +75,117 @@ struct TcParams {
     __nv_bfloat16* out_hi;
     __nv_bfloat16* out_lo;
     int* err;
+    QkNormArgs qk;  // kEpiQkNorm
 };
 
+// ---------------------------------------------------------------------------
+// Split-K summed inside a thread-block cluster (the q|k|v GEMM of the batched
+// step, epilogue kEpiQkNorm): the S CTAs of a tile's splits
+// form one cluster (cluster rank = split).  Each parks its 128 x 64 partial in
+// its own shared memory as [64 rows][128 features]; after a cluster barrier,
+// rank r reads rows [r R, r R + R) of all S partials over DSMEM, sums them in
+// split order and applies the epilogue; a second barrier keeps every partial
+// alive until all ranks have read it.
+constexpr int kClusterMaxSplits = 8;  // portable cluster size
 
+// (the non-.aligned forms: no assumption that the warp has reconverged)
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ unsigned cl_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned cl_map(unsigned local, unsigned rank) {
+    unsigned r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float cl_ld(unsigned addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned cl_ld_u32(unsigned addr) {
+    unsigned v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// launch_pdl with a (1, cy, 1) cluster: the splits of a tile
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cy,
+                               cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 1;
+    at[1].val.clusterDim.y = cy;
+    at[1].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// Rows [b0, b1) of tile n0 (128 features = one head) from the S parked
+// partials at shared::cluster addresses rq[0..S): the per-head q/k norm +
+// RoPE + append, with the q/k-norm kernel's arithmetic (partials summed in
+// split order from 0, INT8 scale after the sum).  (The same in-cluster sum for
+// the gate|up GEMM's SwiGLU measured slower than its reduce kernel: batched
+// step 6.07 -> 6.22 ms, against 6.07 -> 5.93 ms for this one.)
+__device__ __forceinline__ void cluster_epilogue(const TcParams& p, const unsigned* rq, int S, int n0, int b0,
+                                                 int b1, int warp, int lane) {
+    const QkNormArgs& a = p.qk;
+    const int hd = n0 / kTM;
+    const bool isq = hd < a.H, isk = !isq && hd < a.H + a.KVH;
+    const int h = isq ? hd : (isk ? hd - a.H : hd - a.H - a.KVH);
+    for (int b = b0 + warp; b < b1; b += kTThreads / 32) {
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        const unsigned ro = 4u * (unsigned)(b * kTM + lane);
+#pragma unroll
+        for (int q = 0; q < kClusterMaxSplits; q++) {
+            if (q < S) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) x[e] += cl_ld(rq[q] + ro + 128u * (unsigned)e);
+            }
+        }
+        if (p.scales) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) x[e] *= p.scales[n0 + lane + 32 * e];
+        }
+        const int pos = a.pos[b];
+        if (pos < 0 || pos >= a.rope_positions) {
+            if (lane == 0 && a.err) atomicExch(a.err, kErrCacheFull);
+            continue;
+        }
+        if (isq) {
+            float o[4];
+            qk_finish(a, true, pos, x, lane, o);
+            const size_t qo = ((size_t)b * a.H + h) * kTM;
+#pragma unroll
+            for (int e = 0; e < 4; e++) a.q_out[qo + lane + 32 * e] = o[e];
+        } else {
+            const size_t off = (size_t)b * a.stride_b + (size_t)pos * a.stride_pos + (size_t)h * a.stride_h;
+            if (isk) {
+                float o[4];
+                qk_finish(a, false, pos, x, lane, o);
+#pragma unroll
+                for (int e = 0; e < 4; e++) a.kc[off + lane + 32 * e] = o[e];
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++) a.vc[off + lane + 32 * e] = x[e];
+            }
+        }
+    }
+}
 
 // Instruction descriptor, kind::f16: f32 accumulator [4,6) = 1, A bf16 [7,10) = 1,
 // B bf16 [10,13) = 1, both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
@@ -91,7 +200,7 @@ __device__ __forceinline__ void mma_bf16(unsigned tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
-template <int WP, int NS>
+template <int WP, int NS, bool CL>
 __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
                    const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
@@ -103,6 +212,7 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
     __shared__ __align__(8) unsigned long long full[kTStages], empty[kTStages], done;
     __shared__ unsigned tmem_slot;
     __shared__ int fail;
+    __shared__ unsigned cl_ok;  // CL: this CTA's partial is parked
     const unsigned sbase = (smem_addr(smem_raw) + 1023u) & ~1023u;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTM;
@@ -237,7 +347,13 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int n = n0 + 32 * warp + lane;
-        bool mine = true;  // a single split applies the epilogue itself
+        if constexpr (CL) {
+            // park the partial [64 rows][128 features] in the drained ring
+            float* T = reinterpret_cast<float*>(smem_raw + (sbase - smem_addr(smem_raw)));
+#pragma unroll
+            for (int m = 0; m < kTN; m++) T[m * kTM + 32 * warp + lane] = v[m];
+        }
+        bool mine = !CL;  // a single split applies the epilogue itself
         if (p.splits > 1 || p.partials) {  // (split-K runs with one activation tile)
             mine = false;
             float* P = p.P + (size_t)split * p.M * p.N + n;
@@ -282,6 +398,30 @@ __global__ void __launch_bounds__(kTThreads, ctas_per_sm(WP))
         }
     } else if (threadIdx.x == 0 && nch > 0) {
         atomicCAS(p.err, 0, kErrPipeTimeout);
+    }
+    if constexpr (CL) {
+        // every CTA of the cluster passes both barriers, a failed one too
+        if (threadIdx.x == 0) cl_ok = ok ? 1u : 0u;
+        cluster_sync_all();
+        const int S = p.splits;
+        const unsigned tb = sbase;
+        unsigned rq[kClusterMaxSplits];
+        bool all = true;
+#pragma unroll
+        for (int q = 0; q < kClusterMaxSplits; q++) {
+            rq[q] = 0u;
+            if (q < S) {
+                rq[q] = cl_map(tb, (unsigned)q);
+                all = all && cl_ld_u32(cl_map(smem_addr(&cl_ok), (unsigned)q)) != 0u;
+            }
+        }
+        if (all) {
+            const int r = (int)cl_rank();
+            const int R = (Mt + S - 1) / S;
+            const int b0 = r * R, b1 = min(Mt, b0 + R);
+            cluster_epilogue(p, rq, S, n0, b0, b1, warp, lane);
+        }
+        cluster_sync_all();
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -781,6 +921,10 @@ int tc_gemm_splits(int N, int K, bool pair) {
     return (chunks + per - 1) / per;
 }
 
+bool tc_gemm_cluster_reduce(int M, int N, int K, bool pair) {
+    return M >= 1 && M <= kTN && K % kTK == 0 && K > 0 && tc_gemm_splits(N, K, pair) <= kClusterMaxSplits;
+}
+
 size_t tc_gemm_ws_floats(int M, int N, int K) {
     const int s = std::max(tc_gemm_splits(N, K, false), tc_gemm_splits(N, K, true));
     return (size_t)s * M * N;
@@ -818,13 +962,25 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     const int wp = a.w_lo ? 2 : 1;
     // several activation tiles fill the GPU without split-K
     const int splits = mtiles > 1 ? 1 : tc_gemm_splits(a.N, a.K, wp == 2);
-    if ((splits > 1 || a.partials_only) && (size_t)splits * a.M * a.N > a.ws_floats)
+    // the q/k norm epilogue sums the splits inside a cluster
+    const bool cl = a.epi == kEpiQkNorm && mtiles == 1 && !a.partials_only && splits <= kClusterMaxSplits;
+    if (a.epi == kEpiQkNorm) {
+        if (!cl) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: the q/k norm epilogue needs M <= 64, <= 8 splits");
+        const QkNormArgs* q = a.qk;
+        if (!q || q->D != kTM || q->B != a.M || q->rows_per_seq > 0 || q->q_hi || q->k_hi || !q->q_out || !q->pos ||
+            !q->kc || !q->vc || a.N != (q->H + 2 * q->KVH) * kTM)
+            return fail(VB_ERR_ARG, "tensor-core gemm: q/k norm epilogue arguments");
+    }
+    if (!cl && (splits > 1 || a.partials_only) && (size_t)splits * a.M * a.N > a.ws_floats)
         return fail(VB_ERR_ARG, "tensor-core gemm: workspace too small");
     {
-        static std::atomic<unsigned long long> done_pair{0}, done_single{0};
-        const cudaError_t ce = wp == 2 ? smem_attr_once(tc_gemm_kernel<2, kPStages>, (int)tc_smem(2, kPStages), done_pair)
-                                       : smem_attr_once(tc_gemm_kernel<1, kQStages>, (int)tc_smem(1, kQStages),
-                                                        done_single);
+        static std::atomic<unsigned long long> done_pair{0}, done_single{0}, done_pair_cl{0}, done_single_cl{0};
+        cudaError_t ce = wp == 2 ? smem_attr_once(tc_gemm_kernel<2, kPStages, false>, (int)tc_smem(2, kPStages), done_pair)
+                                 : smem_attr_once(tc_gemm_kernel<1, kQStages, false>, (int)tc_smem(1, kQStages),
+                                                  done_single);
+        if (ce == cudaSuccess && cl)
+            ce = wp == 2 ? smem_attr_once(tc_gemm_kernel<2, kPStages, true>, (int)tc_smem(2, kPStages), done_pair_cl)
+                         : smem_attr_once(tc_gemm_kernel<1, kQStages, true>, (int)tc_smem(1, kQStages), done_single_cl);
         if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core gemm: shared memory attribute");
     }
     CUtensorMap mwh, mwl, mah, mal;
@@ -896,7 +1052,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     const int arows = a.M > kTN ? a.M : kTN;
     if ((st = make_map(&mah, a.a_hi, arows, a.K, kTN))) return st;
     if ((st = make_map(&mal, a.a_lo, arows, a.K, kTN))) return st;
-    if (!a.C && !a.partials_only) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
+    if (!a.C && !a.partials_only && a.epi != kEpiQkNorm) return fail(VB_ERR_ARG, "tensor-core gemm: output missing");
     if (a.epi == kEpiSwiGLU && (a.N % 2)) return fail(VB_ERR_ARG, "tensor-core gemm: swiglu needs even N");
     TcParams p;
     p.M = a.M;
@@ -913,6 +1069,7 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     p.out_hi = static_cast<__nv_bfloat16*>(a.out_hi);
     p.out_lo = static_cast<__nv_bfloat16*>(a.out_lo);
     p.err = a.err;
+    p.qk = a.epi == kEpiQkNorm ? *a.qk : QkNormArgs{};
     const dim3 grid((a.N + kTM - 1) / kTM, splits, mtiles);
     // failure-path test: an armed launch (never one being captured) withholds
     // a stage; the hook word is written and complete before the launch
@@ -923,14 +1080,20 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
         VB_CUDA_TRY(set_fault_word(1, s));
         VB_CUDA_TRY(cudaStreamSynchronize(s));
     }
-    const cudaError_t ce =
-        wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages>, grid, kTThreads, tc_smem(2, kPStages), s, mwh, mwl, mah,
-                             mal, p)
-                : launch_pdl(tc_gemm_kernel<1, kQStages>, grid, kTThreads, tc_smem(1, kQStages), s, mwh, mwl, mah,
-                             mal, p);
+    cudaError_t ce;
+    if (cl)
+        ce = wp == 2 ? launch_pdl_cluster(tc_gemm_kernel<2, kPStages, true>, grid, kTThreads, tc_smem(2, kPStages),
+                                          (unsigned)splits, s, mwh, mwl, mah, mal, p)
+                     : launch_pdl_cluster(tc_gemm_kernel<1, kQStages, true>, grid, kTThreads, tc_smem(1, kQStages),
+                                          (unsigned)splits, s, mwh, mwl, mah, mal, p);
+    else
+        ce = wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages, false>, grid, kTThreads, tc_smem(2, kPStages), s, mwh,
+                                  mwl, mah, mal, p)
+                     : launch_pdl(tc_gemm_kernel<1, kQStages, false>, grid, kTThreads, tc_smem(1, kQStages), s, mwh,
+                                  mwl, mah, mal, p);
     if (inject) VB_CUDA_TRY(set_fault_word(0, s));
     if (ce != cudaSuccess) return cuda_fail(ce, "tc_gemm_kernel launch");
-    if (splits == 1 || a.partials_only) return VB_OK;
+    if (cl || splits == 1 || a.partials_only) return VB_OK;
     GemmArgs g{};
     g.scales = a.scales;
     g.C = a.C;
