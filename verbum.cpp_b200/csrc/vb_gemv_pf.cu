@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
     const size_t row_bytes = (size_t)K * (Q8 ? 1 : 4);
     const size_t bytes = (size_t)rows * row_bytes;
     unsigned char* wsm = pf_smem;
-    float* xs = reinterpret_cast<float*>(pf_smem + kPfSliceBytes);
+    float* xs = reinterpret_cast<float*>(pf_smem + a.pf_xs_off);
 
     // 1. the slice: requested before anything else (it depends on no kernel)
     if (tid == 0) {
@@ -333,7 +333,7 @@ vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStrea
     const int unit = epi == kEpiSwiGLU ? 2 : 1;
     const int units = a.N / unit;
     const size_t es = q8 ? 1 : 4;
-    const size_t smem = kPfSliceBytes + sizeof(float) * (size_t)(q8 ? ((a.K + 511) / 512) * 512 : a.K);
+    const size_t xs_bytes = sizeof(float) * (size_t)(q8 ? ((a.K + 511) / 512) * 512 : a.K);
     for (int p = 0; p < parts; p++) {
         const int uu0 = (int)((long long)p * units / parts), uu1 = (int)((long long)(p + 1) * units / parts);
         GemvArgs g = a;
@@ -351,6 +351,18 @@ vb_status launch_gemv_pf(const GemvArgs& a, bool q8, int pro, int epi, cudaStrea
             g.l2_ahead_bytes = b0 < a.l2_ahead_bytes ? (a.l2_ahead_bytes - b0 < share ? a.l2_ahead_bytes - b0 : share) : 0;
         }
         const int grid = g.N / unit < kPfCtas ? g.N / unit : kPfCtas;
+        // f32: shared memory sized to this launch's largest slice, so the o
+        // and down CTAs (56 / 85 KB) share an SM with the next kernel's
+        // (f32 per-op step 1182 -> 1198 tok/s); INT8: the whole budget, one
+        // CTA per SM -- its 14-42 KB slices let up to eight kernels' CTAs in
+        // at once, measured 1190 -> 921
+        size_t slice = kPfSliceBytes;
+        if (!q8) {
+            const size_t max_units = ((size_t)(g.N / unit) + grid - 1) / grid;
+            slice = (max_units * unit * (size_t)a.K * es + 127) & ~size_t(127);
+        }
+        g.pf_xs_off = (unsigned)slice;
+        const size_t smem = slice + xs_bytes;
         cudaError_t ce;
         if (pro == kProMerge)
             ce = q8 ? launch_pdl(gemv_pf_kernel<true, kProMerge, kEpiResidual>, grid, kPfThreads, smem, s, g)

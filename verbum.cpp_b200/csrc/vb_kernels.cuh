@@ -52,6 +52,7 @@ struct GemvArgs {
     // kAttnPart floats: M, L, -, -, 128 weighted sums), K = heads * 128
     const float* attn_parts;
     int attn_splits;
+    unsigned pf_xs_off;  // prefetching GEMV: byte offset of x in its dynamic shared memory (set by the launcher)
 };
 
 // Batch-1 GEMV with its weights prefetched into shared memory before it waits
