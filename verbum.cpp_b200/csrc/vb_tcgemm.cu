@@ -88,53 +88,6 @@ struct TcParams {
 // alive until all ranks have read it.
 constexpr int kClusterMaxSplits = 8;  // portable cluster size
 
-// (the non-.aligned forms: no assumption that the warp has reconverged)
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ unsigned cl_rank() {
-    unsigned r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ unsigned cl_map(unsigned local, unsigned rank) {
-    unsigned r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float cl_ld(unsigned addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-__device__ __forceinline__ unsigned cl_ld_u32(unsigned addr) {
-    unsigned v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-    return v;
-}
-
-// launch_pdl with a (1, cy, 1) cluster: the splits of a tile
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cy,
-                               cudaStream_t s, Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    at[1].id = cudaLaunchAttributeClusterDimension;
-    at[1].val.clusterDim.x = 1;
-    at[1].val.clusterDim.y = cy;
-    at[1].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
 // Rows [b0, b1) of tile n0 (128 features = one head) from the S parked
 // partials at shared::cluster addresses rq[0..S): the per-head q/k norm +
 // RoPE + append, with the q/k-norm kernel's arithmetic (partials summed in
@@ -1083,9 +1036,9 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     cudaError_t ce;
     if (cl)
         ce = wp == 2 ? launch_pdl_cluster(tc_gemm_kernel<2, kPStages, true>, grid, kTThreads, tc_smem(2, kPStages),
-                                          (unsigned)splits, s, mwh, mwl, mah, mal, p)
+                                          dim3(1, splits, 1), s, mwh, mwl, mah, mal, p)
                      : launch_pdl_cluster(tc_gemm_kernel<1, kQStages, true>, grid, kTThreads, tc_smem(1, kQStages),
-                                          (unsigned)splits, s, mwh, mwl, mah, mal, p);
+                                          dim3(1, splits, 1), s, mwh, mwl, mah, mal, p);
     else
         ce = wp == 2 ? launch_pdl(tc_gemm_kernel<2, kPStages, false>, grid, kTThreads, tc_smem(2, kPStages), s, mwh,
                                   mwl, mah, mal, p)
