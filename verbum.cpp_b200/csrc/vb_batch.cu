@@ -36,6 +36,7 @@ struct vb_batch {
     int* d_tok = nullptr;
     int* d_pos = nullptr;
     int* d_next = nullptr;
+    unsigned long long* d_keys = nullptr;  // [B] argmax keys of the decode step (zero between steps)
     int* d_err = nullptr;
     int* h_io = nullptr;  // pinned [2*B + 1]: tokens in, next tokens out, error word
     cudaGraphExec_t graph = nullptr;
@@ -244,8 +245,9 @@ vb_status enqueue_batch_step(vb_batch* b, cudaStream_t s) {
                        e->lm_int8, nullptr, nullptr)))
             return st;
     }
-    if ((st = launch_argmax_rows(b->logits, B, c.vocab, b->d_next, s))) return st;
-    return launch_advance(b->d_pos, b->d_tok, b->d_next, B, s);
+    // (one CTA per row measured ~33 us a step; 16 CTAs per row fold into keys)
+    if ((st = launch_argmax_rows_keys(b->logits, B, c.vocab, b->d_keys, s))) return st;
+    return launch_advance_keys(b->d_pos, b->d_tok, b->d_next, b->d_keys, B, s);
 }
 
 // Device buffers of one prompt chunk of R = B * C rows (row b*C + c is
@@ -641,6 +643,9 @@ vb_status vb_batch_create(vb_engine* e, int batch, int max_seq, vb_batch** out) 
     if ((st = balloc(&b->d_tok, batch, "tok"))) return bail(st);
     if ((st = balloc(&b->d_pos, batch, "pos"))) return bail(st);
     if ((st = balloc(&b->d_next, batch, "next"))) return bail(st);
+    if ((st = balloc(&b->d_keys, batch, "argmax keys"))) return bail(st);
+    if (cudaMemsetAsync(b->d_keys, 0, sizeof(unsigned long long) * batch, es))
+        return bail(fail(VB_ERR_CUDA, "argmax keys memset failed"));
     if ((st = balloc(&b->d_err, 1, "err"))) return bail(st);
     if (cudaMemsetAsync(b->d_pos, 0, sizeof(int) * batch, es) ||
         cudaMemsetAsync(b->d_tok, 0, sizeof(int) * batch, es) ||
@@ -659,7 +664,7 @@ vb_status vb_batch_destroy(vb_batch* b) {
     if (b->graph) cudaGraphExecDestroy(b->graph);
     bfree(b->kc); bfree(b->vc); bfree(b->x); bfree(b->xn); bfree(b->q);
     bfree(b->ctx); bfree(b->h); bfree(b->logits); bfree(b->attn_ws); bfree(b->gemm_ws);
-    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_err);
+    bfree(b->d_tok); bfree(b->d_pos); bfree(b->d_next); bfree(b->d_keys); bfree(b->d_err);
     if (b->arena) cudaFree(b->arena);
     free_tc_weights(b);
     bfree(b->lm_hi); bfree(b->lm_lo); bfree(b->a_hi); bfree(b->a_lo); bfree(b->y_hi); bfree(b->y_lo);

@@ -806,6 +806,77 @@ __global__ void embed_kernel(const float* E, const int* tokens, int dim, int voc
     for (int i = threadIdx.x; i < dim / 4; i += blockDim.x) dst[i] = src[i];
 }
 
+// (value, index) -> a key whose unsigned order is better()'s order: the
+// value's bits mapped to an unsigned order (-0 taken as +0), then the index
+// complemented so that the lower index wins a tie
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    unsigned u = __float_as_uint(v + 0.0f);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+}
+
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxChunks = 16;  // CTAs per row
+
+// grid (kArgmaxChunks, rows): a contiguous slice of one row, 16-byte loads
+// where the row allows them
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_keys_kernel(const float* logits, int64_t n,
+                                                                     unsigned long long* keys) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long sk[kArgmaxThreads / 32];
+    const float* row = logits + (size_t)blockIdx.y * (size_t)n;
+    const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+    const int64_t i0 = (int64_t)blockIdx.x * per < n ? (int64_t)blockIdx.x * per : n;
+    const int64_t i1 = i0 + per < n ? i0 + per : n;
+    unsigned long long best = 0ull;
+    auto take = [&](float v, int64_t i) {
+        if (v == v) {  // NaN is never picked
+            const unsigned long long k = argmax_key(v, (int)i);
+            best = k > best ? k : best;
+        }
+    };
+    // aligned float4 body when the row start and slice start are 16-byte aligned
+    const bool vec = ((reinterpret_cast<uintptr_t>(row + i0) & 15u) == 0);
+    int64_t i = i0;
+    if (vec) {
+        const int64_t nv = (i1 - i0) / 4;
+        const float4* r4 = reinterpret_cast<const float4*>(row + i0);
+        for (int64_t j = threadIdx.x; j < nv; j += kArgmaxThreads) {
+            const float4 v = __ldcg(r4 + j);
+            const int64_t b = i0 + 4 * j;
+            take(v.x, b); take(v.y, b + 1); take(v.z, b + 2); take(v.w, b + 3);
+        }
+        i = i0 + 4 * nv;
+    }
+    for (int64_t j = i + threadIdx.x; j < i1; j += kArgmaxThreads) take(__ldcg(row + j), j);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best, o);
+        best = ok > best ? ok : best;
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sk[w] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < kArgmaxThreads / 32; k++) best = sk[k] > best ? sk[k] : best;
+        if (best) atomicMax(keys + blockIdx.y, best);
+    }
+}
+
+__global__ void advance_keys_kernel(int* pos, int* tokens, int* next, unsigned long long* keys, int B) {
+    pdl_trigger();
+    pdl_wait();
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        const unsigned long long k = keys[b];
+        const int idx = k ? (int)(0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull)) : 0;
+        next[b] = idx;
+        tokens[b] = idx;
+        pos[b] += 1;
+        keys[b] = 0ull;
+    }
+}
+
 __global__ void advance_kernel(int* pos, int* tokens, const int* next, int B) {
     pdl_trigger();
     pdl_wait();
@@ -1049,6 +1120,21 @@ vb_status launch_argmax_rows(const float* logits, int rows, int64_t n, int* out,
     if (rows <= 0 || n <= 0) return fail(VB_ERR_ARG, "argmax: empty input");
     launch_pdl(argmax_rows_kernel, rows, 1024, 0, s, logits, n, out);
     VB_LAUNCH_CHECK("argmax_rows_kernel");
+    return VB_OK;
+}
+
+vb_status launch_argmax_rows_keys(const float* logits, int rows, int64_t n, unsigned long long* keys,
+                                  cudaStream_t s) {
+    if (rows <= 0 || n <= 0 || rows > 65535) return fail(VB_ERR_ARG, "argmax: bad shape");
+    if (n > INT_MAX) return fail(VB_ERR_UNSUPPORTED, "argmax: row longer than INT_MAX");
+    launch_pdl(argmax_keys_kernel, dim3(kArgmaxChunks, rows), kArgmaxThreads, 0, s, logits, n, keys);
+    VB_LAUNCH_CHECK("argmax_keys_kernel");
+    return VB_OK;
+}
+
+vb_status launch_advance_keys(int* pos, int* tokens, int* next, unsigned long long* keys, int B, cudaStream_t s) {
+    launch_pdl(advance_keys_kernel, 1, 128, 0, s, pos, tokens, next, keys, B);
+    VB_LAUNCH_CHECK("advance_keys_kernel");
     return VB_OK;
 }
 

@@ -192,6 +192,15 @@ vb_status launch_cache_append(float* kc, float* vc, const float* kn, const float
                               int pos, int width, cudaStream_t s);
 // pos[b] += 1; tokens[b] = next[b]
 vb_status launch_advance(int* pos, int* tokens, const int* next, int B, cudaStream_t s);
+// Per-row argmax of a decode step's logits [rows][n] over all SMs: each CTA
+// folds its slice into keys[row] (atomicMax of a (value, lowest index) key);
+// keys must be zero before.  launch_advance_keys then turns the keys into
+// next[] (argmax_rows_kernel's result: lowest index on ties, NaN never
+// picked, 0 for a row without a pick), tokens = next, pos += 1, and zeroes
+// the keys for the next step.
+vb_status launch_argmax_rows_keys(const float* logits, int rows, int64_t n, unsigned long long* keys,
+                                  cudaStream_t s);
+vb_status launch_advance_keys(int* pos, int* tokens, int* next, unsigned long long* keys, int B, cudaStream_t s);
 
 // Batched (M <= 64) GEMM, C = A . W^T with split-K partials and a fused
 // reduction epilogue.

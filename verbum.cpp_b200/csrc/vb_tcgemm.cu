@@ -91,9 +91,10 @@ constexpr int kClusterMaxSplits = 8;  // portable cluster size
 // Rows [b0, b1) of tile n0 (128 features = one head) from the S parked
 // partials at shared::cluster addresses rq[0..S): the per-head q/k norm +
 // RoPE + append, with the q/k-norm kernel's arithmetic (partials summed in
-// split order from 0, INT8 scale after the sum).  (The same in-cluster sum for
-// the gate|up GEMM's SwiGLU measured slower than its reduce kernel: batched
-// step 6.07 -> 6.22 ms, against 6.07 -> 5.93 ms for this one.)
+// split order from 0, INT8 scale after the sum).  The same in-cluster sum
+// for the gate|up GEMM's SwiGLU measured slower than its reduce kernel
+// (batched step 5.77 -> 5.93 ms with 2 splits, whose 48 clusters are all
+// resident; 6.07 -> 6.22 ms with 3, which are not).
 __device__ __forceinline__ void cluster_epilogue(const TcParams& p, const unsigned* rq, int S, int n0, int b0,
                                                  int b1, int warp, int lane) {
     const QkNormArgs& a = p.qk;
@@ -874,8 +875,11 @@ int tc_gemm_splits(int N, int K, bool pair) {
     return (chunks + per - 1) / per;
 }
 
+int cluster_splits(int wp, int tiles, int chunks, int splits);
+
 bool tc_gemm_cluster_reduce(int M, int N, int K, bool pair) {
-    return M >= 1 && M <= kTN && K % kTK == 0 && K > 0 && tc_gemm_splits(N, K, pair) <= kClusterMaxSplits;
+    if (M < 1 || M > kTN || K % kTK || K <= 0 || N <= 0) return false;
+    return cluster_splits(pair ? 2 : 1, (N + kTM - 1) / kTM, K / kTK, tc_gemm_splits(N, K, pair)) > 0;
 }
 
 size_t tc_gemm_ws_floats(int M, int N, int K) {
@@ -905,6 +909,65 @@ vb_status launch_weights_bf16(const void* W, bool q8, size_t count, void* hi, vo
     return VB_OK;
 }
 
+// How many (1, cs, 1) clusters of the decode GEMM are resident at once on
+// this device (cached per device, weight form and cluster size).
+int cluster_capacity(int wp, int cs) {
+    static std::atomic<int> cache[8][2][kClusterMaxSplits + 1] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::atomic<int>* slot = dev < 8 ? &cache[dev][wp - 1][cs] : nullptr;
+    if (slot) {
+        const int v = slot->load();
+        if (v) return v;
+    }
+    {
+        // the occupancy query sees the kernel's dynamic shared memory limit
+        static std::atomic<unsigned long long> done_pair{0}, done_single{0};
+        const cudaError_t ce = wp == 2 ? smem_attr_once(tc_gemm_kernel<2, kPStages, true>, (int)tc_smem(2, kPStages),
+                                                        done_pair)
+                                       : smem_attr_once(tc_gemm_kernel<1, kQStages, true>, (int)tc_smem(1, kQStages),
+                                                        done_single);
+        if (ce != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, cs, 1);
+    cfg.blockDim = dim3(kTThreads);
+    cfg.dynamicSmemBytes = wp == 2 ? tc_smem(2, kPStages) : tc_smem(1, kQStages);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = cs;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t ce = wp == 2 ? cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<2, kPStages, true>, &cfg)
+                                   : cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<1, kQStages, true>, &cfg);
+    if (ce != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (slot) slot->store(n > 0 ? n : -1);
+    return n;
+}
+
+// The largest split count <= min(splits, 8) whose clusters (one per tile) are
+// all resident at once: a second wave of clusters would double the GEMM (one
+// CTA per SM on a B200 holds 33 4-CTA clusters -- the q|k|v GEMM's 32 tiles x
+// 4 splits fit -- 45 3-CTA and 15 8-CTA clusters).  Every split gets at least
+// one chunk.  0: none fits.
+int cluster_splits(int wp, int tiles, int chunks, int splits) {
+    for (int cs = std::min(splits, kClusterMaxSplits); cs >= 1; cs--) {
+        const int per = (chunks + cs - 1) / cs;
+        const int eff = (chunks + per - 1) / per;
+        if (cluster_capacity(wp, eff) >= tiles) return eff;
+    }
+    return 0;
+}
+
 vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if (a.M < 1) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: M must be >= 1");
     const int mtiles = (a.M + kTN - 1) / kTN;
@@ -914,11 +977,16 @@ vb_status launch_tc_gemm(const TcGemmArgs& a, cudaStream_t s) {
     if (a.N <= 0) return fail(VB_ERR_ARG, "tensor-core gemm: N <= 0");
     const int wp = a.w_lo ? 2 : 1;
     // several activation tiles fill the GPU without split-K
-    const int splits = mtiles > 1 ? 1 : tc_gemm_splits(a.N, a.K, wp == 2);
-    // the q/k norm epilogue sums the splits inside a cluster
-    const bool cl = a.epi == kEpiQkNorm && mtiles == 1 && !a.partials_only && splits <= kClusterMaxSplits;
+    int splits = mtiles > 1 ? 1 : tc_gemm_splits(a.N, a.K, wp == 2);
+    // the q/k norm sums its splits inside a cluster, with a split count whose
+    // clusters are all resident at once
+    int cl_s = 0;
+    if (a.epi == kEpiQkNorm && mtiles == 1 && !a.partials_only)
+        cl_s = cluster_splits(wp, (a.N + kTM - 1) / kTM, a.K / kTK, splits);
+    const bool cl = cl_s > 0;
+    if (cl) splits = cl_s;
     if (a.epi == kEpiQkNorm) {
-        if (!cl) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: the q/k norm epilogue needs M <= 64, <= 8 splits");
+        if (!cl) return fail(VB_ERR_UNSUPPORTED, "tensor-core gemm: the q/k norm epilogue needs M <= 64");
         const QkNormArgs* q = a.qk;
         if (!q || q->D != kTM || q->B != a.M || q->rows_per_seq > 0 || q->q_hi || q->k_hi || !q->q_out || !q->pos ||
             !q->kc || !q->vc || a.N != (q->H + 2 * q->KVH) * kTM)

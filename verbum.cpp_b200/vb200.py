@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -347,6 +348,10 @@ class Engine:
 
     def close(self):
         if getattr(self, "h", None):
+            # a batch refers to its engine: close the engine's live batches
+            # first (finalizers of a collected cycle run in any order)
+            for b in list(getattr(self, "_batches", ())):
+                b.close()
             lib().vb_engine_destroy(self.h)
             self.h = None
 
@@ -366,6 +371,9 @@ class Batch:
         h = C.c_void_p()
         check(lib().vb_batch_create(engine.h, self.B, int(max_seq), C.byref(h)))
         self.h = h
+        if not hasattr(engine, "_batches"):
+            engine._batches = weakref.WeakSet()
+        engine._batches.add(self)
 
     def step(self, tokens, want_logits=True, want_next=True):
         t = np.ascontiguousarray(tokens, dtype=np.int32)
