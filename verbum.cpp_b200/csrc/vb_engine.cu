@@ -161,30 +161,97 @@ static vb_status step_gemv(vb_engine* e, int j, GemvArgs g, bool q8, int pro, in
     return launch_gemv(g, q8, pro, epi, s);
 }
 
+// The projection k of layer l (0 q|k|v with the input RMSNorm, 1 o with the
+// residual, 2 gate/up with the post-attention RMSNorm and SwiGLU, 3 down with
+// the residual) as a batch-1 GEMV.
+static GemvArgs layer_gemv(const vb_engine* e, int l, int k, int* pro, int* epi) {
+    const vb_config& c = e->cfg;
+    const bool q8 = e->quantized;
+    const vb_layer_dev& L = e->L[l];
+    GemvArgs g{};
+    g.eps = c.eps;
+    g.err = e->d_err;
+    switch (k) {
+        case 0: {
+            const size_t layer_kv = (size_t)c.kv_heads * e->max_seq * c.head_dim;
+            g.x = e->x;
+            g.norm_w = L.in_norm;
+            g.W = q8 ? (const void*)L.qqkv : (const void*)L.wqkv;
+            g.scales = L.sqkv;
+            g.y = e->qkv;
+            g.N = e->qkv_rows;
+            g.K = c.hidden;
+            // this layer's cached K / V rows into L2 for the attention after it
+            g.kv_k = e->kc + l * layer_kv;
+            g.kv_v = e->vc + l * layer_kv;
+            g.kv_pos = e->d_pos;
+            g.kv_heads = c.kv_heads;
+            g.kv_stride_h = (int64_t)e->max_seq * c.head_dim;
+            *pro = kProRms;
+            *epi = kEpiStore;
+            break;
+        }
+        case 1:
+            g.x = e->ctx;
+            g.attn_parts = e->attn_ws;
+            g.attn_splits = e->attn_splits;
+            g.W = q8 ? (const void*)L.qo : (const void*)L.wo;
+            g.scales = L.so;
+            g.y = e->x;
+            g.N = c.hidden;
+            g.K = e->q_width;
+            *pro = kProNone;
+            *epi = kEpiResidual;
+            break;
+        case 2:
+            g.x = e->x;
+            g.norm_w = L.post_norm;
+            g.W = q8 ? (const void*)L.qgu : (const void*)L.wgu;
+            g.scales = L.sgu;
+            g.y = e->h;
+            g.N = 2 * c.ffn;
+            g.K = c.hidden;
+            *pro = kProRms;
+            *epi = kEpiSwiGLU;
+            break;
+        default:
+            g.x = e->h;
+            g.W = q8 ? (const void*)L.qd : (const void*)L.wd;
+            g.scales = L.sd;
+            g.y = e->x;
+            g.N = c.hidden;
+            g.K = c.ffn;
+            *pro = kProNone;
+            *epi = kEpiResidual;
+            break;
+    }
+    return g;
+}
+
+// One decode step of the per-op path.  Per layer: q|k|v GEMV -> split
+// attention (q/k norm, RoPE and cache append inside) [-> split merge] -> o ->
+// gate/up -> down.  (o, gate/up, down and the next layer's q|k|v as one launch
+// with grid barriers between them, every INT8 slice in shared memory from
+// the start, measured slower: INT8 per-op 1181 -> 885 tok/s.)
 vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
     const vb_config& c = e->cfg;
     const bool q8 = e->quantized;
     vb_status st;
     if ((st = launch_embed(e->embed, e->d_tok, 1, c.hidden, c.vocab, e->x, e->d_err, s))) return st;
     const size_t layer_kv = (size_t)c.kv_heads * e->max_seq * c.head_dim;
+    // With few splits the o projection merges the split partials in its
+    // prologue: one launch fewer on the step's dependency chain (f32 at
+    // 3 splits, context <= 168: 1136 -> 1162 tok/s).  Every CTA merges all
+    // heads, a serial pass over the splits: at 13 splits (INT8, context
+    // ~770) that measured slower than the merge launch (1185 -> 1052).
+    const bool merge_in_o = e->attn_splits <= 4 && step_gemv_pf_fits(e, c.hidden, e->q_width, q8, kEpiResidual);
     for (int l = 0; l < c.layers; l++) {
         const vb_layer_dev& L = e->L[l];
-        GemvArgs g{};
-        g.x = e->x;
-        g.norm_w = L.in_norm;
-        g.eps = c.eps;
-        g.W = q8 ? (const void*)L.qqkv : (const void*)L.wqkv;
-        g.scales = L.sqkv;
-        g.y = e->qkv;
-        g.N = e->qkv_rows;
-        g.K = c.hidden;
-        // this layer's cached K / V rows into L2 for the attention below
-        g.kv_k = e->kc + l * layer_kv;
-        g.kv_v = e->vc + l * layer_kv;
-        g.kv_pos = e->d_pos;
-        g.kv_heads = c.kv_heads;
-        g.kv_stride_h = (int64_t)e->max_seq * c.head_dim;
-        if ((st = step_gemv(e, 4 * l + 0, g, q8, kProRms, kEpiStore, s))) return st;
+        int pro = 0, epi = 0;
+        {
+            const GemvArgs g = layer_gemv(e, l, 0, &pro, &epi);
+            if ((st = step_gemv(e, 4 * l + 0, g, q8, pro, epi, s))) return st;
+        }
 
         QkNormArgs qa{};
         qa.qkv = e->qkv;
@@ -233,45 +300,14 @@ vb_status enqueue_step_ops(vb_engine* e, cudaStream_t s) {
         // last split CTA instead of the merge kernel measured slower (1031):
         // its fence and ticket round trip cost more than the launch.
         aa.pos_stable = 1;
-        // With few splits the o projection merges the split partials in its
-        // prologue: one launch fewer on the step's dependency chain (f32 at
-        // 3 splits, context <= 168: 1136 -> 1162 tok/s).  Every CTA merges all
-        // heads, a serial pass over the splits: at 13 splits (INT8, context
-        // ~770) that measured slower than the merge launch (1185 -> 1052).
-        const bool merge_in_o = e->attn_splits <= 4 && step_gemv_pf_fits(e, c.hidden, e->q_width, q8, kEpiResidual);
         aa.no_merge = merge_in_o ? 1 : 0;
         if ((st = launch_attention(aa, s))) return st;
 
-        GemvArgs o{};
-        o.x = e->ctx;
-        o.attn_parts = e->attn_ws;
-        o.attn_splits = e->attn_splits;
-        o.W = q8 ? (const void*)L.qo : (const void*)L.wo;
-        o.scales = L.so;
-        o.y = e->x;
-        o.N = c.hidden;
-        o.K = e->q_width;
-        if ((st = step_gemv(e, 4 * l + 1, o, q8, merge_in_o ? kProMerge : kProNone, kEpiResidual, s))) return st;
-
-        GemvArgs gu{};
-        gu.x = e->x;
-        gu.norm_w = L.post_norm;
-        gu.eps = c.eps;
-        gu.W = q8 ? (const void*)L.qgu : (const void*)L.wgu;
-        gu.scales = L.sgu;
-        gu.y = e->h;
-        gu.N = 2 * c.ffn;
-        gu.K = c.hidden;
-        if ((st = step_gemv(e, 4 * l + 2, gu, q8, kProRms, kEpiSwiGLU, s))) return st;
-
-        GemvArgs dn{};
-        dn.x = e->h;
-        dn.W = q8 ? (const void*)L.qd : (const void*)L.wd;
-        dn.scales = L.sd;
-        dn.y = e->x;
-        dn.N = c.hidden;
-        dn.K = c.ffn;
-        if ((st = step_gemv(e, 4 * l + 3, dn, q8, kProNone, kEpiResidual, s))) return st;
+        for (int k = 1; k <= 3; k++) {
+            GemvArgs g = layer_gemv(e, l, k, &pro, &epi);
+            if (k == 1 && merge_in_o) pro = kProMerge;
+            if ((st = step_gemv(e, 4 * l + k, g, q8, pro, epi, s))) return st;
+        }
     }
     GemvArgs lm{};
     lm.x = e->x;

@@ -42,75 +42,77 @@ __device__ __noinline__ bool pf_wait_slice(unsigned a) {
     }
 }
 
-template <bool Q8, int PRO, int EPI>
-__global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
-    extern __shared__ __align__(128) unsigned char pf_smem[];
-    __shared__ __align__(8) unsigned long long full;
-    __shared__ double red[kPfWarps];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int K = a.K, G = gridDim.x, c = blockIdx.x;
-    constexpr int unit = (EPI == kEpiSwiGLU) ? 2 : 1;  // gate/up rows stay together
+// This CTA's rows of a GEMV: units (rows, or gate/up row pairs) are split
+// evenly over the G CTAs.
+struct PfSlice {
+    int r0, rows;
+    size_t row_bytes, bytes;
+};
+template <bool Q8>
+__device__ __forceinline__ PfSlice pf_slice(const GemvArgs& a, int epi, int c, int G) {
+    const int unit = (epi == kEpiSwiGLU) ? 2 : 1;  // gate/up rows stay together
     const int units = a.N / unit;
     const int u0 = (int)((long long)c * units / G), u1 = (int)((long long)(c + 1) * units / G);
-    const int r0 = u0 * unit, rows = (u1 - u0) * unit;
-    const size_t row_bytes = (size_t)K * (Q8 ? 1 : 4);
-    const size_t bytes = (size_t)rows * row_bytes;
-    unsigned char* wsm = pf_smem;
-    float* xs = reinterpret_cast<float*>(pf_smem + a.pf_xs_off);
+    PfSlice sl;
+    sl.r0 = u0 * unit;
+    sl.rows = (u1 - u0) * unit;
+    sl.row_bytes = (size_t)a.K * (Q8 ? 1 : 4);
+    sl.bytes = (size_t)sl.rows * sl.row_bytes;
+    return sl;
+}
 
-    // 1. the slice: requested before anything else (it depends on no kernel)
-    if (tid == 0) {
-        mbar_init(smem_addr(&full), 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        if (bytes) {
-            unsigned long long pol;
-            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-            mbar_expect_tx(smem_addr(&full), (unsigned)bytes);
-            const char* src = static_cast<const char*>(a.W) + (size_t)r0 * row_bytes;
-            for (size_t off = 0; off < bytes; off += kPfChunk) {
-                const unsigned n = (unsigned)(bytes - off < (size_t)kPfChunk ? bytes - off : (size_t)kPfChunk);
-                bulk_g2s(smem_addr(wsm + off), src + off, n, smem_addr(&full), pol);
-            }
-        }
+// Thread 0: the slice into shared memory (bulk copies completing on `bar`).
+__device__ __forceinline__ void pf_issue_slice(const GemvArgs& a, const PfSlice& sl, unsigned char* dst, unsigned bar) {
+    if (!sl.bytes) return;
+    unsigned long long pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    mbar_expect_tx(bar, (unsigned)sl.bytes);
+    const char* src = static_cast<const char*>(a.W) + (size_t)sl.r0 * sl.row_bytes;
+    for (size_t off = 0; off < sl.bytes; off += kPfChunk) {
+        const unsigned n = (unsigned)(sl.bytes - off < (size_t)kPfChunk ? sl.bytes - off : (size_t)kPfChunk);
+        bulk_g2s(smem_addr(dst + off), src + off, n, bar, pol);
     }
-    // 1b. a later kernel's weights into L2 (this CTA's share, 16-byte pieces),
-    //     so the HBM stream runs ahead of the kernels that consume it
-    if (tid == 32 && a.l2_ahead && a.l2_ahead_bytes) {
-        const size_t share = (a.l2_ahead_bytes / G + 15) & ~size_t(15);
-        const size_t b0 = share * c;
-        const size_t b1 = b0 + share < a.l2_ahead_bytes ? b0 + share : a.l2_ahead_bytes;
-        const char* base = static_cast<const char*>(a.l2_ahead);
+}
+
+// One thread: this CTA's 1/G share of [base, base + total) into L2.
+__device__ __forceinline__ void pf_l2_share(const void* base_, size_t total, int c, int G) {
+    if (!base_ || !total) return;
+    const size_t share = (total / G + 15) & ~size_t(15);
+    const size_t b0 = share * c;
+    const size_t b1 = b0 + share < total ? b0 + share : total;
+    const char* base = static_cast<const char*>(base_);
+    for (size_t off = b0; off + 16 <= b1; off += kPfChunk) {
+        const size_t n = (b1 - off < (size_t)kPfChunk ? b1 - off : (size_t)kPfChunk) & ~size_t(15);
+        if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"((unsigned)n) : "memory");
+    }
+}
+
+// One thread: the attention's cached K / V rows into L2 -- span s = (head, K
+// or V) of pos * 512 bytes, split into G / (2 heads) pieces.
+__device__ __forceinline__ void pf_kv_share(const GemvArgs& a, int c, int G) {
+    if (!a.kv_k || a.kv_heads <= 0) return;
+    const int spans = 2 * a.kv_heads;
+    const int pieces = G / spans > 0 ? G / spans : 1;
+    const int sp = c % spans, pc = c / spans;
+    const int pos = *a.kv_pos;  // written before this step (positions already cached)
+    if (pc < pieces && pos > 0) {
+        const size_t span = (size_t)pos * 512;
+        const size_t share = (span / pieces + 15) & ~size_t(15);
+        const size_t b0 = share * pc, b1 = b0 + share < span ? b0 + share : span;
+        const float* h = ((sp & 1) ? a.kv_v : a.kv_k) + (size_t)(sp >> 1) * a.kv_stride_h;
+        const char* base = reinterpret_cast<const char*>(h);
         for (size_t off = b0; off + 16 <= b1; off += kPfChunk) {
             const size_t n = (b1 - off < (size_t)kPfChunk ? b1 - off : (size_t)kPfChunk) & ~size_t(15);
             if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"((unsigned)n) : "memory");
         }
     }
-    // 1c. the attention's cached K / V rows into L2: span s = (head, K or V)
-    //     of pos * 512 bytes, split into G / (2 heads) pieces
-    if (tid == 64 && a.kv_k && a.kv_heads > 0) {
-        const int spans = 2 * a.kv_heads;
-        const int pieces = G / spans > 0 ? G / spans : 1;
-        const int sp = c % spans, pc = c / spans;
-        const int pos = *a.kv_pos;  // written before this step (positions already cached)
-        if (pc < pieces && pos > 0) {
-            const size_t span = (size_t)pos * 512;
-            const size_t share = (span / pieces + 15) & ~size_t(15);
-            const size_t b0 = share * pc, b1 = b0 + share < span ? b0 + share : span;
-            const float* h = ((sp & 1) ? a.kv_v : a.kv_k) + (size_t)(sp >> 1) * a.kv_stride_h;
-            const char* base = reinterpret_cast<const char*>(h);
-            for (size_t off = b0; off + 16 <= b1; off += kPfChunk) {
-                const size_t n = (b1 - off < (size_t)kPfChunk ? b1 - off : (size_t)kPfChunk) & ~size_t(15);
-                if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"((unsigned)n) : "memory");
-            }
-        }
-    }
-    // 2. let the next kernel start prefetching its own slice, then wait for
-    //    the kernels this one reads from
-    pdl_trigger();
-    pdl_wait();
+}
 
-    // 3. x (normalised when PRO is kProRms, merged from the attention's split
-    //    partials when kProMerge), laid out for conflict-free reads
+// x into shared memory (normalised when PRO is kProRms, merged from the
+// attention's split partials when kProMerge), laid out for conflict-free reads.
+template <bool Q8, int PRO>
+__device__ __forceinline__ void pf_load_x(const GemvArgs& a, float* xs, double* red, int tid, int warp, int lane) {
+    const int K = a.K;
     const float* x = a.x;
     if (a.x_tok) x += (size_t)(*a.x_tok) * (size_t)K;
     float sc = 1.0f;
@@ -174,22 +176,15 @@ __global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
         }
     }
 
-    // 4. the slice has landed (thread 0 waits; every thread then observes the
-    //    completed phase itself, which orders its reads after the copies)
-    int ok = 1;
-    if (tid == 0 && bytes) ok = pf_wait_slice(smem_addr(&full)) ? 1 : 0;
-    if (!__syncthreads_and(ok)) {
-        // a copy that never completed: record it, give the copies in flight
-        // their bound to land (the shared memory goes to the next CTA), leave
-        if (tid == 0) {
-            if (a.err) atomicCAS(a.err, 0, kErrPipeTimeout);
-            mbar_drain(smem_addr(&full), 0u);
-        }
-        return;
-    }
-    if (bytes) (void)mbar_try(smem_addr(&full), 0u);
+}
 
-    // 5. dot products: row pairs (or single rows) round-robin over the warps
+// The slice's dot products (row pairs, or single rows, round-robin over the
+// warps) and the epilogue.
+template <bool Q8, int EPI>
+__device__ __forceinline__ void pf_rows(const GemvArgs& a, const PfSlice& sl, const unsigned char* wsm, const float* xs,
+                                        int warp, int lane) {
+    const int K = a.K, r0 = sl.r0, rows = sl.rows;
+    const size_t row_bytes = sl.row_bytes;
     constexpr int R = 2;
     for (int rg = warp * R; rg < rows; rg += kPfWarps * R) {
         float acc[R];
@@ -259,6 +254,52 @@ __global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
             }
         }
     }
+}
+
+template <bool Q8, int PRO, int EPI>
+__global__ void __launch_bounds__(kPfThreads) gemv_pf_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) unsigned char pf_smem[];
+    __shared__ __align__(8) unsigned long long full;
+    __shared__ double red[kPfWarps];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const PfSlice sl = pf_slice<Q8>(a, EPI, c, G);
+    unsigned char* wsm = pf_smem;
+    float* xs = reinterpret_cast<float*>(pf_smem + a.pf_xs_off);
+
+    // 1. the slice: requested before anything else (it depends on no kernel);
+    //    a later kernel's weights into L2 (this CTA's share), so the HBM stream
+    //    runs ahead of the kernels that consume it; the attention's cached K / V
+    //    rows into L2
+    if (tid == 0) {
+        mbar_init(smem_addr(&full), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        pf_issue_slice(a, sl, wsm, smem_addr(&full));
+    }
+    if (tid == 32) pf_l2_share(a.l2_ahead, a.l2_ahead_bytes, c, G);
+    if (tid == 64) pf_kv_share(a, c, G);
+    // 2. let the next kernel start prefetching its own slice, then wait for
+    //    the kernels this one reads from
+    pdl_trigger();
+    pdl_wait();
+    // 3. x
+    pf_load_x<Q8, PRO>(a, xs, red, tid, warp, lane);
+    // 4. the slice has landed (thread 0 waits; every thread then observes the
+    //    completed phase itself, which orders its reads after the copies)
+    int ok = 1;
+    if (tid == 0 && sl.bytes) ok = pf_wait_slice(smem_addr(&full)) ? 1 : 0;
+    if (!__syncthreads_and(ok)) {
+        // a copy that never completed: record it, give the copies in flight
+        // their bound to land (the shared memory goes to the next CTA), leave
+        if (tid == 0) {
+            if (a.err) atomicCAS(a.err, 0, kErrPipeTimeout);
+            mbar_drain(smem_addr(&full), 0u);
+        }
+        return;
+    }
+    if (sl.bytes) (void)mbar_try(smem_addr(&full), 0u);
+    // 5. dot products and epilogue
+    pf_rows<Q8, EPI>(a, sl, wsm, xs, warp, lane);
 }
 
 template <bool Q8, int PRO>
