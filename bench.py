@@ -483,6 +483,34 @@ def trace_breakdown2(tr, layers=28, stride=2048):
     return out
 
 
+def profile_batched(batch, prompt_len, n_steps, weights, cfg, dev=0):
+    """For ncu --profile-from-start off: n_steps decode steps of the batched
+    INT8 workload bracketed by cudaProfilerStart/Stop after the prompts and a
+    warm-up, so a launch list holds exactly those steps' kernels."""
+    import numpy as np
+    import torch
+
+    import vb200
+    import vbdist
+    import vbsynth
+    eng = vb200.Engine(cfg, device=dev).load(weights)
+    eng.quantize()
+    bt = vb200.Batch(eng, batch, prompt_len + n_steps + 16)
+    prompts = np.stack([vbsynth.prompt_ids(prompt_len, vbdist.sequence_seed(b), cfg["vocab_size"])
+                        for b in range(batch)])
+    nx = bt.prefill(prompts.T.copy())
+    nx = bt.decode(nx, 4)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    bt.decode(nx, n_steps)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    out = {"batch": batch, "prompt": prompt_len, "steps": n_steps, "graph_nodes": bt.graph_nodes()}
+    bt.close()
+    eng.close()
+    return out
+
+
 def profile_bs1(mode, prompt_len, n_tokens, weights, cfg, dev=0, path=-1):
     """For ncu --profile-from-start off: n_tokens greedy decode steps bracketed
     by cudaProfilerStart/Stop after the prompt and a warm-up, so a launch list
@@ -629,15 +657,16 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--no-extras", action="store_true", help="skip the bs1 lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    ap.add_argument("--only", choices=["gemv", "attn", "bs1", "prefill"], help="one workload (for profiling)")
+    ap.add_argument("--only", choices=["gemv", "attn", "bs1", "prefill", "batched"],
+                    help="one workload (for profiling)")
     ap.add_argument("--mode", choices=["f32", "int8"], default="int8", help="--only bs1: weights")
     ap.add_argument("--path", type=int, default=-1,
                     help="--only bs1: 1 per-op graph, 2 clustered step, -1 the engine's automatic choice")
     ap.add_argument("--trace", action="store_true",
                     help="--only bs1: per-phase trace of the clustered step (needs a VB_STEP_TRACE=1 build)")
     ap.add_argument("--profile", type=int, default=0,
-                    help="--only bs1: decode this many tokens inside cudaProfilerStart/Stop (for ncu "
-                         "--profile-from-start off) instead of the timed run")
+                    help="--only bs1 / batched: decode this many tokens (steps) inside "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off) instead of the timed run")
     ap.add_argument("--ctx", type=int, default=2048, help="--only attn: context length")
     ap.add_argument("--shape", default=None, help="--only gemv: one of q,k,v,o,gate,up,down,lm_head")
     args = ap.parse_args()
@@ -664,6 +693,13 @@ def main():
         r = run_bs1(args.mode, P, min(G, args.steps), w, cfg, dev=local_rank, path=args.path,
                     trace=args.trace)
         print(json.dumps({"bs1": r}), flush=True)
+        return 0
+    if args.only == "batched":
+        import vbsynth
+        cfg = vbsynth.qwen3_config()
+        w = vbsynth.make_weights(cfg, seed=WEIGHT_SEED)
+        print(json.dumps({"batched_profile": profile_batched(args.batch, args.prompt, max(1, args.profile), w, cfg,
+                                                             dev=local_rank)}), flush=True)
         return 0
     if args.only == "prefill":
         import vbsynth
