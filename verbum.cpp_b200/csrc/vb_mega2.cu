@@ -752,9 +752,11 @@ __device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, 
 }
 
 // Phase A step 4: attention over this CTA's 32-position chunks c = rank,
-// rank + 8, ...; local chunk j goes to warp j % 8, which keeps an online
-// softmax over its chunks (lane p scores position p with a column skew that
+// rank + 8, ...; each half of local chunk j (16 positions) goes to warp
+// (2 j + half) % 8, which keeps an online softmax over its half-chunks (lanes
+// p and p + 16 score position p over the two dim halves with a column skew that
 // keeps the K reads free of bank conflicts; for PV lane l owns dims 4l..4l+3).
+// Two warps per chunk measured INT8 1224 -> 1237 tok/s, f32 889 -> 906.
 // The warps' partials are then merged (warp order) into S.att_*.
 __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* ring, int l, int rank, int pos,
                                        int nchunks, int g, long long* prof) {
@@ -767,7 +769,12 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     f2 a0lo = 0ull, a0hi = 0ull, a1lo = 0ull, a1hi = 0ull;  // dims 4l..4l+3 of heads 0, 1
     bool ok = true;
-    for (int j = warp; j < njl && ok; j += kCW) {
+    // item it = 2 j + half: local chunk j's positions [16 half, 16 half + 16),
+    // so two warps share a chunk; lanes l and l + 16 score position l & 15
+    // over dims [0, 64) and [64, 128)
+    const int pl = lane & 15, dh = lane >> 4;
+    for (int it = warp; it < 2 * njl && ok; it += kCW) {
+        const int j = it >> 1, half = it & 1;
         const int c = rank + kCS * j;
         const int gk = g + 2 * j, gv = gk + 1;
         const long long tw = tclk();
@@ -779,13 +786,13 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         }
         const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(gk % kStages) * kStageBytes);
         const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(gv % kStages) * kStageBytes);
-        const int p0 = c * kChunk;
-        const bool valid = p0 + lane < n;
-        const float* krow = (p0 + lane == pos) ? S.kn : Kt + lane * 128;
+        const int p0 = c * kChunk + 16 * half;
+        const bool valid = p0 + pl < n;
+        const float* krow = (p0 + pl == pos) ? S.kn : Kt + (16 * half + pl) * 128;
         f2 s0a = 0ull, s0b = 0ull, s1a = 0ull, s1b = 0ull;
 #pragma unroll 4
-        for (int i = 0; i < 32; i++) {
-            const int c4 = 4 * ((i + lane) & 31);
+        for (int i = 0; i < 16; i++) {
+            const int c4 = 4 * (((i + pl) & 15) + 16 * dh);
             const float4 k4 = *reinterpret_cast<const float4*>(krow + c4);
             const float4 qa = *reinterpret_cast<const float4*>(&S.q[0][c4]);
             const float4 qb = *reinterpret_cast<const float4*>(&S.q[1][c4]);
@@ -795,7 +802,9 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
             s1a = f2fma(f2pack(qb.x, qb.y), klo, s1a);
             s1b = f2fma(f2pack(qb.z, qb.w), khi, s1b);
         }
-        const float s0 = f2sum(s0a) + f2sum(s0b), s1 = f2sum(s1a) + f2sum(s1b);
+        float s0 = f2sum(s0a) + f2sum(s0b), s1 = f2sum(s1a) + f2sum(s1b);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 16);  // the two dim halves
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 16);
         const float sc0 = valid ? s0 * inv_sqrt_d : -INFINITY;
         const float sc1 = valid ? s1 * inv_sqrt_d : -INFINITY;
         const float mn0 = fmaxf(m0, warp_max(sc0)), mn1 = fmaxf(m1, warp_max(sc1));
@@ -803,8 +812,9 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         const float f1 = (m1 == -INFINITY) ? 0.f : expf(m1 - mn1);
         const float e0 = valid ? expf(sc0 - mn0) : 0.f;
         const float e1 = valid ? expf(sc1 - mn1) : 0.f;
-        l0 = l0 * f0 + warp_sum(e0);
-        l1 = l1 * f1 + warp_sum(e1);
+        // (each position sits in two lanes: sum one copy)
+        l0 = l0 * f0 + warp_sum(dh ? 0.f : e0);
+        l1 = l1 * f1 + warp_sum(dh ? 0.f : e1);
         const f2 ff0 = f2pack(f0, f0), ff1 = f2pack(f1, f1);
         a0lo = f2mul(a0lo, ff0);
         a0hi = f2mul(a0hi, ff0);
@@ -812,10 +822,10 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         a1hi = f2mul(a1hi, ff1);
         m0 = mn0;
         m1 = mn1;
-        const int nv = min(kChunk, n - p0);
+        const int nv = min(16, n - p0);
 #pragma unroll 4
-        for (int pp = 0; pp < kChunk; pp++) {
-            const float* vrow = (p0 + pp == pos) ? S.vn : Vt + pp * 128;
+        for (int pp = 0; pp < 16; pp++) {
+            const float* vrow = (p0 + pp == pos) ? S.vn : Vt + (16 * half + pp) * 128;
             float4 v4 = *reinterpret_cast<const float4*>(vrow + 4 * lane);
             if (pp >= nv) v4 = make_float4(0.f, 0.f, 0.f, 0.f);  // stale rows past the context
             const float w0 = __shfl_sync(0xffffffffu, e0, pp), w1 = __shfl_sync(0xffffffffu, e1, pp);
@@ -828,8 +838,8 @@ __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* rin
         }
         __syncwarp();
         if (lane == 0) {
-            mbar_arrive(smem_addr(&S.empty[gk % kStages]), (unsigned)kCW);
-            mbar_arrive(smem_addr(&S.empty[gv % kStages]), (unsigned)kCW);
+            mbar_arrive(smem_addr(&S.empty[gk % kStages]), (unsigned)(kCW / 2));
+            mbar_arrive(smem_addr(&S.empty[gv % kStages]), (unsigned)(kCW / 2));
         }
     }
     {
