@@ -14,7 +14,7 @@ Both carry dropin/model_shim.cpp, an extern "C" face for these tests.
 CPU tests: both libraries load (their undefined symbols resolve against
 libverbum_b200.so) and to_cuda() without a device throws the reference's
 "no CUDA device found".  GPU tests: Model(dir) -> [quantize()] -> reset_cache
--> to_cuda -> step x N -> Sampler, against the oracle at the north star's bars
+-> to_cuda -> step x N -> Sampler, against the oracle at the parity bars
 (f32 logits <= 1e-3, INT8 <= 1e-2, greedy tokens identical), and the
 reference's own Sampler picking from both.
 """

@@ -7,7 +7,7 @@ decode steps through vb_batch_step with full logits.  For three sequences
 (first, middle, last) every step's [151936] logits are compared with the
 oracle -- the reference's Model::step restated in C, fed the same prompt (by
 its layer-major prefill, bit-identical to token-by-token steps) and the same
-tokens -- at the north star's INT8 bar, max |diff| <= 1e-2, and every greedy
+tokens -- at the INT8 parity bar, max |diff| <= 1e-2, and every greedy
 pick must agree.  Random-init greedy streams collapse onto an attractor token
 within a few steps, so the per-step logits, not the tokens, are the real gate.
 
