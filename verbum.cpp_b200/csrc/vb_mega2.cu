@@ -756,7 +756,8 @@ __device__ __noinline__ bool qkv_finish(const M2Params& p, S2& S, int l, int k, 
 // (2 j + half) % 8, which keeps an online softmax over its half-chunks (lanes
 // p and p + 16 score position p over the two dim halves with a column skew that
 // keeps the K reads free of bank conflicts; for PV lane l owns dims 4l..4l+3).
-// Two warps per chunk measured INT8 1224 -> 1237 tok/s, f32 889 -> 906.
+// Two warps per chunk measured INT8 1224 -> 1237 tok/s, f32 889 -> 906; four
+// (8 positions each) INT8 1241 -> 1207.
 // The warps' partials are then merged (warp order) into S.att_*.
 __device__ __noinline__ bool attention(const M2Params& p, S2& S, const char* ring, int l, int rank, int pos,
                                        int nchunks, int g, long long* prof) {
